@@ -1,0 +1,52 @@
+// Python bindings of the kore_b200 native extension (_C).
+#include <torch/extension.h>
+
+namespace kore {
+void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn,
+               double alpha, bool accumulate, const c10::optional<at::Tensor>& residual,
+               int64_t max_ctas);
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
+                 const c10::optional<at::Tensor>& rstd, double eps);
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                 const at::Tensor& rstd, const c10::optional<at::Tensor>& dres, at::Tensor& dx,
+                 const c10::optional<at::Tensor>& dw);
+void qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw,
+                      const at::Tensor& pos, const at::Tensor& cos_t, const at::Tensor& sin_t,
+                      at::Tensor& out, const c10::optional<at::Tensor>& rstd, int64_t Hq,
+                      int64_t Hkv, double eps);
+void qk_norm_rope_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& qw,
+                      const at::Tensor& kw, const at::Tensor& pos, const at::Tensor& cos_t,
+                      const at::Tensor& sin_t, at::Tensor& dqkv, at::Tensor& dqw, at::Tensor& dkw,
+                      int64_t Hq, int64_t Hkv, double eps);
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& out);
+void swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu, at::Tensor& dgu);
+void embed_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out);
+void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor& dtable);
+void logprob_fwd_bwd(at::Tensor& logits, const c10::optional<at::Tensor>& targets,
+                     double inv_temp, const c10::optional<at::Tensor>& logp,
+                     const c10::optional<at::Tensor>& entropy, const c10::optional<at::Tensor>& lse,
+                     const c10::optional<at::Tensor>& coef, bool write_grad);
+void sumsq_accumulate(const at::Tensor& g, at::Tensor& out);
+void adamw_step(at::Tensor& p, const c10::optional<at::Tensor>& master, const at::Tensor& g,
+                at::Tensor& m, at::Tensor& v, double lr, double b1, double b2, double eps,
+                double wd, int64_t step, double grad_scale, const c10::optional<at::Tensor>& sumsq,
+                double max_norm, int64_t seed);
+int read_and_clear_device_error();
+}  // namespace kore
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "kore_b200 sm_100a kernels";
+  m.def("gemm_bf16", &kore::gemm_bf16, "tcgen05 bf16 GEMM");
+  m.def("rmsnorm_fwd", &kore::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &kore::rmsnorm_bwd);
+  m.def("qk_norm_rope_fwd", &kore::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &kore::qk_norm_rope_bwd);
+  m.def("swiglu_fwd", &kore::swiglu_fwd);
+  m.def("swiglu_bwd", &kore::swiglu_bwd);
+  m.def("embed_fwd", &kore::embed_fwd);
+  m.def("embed_bwd", &kore::embed_bwd);
+  m.def("logprob_fwd_bwd", &kore::logprob_fwd_bwd);
+  m.def("sumsq_accumulate", &kore::sumsq_accumulate);
+  m.def("adamw_step", &kore::adamw_step);
+  m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
+}

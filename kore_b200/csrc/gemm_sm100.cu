@@ -1,0 +1,386 @@
+// Persistent warp-specialized bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores (tcgen05.mma, accumulators in TMEM, operands staged by TMA).
+//
+//   C[M,N] (=|+=) alpha * op(A)[M,K] . op(B)[N,K]^T  (+ R[M,N])
+//
+// A is either K-major ([M,K] row-major) or MN-major ([K,M] row-major); the same
+// for B ([N,K] or [K,N]). The three combinations cover a linear layer's
+// forward (y = x W^T), data gradient (dx = dy W) and weight gradient
+// (dW = dy^T x) without any transpose copies: UMMA reads MN-major operands
+// straight from the 128B-swizzled tiles TMA writes.
+//
+// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  epilogue: tcgen05.ld -> fp32 math -> bf16/fp32 -> smem -> TMA store
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the epilogue
+// of tile i overlaps the main loop of tile i+1. Every wait is bounded.
+//
+// Reference parity: the reference runs every linear layer through
+// nn.Linear/cuBLAS inside HF transformers (kore/policy/sft.py:288-293,
+// kore/policy/grpo.py:2017-2018); this kernel is the replacement hot path.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace kore {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+constexpr int kEpiWarps = 4;
+constexpr int kStageBytesC = 32 * 128;  // one epilogue staging buffer: 32 rows x 128 B
+
+struct Params {
+  int M, N, K;
+  float alpha;
+  int accumulate;       // C += result (reads old C)
+  int out_f32;          // C is fp32 (else bf16)
+  const void* C_read;   // C base pointer for accumulate reads
+  int ldc;              // C row stride (elements)
+  const __nv_bfloat16* R;  // optional residual (bf16, row stride ldr)
+  int ldr;
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 2 * kStageBytesC;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;  // + barriers + alignment slack
+};
+
+KORE_DEV void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
+  constexpr int G = 8;
+  int per_group = G * num_n;
+  int g = t / per_group;
+  int first_m = g * G;
+  int gsize = min(num_m - first_m, G);
+  int r = t - g * per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmC, Params p) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 2 * BN);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        const int m0 = tm * BM, n0 = tn * BN;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+          uint8_t* sA = smem + stage * S::STAGE_BYTES;
+          uint8_t* sB = sA + S::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], S::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sA + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d(sB, &tmB, &full_bar[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * S::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad = A_MN ? make_sw128_desc(a_addr + k * 2048, 8192, 1024)
+                               : make_sw128_desc(a_addr + k * 32, 16, 1024);
+            uint64_t bd = B_MN ? make_sw128_desc(b_addr + k * 2048, 8192, 1024)
+                               : make_sw128_desc(b_addr + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+        umma_commit(&tfull_bar[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int lane = threadIdx.x & 31;
+    uint8_t* stage_buf = smem + S::EPI_OFF + (warp - 2) * 2 * kStageBytesC;
+    int buf = 0;
+    int it = 0;
+    const int CH = p.out_f32 ? 32 : 64;  // output columns per 128-byte staging row
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      const int m0 = tm * BM, n0 = tn * BN;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      for (int c0 = 0; c0 < BN; c0 += CH) {
+        if (n0 + c0 >= p.N) break;
+        float v[64];
+        {
+          uint32_t r[32];
+          tmem_ld32(t_row + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+          if (!p.out_f32) {
+            tmem_ld32(t_row + c0 + 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]) * p.alpha;
+          }
+        }
+        const bool row_ok = row < p.M;
+        // optional accumulate / residual (row-contiguous per thread)
+        if (row_ok && (p.accumulate || p.R != nullptr)) {
+          const int ncols = min(CH, p.N - (n0 + c0));
+          if (p.R != nullptr) {
+            const __nv_bfloat16* rp = p.R + (size_t)row * p.ldr + n0 + c0;
+#pragma unroll
+            for (int j = 0; j < 64; j += 8) {
+              if (j >= ncols) break;
+              uint4 u = *reinterpret_cast<const uint4*>(rp + j);
+              const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[j + e] += __bfloat162float(h[e]);
+            }
+          }
+          if (p.accumulate) {
+            if (p.out_f32) {
+              const float* cp = reinterpret_cast<const float*>(p.C_read) + (size_t)row * p.ldc + n0 + c0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                if (j >= ncols) break;
+                float4 u = *reinterpret_cast<const float4*>(cp + j);
+                v[j] += u.x; v[j + 1] += u.y; v[j + 2] += u.z; v[j + 3] += u.w;
+              }
+            } else {
+              const __nv_bfloat16* cp =
+                  reinterpret_cast<const __nv_bfloat16*>(p.C_read) + (size_t)row * p.ldc + n0 + c0;
+#pragma unroll
+              for (int j = 0; j < 64; j += 8) {
+                if (j >= ncols) break;
+                uint4 u = *reinterpret_cast<const uint4*>(cp + j);
+                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[j + e] += __bfloat162float(h[e]);
+              }
+            }
+          }
+        }
+        // make sure the TMA store that last used this staging buffer has read it
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        uint8_t* sb = stage_buf + buf * kStageBytesC + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 u;
+          if (p.out_f32) {
+            u.x = __float_as_uint(v[4 * j]);
+            u.y = __float_as_uint(v[4 * j + 1]);
+            u.z = __float_as_uint(v[4 * j + 2]);
+            u.w = __float_as_uint(v[4 * j + 3]);
+          } else {
+            u.x = pack_bf16(v[8 * j], v[8 * j + 1]);
+            u.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+          }
+          *reinterpret_cast<uint4*>(sb + ((j ^ (lane & 7)) * 16)) = u;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, stage_buf + buf * kStageBytesC, n0 + c0, m0 + q * 32);
+          tma_store_commit();
+        }
+        buf ^= 1;
+      }
+      // accumulator fully read: hand it back to the MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, 2 * BN);
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
+            int grid, cudaStream_t stream) {
+  auto k = gemm_kernel<BN, STAGES, A_MN, B_MN>;
+  constexpr int smem = Smem<BN, STAGES>::TOTAL;
+  static bool attr_set = false;  // per template instance; device attributes are per-function
+  if (!attr_set) {
+    check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "cudaFuncSetAttribute(gemm smem)");
+    attr_set = true;
+  }
+  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, p);
+  check_cuda(cudaGetLastError(), "gemm launch");
+}
+
+}  // namespace gemm
+
+// out = alpha * op(a) @ op(b)^T (+ residual) (+ out if accumulate)
+//  a: [M,K] if !a_mn else [K,M];  b: [N,K] if !b_mn else [K,N];  out: [M,N] (row stride may exceed N)
+void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn,
+               double alpha, bool accumulate, const c10::optional<at::Tensor>& residual,
+               int64_t max_ctas) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm: tensors must be CUDA");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "gemm: inputs must be bf16");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm: 2-D tensors expected");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1,
+              "gemm: inner dimension must be contiguous");
+  const bool f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || out.scalar_type() == at::kBFloat16, "gemm: out must be bf16 or fp32");
+  const int M = a_mn ? a.size(1) : a.size(0);
+  const int K = a_mn ? a.size(0) : a.size(1);
+  const int N = b_mn ? b.size(1) : b.size(0);
+  const int Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm: K mismatch");
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm: out shape mismatch");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "gemm: M, N, K must be multiples of 8");
+  if (M == 0 || N == 0) return;
+  c10::cuda::CUDAGuard guard(a.device());
+  if (K == 0) {
+    if (!accumulate) out.zero_();
+    if (residual) out.add_(*residual);
+    return;
+  }
+  gemm::Params p;
+  p.M = M; p.N = N; p.K = K;
+  p.alpha = (float)alpha;
+  p.accumulate = accumulate ? 1 : 0;
+  p.out_f32 = f32 ? 1 : 0;
+  p.C_read = out.data_ptr();
+  p.ldc = out.stride(0);
+  p.R = nullptr;
+  p.ldr = 0;
+  if (residual) {
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 &&
+                    residual->size(0) == M && residual->size(1) == N,
+                "gemm: residual must be bf16 [M,N] with contiguous rows");
+    p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+  }
+  const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  const int BN = use256 ? 256 : 128;
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = a_mn ? make_tmap_2d(a.data_ptr(), bf, 2, M, K, a.stride(0), 64, 64)
+                        : make_tmap_2d(a.data_ptr(), bf, 2, K, M, a.stride(0), 64, 128);
+  CUtensorMap tb = b_mn ? make_tmap_2d(b.data_ptr(), bf, 2, N, K, b.stride(0), 64, 64)
+                        : make_tmap_2d(b.data_ptr(), bf, 2, K, N, b.stride(0), 64, BN);
+  CUtensorMap tc = f32 ? make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M,
+                                      out.stride(0), 32, 32)
+                       : make_tmap_2d(out.data_ptr(), bf, 2, N, M, out.stride(0), 64, 32);
+  const int tiles = ((M + 127) / 128) * ((N + BN - 1) / BN);
+  int grid = std::min(tiles, num_sms(a.get_device()));
+  if (max_ctas > 0) grid = std::min<int>(grid, (int)max_ctas);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+#define KORE_GEMM_DISPATCH(BN_, ST_)                                              \
+  if (!a_mn && !b_mn) gemm::launch<BN_, ST_, false, false>(ta, tb, tc, p, grid, st); \
+  else if (!a_mn && b_mn) gemm::launch<BN_, ST_, false, true>(ta, tb, tc, p, grid, st); \
+  else if (a_mn && !b_mn) gemm::launch<BN_, ST_, true, false>(ta, tb, tc, p, grid, st); \
+  else gemm::launch<BN_, ST_, true, true>(ta, tb, tc, p, grid, st);
+  if (use256) {
+    KORE_GEMM_DISPATCH(256, 4)
+  } else {
+    KORE_GEMM_DISPATCH(128, 6)
+  }
+#undef KORE_GEMM_DISPATCH
+}
+
+}  // namespace kore

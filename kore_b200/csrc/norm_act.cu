@@ -1,0 +1,528 @@
+// Memory-bound fused kernels of the Qwen3 decoder for sm_100a:
+//   * RMSNorm forward / backward (+ fused residual-gradient add, dW reduction)
+//   * per-head q_norm/k_norm RMSNorm fused with rotary embedding, fwd / bwd
+//   * SwiGLU (silu(gate) * up) forward / backward
+//   * token embedding gather / gradient scatter-add
+// All math is fp32 in registers; bf16 in HBM; 16-byte vector accesses.
+//
+// Reference parity: HF Qwen3RMSNorm / apply_rotary_pos_emb / SiLU-gated MLP
+// as used by the reference's trainers (kore/policy/configs.py:550-567 picks the
+// Qwen3 decoder layer; the math itself lives in transformers).
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace kore {
+
+namespace {
+
+KORE_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffff, v, o);
+  return v;
+}
+
+template <int NT>
+KORE_DEV float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x / 32, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) t += red[i];
+  return t;
+}
+
+KORE_DEV void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+KORE_DEV void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  uint4 u;
+  u.x = pack_bf16(f[0], f[1]);
+  u.y = pack_bf16(f[2], f[3]);
+  u.z = pack_bf16(f[4], f[5]);
+  u.w = pack_bf16(f[6], f[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+constexpr int kNormThreads = 128;
+constexpr int kMaxVecPerThread = 8;  // H <= 128 * 8 * 8 = 8192
+
+// ---------------------------------------------------------------- RMSNorm fwd
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+    __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int rows, int H, float eps) {
+  __shared__ float red[kNormThreads / 32];
+  const int nvec = H / 8;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const __nv_bfloat16* xr = x + (size_t)r * H;
+    float v[kMaxVecPerThread][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxVecPerThread; ++i) {
+      int j = threadIdx.x + i * kNormThreads;
+      if (j < nvec) {
+        load8(xr + j * 8, v[i]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+      }
+    }
+    ss = block_sum<kNormThreads>(ss, red);
+    const float rs = rsqrtf(ss / H + eps);
+    if (rstd_out && threadIdx.x == 0) rstd_out[r] = rs;
+#pragma unroll
+    for (int i = 0; i < kMaxVecPerThread; ++i) {
+      int j = threadIdx.x + i * kNormThreads;
+      if (j < nvec) {
+        float wv[8];
+        load8(w + j * 8, wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[i][e] = v[i][e] * rs * wv[e];
+        store8(y + (size_t)r * H + j * 8, v[i]);
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- RMSNorm bwd
+// dx = rstd * (w*dy - xhat * mean(xhat*w*dy)) (+ dres);  dw += sum_rows dy*xhat
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
+    const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+    const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
+    const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
+    float* __restrict__ dw, int rows, int H) {
+  __shared__ float red[kNormThreads / 32];
+  const int nvec = H / 8;
+  float dwacc[kMaxVecPerThread][8];
+#pragma unroll
+  for (int i = 0; i < kMaxVecPerThread; ++i)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) dwacc[i][e] = 0.f;
+  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float rs = rstd[r];
+    float xv[kMaxVecPerThread][8], g[kMaxVecPerThread][8];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxVecPerThread; ++i) {
+      int j = threadIdx.x + i * kNormThreads;
+      if (j < nvec) {
+        float wv[8];
+        load8(x + (size_t)r * H + j * 8, xv[i]);
+        load8(dy + (size_t)r * H + j * 8, g[i]);
+        load8(w + j * 8, wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float xh = xv[i][e] * rs;
+          dwacc[i][e] += g[i][e] * xh;
+          g[i][e] *= wv[e];
+          dot += g[i][e] * xh;
+          xv[i][e] = xh;
+        }
+      }
+    }
+    dot = block_sum<kNormThreads>(dot, red) / H;
+#pragma unroll
+    for (int i = 0; i < kMaxVecPerThread; ++i) {
+      int j = threadIdx.x + i * kNormThreads;
+      if (j < nvec) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = rs * (g[i][e] - xv[i][e] * dot);
+        if (dres) {
+          float d[8];
+          load8(dres + (size_t)r * H + j * 8, d);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] += d[e];
+        }
+        store8(dx + (size_t)r * H + j * 8, o);
+      }
+    }
+  }
+  if (dw) {
+#pragma unroll
+    for (int i = 0; i < kMaxVecPerThread; ++i) {
+      int j = threadIdx.x + i * kNormThreads;
+      if (j < nvec)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) atomicAdd(dw + j * 8 + e, dwacc[i][e]);
+    }
+  }
+}
+
+// ------------------------------------------- q/k per-head RMSNorm + RoPE (fwd)
+// qkv: [T, (Hq + 2*Hkv) * D] raw projections. out: [T, (Hq + Hkv) * D] normed+rotated q,k.
+// One warp per (token, head); D == 128 (4 elements per lane; lane l pairs with l^16).
+// cos/sin tables: [max_pos, D/2] fp32.
+__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
+                                        const __nv_bfloat16* __restrict__ qw,
+                                        const __nv_bfloat16* __restrict__ kw,
+                                        const int* __restrict__ pos, const float* __restrict__ cos_t,
+                                        const float* __restrict__ sin_t,
+                                        __nv_bfloat16* __restrict__ out, float* __restrict__ rstd,
+                                        int T, int Hq, int Hkv, float eps) {
+  constexpr int D = 128;
+  const int lane = threadIdx.x & 31;
+  const int heads = Hq + Hkv;
+  const long gw = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (gw >= (long)T * heads) return;
+  const int t = gw / heads, h = gw % heads;
+  const int in_stride = (Hq + 2 * Hkv) * D;
+  const __nv_bfloat16* src = qkv + (size_t)t * in_stride + h * D + lane * 4;
+  float v[4];
+  {
+    uint2 u = *reinterpret_cast<const uint2*>(src);
+    float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.x));
+    float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.y));
+    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  }
+  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / D + eps);
+  if (rstd && lane == 0) rstd[(size_t)t * heads + h] = rs;
+  const __nv_bfloat16* wt = (h < Hq ? qw : kw) + lane * 4;
+  float n[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) n[e] = v[e] * rs * __bfloat162float(wt[e]);
+  // rotate_half: x1 = n[:64], x2 = n[64:]; out1 = x1*c - x2*s; out2 = x2*c + x1*s
+  float partner[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) partner[e] = __shfl_xor_sync(0xffffffff, n[e], 16);
+  const int p = pos[t];
+  const int fi = (lane & 15) * 4;
+  float o[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    float c = cos_t[(size_t)p * (D / 2) + fi + e];
+    float s = sin_t[(size_t)p * (D / 2) + fi + e];
+    o[e] = lane < 16 ? n[e] * c - partner[e] * s : n[e] * c + partner[e] * s;
+  }
+  uint2 u;
+  u.x = pack_bf16(o[0], o[1]);
+  u.y = pack_bf16(o[2], o[3]);
+  *reinterpret_cast<uint2*>(out + (size_t)t * heads * D + h * D + lane * 4) = u;
+}
+
+// --------------------------------------------------- q/k norm + RoPE (bwd)
+// dout: [T, (Hq+Hkv)*D] grads of the rotated q,k. Writes dqkv[:, :(Hq+Hkv)*D]
+// (row stride (Hq+2Hkv)*D) and accumulates dqw/dkw (fp32, [D]).
+__global__ void qk_norm_rope_bwd_kernel(const __nv_bfloat16* __restrict__ dout,
+                                        const __nv_bfloat16* __restrict__ qkv,
+                                        const __nv_bfloat16* __restrict__ qw,
+                                        const __nv_bfloat16* __restrict__ kw,
+                                        const int* __restrict__ pos, const float* __restrict__ cos_t,
+                                        const float* __restrict__ sin_t,
+                                        __nv_bfloat16* __restrict__ dqkv, float* __restrict__ dqw,
+                                        float* __restrict__ dkw, int T, int Hq, int Hkv,
+                                        float eps) {
+  constexpr int D = 128;
+  const int lane = threadIdx.x & 31;
+  const int heads = Hq + Hkv;
+  const int in_stride = (Hq + 2 * Hkv) * D;
+  float accq[4] = {0, 0, 0, 0}, acck[4] = {0, 0, 0, 0};
+  const long nwarps_total = (long)gridDim.x * (blockDim.x / 32);
+  for (long gw = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32; gw < (long)T * heads;
+       gw += nwarps_total) {
+    const int t = gw / heads, h = gw % heads;
+    float g[4], v[4];
+    {
+      uint2 u = *reinterpret_cast<const uint2*>(dout + (size_t)t * heads * D + h * D + lane * 4);
+      float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.x));
+      float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.y));
+      g[0] = a.x; g[1] = a.y; g[2] = b.x; g[3] = b.y;
+      uint2 w2 = *reinterpret_cast<const uint2*>(qkv + (size_t)t * in_stride + h * D + lane * 4);
+      a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w2.x));
+      b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&w2.y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    }
+    // inverse rotation of the gradient: dn1 = g1*c + g2*s ; dn2 = g2*c - g1*s
+    float gp[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) gp[e] = __shfl_xor_sync(0xffffffff, g[e], 16);
+    const int p = pos[t];
+    const int fi = (lane & 15) * 4;
+    float dn[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float c = cos_t[(size_t)p * (D / 2) + fi + e];
+      float s = sin_t[(size_t)p * (D / 2) + fi + e];
+      dn[e] = lane < 16 ? g[e] * c + gp[e] * s : g[e] * c - gp[e] * s;
+    }
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / D + eps);
+    const __nv_bfloat16* wt = (h < Hq ? qw : kw) + lane * 4;
+    float gw_[4], xh[4], dot = 0.f;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      xh[e] = v[e] * rs;
+      float wv = __bfloat162float(wt[e]);
+      if (h < Hq) accq[e] += dn[e] * xh[e]; else acck[e] += dn[e] * xh[e];
+      gw_[e] = dn[e] * wv;
+      dot += gw_[e] * xh[e];
+    }
+    dot = warp_sum(dot) / D;
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = rs * (gw_[e] - xh[e] * dot);
+    uint2 u;
+    u.x = pack_bf16(o[0], o[1]);
+    u.y = pack_bf16(o[2], o[3]);
+    *reinterpret_cast<uint2*>(dqkv + (size_t)t * in_stride + h * D + lane * 4) = u;
+  }
+  // reduce weight grads within the block, then one atomic per element
+  __shared__ float sq[8][128], sk[8][128];
+  const int w = threadIdx.x / 32;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    sq[w][lane * 4 + e] = accq[e];
+    sk[w][lane * 4 + e] = acck[e];
+  }
+  __syncthreads();
+  if (threadIdx.x < 128) {
+    float a = 0.f, b = 0.f;
+    for (int i = 0; i < (int)(blockDim.x / 32); ++i) {
+      a += sq[i][threadIdx.x];
+      b += sk[i][threadIdx.x];
+    }
+    atomicAdd(dqw + threadIdx.x, a);
+    atomicAdd(dkw + threadIdx.x, b);
+  }
+}
+
+// ---------------------------------------------------------------- SwiGLU
+// gu: [T, 2F] = [gate | up]; out[T, F] = silu(gate) * up
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, __nv_bfloat16* __restrict__ out,
+                                  long T, int F, int ld_in) {
+  const long nvec = T * (F / 8);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long)gridDim.x * blockDim.x) {
+    const long t = i / (F / 8);
+    const int j = (i % (F / 8)) * 8;
+    float g[8], u[8], o[8];
+    load8(gu + t * ld_in + j, g);
+    load8(gu + t * ld_in + F + j, u);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = g[e] / (1.f + __expf(-g[e])) * u[e];
+    store8(out + t * F + j, o);
+  }
+}
+
+// dgu[:, :F] = dout * up * dsilu(gate); dgu[:, F:] = dout * silu(gate). dgu may alias gu.
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* gu,
+                                  __nv_bfloat16* dgu, long T, int F, int ld) {
+  const long nvec = T * (F / 8);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long)gridDim.x * blockDim.x) {
+    const long t = i / (F / 8);
+    const int j = (i % (F / 8)) * 8;
+    float g[8], u[8], d[8], dg[8], du[8];
+    load8(gu + t * ld + j, g);
+    load8(gu + t * ld + F + j, u);
+    load8(dout + t * F + j, d);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float s = 1.f / (1.f + __expf(-g[e]));
+      float si = g[e] * s;
+      du[e] = d[e] * si;
+      dg[e] = d[e] * u[e] * (s + si * (1.f - s));
+    }
+    store8(dgu + t * ld + j, dg);
+    store8(dgu + t * ld + F + j, du);
+  }
+}
+
+// ---------------------------------------------------------------- embedding
+__global__ void embed_fwd_kernel(const long* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
+                                 __nv_bfloat16* __restrict__ out, long T, int H) {
+  const int nvec = H / 8;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < T * nvec; i += (long)gridDim.x * blockDim.x) {
+    const long t = i / nvec;
+    const int j = (i % nvec) * 8;
+    *reinterpret_cast<uint4*>(out + t * H + j) =
+        *reinterpret_cast<const uint4*>(table + ids[t] * (long)H + j);
+  }
+}
+KORE_DEV void atomic_add8(float* dst, const float (&g)[8]) {
+#pragma unroll
+  for (int e = 0; e < 8; ++e) atomicAdd(dst + e, g[e]);
+}
+KORE_DEV void atomic_add8(__nv_bfloat16* dst, const float (&g)[8]) {
+  __nv_bfloat162* d2 = reinterpret_cast<__nv_bfloat162*>(dst);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) atomicAdd(d2 + e, __floats2bfloat162_rn(g[2 * e], g[2 * e + 1]));
+}
+template <typename G>
+__global__ void embed_bwd_kernel(const long* __restrict__ ids, const __nv_bfloat16* __restrict__ dy,
+                                 G* __restrict__ dtable, long T, int H) {
+  const int nvec = H / 8;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < T * nvec; i += (long)gridDim.x * blockDim.x) {
+    const long t = i / nvec;
+    const int j = (i % nvec) * 8;
+    float g[8];
+    load8(dy + t * H + j, g);
+    atomic_add8(dtable + ids[t] * (long)H + j, g);
+  }
+}
+
+int grid_for(long work, int threads, int dev) {
+  long b = (work + threads - 1) / threads;
+  long cap = (long)num_sms(dev) * 16;
+  return (int)std::max<long>(1, std::min(b, cap));
+}
+
+void check_bf16_2d(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.is_contiguous(), name,
+              " must be a contiguous CUDA bf16 tensor");
+}
+
+}  // namespace
+
+// ============================================================== host wrappers
+void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
+                 const c10::optional<at::Tensor>& rstd, double eps) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(w, "w");
+  check_bf16_2d(y, "y");
+  const int H = x.size(-1);
+  const long rows = x.numel() / H;
+  TORCH_CHECK(H % 8 == 0 && H <= kNormThreads * kMaxVecPerThread * 8, "rmsnorm: unsupported H");
+  if (rows == 0) return;
+  c10::cuda::CUDAGuard g(x.device());
+  int grid = (int)std::min<long>(rows, (long)num_sms(x.get_device()) * 8);
+  rmsnorm_fwd_kernel<<<grid, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
+      (__nv_bfloat16*)y.data_ptr(), rstd ? rstd->data_ptr<float>() : nullptr, rows, H, (float)eps);
+  check_cuda(cudaGetLastError(), "rmsnorm_fwd");
+}
+
+void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                 const at::Tensor& rstd, const c10::optional<at::Tensor>& dres, at::Tensor& dx,
+                 const c10::optional<at::Tensor>& dw) {
+  check_bf16_2d(dy, "dy");
+  check_bf16_2d(x, "x");
+  check_bf16_2d(dx, "dx");
+  const int H = x.size(-1);
+  const long rows = x.numel() / H;
+  if (rows == 0) return;
+  if (dw) TORCH_CHECK(dw->scalar_type() == at::kFloat && dw->numel() == H, "dw must be fp32 [H]");
+  c10::cuda::CUDAGuard g(x.device());
+  int grid = (int)std::min<long>(rows, (long)num_sms(x.get_device()) * 4);
+  rmsnorm_bwd_kernel<<<grid, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(),
+      (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(),
+      dres ? (const __nv_bfloat16*)dres->data_ptr() : nullptr, (__nv_bfloat16*)dx.data_ptr(),
+      dw ? dw->data_ptr<float>() : nullptr, rows, H);
+  check_cuda(cudaGetLastError(), "rmsnorm_bwd");
+}
+
+void qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Tensor& kw,
+                      const at::Tensor& pos, const at::Tensor& cos_t, const at::Tensor& sin_t,
+                      at::Tensor& out, const c10::optional<at::Tensor>& rstd, int64_t Hq,
+                      int64_t Hkv, double eps) {
+  check_bf16_2d(qkv, "qkv");
+  const long T = qkv.size(0);
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * 128, "qk_norm_rope: head_dim must be 128");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && pos.numel() == T, "pos must be int32 [T]");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(qkv.device());
+  const long warps = T * (Hq + Hkv);
+  const int threads = 256;
+  const int grid = (int)((warps * 32 + threads - 1) / threads);
+  qk_norm_rope_fwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)qkv.data_ptr(), (const __nv_bfloat16*)qw.data_ptr(),
+      (const __nv_bfloat16*)kw.data_ptr(), pos.data_ptr<int>(), cos_t.data_ptr<float>(),
+      sin_t.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(),
+      rstd ? rstd->data_ptr<float>() : nullptr, T, Hq, Hkv, (float)eps);
+  check_cuda(cudaGetLastError(), "qk_norm_rope_fwd");
+}
+
+void qk_norm_rope_bwd(const at::Tensor& dout, const at::Tensor& qkv, const at::Tensor& qw,
+                      const at::Tensor& kw, const at::Tensor& pos, const at::Tensor& cos_t,
+                      const at::Tensor& sin_t, at::Tensor& dqkv, at::Tensor& dqw, at::Tensor& dkw,
+                      int64_t Hq, int64_t Hkv, double eps) {
+  const long T = qkv.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(dqw.scalar_type() == at::kFloat && dkw.scalar_type() == at::kFloat,
+              "dqw/dkw must be fp32");
+  c10::cuda::CUDAGuard g(qkv.device());
+  const int threads = 256;
+  const int grid = grid_for(T * (Hq + Hkv) * 32, threads, qkv.get_device());
+  qk_norm_rope_bwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)dout.data_ptr(), (const __nv_bfloat16*)qkv.data_ptr(),
+      (const __nv_bfloat16*)qw.data_ptr(), (const __nv_bfloat16*)kw.data_ptr(),
+      pos.data_ptr<int>(), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(),
+      (__nv_bfloat16*)dqkv.data_ptr(), dqw.data_ptr<float>(), dkw.data_ptr<float>(), T, Hq, Hkv,
+      (float)eps);
+  check_cuda(cudaGetLastError(), "qk_norm_rope_bwd");
+}
+
+void swiglu_fwd(const at::Tensor& gu, at::Tensor& out) {
+  const long T = gu.size(0);
+  const int F = gu.size(1) / 2;
+  TORCH_CHECK(F % 8 == 0, "swiglu: F must be a multiple of 8");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(gu.device());
+  swiglu_fwd_kernel<<<grid_for(T * F / 8, 256, gu.get_device()), 256, 0,
+                      at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)gu.data_ptr(), (__nv_bfloat16*)out.data_ptr(), T, F, gu.stride(0));
+  check_cuda(cudaGetLastError(), "swiglu_fwd");
+}
+
+void swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu, at::Tensor& dgu) {
+  const long T = gu.size(0);
+  const int F = gu.size(1) / 2;
+  if (T == 0) return;
+  TORCH_CHECK(gu.stride(0) == dgu.stride(0), "swiglu_bwd: gu/dgu stride mismatch");
+  c10::cuda::CUDAGuard g(gu.device());
+  swiglu_bwd_kernel<<<grid_for(T * F / 8, 256, gu.get_device()), 256, 0,
+                      at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)dout.data_ptr(), (const __nv_bfloat16*)gu.data_ptr(),
+      (__nv_bfloat16*)dgu.data_ptr(), T, F, gu.stride(0));
+  check_cuda(cudaGetLastError(), "swiglu_bwd");
+}
+
+void embed_fwd(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong, "ids must be int64");
+  const long T = ids.numel();
+  const int H = table.size(1);
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(table.device());
+  embed_fwd_kernel<<<grid_for(T * H / 8, 256, table.get_device()), 256, 0,
+                     at::cuda::getCurrentCUDAStream()>>>(
+      ids.data_ptr<long>(), (const __nv_bfloat16*)table.data_ptr(), (__nv_bfloat16*)out.data_ptr(),
+      T, H);
+  check_cuda(cudaGetLastError(), "embed_fwd");
+}
+
+void embed_bwd(const at::Tensor& ids, const at::Tensor& dy, at::Tensor& dtable) {
+  const long T = ids.numel();
+  const int H = dy.size(1);
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(dy.device());
+  const int grid = grid_for(T * H / 8, 256, dy.get_device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (dtable.scalar_type() == at::kFloat)
+    embed_bwd_kernel<float><<<grid, 256, 0, st>>>(ids.data_ptr<long>(),
+                                                  (const __nv_bfloat16*)dy.data_ptr(),
+                                                  dtable.data_ptr<float>(), T, H);
+  else if (dtable.scalar_type() == at::kBFloat16)
+    embed_bwd_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+        ids.data_ptr<long>(), (const __nv_bfloat16*)dy.data_ptr(),
+        (__nv_bfloat16*)dtable.data_ptr(), T, H);
+  else
+    TORCH_CHECK(false, "embed_bwd: dtable must be fp32 or bf16");
+  check_cuda(cudaGetLastError(), "embed_bwd");
+}
+
+}  // namespace kore
