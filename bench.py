@@ -1,0 +1,225 @@
+"""Headline benchmark: SFT tokens/s of the Qwen3-14B-architecture dense model.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kore|reference]
+
+For N > 1 run under ``python -m torch.distributed.run --nproc-per-node N``.
+Config (SFT row): 40 layers, hidden 5120, 40 Q / 8 KV heads,
+head_dim 128, FFN 17408, vocab 151936, RoPE 1e6; random-init bf16 weights,
+fp32 AdamW moments; packed sequences of 8192 uniform-random token ids, loss
+on the last 50% of each sequence; 8 sequences per GPU per step (global batch
+64 on 8 GPUs, weak scaling).
+
+Timing: W untimed warm-up steps, then K steps bracketed by barrier +
+torch.cuda.synchronize and CUDA events on the launching stream; the step
+time is the max over ranks. Every step streams all 29.5 GB of weights plus
+optimizer state, far larger than the 126 MB L2, so no explicit flush is
+needed. A second timed loop (``e2e``) calls the public API
+``CausalLMTrainer.train_step`` with pinned host inputs and reads the loss
+back each step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "sft_tokens_per_s"
+BASELINE_VALUE = None  # BASELINE.md publishes no SFT tokens/s for the reference
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons of the visible GPUs via NVML
+    while the timed region runs (read-only queries)."""
+
+    def __init__(self, index: int, period_s: float = 0.2):
+        self.index = index
+        self.period = period_s
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+
+    def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return self
+        names = {
+            "hw_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwSlowdown", 0x8),
+            "hw_thermal_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+            "sw_thermal_slowdown": getattr(pynvml, "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+            "sw_power_cap": getattr(pynvml, "nvmlClocksEventReasonSwPowerCap", 0x4),
+            "hw_power_brake_slowdown": getattr(pynvml, "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80),
+        }
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for n, bit in names.items():
+                        if r & bit:
+                            self.reasons.add(n)
+                except Exception:
+                    pass
+                self._stop.wait(self.period)
+
+        self._t = threading.Thread(target=run, daemon=True)
+        self._t.start()
+        return self
+
+    def stop(self) -> dict:
+        self._stop.set()
+        if self._t is not None:
+            self._t.join(timeout=2)
+        s = sorted(self.samples)
+        med = s[len(s) // 2] if s else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(s)}
+
+
+def reference_arm(args) -> None:
+    """Run the unmodified reference (baseline/_ref) through its own SFT API."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    reason = None
+    if not os.path.isdir(os.path.join(ref, "kore")):
+        reason = "reference not installed at baseline/_ref"
+    else:
+        probe = subprocess.run(
+            [sys.executable, "-c",
+             "import sys; sys.path.insert(0, %r); import kore.policy.sft as s; "
+             "import trl, accelerate" % ref],
+            capture_output=True, text=True)
+        if probe.returncode != 0:
+            last = (probe.stderr.strip().splitlines() or ["import failed"])[-1]
+            reason = ("reference SFT trainer needs trl + accelerate (TRL SFTTrainer over "
+                      "accelerate FSDP), which are not installed in this offline image: " + last)
+    if reason is not None:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reason}))
+        return
+    raise SystemExit("reference arm: dependencies present but no runner implemented")
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="kore", choices=["kore", "reference"])
+    ap.add_argument("--model", default="qwen3-14b")
+    ap.add_argument("--seq", type=int, default=8192)
+    ap.add_argument("--seqs-per-gpu", type=int, default=8)
+    ap.add_argument("--micro-batch", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count")
+    ap.add_argument("--no-e2e", action="store_true")
+    args = ap.parse_args(argv)
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+
+    from kore_b200 import ops
+    from kore_b200.engine.trainer import CausalLMTrainer
+    from kore_b200.models import PRESETS
+    from kore_b200.parallel.dist import init_distributed
+
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    ctx = init_distributed()
+    assert ctx.world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {ctx.world}"
+    cfg = PRESETS[args.model]()
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
+    ops.native()  # fail loudly if the extension is missing
+    trainer = CausalLMTrainer(cfg, ctx, lr=1e-5, max_grad_norm=1.0, seed=0,
+                              micro_batch_size=args.micro_batch)
+    B, S = args.seqs_per_gpu, args.seq
+    g = torch.Generator().manual_seed(1234 + ctx.rank)
+    ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
+    mask_host = torch.zeros(B, S, dtype=torch.bool)
+    mask_host[:, S // 2:] = True  # loss on the last 50% of each sequence
+    mask_host = mask_host.pin_memory()
+    ids = ids_host.cuda()
+    mask = mask_host.cuda()
+
+    for _ in range(args.warmup):
+        trainer.train_step_device(ids, mask)
+    torch.cuda.synchronize()
+    ctx.barrier()
+
+    # ---------------- device-timed loop
+    ops.reset_launch_count()
+    clk = ClockSampler(ctx.local_rank).start()
+    ctx.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        loss = trainer.train_step_device(ids, mask)
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    clocks = clk.stop()
+    launches = ops.launch_count()
+    dev_ms = e0.elapsed_time(e1) / args.steps
+    ms = ctx.max_over_ranks(dev_ms)
+    loss_v = float(loss.item())
+
+    # ---------------- end-to-end loop through the public API
+    e2e = None
+    if not args.no_e2e:
+        torch.cuda.synchronize()
+        ctx.barrier()
+        t0 = time.perf_counter()
+        s0 = torch.cuda.Event(enable_timing=True)
+        s1 = torch.cuda.Event(enable_timing=True)
+        s0.record()
+        for _ in range(args.steps):
+            trainer.train_step(ids_host, mask_host)
+        s1.record()
+        torch.cuda.synchronize()
+        e2e_ms = ctx.max_over_ranks(s0.elapsed_time(s1) / args.steps)
+        wall_ms = ctx.max_over_ranks((time.perf_counter() - t0) * 1000 / args.steps)
+        tok = B * S * ctx.world
+        e2e = {"value": tok / (e2e_ms / 1000.0), "unit": "tokens/s",
+               "ms_per_step": e2e_ms, "wall_ms_per_step": wall_ms,
+               "h2d_bytes_per_step": int(ids_host.numel() * ids_host.element_size()
+                                         + mask_host.numel() * mask_host.element_size()),
+               "d2h_bytes_per_step": 4}
+
+    tokens = B * S * ctx.world
+    value = tokens / (ms / 1000.0)
+    if ctx.is_main:
+        out = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": ctx.world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None,
+            "dtype": "bf16", "data": "synthetic uniform-random token ids, random-init weights",
+            "config": {"model": "qwen3-14b-arch (dense)" if args.model == "qwen3-14b" else args.model,
+                       "layers": cfg.num_hidden_layers,
+                       "global_batch": B * ctx.world, "seq_len": S,
+                       "parallelism": f"dp{ctx.world}" + ("-zero2" if ctx.world > 1 else ""),
+                       "loss": "last 50% of each sequence", "micro_batch": args.micro_batch,
+                       "optimizer": f"AdamW fp32 moments, master={trainer.master_mode}",
+                       "l2": "inputs larger than L2 (29.5 GB of weights streamed per step)"},
+            "loss": loss_v, "clocks": clocks, "gpu_launches": launches, "e2e": e2e,
+            "impl": "kore",
+        }
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -332,7 +332,12 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
   const int Kb = b_mn ? b.size(0) : b.size(1);
   TORCH_CHECK(K == Kb, "gemm: K mismatch");
   TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm: out shape mismatch");
-  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && M % 8 == 0, "gemm: M, N, K must be multiples of 8");
+  // TMA needs 16-byte aligned row strides and contiguous (inner) extents.
+  TORCH_CHECK(N % 8 == 0, "gemm: N must be a multiple of 8");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0 && out.stride(0) % (f32 ? 4 : 8) == 0,
+              "gemm: row strides must be multiples of 16 bytes");
+  TORCH_CHECK(a_mn ? (M % 8 == 0) : (K % 8 == 0), "gemm: A's contiguous extent must be a multiple of 8");
+  TORCH_CHECK(b_mn ? (N % 8 == 0) : (K % 8 == 0), "gemm: B's contiguous extent must be a multiple of 8");
   if (M == 0 || N == 0) return;
   c10::cuda::CUDAGuard guard(a.device());
   if (K == 0) {

@@ -70,6 +70,23 @@ class Batch:
                      torch.tensor(cu, dtype=torch.int32, device=dev),
                      max(int(c1 - c0) for c0, c1 in zip(cu[:-1], cu[1:])))
 
+    @staticmethod
+    def from_dense(ids: torch.Tensor, loss_mask: Optional[torch.Tensor] = None) -> "Batch":
+        """Pack a [B, S] block of equal-length sequences without host syncs.
+        ``loss_mask[b, j]`` marks token j as a label (predicted from j-1)."""
+        B, S = ids.shape
+        dev = ids.device
+        ids = ids.long()
+        tg = torch.full_like(ids, -1)
+        tg[:, :-1] = ids[:, 1:]
+        if loss_mask is not None:
+            lab = torch.zeros_like(loss_mask, dtype=torch.bool)
+            lab[:, :-1] = loss_mask[:, 1:].bool()
+            tg = torch.where(lab, tg, torch.full_like(tg, -1))
+        pos = torch.arange(S, dtype=torch.int32, device=dev).repeat(B)
+        cu = torch.arange(0, (B + 1) * S, S, dtype=torch.int32, device=dev)
+        return Batch(ids.reshape(-1), tg.reshape(-1), pos, cu, S)
+
     @property
     def num_tokens(self) -> int:
         return int(self.ids.numel())
@@ -102,8 +119,9 @@ class Qwen3Engine:
         self.grads: List[Optional[torch.Tensor]] = [None] * weights.num_units
         self._fresh = [True] * weights.num_units
         if allocate_grads:
-            for u, lay in enumerate(weights.layouts):
-                self.grads[u] = torch.zeros(lay.numel, dtype=self.grad_dtype, device=self.dev)
+            for u in range(weights.num_units):
+                self.grads[u] = torch.zeros(weights.padded_numel(u), dtype=self.grad_dtype,
+                                            device=self.dev)
 
     # ------------------------------------------------------------------ utils
     def zero_grad(self) -> None:
@@ -235,12 +253,14 @@ class Qwen3Engine:
                else self.grad_views(u_head)["lm_head"])
         Wlm = self.w.lm_head_weight()
         dhn = torch.zeros_like(hn)
+        self._last_rows_logp = torch.zeros(rows.numel(), dtype=torch.float32, device=hn.device)
         for s in range(0, rows.numel(), self.logits_chunk):
             r = rows[s: s + self.logits_chunk]
             hrows = hn.index_select(0, r)
             logits = self._head_logits(hrows)
-            ops.logprob(logits, targets.index_select(0, r), self.temperature,
-                        coef=coef[s: s + r.numel()], write_grad=True)
+            lp, _, _ = ops.logprob(logits, targets.index_select(0, r), self.temperature,
+                                   coef=coef[s: s + r.numel()], write_grad=True)
+            self._last_rows_logp[s: s + r.numel()] = lp
             dh = self._mm(logits, Wlm, b_t=False)
             dhn.index_copy_(0, r, dh)
             self._mm(logits, hrows, a_t=True, b_t=False, out=Glm, accumulate=not self._fresh[u_lm])
@@ -307,10 +327,9 @@ class Qwen3Engine:
             loss = None
         dhn = self._head_bwd(hn, b.targets, rows, coef_rows)
         if coef_fn is None:
-            # loss value of a fixed-coefficient objective needs the log-probs:
-            # they are produced by the same kernel pass only as gradients, so
-            # report sum(coef * logp) from a stats pass only when asked.
-            loss = None
+            # the gradient pass also produced log p(target) for the loss rows
+            lp_full[rows] = self._last_rows_logp
+            loss = (coef_rows * self._last_rows_logp).sum()
         dw = torch.zeros(self.cfg.hidden_size, dtype=torch.float32, device=x.device)
         dx = ops.rmsnorm_bwd(dhn, x, Wn, rstd, dw=dw)
         self._acc_norm(self.grad_views(uh)["norm"], dw, not self._fresh[uh])

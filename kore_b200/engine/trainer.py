@@ -1,0 +1,95 @@
+"""Causal-LM training step (SFT / midtrain) over one or more GPUs.
+
+``CausalLMTrainer.train_step(ids, loss_mask)`` is the user-facing call: it
+takes a host [B, S] token block (pinned memory is used when given), copies it
+to the device, runs ``micro_batch_size``-sequence micro-batches through the
+explicit engine with gradient accumulation, applies AdamW (sharded over
+ranks when world > 1) and returns the global mean token loss as a float.
+``train_step_device`` is the same step on device-resident inputs returning a
+device scalar (no host sync).
+
+The loss is the global token mean over every rank's labelled tokens
+(reference: kore/policy/grpo.py:613-701 global token-mean; HF Trainer mean CE
+for SFT, kore/policy/sft.py:346-399).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ..models import Qwen3Config, Qwen3Weights
+from ..parallel.dist import DistContext, get_context
+from .optimizer import AdamW
+from .qwen3_engine import Batch, Qwen3Engine
+
+
+def pick_master_mode(cfg: Qwen3Config, world: int, device: torch.device) -> str:
+    """fp32 master when it fits, else stochastic-rounded bf16 params."""
+    if device.type != "cuda":
+        return "fp32"
+    P = cfg.num_params()
+    total = torch.cuda.get_device_properties(device).total_memory
+    # bf16 params + bf16 grads + (m, v, master) sharded
+    need_fp32 = 2 * P + 2 * P + 12 * P / world
+    return "fp32" if need_fp32 < 0.86 * total else "none"
+
+
+class CausalLMTrainer:
+    def __init__(self, cfg: Qwen3Config, ctx: Optional[DistContext] = None, *, lr: float = 1e-5,
+                 betas=(0.9, 0.95), weight_decay: float = 0.0, max_grad_norm: float = 1.0,
+                 master: str = "auto", dtype: torch.dtype = torch.bfloat16, seed: int = 0,
+                 micro_batch_size: int = 1, logits_chunk: int = 4096, schedule: str = "constant",
+                 warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
+                 weights: Optional[Qwen3Weights] = None):
+        self.ctx = ctx or get_context()
+        self.cfg = cfg
+        dev = self.ctx.device
+        self.w = weights or Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed,
+                                         pad_multiple=128 * max(1, self.ctx.world))
+        self.eng = Qwen3Engine(self.w, logits_chunk=logits_chunk)
+        if master == "auto":
+            master = pick_master_mode(cfg, self.ctx.world, dev)
+        self.master_mode = master
+        self.mbs = micro_batch_size
+        if self.ctx.world > 1:
+            from ..parallel.zero import ShardedAdamW
+            self.opt = ShardedAdamW(self.w, self.eng, self.ctx, lr=lr, betas=betas,
+                                    weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                                    master=master, schedule=schedule, warmup_steps=warmup_steps,
+                                    total_steps=total_steps, seed=seed, comm=comm)
+        else:
+            self.opt = AdamW(self.w, self.eng, lr=lr, betas=betas, weight_decay=weight_decay,
+                             max_grad_norm=max_grad_norm, master=master, schedule=schedule,
+                             warmup_steps=warmup_steps, total_steps=total_steps, seed=seed)
+        self._count = torch.zeros(1, dtype=torch.float32, device=dev)
+
+    @torch.no_grad()
+    def train_step_device(self, ids: torch.Tensor, loss_mask: Optional[torch.Tensor] = None
+                          ) -> torch.Tensor:
+        """ids/loss_mask: [B, S] on the device. Returns the global mean loss (device)."""
+        B, S = ids.shape
+        lab = torch.zeros_like(ids, dtype=torch.bool)
+        lab[:, :-1] = True if loss_mask is None else loss_mask[:, 1:].bool()
+        self._count.fill_(0)
+        self._count += lab.sum()
+        self.ctx.all_reduce(self._count)
+        self.eng.zero_grad()
+        loss = torch.zeros((), dtype=torch.float32, device=ids.device)
+        for s in range(0, B, self.mbs):
+            b = Batch.from_dense(ids[s:s + self.mbs], None if loss_mask is None
+                                 else loss_mask[s:s + self.mbs])
+            coef = torch.where(b.targets >= 0, -1.0 / self._count, torch.zeros((), device=ids.device))
+            out = self.eng.forward_backward(b, coef=coef)
+            loss += out["loss"]
+        self.opt.step()
+        self.ctx.all_reduce(loss)
+        return loss
+
+    def train_step(self, ids_host: torch.Tensor, loss_mask_host: Optional[torch.Tensor] = None
+                   ) -> float:
+        """Host inputs in, host loss out (the end-to-end call)."""
+        dev = self.ctx.device
+        ids = ids_host.to(dev, non_blocking=True)
+        mask = loss_mask_host.to(dev, non_blocking=True) if loss_mask_host is not None else None
+        return float(self.train_step_device(ids, mask).item())

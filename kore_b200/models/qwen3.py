@@ -144,17 +144,23 @@ class Qwen3Weights:
 
     def __init__(self, cfg: Qwen3Config, device="cpu", dtype: Optional[torch.dtype] = None,
                  init: bool = True, seed: int = 0, std: float = 0.02,
-                 allocate: bool = True):
+                 allocate: bool = True, pad_multiple: int = ALIGN):
         self.cfg = cfg
         self.dtype = dtype or _dtype(cfg.torch_dtype)
         self.device = torch.device(device)
         self.layouts = unit_layouts(cfg)
+        # buffers are padded so that data-parallel shards divide them evenly
+        self.pad_multiple = max(ALIGN, int(pad_multiple))
         self.bufs: List[Optional[torch.Tensor]] = [None] * len(self.layouts)
         if allocate:
             for u, lay in enumerate(self.layouts):
-                self.bufs[u] = torch.empty(lay.numel, dtype=self.dtype, device=self.device)
+                self.bufs[u] = torch.empty(self.padded_numel(u), dtype=self.dtype,
+                                           device=self.device)
             if init:
                 self.init_random(seed, std)
+
+    def padded_numel(self, u: int) -> int:
+        return _round_up(self.layouts[u].numel, self.pad_multiple)
 
     # ------------------------------------------------------------------ views
     def views(self, u: int) -> Dict[str, torch.Tensor]:
@@ -237,11 +243,13 @@ class Qwen3Weights:
         return missing
 
     def to(self, device=None, dtype=None) -> "Qwen3Weights":
-        w = Qwen3Weights(self.cfg, device or self.device, dtype or self.dtype, allocate=False)
+        w = Qwen3Weights(self.cfg, device or self.device, dtype or self.dtype, allocate=False,
+                         pad_multiple=self.pad_multiple)
         w.bufs = [b.to(device=w.device, dtype=w.dtype) if b is not None else None for b in self.bufs]
         return w
 
     def clone(self) -> "Qwen3Weights":
-        w = Qwen3Weights(self.cfg, self.device, self.dtype, allocate=False)
+        w = Qwen3Weights(self.cfg, self.device, self.dtype, allocate=False,
+                         pad_multiple=self.pad_multiple)
         w.bufs = [b.clone() if b is not None else None for b in self.bufs]
         return w

@@ -8,7 +8,7 @@ from typing import Optional
 import torch
 
 from . import reference as ref
-from ._lib import available, check_device_error, native
+from ._lib import available, check_device_error, launch_count, native, reset_launch_count
 
 __all__ = [
     "available", "check_device_error", "native", "ref",

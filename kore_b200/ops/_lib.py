@@ -11,6 +11,40 @@ import importlib
 
 _C = None
 _err: Exception | None = None
+_launches = 0
+
+
+class _Counted:
+    """Wraps the extension so every native entry point call (each launches
+    exactly one of our kernels) is counted; used for launch accounting."""
+
+    def __init__(self, mod):
+        self._mod = mod
+        self._cache = {}
+
+    def __getattr__(self, name):
+        fn = self._cache.get(name)
+        if fn is None:
+            raw = getattr(self._mod, name)
+            if not callable(raw) or name == "read_and_clear_device_error":
+                return raw
+
+            def fn(*a, _raw=raw, **k):
+                global _launches
+                _launches += 1
+                return _raw(*a, **k)
+
+            self._cache[name] = fn
+        return fn
+
+
+def launch_count() -> int:
+    return _launches
+
+
+def reset_launch_count() -> None:
+    global _launches
+    _launches = 0
 
 
 def native():
@@ -20,7 +54,7 @@ def native():
         return _C
     if _err is None:
         try:
-            _C = importlib.import_module("kore_b200._C")
+            _C = _Counted(importlib.import_module("kore_b200._C"))
             return _C
         except Exception as e:  # noqa: BLE001 - recorded and re-raised below
             _err = e

@@ -1,0 +1,99 @@
+"""Sharded data parallelism for the flat-unit engine (ZeRO-2 style).
+
+Every rank keeps the full bf16 parameters and accumulates full gradients for
+its micro-batches; at the step boundary each unit's gradient is
+reduce-scattered, the rank updates only its 1/world shard (fp32 moments and
+optional fp32 master live only for the shard), and the updated bf16 shard is
+all-gathered back into every rank's full parameter buffer.
+
+Per step and unit that moves the same bytes as one all-reduce, while the
+optimizer state and AdamW work drop by ``world``. Two data planes:
+
+* ``comm="nccl"``: NCCL reduce-scatter / all-gather (the baseline);
+* ``comm="fused"``: the native peer-memory kernel that fuses the
+  reduce-scatter with the bf16->fp32 cast, the global-norm clip and the AdamW
+  update (``kore_b200.parallel.fused_rs_adamw``), then broadcasts the shard
+  with NVLink stores.
+
+Reference parity: FSDP SHARD_GRAD_OP / FULL_SHARD via accelerate
+(kore/policy/configs.py:580-651, kore/policy/grpo.py:1562-1625). With 180 GB of
+HBM per GPU a 14B model's full bf16 weights stay resident, so no per-layer
+re-gather is needed inside the step.
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..engine.optimizer import lr_lambda_factory
+from .dist import DistContext
+
+
+class ShardedAdamW:
+    def __init__(self, weights, engine, ctx: DistContext, lr: float = 1e-5, betas=(0.9, 0.999),
+                 eps: float = 1e-8, weight_decay: float = 0.0, max_grad_norm: float = 0.0,
+                 master: str = "fp32", schedule: str = "constant", warmup_steps: int = 0,
+                 total_steps: int = 1, seed: int = 0, comm: str = "nccl"):
+        self.w, self.eng, self.ctx = weights, engine, ctx
+        self.lr, (self.b1, self.b2), self.eps, self.wd = lr, betas, eps, weight_decay
+        self.max_grad_norm = max_grad_norm
+        self.lr_fn = lr_lambda_factory(schedule, warmup_steps, total_steps)
+        self.step_count = 0
+        self.seed = seed
+        self.comm = comm
+        W, r = ctx.world, ctx.rank
+        dev = weights.device
+        self.shard_len = []
+        self.m, self.v, self.master, self.gshard = {}, {}, {}, {}
+        for u in range(weights.num_units):
+            n = weights.bufs[u].numel()
+            assert n % W == 0, "weights must be padded to a multiple of world"
+            s = n // W
+            self.shard_len.append(s)
+            self.m[u] = torch.zeros(s, dtype=torch.float32, device=dev)
+            self.v[u] = torch.zeros(s, dtype=torch.float32, device=dev)
+            if master == "fp32":
+                self.master[u] = weights.bufs[u][r * s:(r + 1) * s].float()
+            self.gshard[u] = torch.empty(s, dtype=engine.grad_dtype, device=dev)
+        self._sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
+        self.last_sumsq: Optional[torch.Tensor] = None
+
+    def current_lr(self) -> float:
+        return self.lr * self.lr_fn(self.step_count)
+
+    def reduce_scatter_unit(self, u: int, async_op: bool = False):
+        return dist.reduce_scatter_tensor(self.gshard[u], self.eng.grads[u], op=dist.ReduceOp.SUM,
+                                          group=self.ctx.group, async_op=async_op)
+
+    @torch.no_grad()
+    def step(self, grad_scale: float = 1.0, scattered: bool = False) -> None:
+        W, r = self.ctx.world, self.ctx.rank
+        if not scattered:
+            for u in range(self.w.num_units):
+                self.reduce_scatter_unit(u)
+        sq = None
+        if self.max_grad_norm and self.max_grad_norm > 0:
+            self._sumsq.zero_()
+            for u in range(self.w.num_units):
+                ops.sumsq(self.gshard[u], self._sumsq)
+            dist.all_reduce(self._sumsq, group=self.ctx.group)
+            sq = self._sumsq
+            self.last_sumsq = sq
+        lr = self.current_lr()
+        self.step_count += 1
+        for u in range(self.w.num_units):
+            s = self.shard_len[u]
+            pshard = self.w.bufs[u][r * s:(r + 1) * s]
+            ops.adamw_step(pshard, self.gshard[u], self.m[u], self.v[u], lr=lr, b1=self.b1,
+                           b2=self.b2, eps=self.eps, wd=self.wd, step=self.step_count,
+                           grad_scale=grad_scale, master=self.master.get(u), sumsq_buf=sq,
+                           max_norm=self.max_grad_norm,
+                           seed=self.seed * 7919 + self.step_count * 104729 + u * 31 + r)
+            # in place: NCCL accepts send == recv + rank * count
+            dist.all_gather_into_tensor(self.w.bufs[u], pshard, group=self.ctx.group)
+
+    def grad_norm(self) -> float:
+        return float(self.last_sumsq.sqrt()) if self.last_sumsq is not None else float("nan")
