@@ -1,0 +1,725 @@
+// Causal GQA flash attention for sm_100a (head_dim 128), packed varlen
+// sequences, forward and backward, on tcgen05 tensor cores.
+//
+// Forward (one CTA per (128-row query block, query head)):
+//   warp 0      TMA producer: Q once, then K_j / V_j tiles (2-stage rings)
+//   warp 1      MMA issuer:   S_{j+1} = Q K_{j+1}^T (TMEM, ping-pong) is issued
+//                             before O += P_j V_j, so the next score tile is
+//                             computed while the softmax warps work on this one
+//   warps 2..5  softmax: one query row per thread read from TMEM, online
+//               max/sum in the log2 domain, P (bf16) written to shared memory
+//               in the 128B-swizzled K-major layout UMMA reads; O in TMEM is
+//               only rescaled when the running max grows by more than 2^8
+//               (lazy rescaling), then normalised in the epilogue.
+// Backward (one CTA per (128-row key block, kv head)): loops over the query
+//   heads of the GQA group and the causal query blocks, recomputing
+//   S^T = K Q^T, P^T = exp(S^T - lse), dP^T = V dO^T, dS^T = P^T (dP^T - delta)
+//   with dV += P^T dO and dK += dS^T Q accumulated in TMEM for the whole CTA,
+//   and dQ partials (dS K) added to an fp32 scratch accumulator in global
+//   memory with vector atomics; a final kernel converts it to bf16.
+//
+// Reference parity: the reference runs attention through SDPA /
+// flash_attention_2 inside HF (kore/policy/configs.py:682-700).
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace kore {
+namespace attn {
+
+constexpr int D = 128;
+constexpr int BQ = 128;
+constexpr int BKV = 128;
+constexpr int kThreads = 192;
+constexpr int TILE_BYTES = 128 * D * 2;  // 32 KB: 128 rows x 128 bf16 as two 64-col swizzle atoms
+constexpr float kLog2e = 1.4426950408889634f;
+
+KORE_DEV void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  const uint32_t (&a)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&r[0]);
+  const uint32_t (&b)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&r[16]);
+  tmem_st16(taddr, a);
+  tmem_st16(taddr + 16, b);
+}
+
+// Descriptor of a 128-row, 128-column bf16 tile stored as two K-major
+// 64-column SW128 atoms (16 KB apart), advanced to K-step kk (16 columns).
+KORE_DEV uint64_t kmajor_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+// Same tile read as an MN-major operand (rows = K, the 128 columns = N in two
+// 64-wide blocks 16 KB apart), advanced to K-step kk (16 rows).
+KORE_DEV uint64_t mnmajor_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + kk * 2048, 16384, 1024);
+}
+
+// Write a thread's 128 fp32 values (one tile row) as bf16 into a K-major SW128 tile.
+KORE_DEV void store_row_sw128(uint8_t* tile, int row, const float* v) {
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 values
+    uint4 u;
+    u.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
+    u.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
+    u.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
+    u.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
+    uint8_t* atom = tile + (c >> 3) * 16384;
+    *reinterpret_cast<uint4*>(atom + row * 128 + (((c & 7) ^ (row & 7)) * 16)) = u;
+  }
+}
+
+struct FwdParams {
+  const int* cu_seqlens;
+  int nseq;
+  int nqblk;  // blocks per sequence slot (ceil(max_seqlen / 128))
+  int Hq, Hkv;
+  float scale_log2;
+  __nv_bfloat16* o;  // [T, Hq, D]
+  float* lse;        // [Hq, T] natural log
+  int T;
+};
+
+struct FwdSmem {
+  static constexpr int Q_OFF = 0;
+  static constexpr int K_OFF = TILE_BYTES;             // 2 stages
+  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // 2 stages
+  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;  // 2 buffers
+  static constexpr int BAR_OFF = P_OFF + 2 * TILE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, FwdParams p) {
+  using S = FwdSmem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;  // [2]
+  uint64_t* o_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  // ---- work item: longest (latest) query blocks first
+  const int slot = p.nseq * p.nqblk - 1 - blockIdx.x;
+  const int seq = slot / p.nqblk;
+  const int qb = slot % p.nqblk;
+  const int h = blockIdx.y;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int s0 = p.cu_seqlens[seq];
+  const int len = p.cu_seqlens[seq + 1] - s0;
+  const int q0 = qb * BQ;
+  if (q0 >= len) return;  // whole CTA exits before any barrier / TMEM use
+  const int nkv = qb + 1;  // causal: kv tiles 0..qb
+  const int warp = threadIdx.x / 32;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+    }
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(q_full, TILE_BYTES);
+      tma_load_2d(smem + S::Q_OFF, &tmQ, q_full, h * D, s0 + q0);
+      tma_load_2d(smem + S::Q_OFF + 16384, &tmQ, q_full, h * D + 64, s0 + q0);
+      for (int j = 0; j < nkv && !*abort_flag; ++j) {
+        const int st = j & 1;
+        const uint32_t ph = (j >> 1) & 1;
+        if (!mbar_wait(&k_empty[st], ph ^ 1)) { *abort_flag = 1; break; }
+        uint8_t* kt = smem + S::K_OFF + st * TILE_BYTES;
+        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
+        tma_load_2d(kt, &tmK, &k_full[st], kvh * D, s0 + j * BKV);
+        tma_load_2d(kt + 16384, &tmK, &k_full[st], kvh * D + 64, s0 + j * BKV);
+        if (!mbar_wait(&v_empty[st], ph ^ 1)) { *abort_flag = 1; break; }
+        uint8_t* vt = smem + S::V_OFF + st * TILE_BYTES;
+        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
+        tma_load_2d(vt, &tmV, &v_full[st], kvh * D, s0 + j * BKV);
+        tma_load_2d(vt + 16384, &tmV, &v_full[st], kvh * D + 64, s0 + j * BKV);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    constexpr uint32_t idesc_qk = make_idesc_bf16(BQ, BKV, false, false);
+    constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, false, true);
+    if (elect_one()) {
+      const uint32_t qa = smem_u32(smem + S::Q_OFF);
+      bool ok = mbar_wait(q_full, 0);
+      auto issue_s = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        tc_fence_after();
+        const uint32_t ka = smem_u32(smem + S::K_OFF + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16_ss(tmem + st * 128, kmajor_desc(qa, kk), kmajor_desc(ka, kk), idesc_qk, kk > 0);
+        umma_commit(&k_empty[st]);
+        umma_commit(&s_full[st]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; j < nkv && ok; ++j) {
+        if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
+        const int st = j & 1;
+        if (!mbar_wait(&p_full[st], (j >> 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t pa = smem_u32(smem + S::P_OFF + st * TILE_BYTES);
+        const uint32_t va = smem_u32(smem + S::V_OFF + st * TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_f16_ss(tmem + 256, kmajor_desc(pa, kk), mnmajor_desc(va, kk), idesc_pv,
+                      (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&v_empty[st]);
+        umma_commit(o_done);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- softmax warps
+    const int q = warp & 3;
+    const int lane = threadIdx.x & 31;
+    const int row = q * 32 + lane;  // row within the query block
+    const int qi = q0 + row;        // query position within the sequence
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    float sv[128];
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      const int st = j & 1;
+      if (!mbar_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + st * 128 + c * 32, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
+      }
+      const int kv0 = j * BKV;
+      float mx = -INFINITY;
+      const bool edge = (j == nkv - 1) || (kv0 + BKV > len);
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        if (edge && (kv0 + i > qi || kv0 + i >= len)) sv[i] = -INFINITY;
+        mx = fmaxf(mx, sv[i]);
+      }
+      float m_new = fmaxf(m, mx);
+      const bool need = (m == -INFINITY) ? true : (m_new > m + 8.f);
+      if (j > 0) {
+        if (!mbar_wait(o_done, (j - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const float alpha = need ? exp2f(m - m_new) : 1.f;
+        if (__any_sync(0xffffffff, need && m != -INFINITY)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            const uint32_t a = tmem + lane_base + 256 + c * 32;
+            tmem_ld32(a, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(a, r);
+          }
+          tmem_wait_st();
+        }
+        if (need) l *= alpha;
+      }
+      if (need) m = m_new;
+      const float mref = (m == -INFINITY) ? 0.f : m;
+      float rs = 0.f;
+#pragma unroll
+      for (int i = 0; i < 128; ++i) {
+        sv[i] = exp2f(sv[i] - mref);
+        rs += sv[i];
+      }
+      l += rs;
+      store_row_sw128(smem + S::P_OFF + st * TILE_BYTES, row, sv);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[st]);
+    }
+    if (ok && mbar_wait(o_done, (nkv - 1) & 1)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool valid = qi < len;
+      __nv_bfloat16* orow = p.o + ((size_t)(s0 + qi) * p.Hq + h) * D;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + 256 + c * 32, r);
+        tmem_wait_ld();
+        if (valid) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            uint4 u;
+            u.x = pack_bf16(__uint_as_float(r[8 * i + 0]) * inv, __uint_as_float(r[8 * i + 1]) * inv);
+            u.y = pack_bf16(__uint_as_float(r[8 * i + 2]) * inv, __uint_as_float(r[8 * i + 3]) * inv);
+            u.z = pack_bf16(__uint_as_float(r[8 * i + 4]) * inv, __uint_as_float(r[8 * i + 5]) * inv);
+            u.w = pack_bf16(__uint_as_float(r[8 * i + 6]) * inv, __uint_as_float(r[8 * i + 7]) * inv);
+            *reinterpret_cast<uint4*>(orow + c * 32 + 8 * i) = u;
+          }
+        }
+      }
+      if (valid) p.lse[(size_t)h * p.T + s0 + qi] = (m + __log2f(l)) * 0.6931471805599453f;
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+
+// ============================================================== backward
+// delta[h, t] = sum_d dO[t,h,d] * O[t,h,d];  also zeroes the fp32 dQ accumulator.
+__global__ void attn_bwd_prep_kernel(const __nv_bfloat16* __restrict__ dO, int ld_do,
+                                     const __nv_bfloat16* __restrict__ O, int Hq, int T,
+                                     float* __restrict__ delta, float* __restrict__ dq_acc) {
+  const long gw = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (long)T * Hq) return;
+  const int t = gw / Hq, h = gw % Hq;
+  const __nv_bfloat16* a = dO + (size_t)t * ld_do + h * D + lane * 4;
+  const __nv_bfloat16* b = O + ((size_t)t * Hq + h) * D + lane * 4;
+  float s = 0.f;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) s += __bfloat162float(a[e]) * __bfloat162float(b[e]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffff, s, o);
+  if (lane == 0) delta[(size_t)h * T + t] = s;
+  *reinterpret_cast<float4*>(dq_acc + ((size_t)t * Hq + h) * D + lane * 4) = make_float4(0, 0, 0, 0);
+}
+
+__global__ void attn_dq_convert_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dq,
+                                       int ld_dq, int Hq, int T) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per 8 elements
+  const long total = (long)T * Hq * (D / 8);
+  if (i >= total) return;
+  const long row = i / (Hq * (D / 8));
+  const int rem = i % (Hq * (D / 8));
+  const float* src = dq_acc + row * (long)Hq * D + rem * 8;
+  float4 a = *reinterpret_cast<const float4*>(src);
+  float4 b = *reinterpret_cast<const float4*>(src + 4);
+  uint4 u;
+  u.x = pack_bf16(a.x, a.y);
+  u.y = pack_bf16(a.z, a.w);
+  u.z = pack_bf16(b.x, b.y);
+  u.w = pack_bf16(b.z, b.w);
+  *reinterpret_cast<uint4*>(dq + row * (long)ld_dq + rem * 8) = u;
+}
+
+struct BwdParams {
+  const int* cu_seqlens;
+  int nseq, nkblk;
+  int Hq, Hkv;
+  float scale, scale_log2;
+  const float* lse;    // [Hq, T] natural log
+  const float* delta;  // [Hq, T]
+  float* dq_acc;       // [T, Hq, D] fp32, pre-zeroed
+  __nv_bfloat16* dk;   // [T, Hkv, D] (row stride ld_dk)
+  __nv_bfloat16* dv;
+  int ld_dk, ld_dv;
+  int T;
+};
+
+struct BwdSmem {
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = TILE_BYTES;
+  static constexpr int Q_OFF = 2 * TILE_BYTES;
+  static constexpr int DO_OFF = 3 * TILE_BYTES;
+  static constexpr int PT_OFF = 4 * TILE_BYTES;
+  static constexpr int DS_OFF = 5 * TILE_BYTES;
+  static constexpr int VEC_OFF = 6 * TILE_BYTES;           // lse2[128], delta[128]
+  static constexpr int BAR_OFF = VEC_OFF + 1024;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+};
+
+KORE_DEV void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
+
+// Write 32 values (columns [32c, 32c+32) of a tile row) as bf16 into a K-major SW128 tile.
+KORE_DEV void store_row32_sw128(uint8_t* tile, int row, int c, const float* v) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int chunk = c * 4 + k;  // 0..15
+    uint4 u;
+    u.x = pack_bf16(v[8 * k + 0], v[8 * k + 1]);
+    u.y = pack_bf16(v[8 * k + 2], v[8 * k + 3]);
+    u.z = pack_bf16(v[8 * k + 4], v[8 * k + 5]);
+    u.w = pack_bf16(v[8 * k + 6], v[8 * k + 7]);
+    uint8_t* atom = tile + (chunk >> 3) * 16384;
+    *reinterpret_cast<uint4*>(atom + row * 128 + (((chunk & 7) ^ (row & 7)) * 16)) = u;
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                    BwdParams p) {
+  using S = BwdSmem;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* st_full = bars + 3;
+  uint64_t* p_full = bars + 4;
+  uint64_t* dq_full = bars + 5;
+  uint64_t* dq_empty = bars + 6;
+  uint64_t* all_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* s_lse = reinterpret_cast<float*>(smem + S::VEC_OFF);
+  float* s_delta = s_lse + 128;
+
+  const int seq = blockIdx.x / p.nkblk;
+  const int kb = blockIdx.x % p.nkblk;
+  const int kvh = blockIdx.y;
+  const int G = p.Hq / p.Hkv;
+  const int s0 = p.cu_seqlens[seq];
+  const int len = p.cu_seqlens[seq + 1] - s0;
+  const int k0 = kb * BKV;
+  if (k0 >= len) return;
+  const int nqb = (len + BQ - 1) / BQ;
+  const int per_head = nqb - kb;
+  const int iters = G * per_head;
+  const int warp = threadIdx.x / 32;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(qdo_full, 1);
+    mbar_init(qdo_empty, 1);
+    mbar_init(st_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_empty, 4);
+    mbar_init(all_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: [0,128) S^T then dQ partial, [128,256) dP^T, [256,384) dV, [384,512) dK
+
+  if (warp == 0) {
+    if (elect_one()) {
+      mbar_arrive_expect_tx(kv_full, 2 * TILE_BYTES);
+      tma_load_2d(smem + S::K_OFF, &tmK, kv_full, kvh * D, s0 + k0);
+      tma_load_2d(smem + S::K_OFF + 16384, &tmK, kv_full, kvh * D + 64, s0 + k0);
+      tma_load_2d(smem + S::V_OFF, &tmV, kv_full, kvh * D, s0 + k0);
+      tma_load_2d(smem + S::V_OFF + 16384, &tmV, kv_full, kvh * D + 64, s0 + k0);
+      for (int i = 0; i < iters && !*abort_flag; ++i) {
+        const int h = kvh * G + i / per_head;
+        const int qb = kb + i % per_head;
+        if (!mbar_wait(qdo_empty, (i & 1) ^ 1)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
+        tma_load_2d(smem + S::Q_OFF, &tmQ, qdo_full, h * D, s0 + qb * BQ);
+        tma_load_2d(smem + S::Q_OFF + 16384, &tmQ, qdo_full, h * D + 64, s0 + qb * BQ);
+        tma_load_2d(smem + S::DO_OFF, &tmDO, qdo_full, h * D, s0 + qb * BQ);
+        tma_load_2d(smem + S::DO_OFF + 16384, &tmDO, qdo_full, h * D + 64, s0 + qb * BQ);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    constexpr uint32_t id_s = make_idesc_bf16(128, 128, false, false);   // K Q^T, V dO^T
+    constexpr uint32_t id_dv = make_idesc_bf16(128, 128, false, true);   // P^T dO, dS^T Q
+    constexpr uint32_t id_dq = make_idesc_bf16(128, 128, true, true);    // dS K
+    if (elect_one()) {
+      const uint32_t ka = smem_u32(smem + S::K_OFF), va = smem_u32(smem + S::V_OFF);
+      const uint32_t qa = smem_u32(smem + S::Q_OFF), da = smem_u32(smem + S::DO_OFF);
+      const uint32_t pa = smem_u32(smem + S::PT_OFF), sa = smem_u32(smem + S::DS_OFF);
+      bool ok = mbar_wait(kv_full, 0);
+      for (int i = 0; i < iters && ok; ++i) {
+        const uint32_t ph = i & 1;
+        if (!mbar_wait(qdo_full, ph)) { ok = false; break; }
+        if (i > 0 && !mbar_wait(dq_empty, ph ^ 1)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16_ss(tmem + 0, kmajor_desc(ka, kk), kmajor_desc(qa, kk), id_s, kk > 0);
+          umma_f16_ss(tmem + 128, kmajor_desc(va, kk), kmajor_desc(da, kk), id_s, kk > 0);
+        }
+        umma_commit(st_full);
+        if (!mbar_wait(p_full, ph)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BQ / 16; ++kk) {
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          umma_f16_ss(tmem + 256, kmajor_desc(pa, kk), mnmajor_desc(da, kk), id_dv, acc);
+          umma_f16_ss(tmem + 384, kmajor_desc(sa, kk), mnmajor_desc(qa, kk), id_dv, acc);
+        }
+#pragma unroll
+        for (int kk = 0; kk < BKV / 16; ++kk)
+          umma_f16_ss(tmem + 0, mnmajor_desc(sa, kk), mnmajor_desc(ka, kk), id_dq, kk > 0);
+        umma_commit(qdo_empty);
+        umma_commit(dq_full);
+      }
+      if (ok) umma_commit(all_done);
+      else *abort_flag = 1;
+    }
+    __syncwarp();
+  } else {
+    const int q4 = warp & 3;
+    const int lane = threadIdx.x & 31;
+    const int row = q4 * 32 + lane;    // kv row for S^T/dP^T/dV/dK; q row for dQ
+    const int tid = threadIdx.x - 64;  // 0..127
+    const int kvi = k0 + row;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    bool ok = true;
+    for (int i = 0; i < iters; ++i) {
+      const int h = kvh * G + i / per_head;
+      const int qb = kb + i % per_head;
+      const int q0 = qb * BQ;
+      const uint32_t ph = i & 1;
+      // per-query-row softmax statistics for this block
+      {
+        const int qi = q0 + tid;
+        const bool in = qi < len;
+        s_lse[tid] = in ? p.lse[(size_t)h * p.T + s0 + qi] * kLog2e : INFINITY;
+        s_delta[tid] = in ? p.delta[(size_t)h * p.T + s0 + qi] : 0.f;
+      }
+      named_bar_sync(1, 128);
+      if (!mbar_wait(st_full, ph)) { ok = false; break; }
+      tc_fence_after();
+      const bool diag = (qb == kb);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t rs[32], rp[32];
+        tmem_ld32(tmem + lane_base + c * 32, rs);
+        tmem_ld32(tmem + lane_base + 128 + c * 32, rp);
+        tmem_wait_ld();
+        float pv[32], dv[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qc = c * 32 + e;
+          float pr = exp2f(__uint_as_float(rs[e]) * p.scale_log2 - s_lse[qc]);
+          if ((diag && q0 + qc < kvi) || kvi >= len) pr = 0.f;
+          pv[e] = pr;
+          dv[e] = pr * (__uint_as_float(rp[e]) - s_delta[qc]);
+        }
+        store_row32_sw128(smem + S::PT_OFF, row, c, pv);
+        store_row32_sw128(smem + S::DS_OFF, row, c, dv);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // dQ partial for query rows of this block
+      if (!mbar_wait(dq_full, ph)) { ok = false; break; }
+      tc_fence_after();
+      const int qi = q0 + row;
+      float* dst = p.dq_acc + ((size_t)(s0 + qi) * p.Hq + h) * D;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + c * 32, r);
+        tmem_wait_ld();
+        if (qi < len) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4) {
+            float4 v4 = make_float4(__uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
+                                    __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
+            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e), v4);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      named_bar_sync(1, 128);  // s_lse / s_delta reuse
+    }
+    if (ok && mbar_wait(all_done, 0)) {
+      tc_fence_after();
+      const bool valid = kvi < len;
+      __nv_bfloat16* dvrow = p.dv + (size_t)(s0 + kvi) * p.ld_dv + kvh * D;
+      __nv_bfloat16* dkrow = p.dk + (size_t)(s0 + kvi) * p.ld_dk + kvh * D;
+#pragma unroll
+      for (int part = 0; part < 2; ++part) {
+        __nv_bfloat16* out = part == 0 ? dvrow : dkrow;
+        const float mul = part == 0 ? 1.f : p.scale;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tmem + lane_base + 256 + part * 128 + c * 32, r);
+          tmem_wait_ld();
+          if (valid) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              uint4 u;
+              u.x = pack_bf16(__uint_as_float(r[8 * k + 0]) * mul, __uint_as_float(r[8 * k + 1]) * mul);
+              u.y = pack_bf16(__uint_as_float(r[8 * k + 2]) * mul, __uint_as_float(r[8 * k + 3]) * mul);
+              u.z = pack_bf16(__uint_as_float(r[8 * k + 4]) * mul, __uint_as_float(r[8 * k + 5]) * mul);
+              u.w = pack_bf16(__uint_as_float(r[8 * k + 6]) * mul, __uint_as_float(r[8 * k + 7]) * mul);
+              *reinterpret_cast<uint4*>(out + c * 32 + 8 * k) = u;
+            }
+          }
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+void check_qkv(const at::Tensor& t, const char* n) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.dim() == 3 && t.size(2) == D &&
+                  t.stride(2) == 1 && t.stride(1) == D,
+              n, ": expected bf16 [T, H, 128] with contiguous heads");
+  TORCH_CHECK(t.stride(0) % 8 == 0, n, ": row stride must be a multiple of 8 elements");
+}
+
+}  // namespace attn
+
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+              const at::Tensor& cu_seqlens, int64_t max_seqlen, double scale, at::Tensor& o,
+              at::Tensor& lse) {
+  using namespace attn;
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  TORCH_CHECK(o.is_contiguous() && o.scalar_type() == at::kBFloat16, "o must be contiguous bf16");
+  TORCH_CHECK(lse.is_contiguous() && lse.scalar_type() == at::kFloat, "lse must be fp32");
+  TORCH_CHECK(cu_seqlens.scalar_type() == at::kInt && cu_seqlens.is_cuda(), "cu_seqlens int32 cuda");
+  const int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
+  TORCH_CHECK(Hq % Hkv == 0, "GQA: Hq must be a multiple of Hkv");
+  const int nseq = cu_seqlens.numel() - 1;
+  if (T == 0 || nseq <= 0) return;
+  c10::cuda::CUDAGuard g(q.device());
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tq = make_tmap_2d(q.data_ptr(), bf, 2, (uint64_t)Hq * D, T, q.stride(0), 64, 128);
+  CUtensorMap tk = make_tmap_2d(k.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, k.stride(0), 64, 128);
+  CUtensorMap tv = make_tmap_2d(v.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, v.stride(0), 64, 128);
+  FwdParams p;
+  p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.nseq = nseq;
+  p.nqblk = (int)((max_seqlen + BQ - 1) / BQ);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = (float)scale * kLog2e;
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.lse = lse.data_ptr<float>();
+  p.T = T;
+  constexpr int smem = FwdSmem::TOTAL;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "attn_fwd smem attr");
+    attr = true;
+  }
+  dim3 grid(nseq * p.nqblk, Hq);
+  attn_fwd_kernel<<<grid, kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
+  check_cuda(cudaGetLastError(), "attn_fwd launch");
+}
+
+// dq/dk/dv may be strided views [T, H, 128] of larger buffers.
+// dq_acc: fp32 scratch [T, Hq, 128] (zeroed here), delta: fp32 scratch [Hq, T].
+void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+              const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+              const at::Tensor& cu_seqlens, int64_t max_seqlen, double scale, at::Tensor& dq,
+              at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc, at::Tensor& delta) {
+  using namespace attn;
+  check_qkv(dout, "dout");
+  check_qkv(q, "q");
+  check_qkv(k, "k");
+  check_qkv(v, "v");
+  check_qkv(dq, "dq");
+  check_qkv(dk, "dk");
+  check_qkv(dv, "dv");
+  TORCH_CHECK(o.is_contiguous(), "o must be contiguous [T, Hq, 128]");
+  const int T = q.size(0), Hq = q.size(1), Hkv = k.size(1);
+  TORCH_CHECK(dq_acc.scalar_type() == at::kFloat && dq_acc.numel() >= (int64_t)T * Hq * D,
+              "dq_acc must be fp32 with T*Hq*128 elements");
+  TORCH_CHECK(delta.scalar_type() == at::kFloat && delta.numel() >= (int64_t)T * Hq,
+              "delta must be fp32 with Hq*T elements");
+  const int nseq = cu_seqlens.numel() - 1;
+  if (T == 0 || nseq <= 0) return;
+  c10::cuda::CUDAGuard g(q.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  {
+    const long warps = (long)T * Hq;
+    attn_bwd_prep_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), dout.stride(0),
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), Hq, T, delta.data_ptr<float>(),
+        dq_acc.data_ptr<float>());
+    check_cuda(cudaGetLastError(), "attn_bwd_prep");
+  }
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tq = make_tmap_2d(q.data_ptr(), bf, 2, (uint64_t)Hq * D, T, q.stride(0), 64, 128);
+  CUtensorMap tk = make_tmap_2d(k.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, k.stride(0), 64, 128);
+  CUtensorMap tv = make_tmap_2d(v.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, v.stride(0), 64, 128);
+  CUtensorMap tdo = make_tmap_2d(dout.data_ptr(), bf, 2, (uint64_t)Hq * D, T, dout.stride(0), 64, 128);
+  BwdParams p;
+  p.cu_seqlens = cu_seqlens.data_ptr<int>();
+  p.nseq = nseq;
+  p.nkblk = (int)((max_seqlen + BKV - 1) / BKV);
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = (float)scale;
+  p.scale_log2 = (float)scale * kLog2e;
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.ld_dk = dk.stride(0);
+  p.ld_dv = dv.stride(0);
+  p.T = T;
+  constexpr int smem = BwdSmem::TOTAL;
+  static bool attr = false;
+  if (!attr) {
+    check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "attn_bwd smem attr");
+    attr = true;
+  }
+  dim3 grid(nseq * p.nkblk, Hkv);
+  attn_bwd_kernel<<<grid, kThreads, smem, st>>>(tq, tk, tv, tdo, p);
+  check_cuda(cudaGetLastError(), "attn_bwd launch");
+  const long n8 = (long)T * Hq * (D / 8);
+  attn_dq_convert_kernel<<<(int)((n8 + 255) / 256), 256, 0, st>>>(
+      dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), Hq, T);
+  check_cuda(cudaGetLastError(), "attn_dq_convert");
+}
+
+}  // namespace kore

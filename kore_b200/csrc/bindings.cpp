@@ -31,6 +31,13 @@ void adamw_step(at::Tensor& p, const c10::optional<at::Tensor>& master, const at
                 at::Tensor& m, at::Tensor& v, double lr, double b1, double b2, double eps,
                 double wd, int64_t step, double grad_scale, const c10::optional<at::Tensor>& sumsq,
                 double max_norm, int64_t seed);
+void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+              const at::Tensor& cu_seqlens, int64_t max_seqlen, double scale, at::Tensor& o,
+              at::Tensor& lse);
+void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+              const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
+              const at::Tensor& cu_seqlens, int64_t max_seqlen, double scale, at::Tensor& dq,
+              at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc, at::Tensor& delta);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -48,5 +55,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("logprob_fwd_bwd", &kore::logprob_fwd_bwd);
   m.def("sumsq_accumulate", &kore::sumsq_accumulate);
   m.def("adamw_step", &kore::adamw_step);
+  m.def("attn_fwd", &kore::attn_fwd, "tcgen05 causal GQA flash attention forward");
+  m.def("attn_bwd", &kore::attn_bwd, "tcgen05 causal GQA flash attention backward");
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

@@ -54,7 +54,11 @@ def attn_bwd(do, q, k, v, o, lse, cu_seqlens=None, max_seqlen: int = 0,
     dv = dv if dv is not None else torch.empty(v.shape, dtype=v.dtype, device=v.device)
     if q.is_cuda and _has_native_attn() and hasattr(native(), "attn_bwd"):
         cu = cu_seqlens if cu_seqlens is not None else torch.tensor([0, T], dtype=torch.int32, device=q.device)
-        native().attn_bwd(do, q, k, v, o, lse, cu, int(max_seqlen or T), float(scale), dq, dk, dv)
+        # fp32 dQ accumulator and per-row delta: scratch of this call
+        dq_acc = torch.empty(T, hq, D, dtype=torch.float32, device=q.device)
+        delta = torch.empty(hq, T, dtype=torch.float32, device=q.device)
+        native().attn_bwd(do, q, k, v, o.reshape(T, hq, D), lse, cu, int(max_seqlen or T),
+                          float(scale), dq, dk, dv, dq_acc, delta)
         return dq, dk, dv
     with torch.enable_grad():
         qq = q.detach().requires_grad_(True)
