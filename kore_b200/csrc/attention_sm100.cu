@@ -723,3 +723,118 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
 }
 
 }  // namespace kore
+
+// ============================================================== allocation-free variant
+// See attention_noalloc.h: same kernels as kore::attn_bwd, with the scratch
+// (fp32 dQ accumulator + delta) in a fixed device array instead of
+// caller-provided tensors. Nothing here allocates memory.
+#include <mutex>
+
+#include "attention_noalloc.h"
+
+namespace kore {
+namespace attn {
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[KORE_ATTN_NOALLOC_SCRATCH_BYTES];
+
+struct NoallocDeviceState {
+  void* scratch = nullptr;  // device address of g_noalloc_scratch on this device
+  bool smem_attr = false;
+};
+
+static int noalloc_setup(int dev, NoallocDeviceState** out) {
+  static std::mutex mu;
+  static NoallocDeviceState states[64];
+  if (dev < 0 || dev >= 64) return KORE_NOALLOC_ERR_SETUP;
+  std::lock_guard<std::mutex> lock(mu);
+  NoallocDeviceState& s = states[dev];
+  if (s.scratch == nullptr) {
+    // host code must not use the array's name as an address: ask the runtime
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+      return KORE_NOALLOC_ERR_SETUP;
+    s.scratch = ptr;
+  }
+  if (!s.smem_attr) {
+    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             BwdSmem::TOTAL) != cudaSuccess)
+      return KORE_NOALLOC_ERR_SETUP;
+    s.smem_attr = true;
+  }
+  *out = &s;
+  return KORE_NOALLOC_OK;
+}
+
+}  // namespace attn
+}  // namespace kore
+
+extern "C" int kore_attn_bwd_noalloc(const void* dout, int64_t ld_dout, const void* q,
+                                     int64_t ld_q, const void* k, int64_t ld_k, const void* v,
+                                     int64_t ld_v, const void* o, const float* lse,
+                                     const int* cu_seqlens, int nseq, int max_seqlen, int T,
+                                     int Hq, int Hkv, float scale, void* dq, int64_t ld_dq,
+                                     void* dk, int64_t ld_dk, void* dv, int64_t ld_dv,
+                                     cudaStream_t stream) {
+  using namespace kore;
+  using namespace kore::attn;
+  if (T <= 0 || nseq <= 0 || max_seqlen <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
+    return KORE_NOALLOC_ERR_ARGS;
+  const int64_t ld[7] = {ld_dout, ld_q, ld_k, ld_v, ld_dq, ld_dk, ld_dv};
+  for (int64_t x : ld)
+    if (x <= 0 || x % 8 != 0) return KORE_NOALLOC_ERR_ARGS;
+  const void* ptrs[10] = {dout, q, k, v, o, lse, cu_seqlens, dq, dk, dv};
+  for (const void* ptr : ptrs)
+    if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return KORE_NOALLOC_ERR_ARGS;
+  const uint64_t acc_bytes = (uint64_t)T * Hq * D * sizeof(float);
+  const uint64_t delta_bytes = (uint64_t)T * Hq * sizeof(float);
+  if (acc_bytes + delta_bytes > KORE_ATTN_NOALLOC_SCRATCH_BYTES) return KORE_NOALLOC_ERR_TOO_LARGE;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KORE_NOALLOC_ERR_SETUP;
+  NoallocDeviceState* st = nullptr;
+  int rc = noalloc_setup(dev, &st);
+  if (rc != KORE_NOALLOC_OK) return rc;
+  float* dq_acc = reinterpret_cast<float*>(st->scratch);
+  float* delta = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(st->scratch) + acc_bytes);
+  CUtensorMap tq, tk, tv, tdo;
+  try {
+    auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    tq = make_tmap_2d(q, bf, 2, (uint64_t)Hq * D, T, ld_q, 64, 128);
+    tk = make_tmap_2d(k, bf, 2, (uint64_t)Hkv * D, T, ld_k, 64, 128);
+    tv = make_tmap_2d(v, bf, 2, (uint64_t)Hkv * D, T, ld_v, 64, 128);
+    tdo = make_tmap_2d(dout, bf, 2, (uint64_t)Hq * D, T, ld_dout, 64, 128);
+  } catch (...) {
+    return KORE_NOALLOC_ERR_ARGS;
+  }
+  // delta and a zeroed dQ accumulator (the array keeps the previous call's data)
+  {
+    const long warps = (long)T * Hq;
+    attn_bwd_prep_kernel<<<(int)((warps * 32 + 255) / 256), 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(dout), (int)ld_dout,
+        reinterpret_cast<const __nv_bfloat16*>(o), Hq, T, delta, dq_acc);
+    if (cudaGetLastError() != cudaSuccess) return KORE_NOALLOC_ERR_LAUNCH;
+  }
+  BwdParams p;
+  p.cu_seqlens = cu_seqlens;
+  p.nseq = nseq;
+  p.nkblk = (max_seqlen + BKV - 1) / BKV;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale = scale;
+  p.scale_log2 = scale * kLog2e;
+  p.lse = lse;
+  p.delta = delta;
+  p.dq_acc = dq_acc;
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk);
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv);
+  p.ld_dk = (int)ld_dk;
+  p.ld_dv = (int)ld_dv;
+  p.T = T;
+  dim3 grid(nseq * p.nkblk, Hkv);
+  attn_bwd_kernel<<<grid, kThreads, BwdSmem::TOTAL, stream>>>(tq, tk, tv, tdo, p);
+  if (cudaGetLastError() != cudaSuccess) return KORE_NOALLOC_ERR_LAUNCH;
+  const long n8 = (long)T * Hq * (D / 8);
+  attn_dq_convert_kernel<<<(int)((n8 + 255) / 256), 256, 0, stream>>>(
+      dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), (int)ld_dq, Hq, T);
+  if (cudaGetLastError() != cudaSuccess) return KORE_NOALLOC_ERR_LAUNCH;
+  return KORE_NOALLOC_OK;
+}
