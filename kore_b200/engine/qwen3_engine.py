@@ -101,7 +101,8 @@ class Qwen3Engine:
     """
 
     def __init__(self, weights: Qwen3Weights, *, grad_dtype: Optional[torch.dtype] = None,
-                 logits_chunk: int = 4096, temperature: float = 1.0, allocate_grads: bool = True):
+                 logits_chunk: int = 4096, temperature: float = 1.0, allocate_grads: bool = True,
+                 save_attention: bool = True):
         self.w = weights
         self.cfg = weights.cfg
         if self.cfg.is_moe:
@@ -110,6 +111,9 @@ class Qwen3Engine:
         self.dtype = weights.dtype
         self.grad_dtype = grad_dtype or self.dtype
         self.logits_chunk = logits_chunk
+        # selective activation checkpointing: keep attention outputs (T x Hq*D
+        # bf16 + lse per layer) so the backward recomputes only the GEMMs
+        self.save_attention = save_attention
         self.temperature = temperature
         c = self.cfg
         self.hq, self.hkv, self.D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
@@ -142,7 +146,8 @@ class Qwen3Engine:
         return ops.mm(a, b, **kw)
 
     # ------------------------------------------------------------------ layer
-    def _layer_fwd(self, u: int, x: torch.Tensor, b: Batch, keep: bool):
+    def _layer_fwd(self, u: int, x: torch.Tensor, b: Batch, keep: bool, attn_saved=None,
+                   save_attn: Optional[list] = None):
         W = self.w.views(u)
         T = x.shape[0]
         qd, kd = self.hq * self.D, self.hkv * self.D
@@ -155,7 +160,12 @@ class Qwen3Engine:
         q = qk[:, :qd].view(T, self.hq, self.D)
         k = qk[:, qd:].view(T, self.hkv, self.D)
         v = qkv[:, qd + kd:].view(T, self.hkv, self.D)
-        o, lse = attn.attn_fwd(q, k, v, b.cu_seqlens, b.max_seqlen)
+        if attn_saved is not None:
+            o, lse = attn_saved           # selective checkpoint: no attention recompute
+        else:
+            o, lse = attn.attn_fwd(q, k, v, b.cu_seqlens, b.max_seqlen)
+        if save_attn is not None:
+            save_attn.append((o, lse))
         o2 = o.reshape(T, qd)
         x2 = self._mm(o2, W["o"], residual=x)
         rstd2 = torch.empty(T, **f32)
@@ -270,12 +280,17 @@ class Qwen3Engine:
 
     # ------------------------------------------------------------------ public
     @torch.no_grad()
-    def forward_hidden(self, b: Batch, checkpoints: Optional[list] = None) -> torch.Tensor:
+    def forward_hidden(self, b: Batch, checkpoints: Optional[list] = None,
+                       attn_saves: Optional[list] = None) -> torch.Tensor:
+        """Forward to the last hidden state. ``checkpoints`` collects each
+        layer's input; ``attn_saves`` (selective checkpointing) also keeps each
+        layer's attention output and logsumexp so the backward does not
+        recompute attention."""
         x = ops.embed_fwd(b.ids, self.w.views(0)["embed"])
         for u in range(1, self.w.num_units - 1):
             if checkpoints is not None:
                 checkpoints.append(x)
-            x, _ = self._layer_fwd(u, x, b, keep=False)
+            x, _ = self._layer_fwd(u, x, b, keep=False, save_attn=attn_saves)
         return x
 
     @torch.no_grad()
@@ -306,7 +321,8 @@ class Qwen3Engine:
         """
         assert (coef is None) != (coef_fn is None), "pass exactly one of coef / coef_fn"
         ckpts: list = []
-        x = self.forward_hidden(b, ckpts)
+        asaves: Optional[list] = [] if self.save_attention else None
+        x = self.forward_hidden(b, ckpts, asaves)
         uh = self.w.num_units - 1
         Wn = self.w.views(uh)["norm"]
         T = b.num_tokens
@@ -337,10 +353,13 @@ class Qwen3Engine:
         del dhn, hn, x
         for u in range(self.w.num_units - 2, 0, -1):
             xin = ckpts[u - 1]
-            _, ctx = self._layer_fwd(u, xin, b, keep=True)
+            saved = asaves[u - 1] if asaves is not None else None
+            _, ctx = self._layer_fwd(u, xin, b, keep=True, attn_saved=saved)
             dx = self._layer_bwd(u, xin, dx, ctx, b)
-            del ctx
+            del ctx, saved
             ckpts[u - 1] = None
+            if asaves is not None:
+                asaves[u - 1] = None
         # embedding
         Ge = self.grad_views(0)["embed"]
         if self._fresh[0] and not self.cfg.tie_word_embeddings:
