@@ -38,6 +38,15 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
               const at::Tensor& v, const at::Tensor& o, const at::Tensor& lse,
               const at::Tensor& cu_seqlens, int64_t max_seqlen, double scale, at::Tensor& dq,
               at::Tensor& dk, at::Tensor& dv, at::Tensor& dq_acc, at::Tensor& delta);
+void kv_append(const at::Tensor& k, const at::Tensor& v, const at::Tensor& slots, at::Tensor& kc,
+               at::Tensor& vc);
+void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc,
+                     const at::Tensor& block_table, const at::Tensor& seq_lens,
+                     const at::Tensor& q_start, int64_t max_q, int64_t page_size, double scale,
+                     int64_t nsplit, at::Tensor& out, const c10::optional<at::Tensor>& part_o,
+                     const c10::optional<at::Tensor>& part_ml);
+void sample_tokens(const at::Tensor& logits, double temperature, double top_p, int64_t seed,
+                   int64_t step, at::Tensor& tokens, at::Tensor& logprobs);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -57,5 +66,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &kore::adamw_step);
   m.def("attn_fwd", &kore::attn_fwd, "tcgen05 causal GQA flash attention forward");
   m.def("attn_bwd", &kore::attn_bwd, "tcgen05 causal GQA flash attention backward");
+  m.def("kv_append", &kore::kv_append);
+  m.def("paged_attention", &kore::paged_attention);
+  m.def("sample_tokens", &kore::sample_tokens);
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

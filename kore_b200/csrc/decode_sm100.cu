@@ -1,0 +1,377 @@
+// Rollout-engine kernels for sm_100a:
+//   * kv_append:     write new tokens' K/V (already normalised and rotated) into
+//                    the paged KV cache through each sequence's block table
+//   * paged_attn:    causal GQA attention of the newest q_len tokens of each
+//                    sequence over its paged KV history (decode when q_len == 1,
+//                    chunked "extend" prefill otherwise), split over the KV
+//                    length (flash-decoding) with an in-kernel online softmax
+//   * paged_combine: merges the per-split partial results
+//   * sample_tokens: temperature / top-p sampling with the Gumbel-max trick
+//                    (no sort: the nucleus threshold is found by bisection on
+//                    probability mass), returns the token and its log-prob
+// Decode attention is memory-bound (5 FLOP/byte for GQA 5:1), so it runs on
+// the CUDA cores with 16-byte vector loads; the GEMMs around it use tcgen05.
+//
+// Reference parity: the reference samples with HF generate on a dense cache
+// (kore/policy/grpo.py:2421-2425, temperature/top_p from
+// kore/policy/configs.py:247-248); paging and split-KV are new here.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace kore {
+namespace dec {
+
+constexpr int D = 128;
+
+// new_kv: [T, 2, Hkv, D] given as separate k [T, Hkv, D] / v [T, Hkv, D] views.
+// slot[t] = page * page_size + offset (precomputed on host side of the engine).
+__global__ void kv_append_kernel(const __nv_bfloat16* __restrict__ k, int ldk,
+                                 const __nv_bfloat16* __restrict__ v, int ldv,
+                                 const int* __restrict__ slots, __nv_bfloat16* __restrict__ kc,
+                                 __nv_bfloat16* __restrict__ vc, int T, int Hkv) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // one thread per 8 elements
+  const long per_tok = (long)Hkv * D / 8;
+  if (i >= (long)T * per_tok) return;
+  const long t = i / per_tok;
+  const int r = (int)(i % per_tok) * 8;
+  const long dst = (long)slots[t] * Hkv * D + r;
+  *reinterpret_cast<uint4*>(kc + dst) = *reinterpret_cast<const uint4*>(k + t * ldk + r);
+  *reinterpret_cast<uint4*>(vc + dst) = *reinterpret_cast<const uint4*>(v + t * ldv + r);
+}
+
+struct AttnParams {
+  const __nv_bfloat16* q;  // [Tq, Hq, D] (row stride ldq)
+  int ldq;
+  const __nv_bfloat16* kc;  // [pages * page_size, Hkv, D]
+  const __nv_bfloat16* vc;
+  const int* block_table;   // [nseq, max_pages]
+  int max_pages;
+  const int* seq_lens;      // [nseq] total tokens in cache (including the new ones)
+  const int* q_start;       // [nseq + 1] offsets of each sequence's query rows
+  int page_size;
+  int Hq, Hkv;
+  float scale_log2;
+  int nsplit;
+  float* part_o;    // [nsplit, Tq, Hq, D]
+  float* part_ml;   // [nsplit, Tq, Hq, 2] (max, sum) in log2 domain
+  __nv_bfloat16* out;  // [Tq, Hq, D]
+};
+
+constexpr int kGroupMax = 8;  // q heads per kv head handled by one CTA
+constexpr int kWarps = 4;
+
+// grid: (nseq * max_q_len, Hkv, nsplit); block: 128 threads. One CTA handles
+// ONE query token of one sequence and all G query heads of one kv head over
+// one split of the key range.
+__global__ void __launch_bounds__(kWarps * 32) paged_attn_kernel(AttnParams p, int max_q) {
+  const int seq = blockIdx.x / max_q;
+  const int qi = blockIdx.x % max_q;
+  const int kvh = blockIdx.y;
+  const int split = blockIdx.z;
+  const int q0 = p.q_start[seq], q1 = p.q_start[seq + 1];
+  const int qlen = q1 - q0;
+  if (qi >= qlen) return;
+  const int L = p.seq_lens[seq];
+  const int qpos = L - qlen + qi;      // absolute position of this query token
+  const int nkeys = qpos + 1;          // causal: keys 0..qpos
+  const int per = (nkeys + p.nsplit - 1) / p.nsplit;
+  const int k_begin = split * per;
+  const int k_end = min(nkeys, k_begin + per);
+  const int G = p.Hq / p.Hkv;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int trow = q0 + qi;
+
+  float qv[kGroupMax][4];
+#pragma unroll
+  for (int g = 0; g < kGroupMax; ++g) {
+    if (g < G) {
+      const __nv_bfloat16* qp = p.q + (size_t)trow * p.ldq + (kvh * G + g) * D + lane * 4;
+      uint2 u = *reinterpret_cast<const uint2*>(qp);
+      float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.x));
+      float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.y));
+      qv[g][0] = a.x * p.scale_log2; qv[g][1] = a.y * p.scale_log2;
+      qv[g][2] = b.x * p.scale_log2; qv[g][3] = b.y * p.scale_log2;
+    }
+  }
+  float m[kGroupMax], l[kGroupMax], acc[kGroupMax][4];
+#pragma unroll
+  for (int g = 0; g < kGroupMax; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+  }
+  const int* bt = p.block_table + (size_t)seq * p.max_pages;
+  for (int key = k_begin + warp; key < k_end; key += kWarps) {
+    const int page = bt[key / p.page_size];
+    const size_t row = ((size_t)page * p.page_size + key % p.page_size) * p.Hkv + kvh;
+    uint2 ku = *reinterpret_cast<const uint2*>(p.kc + row * D + lane * 4);
+    uint2 vu = *reinterpret_cast<const uint2*>(p.vc + row * D + lane * 4);
+    float2 ka = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&ku.x));
+    float2 kb = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&ku.y));
+    float2 va = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&vu.x));
+    float2 vb = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&vu.y));
+    float s[kGroupMax];
+#pragma unroll
+    for (int g = 0; g < kGroupMax; ++g)
+      s[g] = g < G ? qv[g][0] * ka.x + qv[g][1] * ka.y + qv[g][2] * kb.x + qv[g][3] * kb.y : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int g = 0; g < kGroupMax; ++g) s[g] += __shfl_xor_sync(0xffffffff, s[g], o);
+#pragma unroll
+    for (int g = 0; g < kGroupMax; ++g) {
+      if (g >= G) continue;
+      const float mn = fmaxf(m[g], s[g]);
+      const float c = exp2f(m[g] - mn);
+      const float e = exp2f(s[g] - mn);
+      l[g] = l[g] * c + e;
+      acc[g][0] = acc[g][0] * c + e * va.x;
+      acc[g][1] = acc[g][1] * c + e * va.y;
+      acc[g][2] = acc[g][2] * c + e * vb.x;
+      acc[g][3] = acc[g][3] * c + e * vb.y;
+      m[g] = mn;
+    }
+  }
+  // combine the 4 warps through shared memory
+  __shared__ float sm_m[kWarps][kGroupMax], sm_l[kWarps][kGroupMax];
+  __shared__ float sm_acc[kWarps][kGroupMax][D];
+  if (lane == 0) {
+#pragma unroll
+    for (int g = 0; g < kGroupMax; ++g) { sm_m[warp][g] = m[g]; sm_l[warp][g] = l[g]; }
+  }
+#pragma unroll
+  for (int g = 0; g < kGroupMax; ++g)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sm_acc[warp][g][lane * 4 + e] = acc[g][e];
+  __syncthreads();
+  // thread t handles (g, d) pairs
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int g = idx / D, d = idx % D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, sm_m[w][g]);
+    float ll = 0.f, aa = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      if (sm_m[w][g] == -INFINITY) continue;
+      const float c = exp2f(sm_m[w][g] - mm);
+      ll += sm_l[w][g] * c;
+      aa += sm_acc[w][g][d] * c;
+    }
+    const int h = kvh * G + g;
+    if (p.nsplit == 1) {
+      p.out[((size_t)trow * p.Hq + h) * D + d] = __float2bfloat16(ll > 0.f ? aa / ll : 0.f);
+    } else {
+      const size_t tq = (size_t)p.q_start[gridDim.x / max_q];  // total query rows
+      const size_t o = (((size_t)split * tq + trow) * p.Hq + h);
+      p.part_o[o * D + d] = aa;
+      if (d == 0) {
+        p.part_ml[o * 2 + 0] = mm;
+        p.part_ml[o * 2 + 1] = ll;
+      }
+    }
+  }
+}
+
+__global__ void paged_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
+                                     __nv_bfloat16* __restrict__ out, int Tq, int Hq, int nsplit) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // over Tq * Hq * D
+  if (i >= (long)Tq * Hq * D) return;
+  const long row = i / D;  // (t, h)
+  const int d = i % D;
+  float mm = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mm = fmaxf(mm, part_ml[((size_t)s * Tq * Hq + row) * 2]);
+  float ll = 0.f, aa = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const size_t o = (size_t)s * Tq * Hq + row;
+    const float ms = part_ml[o * 2];
+    if (ms == -INFINITY) continue;
+    const float c = exp2f(ms - mm);
+    ll += part_ml[o * 2 + 1] * c;
+    aa += part_o[o * D + d] * c;
+  }
+  out[row * D + d] = __float2bfloat16(ll > 0.f ? aa / ll : 0.f);
+}
+
+// ---------------------------------------------------------------- sampling
+// Counter-based hash ("lowbias32", C. Wellons 2018) -> uniform in (0, 1).
+KORE_DEV uint32_t hash32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+KORE_DEV float uniform01(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t h = hash32(a ^ hash32(b ^ hash32(c)));
+  return ((h >> 8) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+constexpr int kSampThreads = 1024;
+
+template <typename T>
+KORE_DEV float blk_reduce(float v, float* red, bool is_max) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float w = __shfl_xor_sync(0xffffffff, v, o);
+    v = is_max ? fmaxf(v, w) : v + w;
+  }
+  const int wid = threadIdx.x / 32, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float r = is_max ? -INFINITY : 0.f;
+  for (int i = 0; i < (int)(blockDim.x / 32); ++i) r = is_max ? fmaxf(r, red[i]) : r + red[i];
+  return r;
+}
+
+// One CTA per row. logits [B, V] bf16. Writes token[b] and its log-prob under
+// the temperature-scaled full distribution.
+__global__ void __launch_bounds__(kSampThreads) sample_kernel(
+    const __nv_bfloat16* __restrict__ logits, int ld, int V, float inv_temp, float top_p,
+    uint32_t seed, uint32_t step, int greedy, long* __restrict__ out_tok, float* __restrict__ out_lp) {
+  __shared__ float red[32];
+  __shared__ float s_best[32];
+  __shared__ int s_bidx[32];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* z = logits + (size_t)row * ld;
+  // pass 1: max and sum of exp
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) mx = fmaxf(mx, __bfloat162float(z[j]) * inv_temp);
+  mx = blk_reduce<float>(mx, red, true);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) sum += exp2f((__bfloat162float(z[j]) * inv_temp - mx) * 1.4426950408889634f);
+  sum = blk_reduce<float>(sum, red, false);
+  const float lse = mx + __logf(sum);
+  // nucleus threshold (in logit units): largest t with mass(z >= t) >= top_p
+  float thr = -INFINITY;
+  if (top_p < 1.f) {
+    float lo = mx - 40.f, hi = mx;  // mass(z >= lo) ~ 1, mass(z >= hi) small
+    for (int it = 0; it < 24; ++it) {
+      const float mid = 0.5f * (lo + hi);
+      float mass = 0.f;
+      for (int j = threadIdx.x; j < V; j += blockDim.x) {
+        const float zz = __bfloat162float(z[j]) * inv_temp;
+        if (zz >= mid) mass += __expf(zz - lse);
+      }
+      mass = blk_reduce<float>(mass, red, false);
+      if (mass >= top_p) lo = mid; else hi = mid;
+    }
+    thr = lo;
+  }
+  // Gumbel-max over the nucleus
+  float best = -INFINITY;
+  int bidx = 0;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    const float zz = __bfloat162float(z[j]) * inv_temp;
+    if (zz < thr) continue;
+    float g = zz;
+    if (!greedy) {
+      const float u = uniform01(seed, step * 0x9E3779B9u + row, (uint32_t)j);
+      g -= __logf(-__logf(u));
+    }
+    if (g > best) { best = g; bidx = j; }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float b2 = __shfl_xor_sync(0xffffffff, best, o);
+    int i2 = __shfl_xor_sync(0xffffffff, bidx, o);
+    if (b2 > best || (b2 == best && i2 < bidx)) { best = b2; bidx = i2; }
+  }
+  const int wid = threadIdx.x / 32, lane = threadIdx.x & 31;
+  if (lane == 0) { s_best[wid] = best; s_bidx[wid] = bidx; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float bb = -INFINITY;
+    int bi = 0;
+    for (int i = 0; i < (int)(blockDim.x / 32); ++i)
+      if (s_best[i] > bb || (s_best[i] == bb && s_bidx[i] < bi)) { bb = s_best[i]; bi = s_bidx[i]; }
+    out_tok[row] = bi;
+    out_lp[row] = __bfloat162float(z[bi]) * inv_temp - lse;
+  }
+}
+
+}  // namespace dec
+
+void kv_append(const at::Tensor& k, const at::Tensor& v, const at::Tensor& slots, at::Tensor& kc,
+               at::Tensor& vc) {
+  using namespace dec;
+  const int T = k.size(0), Hkv = k.size(1);
+  TORCH_CHECK(k.size(2) == D && v.size(2) == D && k.stride(2) == 1 && k.stride(1) == D &&
+                  v.stride(1) == D, "kv_append: expected [T, Hkv, 128] views with contiguous heads");
+  TORCH_CHECK(slots.scalar_type() == at::kInt && slots.numel() == T, "slots int32 [T]");
+  if (T == 0) return;
+  c10::cuda::CUDAGuard g(k.device());
+  const long n = (long)T * Hkv * D / 8;
+  kv_append_kernel<<<(int)((n + 255) / 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)k.data_ptr(), k.stride(0), (const __nv_bfloat16*)v.data_ptr(), v.stride(0),
+      slots.data_ptr<int>(), (__nv_bfloat16*)kc.data_ptr(), (__nv_bfloat16*)vc.data_ptr(), T, Hkv);
+  check_cuda(cudaGetLastError(), "kv_append");
+}
+
+// q: [Tq, Hq, 128] (row stride); caches [slots, Hkv, 128]; returns out [Tq, Hq, 128].
+void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc,
+                     const at::Tensor& block_table, const at::Tensor& seq_lens,
+                     const at::Tensor& q_start, int64_t max_q, int64_t page_size, double scale,
+                     int64_t nsplit, at::Tensor& out, const c10::optional<at::Tensor>& part_o,
+                     const c10::optional<at::Tensor>& part_ml) {
+  using namespace dec;
+  const int Tq = q.size(0), Hq = q.size(1), Hkv = kc.size(1);
+  TORCH_CHECK(q.size(2) == D && q.stride(2) == 1 && q.stride(1) == D, "q layout");
+  TORCH_CHECK(Hq % Hkv == 0 && Hq / Hkv <= kGroupMax, "GQA group too large");
+  const int nseq = seq_lens.numel();
+  if (Tq == 0 || nseq == 0) return;
+  if (nsplit > 1)
+    TORCH_CHECK(part_o.has_value() && part_ml.has_value() &&
+                    part_o->numel() >= (int64_t)nsplit * Tq * Hq * D && part_ml->numel() >= (int64_t)nsplit * Tq * Hq * 2,
+                "split-KV needs partial buffers");
+  c10::cuda::CUDAGuard g(q.device());
+  AttnParams p;
+  p.q = (const __nv_bfloat16*)q.data_ptr();
+  p.ldq = q.stride(0);
+  p.kc = (const __nv_bfloat16*)kc.data_ptr();
+  p.vc = (const __nv_bfloat16*)vc.data_ptr();
+  p.block_table = block_table.data_ptr<int>();
+  p.max_pages = block_table.size(1);
+  p.seq_lens = seq_lens.data_ptr<int>();
+  p.q_start = q_start.data_ptr<int>();
+  p.page_size = page_size;
+  p.Hq = Hq;
+  p.Hkv = Hkv;
+  p.scale_log2 = (float)scale * 1.4426950408889634f;
+  p.nsplit = nsplit;
+  p.part_o = nsplit > 1 ? part_o->data_ptr<float>() : nullptr;
+  p.part_ml = nsplit > 1 ? part_ml->data_ptr<float>() : nullptr;
+  p.out = (__nv_bfloat16*)out.data_ptr();
+  auto st = at::cuda::getCurrentCUDAStream();
+  dim3 grid(nseq * max_q, Hkv, nsplit);
+  paged_attn_kernel<<<grid, kWarps * 32, 0, st>>>(p, (int)max_q);
+  check_cuda(cudaGetLastError(), "paged_attn");
+  if (nsplit > 1) {
+    const long n = (long)Tq * Hq * D;
+    paged_combine_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(p.part_o, p.part_ml, p.out, Tq, Hq, nsplit);
+    check_cuda(cudaGetLastError(), "paged_combine");
+  }
+}
+
+void sample_tokens(const at::Tensor& logits, double temperature, double top_p, int64_t seed,
+                   int64_t step, at::Tensor& tokens, at::Tensor& logprobs) {
+  using namespace dec;
+  TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1, "logits bf16 rows");
+  const int B = logits.size(0), V = logits.size(1);
+  if (B == 0) return;
+  c10::cuda::CUDAGuard g(logits.device());
+  const bool greedy = temperature <= 0.0;
+  sample_kernel<<<B, kSampThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
+      greedy ? 1.f : (float)(1.0 / temperature), greedy ? 1.f : (float)top_p, (uint32_t)seed,
+      (uint32_t)step, greedy ? 1 : 0, tokens.data_ptr<long>(), logprobs.data_ptr<float>());
+  check_cuda(cudaGetLastError(), "sample_tokens");
+}
+
+}  // namespace kore

@@ -1,0 +1,396 @@
+"""Multi-turn GRPO trainer (Kevin credit + anti-collapse ladder) on the
+explicit engine and the paged rollout engine.
+
+One optimizer step:
+  1. rollout: for each task group, ``num_trajectories`` trajectories refine
+     their answer over ``num_turns`` turns (serial refinement); each turn's
+     context is the transcript so far plus the environment's feedback. The
+     rollout engine generates every trajectory of the group in one continuous
+     batch, sharing the prompt's KV pages inside the group. Trajectories are
+     split over ranks with a strided slice (replicated rollout on every rank);
+  2. credit: per-turn Kevin returns (correctness-gated, gamma look-ahead,
+     optional potential-based shaping), infra turns dropped; group-relative
+     AVSPO advantages over the group's per-turn samples gathered from all
+     ranks; StarPO-S / DAPO dynamic sampling keep the informative groups;
+  3. old/ref log-probs: old = the sampler's temperature-scaled log-probs of
+     the generated tokens (token mean), ref = a frozen reference model
+     forward (token mean);
+  4. update: global token-mean clip-higher surrogate + k3 KL anchor, as
+     per-token coefficients into the engine's two-phase head (packed
+     micro-batches, no autograd graph), one AdamW step (sharded over ranks),
+     then the weight sync back to the rollout engine (free on one GPU: the
+     engine reads the trainer's buffers).
+
+Behavioural parity: kore/policy/grpo.py:565-2331 (train_grpo, Kevin credit,
+_accumulate_grpo_grads, the distributed loop).
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import sys
+import time
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Callable, Dict, List, Optional, Sequence
+
+import torch
+
+from ..env.base import RolloutEnv, SyntheticRewardEnv, TurnResult
+from ..obs import configure, get_logger
+from ..parallel.dist import DistContext, get_context, init_distributed
+from . import rl_math as M
+from .configs import GRPOConfig, grpo_config_from_dict
+
+log = get_logger("policy.grpo")
+
+
+@dataclass
+class Trajectory:
+    traj: int
+    contexts: List[List[int]] = field(default_factory=list)   # prompt ids of each turn
+    gens: List[List[int]] = field(default_factory=list)       # generated ids of each turn
+    gen_logps: List[List[float]] = field(default_factory=list)
+    results: List[TurnResult] = field(default_factory=list)
+    finish: List[str] = field(default_factory=list)
+
+
+@dataclass
+class TrainSample:
+    ids: List[int]          # context + generation
+    n_ctx: int
+    ret: float
+    adv: float = 0.0
+    old_logp: Optional[float] = None
+    ref_logp: Optional[float] = None
+    overlong: bool = False
+
+    @property
+    def n_gen(self) -> int:
+        return len(self.ids) - self.n_ctx
+
+
+class GRPOTrainer:
+    """GRPO over a :class:`CausalLMTrainer`-style engine/optimizer pair."""
+
+    def __init__(self, config: GRPOConfig, *, weights=None, ref_weights=None, env: Optional[RolloutEnv] = None,
+                 ctx: Optional[DistContext] = None, tokenizer=None, model_cfg=None,
+                 rollout_kwargs: Optional[dict] = None):
+        from ..engine.qwen3_engine import Qwen3Engine
+        from ..engine.rollout import RolloutEngine
+        from ..engine.trainer import CausalLMTrainer
+        from ..models import Qwen3Config, Qwen3Weights
+        self.cfg = config
+        self.ctx = ctx or get_context()
+        self.env = env or SyntheticRewardEnv(seed=config.seed)
+        self.tok = tokenizer
+        if weights is None:
+            mc = model_cfg or Qwen3Config()
+            dtype = torch.bfloat16 if (config.bf16 and self.ctx.device.type == "cuda") else torch.float32
+            weights = Qwen3Weights(mc, device=self.ctx.device, dtype=dtype, seed=config.seed,
+                                   pad_multiple=128 * max(1, self.ctx.world))
+        self.trainer = CausalLMTrainer(weights.cfg, self.ctx, lr=config.learning_rate,
+                                       max_grad_norm=config.max_grad_norm, seed=config.seed,
+                                       schedule=config.lr_scheduler_type,
+                                       warmup_steps=int(config.warmup_ratio * config.total_steps),
+                                       total_steps=config.total_steps, weights=weights,
+                                       comm=getattr(config, "comm", "nccl"))
+        self.trainer.eng.temperature = config.temperature
+        self.w = weights
+        self.ref_w = ref_weights if ref_weights is not None else (
+            weights.clone() if config.ref_anchor_coef else None)
+        self.ref_eng = (Qwen3Engine(self.ref_w, allocate_grads=False, temperature=config.temperature)
+                        if self.ref_w is not None else None)
+        rk = dict(max_batch=config.rollout_max_batch, page_size=min(config.kv_page_size, 128),
+                  kv_fraction=config.kv_cache_fraction)
+        rk.update(rollout_kwargs or {})
+        self.rollout = RolloutEngine(self.w, **rk)
+        self.step_idx = 0
+        self.controller = (M.DynamicStepController(config.min_steps, config.total_steps,
+                                                   config.plateau_patience, config.plateau_min_delta)
+                           if config.adaptive_steps else None)
+        self.eos = []
+        if tokenizer is not None:
+            from ..data.tokenizer import eos_ids
+            self.eos = eos_ids(tokenizer)
+
+    # ------------------------------------------------------------ rollout
+    def _decode(self, ids: Sequence[int]) -> str:
+        if self.tok is None:
+            return ""
+        return self.tok.decode(list(ids))
+
+    def _initial_context(self, task) -> List[int]:
+        if isinstance(self.env, SyntheticRewardEnv):
+            return self.env.prompt_ids(task)
+        from ..data.tokenizer import render_chat
+        ids, _ = render_chat(self.tok, self.env.prompt_messages(task), add_generation_prompt=True)
+        return ids[-self.cfg.max_prompt_length:]
+
+    def _feedback_ids(self, task, tr: TurnResult, turn: int, traj: int) -> List[int]:
+        if isinstance(self.env, SyntheticRewardEnv):
+            return self.env.feedback_ids(task, turn, traj)
+        from ..data.tokenizer import render_chat
+        ids, _ = render_chat(self.tok, [{"role": "user", "content": f"Verifier feedback:\n{tr.feedback}"}],
+                             add_generation_prompt=True)
+        return ids
+
+    def rollout_group(self, task, traj_ids: Sequence[int], *, max_new_tokens: Optional[int] = None
+                      ) -> List[Trajectory]:
+        cfg = self.cfg
+        max_new = max_new_tokens or cfg.max_response_length
+        base = self._initial_context(task)
+        trajs = [Trajectory(t) for t in traj_ids]
+        ctxs = [list(base) for _ in trajs]
+        for turn in range(cfg.num_turns):
+            from ..engine.rollout import GenRequest
+            reqs = []
+            for i, (tr, c) in enumerate(zip(trajs, ctxs)):
+                c = c[-cfg.max_prompt_length:]
+                ctxs[i] = c
+                reqs.append(GenRequest(prompt=c, max_new_tokens=max_new, rid=i,
+                                       share_key=(task, "t0") if turn == 0 else None))
+            outs = self.rollout.generate(reqs, temperature=cfg.temperature, top_p=cfg.top_p,
+                                         eos_ids=self.eos, seed=cfg.seed * 1000003 + self.step_idx * 97 + turn)
+            for i, (tr, o) in enumerate(zip(trajs, outs)):
+                tr.contexts.append(list(ctxs[i]))
+                tr.gens.append(list(o.tokens))
+                tr.gen_logps.append(list(o.logps))
+                tr.finish.append(o.finish_reason)
+                res = self.env.step(task, self._decode(o.tokens), turn, tr.traj, tr.results)
+                tr.results.append(res)
+                ctxs[i] = ctxs[i] + list(o.tokens) + self._feedback_ids(task, res, turn, tr.traj)
+        return trajs
+
+    # ------------------------------------------------------------ credit
+    def samples_from_group(self, trajs: List[Trajectory]) -> List[TrainSample]:
+        cfg = self.cfg
+        rewards = [[r.reward for r in t.results] for t in trajs]
+        correct = [[r.correct for r in t.results] for t in trajs]
+        infra = [[r.infra for r in t.results] for t in trajs]
+        phis = [[r.phi for r in t.results] for t in trajs] if cfg.physics_shaping_weight else None
+        rets, idx = M.build_kevin_samples(rewards, correct, cfg.gamma, infra,
+                                          credit_incorrect=cfg.credit_incorrect_turns,
+                                          traj_phis=phis, phi_weight=cfg.physics_shaping_weight)
+        out = []
+        for r, (ti, tu) in zip(rets, idx):
+            t = trajs[ti]
+            gl = t.gen_logps[tu]
+            n = len(t.gens[tu])
+            if n == 0:
+                continue
+            over = cfg.overlong_mask and M.is_overlong(n, cfg.max_response_length, cfg.overlong_buffer_len) \
+                and t.finish[tu] == "length"
+            out.append(TrainSample(ids=t.contexts[tu] + t.gens[tu], n_ctx=len(t.contexts[tu]), ret=r,
+                                   old_logp=sum(gl) / max(1, len(gl)), overlong=over))
+        return out
+
+    def assign_advantages(self, groups: List[List[TrainSample]]) -> List[List[TrainSample]]:
+        """Cross-rank group advantages; then StarPO-S selection of groups."""
+        cfg = self.cfg
+        kept_idx = list(range(len(groups)))
+        per_group_returns = []
+        for g in groups:
+            per_rank = self.ctx.all_gather_object([s.ret for s in g])
+            per_group_returns.append(per_rank)
+            adv = M.distributed_group_advantages(per_rank, cfg.variance_floor, cfg.avspo_virtual_k,
+                                                 cfg.adv_eps)[self.ctx.rank]
+            for s, a in zip(g, adv):
+                s.adv = a
+        if cfg.starpo_s:
+            full = [M.merge_across_ranks(pr) for pr in per_group_returns]
+            kept_idx = M.starpo_select_high_variance(full, cfg.starpo_keep_frac, cfg.starpo_min_std)
+        return [groups[i] for i in kept_idx]
+
+    # ------------------------------------------------------------ update
+    def _pack(self, samples: List[TrainSample], budget: int):
+        cur, n = [], 0
+        for s in samples:
+            if cur and n + len(s.ids) > budget:
+                yield cur
+                cur, n = [], 0
+            cur.append(s)
+            n += len(s.ids)
+        if cur:
+            yield cur
+
+    def _batch(self, samples: List[TrainSample]):
+        from ..engine.qwen3_engine import Batch
+        dev = self.ctx.device
+        seqs, masks = [], []
+        for s in samples:
+            seqs.append(torch.tensor(s.ids, dtype=torch.long))
+            m = torch.zeros(len(s.ids), dtype=torch.bool)
+            m[s.n_ctx:] = True
+            masks.append(m)
+        return Batch.from_sequences(seqs, masks, device=dev)
+
+    @staticmethod
+    def _segments(b, samples):
+        """Per-token sample index for label positions (target >= 0)."""
+        seg = torch.full((b.num_tokens,), -1, dtype=torch.long)
+        off = 0
+        for i, s in enumerate(samples):
+            L = len(s.ids)
+            seg[off + s.n_ctx - 1: off + L - 1] = i  # label positions predict generated tokens
+            off += L
+        return seg.to(b.ids.device)
+
+    @torch.no_grad()
+    def fill_ref_logps(self, samples: List[TrainSample], budget: int):
+        if self.ref_eng is None:
+            return
+        for chunk in self._pack(samples, budget):
+            b = self._batch(chunk)
+            lp, _ = self.ref_eng.token_logprobs(b)
+            seg = self._segments(b, chunk)
+            sums = torch.zeros(len(chunk), dtype=torch.float64, device=lp.device)
+            sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, lp.double(), torch.zeros_like(lp.double())))
+            for s, v in zip(chunk, sums.tolist()):
+                s.ref_logp = v / max(1, s.n_gen)
+
+    def update(self, samples: List[TrainSample], budget: int) -> Dict[str, float]:
+        cfg = self.cfg
+        train = [s for s in samples if not s.overlong]
+        eng = self.trainer.eng
+        tot = torch.tensor([float(sum(s.n_gen for s in train))], dtype=torch.float64,
+                           device=self.ctx.device if self.ctx.backend == "nccl" else "cpu")
+        self.ctx.all_reduce(tot)
+        total_tokens = max(1.0, float(tot.item()))
+        eng.zero_grad()
+        loss_sum = 0.0
+        kl_sum, kl_n = 0.0, 0
+        for chunk in self._pack(train, budget):
+            b = self._batch(chunk)
+            seg = self._segments(b, chunk)
+            gs = [M.GRPOSample(adv=s.adv, n_tokens=s.n_gen, old_logp=s.old_logp,
+                               ref_logp=s.ref_logp if cfg.ref_anchor_coef else None) for s in chunk]
+
+            def coef_fn(lp_full, seg=seg, chunk=chunk, gs=gs):
+                sums = torch.zeros(len(chunk), dtype=torch.float64, device=lp_full.device)
+                sums.index_add_(0, seg.clamp_min(0),
+                                torch.where(seg >= 0, lp_full.double(), torch.zeros_like(lp_full.double())))
+                lps = [v / max(1, s.n_gen) for v, s in zip(sums.tolist(), chunk)]
+                loss, coefs = M.grpo_token_coefficients(gs, lps, clip_lo=cfg.clip_ratio_low,
+                                                        clip_hi=cfg.clip_ratio_high,
+                                                        ref_coef=cfg.ref_anchor_coef,
+                                                        total_tokens=int(total_tokens))
+                cvec = torch.tensor(coefs, dtype=torch.float32, device=lp_full.device)
+                coef = torch.where(seg >= 0, cvec[seg.clamp_min(0)], torch.zeros_like(lp_full))
+                nonlocal kl_sum, kl_n
+                for s, lp in zip(chunk, lps):
+                    if s.ref_logp is not None:
+                        kl_sum += M.kl_k3(lp, s.ref_logp)
+                        kl_n += 1
+                return coef, loss
+
+            out = eng.forward_backward(b, coef_fn=coef_fn)
+            loss_sum += float(out["loss"])
+        self.trainer.opt.step()
+        return {"loss": loss_sum, "kl": kl_sum / max(1, kl_n), "tokens": total_tokens}
+
+    # ------------------------------------------------------------ step
+    def train_step(self, tasks: Sequence[Any], *, max_new_tokens: Optional[int] = None,
+                   micro_batch_tokens: int = 16384) -> Dict[str, float]:
+        cfg = self.cfg
+        t0 = time.time()
+        G = cfg.num_trajectories
+        W = self.ctx.world
+        if G % W:
+            G += W - G % W  # every rank rolls the same number of trajectories
+        mine = M.rank_slice(G, self.ctx.rank, W)
+        groups: List[List[TrainSample]] = []
+        rewards_all: List[float] = []
+        gen_tokens = 0
+
+        def roll(attempt):
+            task = tasks[attempt % len(tasks)]
+            trajs = self.rollout_group(task, mine, max_new_tokens=max_new_tokens)
+            nonlocal gen_tokens
+            gen_tokens += sum(len(g) for t in trajs for g in t.gens)
+            return self.samples_from_group(trajs), [M.kevin_trajectory_score(
+                [r.reward for r in t.results], [r.correct for r in t.results]) for t in trajs]
+
+        target = cfg.target_groups or len(tasks)
+        if cfg.dynamic_sampling and W == 1:
+            kept, attempts = M.dynamic_sampling_refill(
+                roll, target, min_std=cfg.starpo_min_std,
+                max_attempts=cfg.max_sampling_attempts or 0,
+                std_key=lambda g: M.group_reward_std([s.ret for s in g[0]]))
+        else:  # ranks must roll identical group counts: no data-dependent refill
+            kept = [roll(i) for i in range(target)]
+        for g, scores in kept:
+            groups.append(g)
+            rewards_all.extend(scores)
+        groups = self.assign_advantages(groups)
+        samples = [s for g in groups for s in g]
+        self.fill_ref_logps(samples, micro_batch_tokens)
+        t_roll = time.time() - t0
+        stats = self.update(samples, micro_batch_tokens)
+        self.step_idx += 1
+        stats.update({"step": self.step_idx, "reward_mean": sum(rewards_all) / max(1, len(rewards_all)),
+                      "reward_std": M.group_reward_std(rewards_all), "groups": len(groups),
+                      "samples": len(samples), "gen_tokens": gen_tokens,
+                      "adv_absmean": sum(abs(s.adv) for s in samples) / max(1, len(samples)),
+                      "rollout_s": t_roll, "step_s": time.time() - t0,
+                      "grad_norm": self.trainer.opt.grad_norm()})
+        if self.ctx.is_main and (self.step_idx % max(1, cfg.logging_steps) == 0):
+            log.event("grpo_step", **{k: (round(v, 5) if isinstance(v, float) else v) for k, v in stats.items()})
+        return stats
+
+
+def train_grpo(config: GRPOConfig, tasks: Optional[List[str]] = None, backend: str = "inprocess",
+               env: Optional[RolloutEnv] = None, model_cfg=None, tokenizer=None) -> Dict[str, Any]:
+    """Run ``config.total_steps`` GRPO steps (or until the plateau controller
+    stops) and save an HF-format checkpoint to ``config.output_dir``."""
+    from ..data.tokenizer import load_tokenizer
+    from ..models.hf_io import load_pretrained_or_init, save_pretrained
+    ctx = init_distributed()
+    configure(config.output_dir)
+    tok = tokenizer or load_tokenizer(config.model_id)
+    weights = load_pretrained_or_init(config.model_id, ctx, model_cfg=model_cfg, bf16=config.bf16,
+                                      seed=config.seed)
+    if env is None:
+        env = SyntheticRewardEnv(seed=config.seed, vocab_size=weights.cfg.vocab_size) \
+            if config.reward_env == "synthetic" else _kernel_env(config)
+    tr = GRPOTrainer(config, weights=weights, env=env, ctx=ctx, tokenizer=tok)
+    tasks = list(tasks or ["synthetic-0"])
+    history = []
+    for step in range(config.total_steps):
+        k = config.tasks_per_step
+        batch = [tasks[(step * k + i) % len(tasks)] for i in range(k)]
+        st = tr.train_step(batch)
+        history.append(st)
+        if config.save_steps and (step + 1) % config.save_steps == 0 and ctx.is_main:
+            save_pretrained(weights, os.path.join(config.output_dir, f"checkpoint-{step + 1}"), tok,
+                            keep_last=1, trainer_state={"global_step": step + 1})
+        if tr.controller is not None and tr.controller.update(step, st["reward_mean"]):
+            log.info("adaptive stop", reason=tr.controller.stopped_reason)
+            break
+    if ctx.is_main:
+        save_pretrained(weights, config.output_dir, tok)
+    ctx.barrier()
+    return {"output_dir": config.output_dir, "history": history}
+
+
+def _kernel_env(config: GRPOConfig):
+    from ..env.kore_env import KernelRolloutEnv
+    return KernelRolloutEnv(config)
+
+
+def _main(argv: Optional[list] = None) -> int:
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if not argv:
+        print("usage: python -m kore_b200.policy.grpo <config.json>", file=sys.stderr)
+        return 2
+    raw = json.loads(Path(argv[0]).read_text())
+    tasks = raw.get("tasks")
+    cfg = grpo_config_from_dict(raw)
+    out = train_grpo(cfg, tasks=tasks)
+    print(f"[grpo] -> {out['output_dir']}")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(_main())
