@@ -65,8 +65,26 @@ class ShardedAdamW:
         return self.lr * self.lr_fn(self.step_count)
 
     def reduce_scatter_unit(self, u: int, async_op: bool = False):
+        if self.ctx.backend != "nccl":   # gloo has no reduce-scatter: all-reduce + slice
+            g = self.eng.grads[u]
+            dist.all_reduce(g, group=self.ctx.group)
+            s = self.shard_len[u]
+            self.gshard[u].copy_(g[self.ctx.rank * s:(self.ctx.rank + 1) * s])
+            return None
         return dist.reduce_scatter_tensor(self.gshard[u], self.eng.grads[u], op=dist.ReduceOp.SUM,
                                           group=self.ctx.group, async_op=async_op)
+
+    def all_gather_unit(self, u: int) -> None:
+        s = self.shard_len[u]
+        r = self.ctx.rank
+        if self.ctx.backend != "nccl":
+            parts = [torch.empty_like(self.w.bufs[u][:s]) for _ in range(self.ctx.world)]
+            dist.all_gather(parts, self.w.bufs[u][r * s:(r + 1) * s].clone(), group=self.ctx.group)
+            self.w.bufs[u].copy_(torch.cat(parts))
+            return
+        # in place: NCCL accepts send == recv + rank * count
+        dist.all_gather_into_tensor(self.w.bufs[u], self.w.bufs[u][r * s:(r + 1) * s],
+                                    group=self.ctx.group)
 
     @torch.no_grad()
     def step(self, grad_scale: float = 1.0, scattered: bool = False) -> None:
@@ -92,8 +110,7 @@ class ShardedAdamW:
                            grad_scale=grad_scale, master=self.master.get(u), sumsq_buf=sq,
                            max_norm=self.max_grad_norm,
                            seed=self.seed * 7919 + self.step_count * 104729 + u * 31 + r)
-            # in place: NCCL accepts send == recv + rank * count
-            dist.all_gather_into_tensor(self.w.bufs[u], pshard, group=self.ctx.group)
+            self.all_gather_unit(u)
 
     def grad_norm(self) -> float:
         return float(self.last_sumsq.sqrt()) if self.last_sumsq is not None else float("nan")
