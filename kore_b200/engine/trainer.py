@@ -86,6 +86,43 @@ class CausalLMTrainer:
         self.ctx.all_reduce(loss)
         return loss
 
+    @torch.no_grad()
+    def train_step_sequences(self, seqs, label_masks, *, micro_tokens: int = 16384,
+                             sample_weights=None) -> float:
+        """Variable-length sequences (lists of token ids) packed into micro-batches
+        of <= ``micro_tokens`` tokens; loss = global token mean of -logp over
+        label tokens (optionally weighted per sample). Returns the loss."""
+        dev = self.ctx.device
+        n_lab = sum(int(torch.as_tensor(m)[1:].sum()) * (sample_weights[i] if sample_weights else 1.0)
+                    for i, m in enumerate(label_masks))
+        tot = torch.tensor([float(n_lab)], dtype=torch.float32, device=dev)
+        self.ctx.all_reduce(tot)
+        self.eng.zero_grad()
+        loss = torch.zeros((), dtype=torch.float32, device=dev)
+        order = list(range(len(seqs)))
+        i = 0
+        while i < len(order):
+            chunk, ntok = [], 0
+            while i < len(order) and (not chunk or ntok + len(seqs[order[i]]) <= micro_tokens):
+                chunk.append(order[i])
+                ntok += len(seqs[order[i]])
+                i += 1
+            b = Batch.from_sequences([torch.as_tensor(seqs[j]) for j in chunk],
+                                     [torch.as_tensor(label_masks[j]) for j in chunk], device=dev)
+            coef = torch.zeros(b.num_tokens, dtype=torch.float32)
+            off = 0
+            for j in chunk:
+                L = len(seqs[j])
+                w = sample_weights[j] if sample_weights else 1.0
+                coef[off:off + L] = -w
+                off += L
+            coef = coef.to(dev) / tot
+            coef = torch.where(b.targets >= 0, coef, torch.zeros_like(coef))
+            loss += self.eng.forward_backward(b, coef=coef)["loss"]
+        self.opt.step()
+        self.ctx.all_reduce(loss)
+        return float(loss.item())
+
     def train_step(self, ids_host: torch.Tensor, loss_mask_host: Optional[torch.Tensor] = None
                    ) -> float:
         """Host inputs in, host loss out (the end-to-end call)."""
