@@ -47,6 +47,20 @@ void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor
                      const c10::optional<at::Tensor>& part_ml);
 void sample_tokens(const at::Tensor& logits, double temperature, double top_p, int64_t seed,
                    int64_t step, at::Tensor& tokens, at::Tensor& logprobs);
+int64_t symm_heap_create(int64_t bytes, int64_t rank, int64_t world);
+at::Tensor symm_heap_handle(int64_t id);
+void symm_heap_open(int64_t id, const at::Tensor& handles);
+at::Tensor symm_heap_tensor(int64_t id, int64_t offset, const std::vector<int64_t>& shape,
+                            at::ScalarType dtype);
+void symm_barrier(int64_t id, int64_t sig_offset, int64_t epoch);
+void symm_rs_sumsq(int64_t id, int64_t grad_offset, int64_t n, at::Tensor& out, at::Tensor& sumsq,
+                   double scale);
+void symm_scalar_allreduce(int64_t id, int64_t sig_offset, int64_t epoch, const at::Tensor& local,
+                           at::Tensor& out);
+void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t n, const at::Tensor& g,
+                      const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v, double lr,
+                      double b1, double b2, double eps, double wd, int64_t step,
+                      const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -69,5 +83,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_append", &kore::kv_append);
   m.def("paged_attention", &kore::paged_attention);
   m.def("sample_tokens", &kore::sample_tokens);
+  m.def("symm_heap_create", &kore::symm_heap_create);
+  m.def("symm_heap_handle", &kore::symm_heap_handle);
+  m.def("symm_heap_open", &kore::symm_heap_open);
+  m.def("symm_heap_tensor", &kore::symm_heap_tensor);
+  m.def("symm_barrier", &kore::symm_barrier);
+  m.def("symm_rs_sumsq", &kore::symm_rs_sumsq);
+  m.def("symm_scalar_allreduce", &kore::symm_scalar_allreduce);
+  m.def("symm_adamw_bcast", &kore::symm_adamw_bcast);
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

@@ -1,0 +1,349 @@
+// Symmetric peer memory over NVLink/NVSwitch and the fused collective kernels
+// of the sharded optimizer.
+//
+// SymmetricHeap: one cudaMalloc'd region per rank, exported with a CUDA IPC
+// handle, exchanged over the process group by the Python side, and mapped on
+// every peer (cudaIpcOpenMemHandle). Tensors carved from the heap therefore
+// have the same offset on every rank, and kernels address a peer's copy as
+// peer_base[p] + offset with plain loads/stores over NVLink.
+//
+// Kernels (all waits bounded; a timeout records error code 2 and returns):
+//   * symm_barrier:    epoch-tagged flag barrier across ranks
+//                      (st.release.sys / ld.acquire.sys)
+//   * rs_sumsq:        reduce-scatter of bf16 gradients (this rank's shard, summed
+//                      over all peers' full gradient buffers with P2P loads) into
+//                      an fp32 shard, fused with the sum of squares for clipping
+//   * scalar_allreduce: every rank publishes its partial sum-of-squares to all
+//                      peers; each rank then sums the world's values
+//   * adamw_bcast:     AdamW on the fp32 shard (global-norm clip read on device),
+//                      then the new bf16 parameters are stored straight into every
+//                      peer's parameter buffer (the all-gather fused into the
+//                      update, path b of the north star).
+// No TMA and no multicast loads touch peer memory here.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <cstring>
+#include <memory>
+#include <vector>
+
+#include "common.cuh"
+#include "tma_host.h"
+
+namespace kore {
+namespace symm {
+
+constexpr int kMaxWorld = 8;
+
+struct PeerPtrs {
+  char* p[kMaxWorld];
+};
+
+KORE_DEV void st_release_sys(unsigned long long* a, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(a), "l"(v) : "memory");
+}
+KORE_DEV unsigned long long ld_acquire_sys(const unsigned long long* a) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(a) : "memory");
+  return v;
+}
+
+// Wait until *a >= want (epoch compare on the high 32 bits). Bounded.
+KORE_DEV bool wait_epoch(const unsigned long long* a, unsigned int want) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    unsigned long long v = ld_acquire_sys(a);
+    if ((unsigned int)(v >> 32) >= want) return true;
+    if (it == 64) t0 = globaltimer();
+    if (it > 64 && globaltimer() - t0 > kWaitTimeoutNs) {
+      atomicExch(&g_error, 2);
+      return false;
+    }
+  }
+}
+
+// signal pad layout (per rank, in the heap): slot[0..world) barrier flags,
+// slot[16..16+world) scalar all-reduce values.
+__global__ void barrier_kernel(PeerPtrs sig, int rank, int world, unsigned int epoch,
+                               unsigned long long sig_off) {
+  const int p = threadIdx.x;
+  if (p < world) {
+    __threadfence_system();
+    unsigned long long* remote = reinterpret_cast<unsigned long long*>(sig.p[p] + sig_off) + rank;
+    st_release_sys(remote, ((unsigned long long)epoch) << 32);
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(sig.p[rank] + sig_off) + p;
+    wait_epoch(mine, epoch);
+  }
+}
+
+template <int W>
+__global__ void rs_sumsq_kernel(PeerPtrs grads, long shard_off, long n, float* __restrict__ out,
+                                float* __restrict__ sumsq, float scale) {
+  float acc = 0.f;
+  const long nvec = n / 8;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long)gridDim.x * blockDim.x) {
+    float s[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < W; ++p) {
+      const uint4 u = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(grads.p[p]) + shard_off + i * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        s[2 * e] += f.x;
+        s[2 * e + 1] += f.y;
+      }
+    }
+    float4 a = make_float4(s[0] * scale, s[1] * scale, s[2] * scale, s[3] * scale);
+    float4 b = make_float4(s[4] * scale, s[5] * scale, s[6] * scale, s[7] * scale);
+    *reinterpret_cast<float4*>(out + i * 8) = a;
+    *reinterpret_cast<float4*>(out + i * 8 + 4) = b;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc += s[e] * scale * s[e] * scale;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffff, acc, o);
+  __shared__ float red[32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = acc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < (int)(blockDim.x / 32); ++i) t += red[i];
+    atomicAdd(sumsq, t);
+  }
+}
+
+// Publish local value to every peer's slot[16 + rank]; wait for all and sum.
+__global__ void scalar_allreduce_kernel(PeerPtrs sig, int rank, int world, unsigned int epoch,
+                                        unsigned long long sig_off, const float* __restrict__ local,
+                                        float* __restrict__ out) {
+  __shared__ float vals[kMaxWorld];
+  const int p = threadIdx.x;
+  if (p < world) {
+    const float v = *local;
+    unsigned long long* remote = reinterpret_cast<unsigned long long*>(sig.p[p] + sig_off) + 16 + rank;
+    st_release_sys(remote, (((unsigned long long)epoch) << 32) | __float_as_uint(v));
+    const unsigned long long* mine = reinterpret_cast<const unsigned long long*>(sig.p[rank] + sig_off) + 16 + p;
+    float got = 0.f;
+    if (wait_epoch(mine, epoch)) got = __uint_as_float((unsigned int)(ld_acquire_sys(mine) & 0xffffffffu));
+    vals[p] = got;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < world; ++i) t += vals[i];
+    *out = t;
+  }
+}
+
+KORE_DEV uint32_t hash32(uint32_t x) {
+  x ^= x >> 16;
+  x *= 0x7feb352du;
+  x ^= x >> 15;
+  x *= 0x846ca68bu;
+  x ^= x >> 16;
+  return x;
+}
+
+template <int W>
+__global__ void adamw_bcast_kernel(const float* __restrict__ g, float* __restrict__ master,
+                                   float* __restrict__ m, float* __restrict__ v, PeerPtrs params,
+                                   long shard_off, long n, float lr, float b1, float b2, float eps,
+                                   float wd, float bc1, float bc2, const float* __restrict__ sumsq,
+                                   float max_norm, uint32_t seed) {
+  float scale = 1.f;
+  if (sumsq != nullptr && max_norm > 0.f) scale = fminf(1.f, max_norm / (sqrtf(*sumsq) + 1e-6f));
+  const long nvec = n / 8;
+  const __nv_bfloat16* own = reinterpret_cast<const __nv_bfloat16*>(params.p[0]);  // slot 0 = this rank
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long)gridDim.x * blockDim.x) {
+    uint32_t packed[4];
+    const uint4 cur = *reinterpret_cast<const uint4*>(own + shard_off + i * 8);
+    const __nv_bfloat162* ch = reinterpret_cast<const __nv_bfloat162*>(&cur);
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+      float w2[2];
+      float2 cf = __bfloat1622float2(ch[e / 2]);
+      w2[0] = cf.x;
+      w2[1] = cf.y;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const long j = i * 8 + e + k;
+        const float gi = g[j] * scale;
+        const float mi = b1 * m[j] + (1.f - b1) * gi;
+        const float vi = b2 * v[j] + (1.f - b2) * gi * gi;
+        m[j] = mi;
+        v[j] = vi;
+        float w = master ? master[j] : w2[k];
+        w = w * (1.f - lr * wd) - lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
+        if (master) {
+          master[j] = w;
+          w2[k] = w;
+        } else {  // stochastic rounding to bf16 (unbiased)
+          uint32_t b = __float_as_uint(w);
+          b += hash32((uint32_t)(shard_off + j) * 0x9E3779B9u ^ seed) & 0xffffu;
+          w2[k] = __uint_as_float(b & 0xffff0000u);
+        }
+      }
+      packed[e / 2] = pack_bf16(w2[0], w2[1]);
+    }
+    const uint4 out = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+#pragma unroll
+    for (int p = 0; p < W; ++p)
+      *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(params.p[p]) + shard_off + i * 8) = out;
+  }
+}
+
+// ------------------------------------------------------------------ heap
+struct Heap {
+  int device = -1;
+  int rank = 0, world = 1;
+  char* base = nullptr;
+  size_t bytes = 0;
+  std::vector<char*> peers;  // peers[p] = base of rank p's heap mapped here (peers[rank] = base)
+};
+
+}  // namespace symm
+
+// Python-facing handle (opaque int id).
+static std::vector<std::unique_ptr<symm::Heap>> g_heaps;
+
+int64_t symm_heap_create(int64_t bytes, int64_t rank, int64_t world) {
+  TORCH_CHECK(world >= 1 && world <= symm::kMaxWorld, "world must be 1..8");
+  auto h = std::make_unique<symm::Heap>();
+  check_cuda(cudaGetDevice(&h->device), "cudaGetDevice");
+  h->rank = rank;
+  h->world = world;
+  h->bytes = (size_t)bytes;
+  void* p = nullptr;
+  check_cuda(cudaMalloc(&p, h->bytes), "symm heap cudaMalloc");
+  check_cuda(cudaMemset(p, 0, h->bytes), "symm heap memset");
+  h->base = static_cast<char*>(p);
+  h->peers.assign(world, nullptr);
+  h->peers[rank] = h->base;
+  g_heaps.push_back(std::move(h));
+  return (int64_t)g_heaps.size() - 1;
+}
+
+// The 64-byte cudaIpcMemHandle_t as a uint8 CPU tensor.
+at::Tensor symm_heap_handle(int64_t id) {
+  auto& h = g_heaps.at(id);
+  cudaIpcMemHandle_t hd;
+  check_cuda(cudaIpcGetMemHandle(&hd, h->base), "cudaIpcGetMemHandle");
+  auto t = at::empty({(int64_t)sizeof(hd)}, at::kByte);
+  std::memcpy(t.data_ptr(), &hd, sizeof(hd));
+  return t;
+}
+
+// handles: uint8 [world, 64] from all ranks (row r = rank r).
+void symm_heap_open(int64_t id, const at::Tensor& handles) {
+  auto& h = g_heaps.at(id);
+  TORCH_CHECK(handles.size(0) == h->world && handles.size(1) == (int64_t)sizeof(cudaIpcMemHandle_t),
+              "handles must be [world, 64]");
+  auto hc = handles.contiguous();
+  for (int p = 0; p < h->world; ++p) {
+    if (p == h->rank) continue;
+    cudaIpcMemHandle_t hd;
+    std::memcpy(&hd, hc.data_ptr<uint8_t>() + p * sizeof(hd), sizeof(hd));
+    void* ptr = nullptr;
+    check_cuda(cudaIpcOpenMemHandle(&ptr, hd, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle");
+    h->peers[p] = static_cast<char*>(ptr);
+  }
+}
+
+// A tensor view of the local heap at a byte offset (no ownership).
+at::Tensor symm_heap_tensor(int64_t id, int64_t offset, const std::vector<int64_t>& shape,
+                            at::ScalarType dtype) {
+  auto& h = g_heaps.at(id);
+  int64_t n = 1;
+  for (auto s : shape) n *= s;
+  TORCH_CHECK(offset >= 0 && offset % 256 == 0 &&
+                  (size_t)(offset + n * (int64_t)c10::elementSize(dtype)) <= h->bytes,
+              "symm tensor out of heap bounds");
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, h->device);
+  return at::from_blob(h->base + offset, shape, [](void*) {}, opts);
+}
+
+static symm::PeerPtrs peer_ptrs(const symm::Heap& h, int64_t offset, bool self_first) {
+  symm::PeerPtrs pp;
+  for (int i = 0; i < symm::kMaxWorld; ++i) pp.p[i] = nullptr;
+  for (int p = 0; p < h.world; ++p) {
+    const int idx = self_first ? (p == 0 ? h.rank : (p <= h.rank ? p - 1 : p)) : p;
+    pp.p[p] = h.peers[idx] + offset;
+  }
+  return pp;
+}
+
+void symm_barrier(int64_t id, int64_t sig_offset, int64_t epoch) {
+  auto& h = *g_heaps.at(id);
+  symm::PeerPtrs sig = peer_ptrs(h, 0, false);
+  symm::barrier_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(sig, h.rank, h.world, (unsigned)epoch,
+                                                                        (unsigned long long)sig_offset);
+  check_cuda(cudaGetLastError(), "symm_barrier");
+}
+
+// grads: heap offset of the FULL bf16 gradient buffer (same on every rank);
+// this rank's shard [rank*n, (rank+1)*n) is summed over peers into out (fp32).
+void symm_rs_sumsq(int64_t id, int64_t grad_offset, int64_t n, at::Tensor& out, at::Tensor& sumsq,
+                   double scale) {
+  auto& h = *g_heaps.at(id);
+  TORCH_CHECK(n % 8 == 0, "shard length must be a multiple of 8");
+  symm::PeerPtrs g = peer_ptrs(h, grad_offset, false);
+  const long shard_off = (long)h.rank * n;
+  const int grid = (int)std::min<long>((n / 8 + 255) / 256, (long)num_sms(h.device) * 4);
+  auto st = at::cuda::getCurrentCUDAStream();
+#define KORE_RS(W) symm::rs_sumsq_kernel<W><<<grid, 256, 0, st>>>(g, shard_off, n, out.data_ptr<float>(), \
+                                                                  sumsq.data_ptr<float>(), (float)scale)
+  switch (h.world) {
+    case 1: KORE_RS(1); break;
+    case 2: KORE_RS(2); break;
+    case 4: KORE_RS(4); break;
+    case 8: KORE_RS(8); break;
+    default: TORCH_CHECK(false, "world must be 1, 2, 4 or 8");
+  }
+#undef KORE_RS
+  check_cuda(cudaGetLastError(), "symm_rs_sumsq");
+}
+
+void symm_scalar_allreduce(int64_t id, int64_t sig_offset, int64_t epoch, const at::Tensor& local,
+                           at::Tensor& out) {
+  auto& h = *g_heaps.at(id);
+  symm::PeerPtrs sig = peer_ptrs(h, 0, false);
+  symm::scalar_allreduce_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      sig, h.rank, h.world, (unsigned)epoch, (unsigned long long)sig_offset, local.data_ptr<float>(),
+      out.data_ptr<float>());
+  check_cuda(cudaGetLastError(), "symm_scalar_allreduce");
+}
+
+void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t n, const at::Tensor& g,
+                      const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v, double lr,
+                      double b1, double b2, double eps, double wd, int64_t step,
+                      const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed) {
+  auto& h = *g_heaps.at(id);
+  TORCH_CHECK(n % 8 == 0, "shard length must be a multiple of 8");
+  symm::PeerPtrs prm = peer_ptrs(h, param_offset, true);  // slot 0 = own buffer
+  const long shard_off = (long)h.rank * n;
+  const float bc1 = 1.f - std::pow((float)b1, (float)step);
+  const float bc2 = 1.f - std::pow((float)b2, (float)step);
+  const int grid = (int)std::min<long>((n / 8 + 255) / 256, (long)num_sms(h.device) * 4);
+  auto st = at::cuda::getCurrentCUDAStream();
+  float* mp = master ? master->data_ptr<float>() : nullptr;
+  const float* sq = sumsq ? sumsq->data_ptr<float>() : nullptr;
+#define KORE_AB(W)                                                                                  \
+  symm::adamw_bcast_kernel<W><<<grid, 256, 0, st>>>(g.data_ptr<float>(), mp, m.data_ptr<float>(),   \
+                                                    v.data_ptr<float>(), prm, shard_off, n, lr, b1, b2, \
+                                                    eps, wd, bc1, bc2, sq, max_norm, (uint32_t)seed)
+  switch (h.world) {
+    case 1: KORE_AB(1); break;
+    case 2: KORE_AB(2); break;
+    case 4: KORE_AB(4); break;
+    case 8: KORE_AB(8); break;
+    default: TORCH_CHECK(false, "world must be 1, 2, 4 or 8");
+  }
+#undef KORE_AB
+  check_cuda(cudaGetLastError(), "symm_adamw_bcast");
+}
+
+}  // namespace kore

@@ -102,7 +102,7 @@ class Qwen3Engine:
 
     def __init__(self, weights: Qwen3Weights, *, grad_dtype: Optional[torch.dtype] = None,
                  logits_chunk: int = 4096, temperature: float = 1.0, allocate_grads: bool = True,
-                 save_attention: bool = True):
+                 save_attention: bool = True, grad_alloc=None):
         self.w = weights
         self.cfg = weights.cfg
         if self.cfg.is_moe:
@@ -124,8 +124,12 @@ class Qwen3Engine:
         self._fresh = [True] * weights.num_units
         if allocate_grads:
             for u in range(weights.num_units):
-                self.grads[u] = torch.zeros(weights.padded_numel(u), dtype=self.grad_dtype,
-                                            device=self.dev)
+                if grad_alloc is not None:
+                    self.grads[u] = grad_alloc(weights.padded_numel(u), self.grad_dtype)
+                    self.grads[u].zero_()
+                else:
+                    self.grads[u] = torch.zeros(weights.padded_numel(u), dtype=self.grad_dtype,
+                                                device=self.dev)
 
     # ------------------------------------------------------------------ utils
     def zero_grad(self) -> None:

@@ -45,14 +45,40 @@ class CausalLMTrainer:
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device
+        self.heap = None
+        grad_alloc = None
+        fused = comm == "fused" and self.ctx.world > 1 and dev.type == "cuda"
+        if fused:
+            from ..parallel.symmetric import SymmetricHeap
+            per = 128 * self.ctx.world
+            from ..models.qwen3 import unit_layouts, _round_up
+            tot = sum(_round_up(l.numel, per) for l in unit_layouts(cfg))
+            self.heap = SymmetricHeap(self.ctx, 2 * tot * 2 + 256 * 4 * len(unit_layouts(cfg)))
+            alloc = lambda n, dt: self.heap.alloc(n, dt)[1]
+            grad_alloc = alloc
+            if weights is None:
+                weights = Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed, pad_multiple=per,
+                                       alloc=alloc)
+            else:  # move existing weights into the heap
+                nw = Qwen3Weights(cfg, device=dev, dtype=weights.dtype, init=False, pad_multiple=per,
+                                  alloc=alloc)
+                for a, b in zip(nw.bufs, weights.bufs):
+                    a[: b.numel()].copy_(b[: a.numel()])
+                weights = nw
         self.w = weights or Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed,
                                          pad_multiple=128 * max(1, self.ctx.world))
-        self.eng = Qwen3Engine(self.w, logits_chunk=logits_chunk)
+        self.eng = Qwen3Engine(self.w, logits_chunk=logits_chunk, grad_alloc=grad_alloc)
         if master == "auto":
             master = pick_master_mode(cfg, self.ctx.world, dev)
         self.master_mode = master
         self.mbs = micro_batch_size
-        if self.ctx.world > 1:
+        if fused:
+            from ..parallel.zero import FusedShardedAdamW
+            self.opt = FusedShardedAdamW(self.w, self.eng, self.ctx, self.heap, lr=lr, betas=betas,
+                                         weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                                         master=master, schedule=schedule, warmup_steps=warmup_steps,
+                                         total_steps=total_steps, seed=seed)
+        elif self.ctx.world > 1:
             from ..parallel.zero import ShardedAdamW
             self.opt = ShardedAdamW(self.w, self.eng, self.ctx, lr=lr, betas=betas,
                                     weight_decay=weight_decay, max_grad_norm=max_grad_norm,

@@ -144,7 +144,7 @@ class Qwen3Weights:
 
     def __init__(self, cfg: Qwen3Config, device="cpu", dtype: Optional[torch.dtype] = None,
                  init: bool = True, seed: int = 0, std: float = 0.02,
-                 allocate: bool = True, pad_multiple: int = ALIGN):
+                 allocate: bool = True, pad_multiple: int = ALIGN, alloc=None):
         self.cfg = cfg
         self.dtype = dtype or _dtype(cfg.torch_dtype)
         self.device = torch.device(device)
@@ -154,8 +154,10 @@ class Qwen3Weights:
         self.bufs: List[Optional[torch.Tensor]] = [None] * len(self.layouts)
         if allocate:
             for u, lay in enumerate(self.layouts):
-                self.bufs[u] = torch.empty(self.padded_numel(u), dtype=self.dtype,
-                                           device=self.device)
+                # ``alloc(numel, dtype)`` lets callers place the buffers (e.g. in
+                # the symmetric peer-memory heap of the fused collectives)
+                self.bufs[u] = (alloc(self.padded_numel(u), self.dtype) if alloc is not None else
+                                torch.empty(self.padded_numel(u), dtype=self.dtype, device=self.device))
             if init:
                 self.init_random(seed, std)
 
