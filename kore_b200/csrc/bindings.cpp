@@ -53,11 +53,11 @@ void symm_heap_open(int64_t id, const at::Tensor& handles);
 at::Tensor symm_heap_tensor(int64_t id, int64_t offset, const std::vector<int64_t>& shape,
                             at::ScalarType dtype);
 void symm_barrier(int64_t id, int64_t sig_offset, int64_t epoch);
-void symm_rs_sumsq(int64_t id, int64_t grad_offset, int64_t n, at::Tensor& out, at::Tensor& sumsq,
-                   double scale);
+void symm_rs_sumsq(int64_t id, int64_t grad_offset, int64_t n, const c10::optional<at::Tensor>& out,
+                   at::Tensor& sumsq, double scale);
 void symm_scalar_allreduce(int64_t id, int64_t sig_offset, int64_t epoch, const at::Tensor& local,
                            at::Tensor& out);
-void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t n, const at::Tensor& g,
+void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t grad_offset, int64_t n, double gscale,
                       const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v, double lr,
                       double b1, double b2, double eps, double wd, int64_t step,
                       const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed);

@@ -97,10 +97,12 @@ __global__ void rs_sumsq_kernel(PeerPtrs grads, long shard_off, long n, float* _
         s[2 * e + 1] += f.y;
       }
     }
-    float4 a = make_float4(s[0] * scale, s[1] * scale, s[2] * scale, s[3] * scale);
-    float4 b = make_float4(s[4] * scale, s[5] * scale, s[6] * scale, s[7] * scale);
-    *reinterpret_cast<float4*>(out + i * 8) = a;
-    *reinterpret_cast<float4*>(out + i * 8 + 4) = b;
+    if (out != nullptr) {
+      *reinterpret_cast<float4*>(out + i * 8) =
+          make_float4(s[0] * scale, s[1] * scale, s[2] * scale, s[3] * scale);
+      *reinterpret_cast<float4*>(out + i * 8 + 4) =
+          make_float4(s[4] * scale, s[5] * scale, s[6] * scale, s[7] * scale);
+    }
 #pragma unroll
     for (int e = 0; e < 8; ++e) acc += s[e] * scale * s[e] * scale;
   }
@@ -149,7 +151,7 @@ KORE_DEV uint32_t hash32(uint32_t x) {
 }
 
 template <int W>
-__global__ void adamw_bcast_kernel(const float* __restrict__ g, float* __restrict__ master,
+__global__ void adamw_bcast_kernel(PeerPtrs grads, float gscale, float* __restrict__ master,
                                    float* __restrict__ m, float* __restrict__ v, PeerPtrs params,
                                    long shard_off, long n, float lr, float b1, float b2, float eps,
                                    float wd, float bc1, float bc2, const float* __restrict__ sumsq,
@@ -160,6 +162,19 @@ __global__ void adamw_bcast_kernel(const float* __restrict__ g, float* __restric
   const __nv_bfloat16* own = reinterpret_cast<const __nv_bfloat16*>(params.p[0]);  // slot 0 = this rank
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += (long)gridDim.x * blockDim.x) {
     uint32_t packed[4];
+    float gs[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int p = 0; p < W; ++p) {  // reduce-scatter fused into the update: P2P loads
+      const uint4 u = *reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(grads.p[p]) + shard_off + i * 8);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        gs[2 * e] += f.x;
+        gs[2 * e + 1] += f.y;
+      }
+    }
     const uint4 cur = *reinterpret_cast<const uint4*>(own + shard_off + i * 8);
     const __nv_bfloat162* ch = reinterpret_cast<const __nv_bfloat162*>(&cur);
 #pragma unroll
@@ -171,7 +186,7 @@ __global__ void adamw_bcast_kernel(const float* __restrict__ g, float* __restric
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const long j = i * 8 + e + k;
-        const float gi = g[j] * scale;
+        const float gi = gs[e + k] * gscale * scale;
         const float mi = b1 * m[j] + (1.f - b1) * gi;
         const float vi = b2 * v[j] + (1.f - b2) * gi * gi;
         m[j] = mi;
@@ -286,15 +301,15 @@ void symm_barrier(int64_t id, int64_t sig_offset, int64_t epoch) {
 
 // grads: heap offset of the FULL bf16 gradient buffer (same on every rank);
 // this rank's shard [rank*n, (rank+1)*n) is summed over peers into out (fp32).
-void symm_rs_sumsq(int64_t id, int64_t grad_offset, int64_t n, at::Tensor& out, at::Tensor& sumsq,
-                   double scale) {
+void symm_rs_sumsq(int64_t id, int64_t grad_offset, int64_t n, const c10::optional<at::Tensor>& out,
+                   at::Tensor& sumsq, double scale) {
   auto& h = *g_heaps.at(id);
   TORCH_CHECK(n % 8 == 0, "shard length must be a multiple of 8");
   symm::PeerPtrs g = peer_ptrs(h, grad_offset, false);
   const long shard_off = (long)h.rank * n;
   const int grid = (int)std::min<long>((n / 8 + 255) / 256, (long)num_sms(h.device) * 4);
   auto st = at::cuda::getCurrentCUDAStream();
-#define KORE_RS(W) symm::rs_sumsq_kernel<W><<<grid, 256, 0, st>>>(g, shard_off, n, out.data_ptr<float>(), \
+#define KORE_RS(W) symm::rs_sumsq_kernel<W><<<grid, 256, 0, st>>>(g, shard_off, n, out ? out->data_ptr<float>() : nullptr, \
                                                                   sumsq.data_ptr<float>(), (float)scale)
   switch (h.world) {
     case 1: KORE_RS(1); break;
@@ -317,13 +332,14 @@ void symm_scalar_allreduce(int64_t id, int64_t sig_offset, int64_t epoch, const 
   check_cuda(cudaGetLastError(), "symm_scalar_allreduce");
 }
 
-void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t n, const at::Tensor& g,
+void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t grad_offset, int64_t n, double gscale,
                       const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v, double lr,
                       double b1, double b2, double eps, double wd, int64_t step,
                       const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed) {
   auto& h = *g_heaps.at(id);
   TORCH_CHECK(n % 8 == 0, "shard length must be a multiple of 8");
   symm::PeerPtrs prm = peer_ptrs(h, param_offset, true);  // slot 0 = own buffer
+  symm::PeerPtrs grd = peer_ptrs(h, grad_offset, false);
   const long shard_off = (long)h.rank * n;
   const float bc1 = 1.f - std::pow((float)b1, (float)step);
   const float bc2 = 1.f - std::pow((float)b2, (float)step);
@@ -332,7 +348,7 @@ void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t n, const at::Ten
   float* mp = master ? master->data_ptr<float>() : nullptr;
   const float* sq = sumsq ? sumsq->data_ptr<float>() : nullptr;
 #define KORE_AB(W)                                                                                  \
-  symm::adamw_bcast_kernel<W><<<grid, 256, 0, st>>>(g.data_ptr<float>(), mp, m.data_ptr<float>(),   \
+  symm::adamw_bcast_kernel<W><<<grid, 256, 0, st>>>(grd, (float)gscale, mp, m.data_ptr<float>(),    \
                                                     v.data_ptr<float>(), prm, shard_off, n, lr, b1, b2, \
                                                     eps, wd, bc1, bc2, sq, max_norm, (uint32_t)seed)
   switch (h.world) {

@@ -57,7 +57,8 @@ class ShardedAdamW:
             self.v[u] = torch.zeros(s, dtype=torch.float32, device=dev)
             if master == "fp32":
                 self.master[u] = weights.bufs[u][r * s:(r + 1) * s].float()
-            self.gshard[u] = torch.empty(s, dtype=engine.grad_dtype, device=dev)
+            if comm != "fused":   # the fused path reads peers' gradients in place
+                self.gshard[u] = torch.empty(s, dtype=engine.grad_dtype, device=dev)
         self._sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
         self.last_sumsq: Optional[torch.Tensor] = None
 
@@ -119,11 +120,13 @@ class ShardedAdamW:
 class FusedShardedAdamW(ShardedAdamW):
     """ZeRO-2 step on the symmetric peer-memory heap with fused kernels:
 
-    device barrier -> per unit: reduce-scatter of the bf16 gradients over
-    NVLink (P2P loads from every peer) fused with the fp32 cast and the
-    sum of squares -> device all-reduce of the norm -> per unit: AdamW on the
-    shard fused with the all-gather (P2P stores of the new bf16 parameters
-    into every peer) -> device barrier. No NCCL call and no host sync.
+    device barrier -> (with clipping) per unit: the sum of squares of this
+    rank's gradient shard, reduced over peers with NVLink P2P loads -> device
+    all-reduce of the norm -> per unit: ONE kernel that reduce-scatters the
+    bf16 gradients (P2P loads from every peer, fp32 sum), applies the clipped
+    AdamW update to the fp32 shard state and all-gathers the result (P2P
+    stores of the new bf16 parameters into every peer) -> device barrier.
+    No NCCL call, no host sync, and no gradient-shard buffer.
     Parameters and gradients must live in ``heap`` (see
     :meth:`CausalLMTrainer` with ``comm="fused"``)."""
 
@@ -132,8 +135,6 @@ class FusedShardedAdamW(ShardedAdamW):
         super().__init__(weights, engine, ctx, **kw)
         self.heap = heap
         dev = weights.device
-        self.gshard = {u: torch.empty(self.shard_len[u], dtype=torch.float32, device=dev)
-                       for u in range(weights.num_units)}
         self._local = torch.zeros(1, dtype=torch.float32, device=dev)
         self.p_off = [heap.offset_of(b) for b in weights.bufs]
         self.g_off = [heap.offset_of(g) for g in engine.grads]
@@ -144,19 +145,19 @@ class FusedShardedAdamW(ShardedAdamW):
         C = ops.native()
         h = self.heap
         h.barrier()                                   # every rank's gradients are final
-        self._local.zero_()
-        for u in range(self.w.num_units):
-            C.symm_rs_sumsq(h.id, self.g_off[u], self.shard_len[u], self.gshard[u], self._local,
-                            float(grad_scale))
         sq = None
         if self.max_grad_norm and self.max_grad_norm > 0:
+            self._local.zero_()
+            for u in range(self.w.num_units):
+                C.symm_rs_sumsq(h.id, self.g_off[u], self.shard_len[u], None, self._local, float(grad_scale))
             C.symm_scalar_allreduce(h.id, 0, h.next_epoch(), self._local, self._sumsq)
             sq = self._sumsq
             self.last_sumsq = sq
         lr = self.current_lr()
         self.step_count += 1
         for u in range(self.w.num_units):
-            C.symm_adamw_bcast(h.id, self.p_off[u], self.shard_len[u], self.gshard[u], self.master.get(u),
+            C.symm_adamw_bcast(h.id, self.p_off[u], self.g_off[u], self.shard_len[u], float(grad_scale),
+                               self.master.get(u),
                                self.m[u], self.v[u], lr, self.b1, self.b2, self.eps, self.wd,
                                self.step_count, sq, float(self.max_grad_norm or 0.0),
                                self.seed * 7919 + self.step_count * 104729 + u * 31 + self.ctx.rank)
