@@ -61,6 +61,16 @@ void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t grad_offset, int
                       const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v, double lr,
                       double b1, double b2, double eps, double wd, int64_t step,
                       const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed);
+void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out,
+                       const std::vector<int64_t>& offsets, bool b_mn, bool accumulate);
+void moe_route_fwd(const at::Tensor& logits, int64_t k, bool norm, at::Tensor& probs, at::Tensor& idx,
+                   at::Tensor& w);
+void moe_route_bwd(const at::Tensor& probs, const at::Tensor& idx, const at::Tensor& w, const at::Tensor& dw,
+                   bool norm, at::Tensor& dlogits);
+void moe_combine(const at::Tensor& src, const at::Tensor& pos, const c10::optional<at::Tensor>& w,
+                 const c10::optional<at::Tensor>& resid, at::Tensor& out);
+void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& src, const at::Tensor& pos, const at::Tensor& w,
+                     at::Tensor& dsrc, at::Tensor& dw);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -91,5 +101,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_rs_sumsq", &kore::symm_rs_sumsq);
   m.def("symm_scalar_allreduce", &kore::symm_scalar_allreduce);
   m.def("symm_adamw_bcast", &kore::symm_adamw_bcast);
+  m.def("gemm_grouped_bf16", &kore::gemm_grouped_bf16, "grouped (MoE) tcgen05 GEMM");
+  m.def("moe_route_fwd", &kore::moe_route_fwd);
+  m.def("moe_route_bwd", &kore::moe_route_bwd);
+  m.def("moe_combine", &kore::moe_combine);
+  m.def("moe_combine_bwd", &kore::moe_combine_bwd);
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

@@ -45,6 +45,10 @@ struct Params {
   int ldc;              // C row stride (elements)
   const __nv_bfloat16* R;  // optional residual (bf16, row stride ldr)
   int ldr;
+  // grouped mode (MoE experts): per M-tile {expert, first row, row limit, 0};
+  // B is a 3-D tensor map indexed by expert; rows >= limit are not stored.
+  const int4* tiles;
+  void* C_write;  // output base for the masked direct-store epilogue (grouped mode)
 };
 
 template <int BN, int STAGES>
@@ -118,7 +122,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int tm, tn;
         tile_coords(t, num_m, num_n, tm, tn);
-        const int m0 = tm * BM, n0 = tn * BN;
+        int m0 = tm * BM, ex = 0;
+        const int n0 = tn * BN;
+        if (p.tiles != nullptr) {
+          const int4 ti = p.tiles[tm];
+          ex = ti.x;
+          m0 = ti.y;
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
@@ -132,7 +142,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < BM / 64; ++j)
               tma_load_2d(sA + j * 8192, &tmA, &full_bar[stage], m0 + 64 * j, k0);
           }
-          if (!B_MN) {
+          if (p.tiles != nullptr) {  // per-expert weights: 3-D map (inner, outer, expert)
+            if (!B_MN) {
+              tma_load_3d(sB, &tmB, &full_bar[stage], k0, n0, ex);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(sB + j * 8192, &tmB, &full_bar[stage], n0 + 64 * j, k0, ex);
+            }
+          } else if (!B_MN) {
             tma_load_2d(sB, &tmB, &full_bar[stage], k0, n0);
           } else {
 #pragma unroll
@@ -190,7 +208,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
       int tm, tn;
       tile_coords(t, num_m, num_n, tm, tn);
-      const int m0 = tm * BM, n0 = tn * BN;
+      int m0 = tm * BM, m_lim = p.M;
+      const int n0 = tn * BN;
+      if (p.tiles != nullptr) {
+        const int4 ti = p.tiles[tm];
+        m0 = ti.y;
+        m_lim = ti.z;
+      }
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
@@ -213,7 +237,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]) * p.alpha;
           }
         }
-        const bool row_ok = row < p.M;
+        const bool row_ok = row < m_lim;
         // optional accumulate / residual (row-contiguous per thread)
         if (row_ok && (p.accumulate || p.R != nullptr)) {
           const int ncols = min(CH, p.N - (n0 + c0));
@@ -250,6 +274,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+        }
+        if (p.tiles != nullptr) {
+          // grouped: masked direct stores (a tile may end inside another expert's rows)
+          const int ncols = min(CH, p.N - (n0 + c0));
+          if (row_ok) {
+            if (p.out_f32) {
+              float* cp = reinterpret_cast<float*>(p.C_write) + (size_t)row * p.ldc + n0 + c0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                if (j >= ncols) break;
+                *reinterpret_cast<float4*>(cp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              }
+            } else {
+              __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(p.C_write) + (size_t)row * p.ldc + n0 + c0;
+#pragma unroll
+              for (int j = 0; j < 64; j += 8) {
+                if (j >= ncols) break;
+                *reinterpret_cast<uint4*>(cp + j) =
+                    make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
+                               pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
+              }
+            }
+          }
+          continue;
         }
         // make sure the TMA store that last used this staging buffer has read it
         if (lane == 0) tma_store_wait_read<1>();
@@ -354,6 +402,8 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
   p.ldc = out.stride(0);
   p.R = nullptr;
   p.ldr = 0;
+  p.tiles = nullptr;
+  p.C_write = out.data_ptr();
   if (residual) {
     TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 &&
                     residual->size(0) == M && residual->size(1) == N,
@@ -386,6 +436,72 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
     KORE_GEMM_DISPATCH(128, 6)
   }
 #undef KORE_GEMM_DISPATCH
+}
+
+
+// Grouped GEMM over experts (MoE): rows of ``a`` are grouped by expert with
+// boundaries ``offsets`` (host int64 list, length E+1). For expert e:
+//   out[rows_e] (=|+=) a[rows_e] . op(b[e])^T,  b: [E, N, K] (K-major) or [E, K, N] (b_mn)
+void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out,
+                       const std::vector<int64_t>& offsets, bool b_mn, bool accumulate) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16, "grouped gemm: bf16 CUDA tensors");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 3 && out.dim() == 2 && a.stride(1) == 1 && b.is_contiguous() &&
+                  out.stride(1) == 1, "grouped gemm: a [M,K], b [E,..] contiguous, out [M,N]");
+  const int E = b.size(0);
+  TORCH_CHECK((int)offsets.size() == E + 1, "offsets must have E+1 entries");
+  const int K = a.size(1);
+  const int N = b_mn ? b.size(2) : b.size(1);
+  TORCH_CHECK((b_mn ? b.size(1) : b.size(2)) == K, "grouped gemm: K mismatch");
+  TORCH_CHECK(out.size(1) == N && out.size(0) == a.size(0), "grouped gemm: out shape");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && a.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "alignment");
+  const bool f32 = out.scalar_type() == at::kFloat;
+  std::vector<int32_t> tiles;
+  for (int e = 0; e < E; ++e)
+    for (int64_t m = offsets[e]; m < offsets[e + 1]; m += 128) {
+      tiles.push_back(e);
+      tiles.push_back((int32_t)m);
+      tiles.push_back((int32_t)offsets[e + 1]);
+      tiles.push_back(0);
+    }
+  const int ntm = (int)tiles.size() / 4;
+  if (ntm == 0) return;
+  c10::cuda::CUDAGuard guard(a.device());
+  auto tt = at::empty({(int64_t)tiles.size()}, at::TensorOptions().dtype(at::kInt))
+                .copy_(at::from_blob(tiles.data(), {(int64_t)tiles.size()}, at::kInt))
+                .to(a.device(), /*non_blocking=*/false);
+  gemm::Params p;
+  p.M = a.size(0); p.N = N; p.K = K;
+  p.alpha = 1.f;
+  p.accumulate = accumulate ? 1 : 0;
+  p.out_f32 = f32 ? 1 : 0;
+  p.C_read = out.data_ptr();
+  p.C_write = out.data_ptr();
+  p.ldc = out.stride(0);
+  p.R = nullptr;
+  p.ldr = 0;
+  p.tiles = reinterpret_cast<const int4*>(tt.data_ptr<int>());
+  const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  const int BN = use256 ? 256 : 128;
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), bf, 2, K, a.size(0), a.stride(0), 64, 128);
+  CUtensorMap tb = b_mn ? make_tmap_3d(b.data_ptr(), bf, 2, N, K, E, N, (uint64_t)N * K, 64, 64, 1)
+                        : make_tmap_3d(b.data_ptr(), bf, 2, K, N, E, K, (uint64_t)N * K, 64, BN, 1);
+  CUtensorMap tc = ta;  // unused by the grouped epilogue (masked direct stores)
+  // num_m = number of M tiles in the table; tile_coords maps onto it
+  p.M = ntm * 128;
+  const int tiles_total = ntm * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles_total, num_sms(a.get_device()));
+  auto cst = at::cuda::getCurrentCUDAStream();
+  cudaStream_t st = cst;
+  if (use256) {
+    if (b_mn) gemm::launch<256, 4, false, true>(ta, tb, tc, p, grid, st);
+    else gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st);
+  } else {
+    if (b_mn) gemm::launch<128, 6, false, true>(ta, tb, tc, p, grid, st);
+    else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st);
+  }
+  tt.record_stream(cst);
 }
 
 }  // namespace kore

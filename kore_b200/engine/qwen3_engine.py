@@ -105,8 +105,6 @@ class Qwen3Engine:
                  save_attention: bool = True, grad_alloc=None):
         self.w = weights
         self.cfg = weights.cfg
-        if self.cfg.is_moe:
-            raise NotImplementedError("Qwen3Engine handles dense layers; use MoEEngine for MoE")
         self.dev = weights.device
         self.dtype = weights.dtype
         self.grad_dtype = grad_dtype or self.dtype
@@ -114,6 +112,7 @@ class Qwen3Engine:
         # selective activation checkpointing: keep attention outputs (T x Hq*D
         # bf16 + lse per layer) so the backward recomputes only the GEMMs
         self.save_attention = save_attention
+        self.ep = None          # expert-parallel dispatcher (kore_b200.parallel.ep) when attached
         self.temperature = temperature
         c = self.cfg
         self.hq, self.hkv, self.D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
@@ -174,14 +173,69 @@ class Qwen3Engine:
         x2 = self._mm(o2, W["o"], residual=x)
         rstd2 = torch.empty(T, **f32)
         hn2 = ops.rmsnorm_fwd(x2, W["ln2"], self.eps, rstd=rstd2)
+        ctx = None
+        if self.w.layouts[u].kind == "moe_layer":
+            x3, mctx = self._moe_fwd(W, hn2, x2)
+            if keep:
+                ctx = dict(rstd1=rstd1, hn=hn, qkv=qkv, qk=qk, o=o, lse=lse, x2=x2, rstd2=rstd2,
+                           hn2=hn2, **mctx)
+            return x3, ctx
         gu = self._mm(hn2, W["gate_up"])
         a = ops.swiglu_fwd(gu)
         x3 = self._mm(a, W["down"], residual=x2)
-        ctx = None
         if keep:
             ctx = dict(rstd1=rstd1, hn=hn, qkv=qkv, qk=qk, o=o, lse=lse, x2=x2, rstd2=rstd2,
                        hn2=hn2, gu=gu, a=a)
         return x3, ctx
+
+    # ------------------------------------------------------------------ MoE
+    def _moe_fwd(self, W, hn2, x2):
+        """Router -> top-k -> expert-major permutation -> grouped SwiGLU experts
+        -> weighted combine (+ residual). Experts outside this rank's range (EP)
+        are handled by the expert-parallel dispatcher when one is attached."""
+        from ..ops import moe
+        c = self.cfg
+        logits = ops.mm(hn2, W["router"], out_dtype=torch.float32)
+        probs, idx, wts = moe.route(logits, c.num_experts_per_tok, c.norm_topk_prob)
+        if self.ep is not None:
+            return self.ep.forward(self, W, hn2, x2, probs, idx, wts)
+        src, pos, offs = moe.permutation(idx, c.num_experts)
+        xp = moe.gather_rows(hn2, src)
+        gu = moe.grouped_mm(xp, W["experts_gate_up"], offs)
+        a = ops.swiglu_fwd(gu)
+        yp = moe.grouped_mm(a, W["experts_down"], offs)
+        x3 = moe.combine(yp, pos, wts, resid=x2)
+        return x3, dict(probs=probs, idx=idx, wts=wts, src=src, pos=pos, offs=offs, xp=xp, gu=gu, a=a, yp=yp)
+
+    def _moe_bwd(self, W, G, ctx, dx3, acc):
+        """Returns d(hn2) of the MoE block; accumulates expert and router grads."""
+        from ..ops import moe
+        c = self.cfg
+        if self.ep is not None:
+            dhn2, dw = self.ep.backward(self, W, G, ctx, dx3)
+        else:
+            offs = ctx["offs"]
+            dyp, dw = moe.combine_bwd(dx3, ctx["yp"], ctx["pos"], ctx["wts"])
+            da = moe.grouped_mm(dyp, W["experts_down"], offs, w_t=False)
+            self._expert_wgrad(G["experts_down"], dyp, ctx["a"], offs)
+            dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])
+            del da
+            dxp = moe.grouped_mm(dgu, W["experts_gate_up"], offs, w_t=False)
+            self._expert_wgrad(G["experts_gate_up"], dgu, ctx["xp"], offs)
+            dhn2 = moe.combine(dxp, ctx["pos"], None)
+        dlogits = moe.route_bwd(ctx["probs"], ctx["idx"], ctx["wts"], dw, c.norm_topk_prob)
+        dl = dlogits.to(self.dtype)
+        self._mm(dl, W["router"], b_t=False, out=dhn2, accumulate=True)
+        self._mm(dl, ctx["hn2"], a_t=True, b_t=False, out=G["router"], accumulate=acc)
+        return dhn2
+
+    def _expert_wgrad(self, Gw, dy, x, offs, expert_base: int = 0):
+        """dW[e] += dy_e^T x_e for each expert with rows (gradients are zeroed
+        at zero_grad, so experts always accumulate)."""
+        for e in range(len(offs) - 1):
+            s, t = offs[e], offs[e + 1]
+            if t > s:
+                self._mm(dy[s:t], x[s:t], a_t=True, b_t=False, out=Gw[expert_base + e], accumulate=True)
 
     def _layer_bwd(self, u: int, x: torch.Tensor, dx3: torch.Tensor, ctx: dict, b: Batch):
         W = self.w.views(u)
@@ -189,14 +243,17 @@ class Qwen3Engine:
         acc = not self._fresh[u]
         T = x.shape[0]
         qd, kd = self.hq * self.D, self.hkv * self.D
-        # MLP
-        da = self._mm(dx3, W["down"], b_t=False)                       # [T, F]
-        self._mm(dx3, ctx["a"], a_t=True, b_t=False, out=G["down"], accumulate=acc)
-        dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])                  # in place
-        del da
-        dhn2 = self._mm(dgu, W["gate_up"], b_t=False)                  # [T, H]
-        self._mm(dgu, ctx["hn2"], a_t=True, b_t=False, out=G["gate_up"], accumulate=acc)
-        del dgu
+        # MLP (dense SwiGLU or MoE experts)
+        if self.w.layouts[u].kind == "moe_layer":
+            dhn2 = self._moe_bwd(W, G, ctx, dx3, acc)
+        else:
+            da = self._mm(dx3, W["down"], b_t=False)                       # [T, F]
+            self._mm(dx3, ctx["a"], a_t=True, b_t=False, out=G["down"], accumulate=acc)
+            dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])                  # in place
+            del da
+            dhn2 = self._mm(dgu, W["gate_up"], b_t=False)                  # [T, H]
+            self._mm(dgu, ctx["hn2"], a_t=True, b_t=False, out=G["gate_up"], accumulate=acc)
+            del dgu
         dw = torch.zeros(self.cfg.hidden_size, dtype=torch.float32, device=x.device)
         dx2 = ops.rmsnorm_bwd(dhn2, ctx["x2"], W["ln2"], ctx["rstd2"], dres=dx3, dw=dw)
         self._acc_norm(G["ln2"], dw, acc)

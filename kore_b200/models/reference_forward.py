@@ -37,8 +37,11 @@ def forward_logprobs(w: Qwen3Weights, bufs: List[torch.Tensor], batch, temperatu
         o = ref.causal_attention(q, k, v, cu_seqlens=batch.cu_seqlens)
         x = x + o.reshape(T, qd) @ W["o"].t()
         hn2 = ref.rmsnorm(x, W["ln2"], eps)
-        a = ref.swiglu(hn2 @ W["gate_up"].t())
-        x = x + a @ W["down"].t()
+        if w.layouts[u].kind == "moe_layer":
+            x = x + moe_block(cfg, W, hn2)
+        else:
+            a = ref.swiglu(hn2 @ W["gate_up"].t())
+            x = x + a @ W["down"].t()
     Wh = V[-1]
     hn = ref.rmsnorm(x, Wh["norm"], eps)
     lm = V[0]["embed"] if cfg.tie_word_embeddings else Wh["lm_head"]
@@ -46,3 +49,23 @@ def forward_logprobs(w: Qwen3Weights, bufs: List[torch.Tensor], batch, temperatu
     lp, ent, _ = ref.token_logprobs(logits, batch.targets, temperature)
     lp = torch.where(batch.targets >= 0, lp, torch.zeros_like(lp))
     return lp, ent
+
+
+def moe_block(cfg, W, h):
+    """Qwen3-MoE sparse block: softmax router, top-k, renormalised weights,
+    SwiGLU experts, weighted sum (dense loop over experts; oracle only)."""
+    logits = h @ W["router"].t()
+    probs = torch.softmax(logits.float(), -1)
+    wts, idx = probs.topk(cfg.num_experts_per_tok, -1)
+    if cfg.norm_topk_prob:
+        wts = wts / wts.sum(-1, keepdim=True)
+    out = torch.zeros_like(h, dtype=torch.float32)
+    for e in range(cfg.num_experts):
+        sel = (idx == e)
+        rows = sel.any(-1)
+        if not rows.any():
+            continue
+        we = (wts * sel).sum(-1)[rows]
+        a = ref.swiglu(h[rows] @ W["experts_gate_up"][e].t())
+        out = out.index_add(0, rows.nonzero()[:, 0], (a @ W["experts_down"][e].t()).float() * we[:, None])
+    return out.to(h.dtype)
