@@ -11,7 +11,8 @@ pytestmark = pytest.mark.gpu
 
 
 def _rel(a, b):
-    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
 
 
 @pytest.mark.parametrize("w_t", [True, False])
