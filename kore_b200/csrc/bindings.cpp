@@ -71,6 +71,13 @@ void moe_combine(const at::Tensor& src, const at::Tensor& pos, const c10::option
                  const c10::optional<at::Tensor>& resid, at::Tensor& out);
 void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& src, const at::Tensor& pos, const at::Tensor& w,
                      at::Tensor& dsrc, at::Tensor& dw);
+void symm_ep_scatter(int64_t id, int64_t buf_offset, const at::Tensor& x, const at::Tensor& src_row,
+                     const at::Tensor& dst_rank, const at::Tensor& dst_row,
+                     const c10::optional<at::Tensor>& scale);
+void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, const at::Tensor& row,
+                    const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& resid,
+                    at::Tensor& y, const c10::optional<at::Tensor>& g, const c10::optional<at::Tensor>& dw,
+                    int64_t H);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -106,5 +113,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_route_bwd", &kore::moe_route_bwd);
   m.def("moe_combine", &kore::moe_combine);
   m.def("moe_combine_bwd", &kore::moe_combine_bwd);
+  m.def("symm_ep_scatter", &kore::symm_ep_scatter);
+  m.def("symm_ep_gather", &kore::symm_ep_gather);
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

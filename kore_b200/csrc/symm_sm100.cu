@@ -363,3 +363,126 @@ void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t grad_offset, int
 }
 
 }  // namespace kore
+
+// ============================================================== expert-parallel rows
+namespace kore {
+namespace symm {
+
+// Row scatter to peers: for pair i, row src_row[i] of the local matrix x [*, H]
+// (times scale[i] when given) is stored into peer dst_rank[i]'s buffer at row
+// dst_row[i] (P2P stores over NVLink). One warp per pair, 16-byte vectors.
+__global__ void ep_scatter_kernel(const __nv_bfloat16* __restrict__ x, const long* __restrict__ src_row,
+                                  const int* __restrict__ dst_rank, const long* __restrict__ dst_row,
+                                  const float* __restrict__ scale, PeerPtrs dst, int n, int H) {
+  const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (i >= n) return;
+  const __nv_bfloat16* s = x + src_row[i] * (long)H;
+  __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst.p[dst_rank[i]]) + dst_row[i] * (long)H;
+  const float sc = scale ? scale[i] : 1.f;
+  for (int c = lane * 8; c < H; c += 256) {
+    uint4 u = *reinterpret_cast<const uint4*>(s + c);
+    if (scale) {
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        h[e] = __floats2bfloat162_rn(f.x * sc, f.y * sc);
+      }
+    }
+    *reinterpret_cast<uint4*>(d + c) = u;
+  }
+}
+
+// Pull-combine from peers: y[t] = sum_j w[t,j] * peer[rank[t,j]][row[t,j]] (+ resid[t]);
+// with dw != nullptr also dw[t,j] = <g[t], peer row> (the combine backward's weight grad).
+__global__ void ep_gather_kernel(PeerPtrs src, const int* __restrict__ rank, const long* __restrict__ row,
+                                 const float* __restrict__ w, const __nv_bfloat16* __restrict__ resid,
+                                 __nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ g,
+                                 float* __restrict__ dw, int T, int k, int H) {
+  const long t = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  if (dw != nullptr) {
+    for (int j = 0; j < k; ++j) {
+      const __nv_bfloat16* pr = reinterpret_cast<const __nv_bfloat16*>(src.p[rank[t * k + j]]) + row[t * k + j] * (long)H;
+      float dot = 0.f;
+      for (int c = lane * 8; c < H; c += 256) {
+        const uint4 a = *reinterpret_cast<const uint4*>(pr + c);
+        const uint4 b = *reinterpret_cast<const uint4*>(g + t * H + c);
+        const __nv_bfloat162* ha = reinterpret_cast<const __nv_bfloat162*>(&a);
+        const __nv_bfloat162* hb = reinterpret_cast<const __nv_bfloat162*>(&b);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float2 fa = __bfloat1622float2(ha[e]), fb = __bfloat1622float2(hb[e]);
+          dot += fa.x * fb.x + fa.y * fb.y;
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffff, dot, o);
+      if (lane == 0) dw[t * k + j] = dot;
+    }
+    return;
+  }
+  for (int c = lane * 8; c < H; c += 256) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (resid) {
+      const uint4 u = *reinterpret_cast<const uint4*>(resid + t * H + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        acc[2 * e] = f.x;
+        acc[2 * e + 1] = f.y;
+      }
+    }
+    for (int j = 0; j < k; ++j) {
+      const float ww = w ? w[t * k + j] : 1.f;
+      const __nv_bfloat16* pr = reinterpret_cast<const __nv_bfloat16*>(src.p[rank[t * k + j]]) + row[t * k + j] * (long)H;
+      const uint4 u = *reinterpret_cast<const uint4*>(pr + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        acc[2 * e] += ww * f.x;
+        acc[2 * e + 1] += ww * f.y;
+      }
+    }
+    *reinterpret_cast<uint4*>(y + t * H + c) =
+        make_uint4(pack_bf16(acc[0], acc[1]), pack_bf16(acc[2], acc[3]), pack_bf16(acc[4], acc[5]),
+                   pack_bf16(acc[6], acc[7]));
+  }
+}
+
+}  // namespace symm
+
+void symm_ep_scatter(int64_t id, int64_t buf_offset, const at::Tensor& x, const at::Tensor& src_row,
+                     const at::Tensor& dst_rank, const at::Tensor& dst_row,
+                     const c10::optional<at::Tensor>& scale) {
+  auto& h = *g_heaps.at(id);
+  const int n = src_row.numel(), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && x.is_contiguous(), "ep_scatter: contiguous rows, H % 8");
+  if (n == 0) return;
+  symm::PeerPtrs dst = peer_ptrs(h, buf_offset, false);
+  symm::ep_scatter_kernel<<<(n + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)x.data_ptr(), src_row.data_ptr<long>(), dst_rank.data_ptr<int>(),
+      dst_row.data_ptr<long>(), scale ? scale->data_ptr<float>() : nullptr, dst, n, H);
+  check_cuda(cudaGetLastError(), "ep_scatter");
+}
+
+void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, const at::Tensor& row,
+                    const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& resid,
+                    at::Tensor& y, const c10::optional<at::Tensor>& g, const c10::optional<at::Tensor>& dw,
+                    int64_t H) {
+  auto& h = *g_heaps.at(id);
+  const int T = rank.size(0), k = rank.size(1);
+  if (T == 0) return;
+  symm::PeerPtrs src = peer_ptrs(h, buf_offset, false);
+  symm::ep_gather_kernel<<<(T + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      src, rank.data_ptr<int>(), row.data_ptr<long>(), w ? w->data_ptr<float>() : nullptr,
+      resid ? (const __nv_bfloat16*)resid->data_ptr() : nullptr, (__nv_bfloat16*)y.data_ptr(),
+      g ? (const __nv_bfloat16*)g->data_ptr() : nullptr, dw ? dw->data_ptr<float>() : nullptr, T, k, (int)H);
+  check_cuda(cudaGetLastError(), "ep_gather");
+}
+
+}  // namespace kore

@@ -128,3 +128,39 @@ class AdamW:
             self.v[int(u)].copy_(t)
         for u, t in sd.get("master", {}).items():
             self.master[int(u)].copy_(t)
+
+
+class ListAdamW:
+    """AdamW over an explicit {key: (param, grad)} set (expert-parallel expert
+    weights, which are local to their rank and never sharded)."""
+
+    def __init__(self, params: dict, grads: dict, lr: float, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.0, master: str = "fp32", schedule: str = "constant",
+                 warmup_steps: int = 0, total_steps: int = 1, seed: int = 0):
+        self.p, self.g = params, grads
+        self.lr, (self.b1, self.b2), self.eps, self.wd = lr, betas, eps, weight_decay
+        self.lr_fn = lr_lambda_factory(schedule, warmup_steps, total_steps)
+        self.step_count = 0
+        self.seed = seed
+        self.m = {k: torch.zeros(v.numel(), dtype=torch.float32, device=v.device) for k, v in params.items()}
+        self.v = {k: torch.zeros(v.numel(), dtype=torch.float32, device=v.device) for k, v in params.items()}
+        self.master = ({k: v.float().clone() for k, v in params.items()}
+                       if master == "fp32" and any(v.dtype != torch.float32 for v in params.values()) else {})
+
+    def add_sumsq(self, acc: torch.Tensor) -> None:
+        for g in self.g.values():
+            ops.sumsq(g, acc)
+
+    @torch.no_grad()
+    def step(self, sumsq: Optional[torch.Tensor] = None, max_norm: float = 0.0) -> None:
+        lr = self.lr * self.lr_fn(self.step_count)
+        self.step_count += 1
+        for k, p in self.p.items():
+            if p.dtype == torch.float32:
+                ops.adamw_step_f32(p, self.g[k], self.m[k], self.v[k], lr=lr, b1=self.b1, b2=self.b2,
+                                   eps=self.eps, wd=self.wd, step=self.step_count, sumsq_buf=sumsq,
+                                   max_norm=max_norm)
+            else:
+                ops.adamw_step(p, self.g[k], self.m[k], self.v[k], lr=lr, b1=self.b1, b2=self.b2, eps=self.eps,
+                               wd=self.wd, step=self.step_count, master=self.master.get(k), sumsq_buf=sumsq,
+                               max_norm=max_norm, seed=self.seed * 31 + self.step_count * 7 + int(k))

@@ -120,6 +120,9 @@ class Qwen3Engine:
         self.cos, self.sin = ref.rope_tables(c.max_position_embeddings, c.head_dim, c.rope_theta,
                                              self.dev)
         self.grads: List[Optional[torch.Tensor]] = [None] * weights.num_units
+        # expert-parallel runs: gradients of this rank's own experts (never reduced)
+        self.expert_grads = {u: torch.zeros(b.numel(), dtype=self.grad_dtype, device=self.dev)
+                             for u, b in weights.expert_bufs.items()} if allocate_grads else {}
         self._fresh = [True] * weights.num_units
         if allocate_grads:
             for u in range(weights.num_units):
@@ -137,9 +140,14 @@ class Qwen3Engine:
         for g in self.grads:
             if g is not None:
                 g.zero_()
+        for g in self.expert_grads.values():
+            g.zero_()
 
     def grad_views(self, u: int):
-        return self.w.layouts[u].views(self.grads[u])
+        v = self.w.layouts[u].views(self.grads[u])
+        if u in self.expert_grads:
+            v.update(self.w.expert_layouts[u].views(self.expert_grads[u]))
+        return v
 
     def _acc_vec(self, dst: torch.Tensor, src_f32: torch.Tensor) -> None:
         dst.add_(src_f32.to(dst.dtype))

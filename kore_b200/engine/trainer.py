@@ -41,12 +41,14 @@ class CausalLMTrainer:
                  master: str = "auto", dtype: torch.dtype = torch.bfloat16, seed: int = 0,
                  micro_batch_size: int = 1, logits_chunk: int = 4096, schedule: str = "constant",
                  warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
-                 weights: Optional[Qwen3Weights] = None):
+                 weights: Optional[Qwen3Weights] = None, micro_tokens_hint: int = 8192,
+                 ep_capacity: float = 2.0):
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device
         self.heap = None
         grad_alloc = None
+        ep = (self.ctx.rank, self.ctx.world) if (cfg.is_moe and self.ctx.world > 1) else None
         fused = comm == "fused" and self.ctx.world > 1 and dev.type == "cuda"
         if fused:
             from ..parallel.symmetric import SymmetricHeap
@@ -58,16 +60,27 @@ class CausalLMTrainer:
             grad_alloc = alloc
             if weights is None:
                 weights = Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed, pad_multiple=per,
-                                       alloc=alloc)
+                                       alloc=alloc, ep=ep)
             else:  # move existing weights into the heap
                 nw = Qwen3Weights(cfg, device=dev, dtype=weights.dtype, init=False, pad_multiple=per,
-                                  alloc=alloc)
+                                  alloc=alloc, ep=weights.ep)
                 for a, b in zip(nw.bufs, weights.bufs):
                     a[: b.numel()].copy_(b[: a.numel()])
+                for u, b in weights.expert_bufs.items():
+                    nw.expert_bufs[u].copy_(b)
                 weights = nw
         self.w = weights or Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed,
-                                         pad_multiple=128 * max(1, self.ctx.world))
+                                         pad_multiple=128 * max(1, self.ctx.world), ep=ep)
         self.eng = Qwen3Engine(self.w, logits_chunk=logits_chunk, grad_alloc=grad_alloc)
+        if self.w.ep is not None:
+            from ..parallel.ep import ExpertParallel, FusedExpertParallel
+            if fused:
+                cap = int(ep_capacity * micro_tokens_hint * cfg.num_experts_per_tok)
+                ehp = __import__("kore_b200.parallel.symmetric", fromlist=["SymmetricHeap"]).SymmetricHeap(
+                    self.ctx, 4 * cap * cfg.hidden_size * 2 + (1 << 20))
+                self.eng.ep = FusedExpertParallel(self.ctx, cfg, self.w.expert_lo, self.w.expert_hi, ehp, cap)
+            else:
+                self.eng.ep = ExpertParallel(self.ctx, cfg, self.w.expert_lo, self.w.expert_hi)
         if master == "auto":
             master = pick_master_mode(cfg, self.ctx.world, dev)
         self.master_mode = master
@@ -84,7 +97,12 @@ class CausalLMTrainer:
                                     weight_decay=weight_decay, max_grad_norm=max_grad_norm,
                                     master=master, schedule=schedule, warmup_steps=warmup_steps,
                                     total_steps=total_steps, seed=seed, comm=comm)
-        else:
+        if self.w.ep is not None:
+            from .optimizer import ListAdamW
+            self.opt.local = ListAdamW(dict(self.w.expert_bufs), dict(self.eng.expert_grads), lr=lr, betas=betas,
+                                       weight_decay=weight_decay, master=master, schedule=schedule,
+                                       warmup_steps=warmup_steps, total_steps=total_steps, seed=seed)
+        if self.ctx.world <= 1:
             self.opt = AdamW(self.w, self.eng, lr=lr, betas=betas, weight_decay=weight_decay,
                              max_grad_norm=max_grad_norm, master=master, schedule=schedule,
                              warmup_steps=warmup_steps, total_steps=total_steps, seed=seed)

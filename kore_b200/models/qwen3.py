@@ -61,7 +61,24 @@ class UnitLayout:
         return {n: buf[s.offset: s.offset + s.numel].view(s.shape) for n, s in self.segments.items()}
 
 
-def layer_layout(cfg: Qwen3Config, i: int) -> UnitLayout:
+def expert_range(cfg: Qwen3Config, ep: Optional[Tuple[int, int]]) -> Tuple[int, int]:
+    """Global expert ids [lo, hi) owned by rank ``ep[0]`` of ``ep[1]`` (all when no EP)."""
+    if not ep or ep[1] <= 1:
+        return 0, cfg.num_experts
+    r, w = ep
+    if cfg.num_experts % w:
+        raise ValueError("num_experts must be divisible by the expert-parallel size")
+    n = cfg.num_experts // w
+    return r * n, (r + 1) * n
+
+
+def expert_layout(cfg: Qwen3Config, n_local: int) -> UnitLayout:
+    H, I = cfg.hidden_size, cfg.moe_intermediate_size
+    return UnitLayout("experts", [("experts_gate_up", (n_local, 2 * I, H), "normal"),
+                                  ("experts_down", (n_local, H, I), "normal")])
+
+
+def layer_layout(cfg: Qwen3Config, i: int, with_experts: bool = True) -> UnitLayout:
     H, D = cfg.hidden_size, cfg.head_dim
     segs = [
         ("ln1", (H,), "ones"),
@@ -73,19 +90,20 @@ def layer_layout(cfg: Qwen3Config, i: int) -> UnitLayout:
     ]
     if cfg.layer_is_moe(i):
         E, I = cfg.num_experts, cfg.moe_intermediate_size
-        segs += [("router", (E, H), "normal"),
-                 ("experts_gate_up", (E, 2 * I, H), "normal"),
-                 ("experts_down", (E, H, I), "normal")]
+        segs += [("router", (E, H), "normal")]
+        if with_experts:
+            segs += [("experts_gate_up", (E, 2 * I, H), "normal"),
+                     ("experts_down", (E, H, I), "normal")]
         return UnitLayout("moe_layer", segs)
     F = cfg.intermediate_size
     segs += [("gate_up", (2 * F, H), "normal"), ("down", (H, F), "normal")]
     return UnitLayout("layer", segs)
 
 
-def unit_layouts(cfg: Qwen3Config) -> List[UnitLayout]:
+def unit_layouts(cfg: Qwen3Config, with_experts: bool = True) -> List[UnitLayout]:
     H, V = cfg.hidden_size, cfg.vocab_size
     units = [UnitLayout("embed", [("embed", (V, H), "normal")])]
-    units += [layer_layout(cfg, i) for i in range(cfg.num_hidden_layers)]
+    units += [layer_layout(cfg, i, with_experts) for i in range(cfg.num_hidden_layers)]
     head = [("norm", (H,), "ones")]
     if not cfg.tie_word_embeddings:
         head.append(("lm_head", (V, H), "normal"))
@@ -93,7 +111,7 @@ def unit_layouts(cfg: Qwen3Config) -> List[UnitLayout]:
     return units
 
 
-def hf_names(cfg: Qwen3Config, unit: int, layout: UnitLayout):
+def hf_names(cfg: Qwen3Config, unit: int, layout: UnitLayout, expert_base: int = 0):
     """Yield (hf_key, segment_name, row_slice or None, expert index or None)."""
     L = cfg.num_hidden_layers
     if unit == 0:
@@ -107,6 +125,9 @@ def hf_names(cfg: Qwen3Config, unit: int, layout: UnitLayout):
     i = unit - 1
     p = f"model.layers.{i}."
     qd, kd = cfg.q_dim, cfg.kv_dim
+    if layout.kind == "experts":
+        yield from _expert_names(cfg, p, layout, expert_base)
+        return
     yield p + "input_layernorm.weight", "ln1", None, None
     yield p + "self_attn.q_proj.weight", "qkv", (0, qd), None
     yield p + "self_attn.k_proj.weight", "qkv", (qd, qd + kd), None
@@ -116,18 +137,24 @@ def hf_names(cfg: Qwen3Config, unit: int, layout: UnitLayout):
     yield p + "self_attn.o_proj.weight", "o", None, None
     yield p + "post_attention_layernorm.weight", "ln2", None, None
     if layout.kind == "moe_layer":
-        I = cfg.moe_intermediate_size
         yield p + "mlp.gate.weight", "router", None, None
-        for e in range(cfg.num_experts):
-            q = p + f"mlp.experts.{e}."
-            yield q + "gate_proj.weight", "experts_gate_up", (0, I), e
-            yield q + "up_proj.weight", "experts_gate_up", (I, 2 * I), e
-            yield q + "down_proj.weight", "experts_down", None, e
+        yield from _expert_names(cfg, p, layout, expert_base)
     else:
         F = cfg.intermediate_size
         yield p + "mlp.gate_proj.weight", "gate_up", (0, F), None
         yield p + "mlp.up_proj.weight", "gate_up", (F, 2 * F), None
         yield p + "mlp.down_proj.weight", "down", None, None
+
+
+def _expert_names(cfg, p, layout, expert_base):
+    if "experts_gate_up" not in layout.segments:
+        return
+    I = cfg.moe_intermediate_size
+    for e in range(layout.segments["experts_gate_up"].shape[0]):
+        q = p + f"mlp.experts.{expert_base + e}."
+        yield q + "gate_proj.weight", "experts_gate_up", (0, I), e
+        yield q + "up_proj.weight", "experts_gate_up", (I, 2 * I), e
+        yield q + "down_proj.weight", "experts_down", None, e
 
 
 def _dtype(name: str) -> torch.dtype:
@@ -144,11 +171,22 @@ class Qwen3Weights:
 
     def __init__(self, cfg: Qwen3Config, device="cpu", dtype: Optional[torch.dtype] = None,
                  init: bool = True, seed: int = 0, std: float = 0.02,
-                 allocate: bool = True, pad_multiple: int = ALIGN, alloc=None):
+                 allocate: bool = True, pad_multiple: int = ALIGN, alloc=None,
+                 ep: Optional[Tuple[int, int]] = None):
         self.cfg = cfg
         self.dtype = dtype or _dtype(cfg.torch_dtype)
         self.device = torch.device(device)
-        self.layouts = unit_layouts(cfg)
+        # expert parallelism: MoE expert weights live in separate per-rank
+        # buffers (only this rank's experts); everything else is replicated
+        self.ep = ep if (ep and ep[1] > 1 and cfg.is_moe) else None
+        self.expert_lo, self.expert_hi = expert_range(cfg, self.ep)
+        self.layouts = unit_layouts(cfg, with_experts=self.ep is None)
+        self.expert_layouts: Dict[int, UnitLayout] = {}
+        self.expert_bufs: Dict[int, torch.Tensor] = {}
+        if self.ep is not None:
+            for i in range(cfg.num_hidden_layers):
+                if cfg.layer_is_moe(i):
+                    self.expert_layouts[i + 1] = expert_layout(cfg, self.expert_hi - self.expert_lo)
         # buffers are padded so that data-parallel shards divide them evenly
         self.pad_multiple = max(ALIGN, int(pad_multiple))
         self.bufs: List[Optional[torch.Tensor]] = [None] * len(self.layouts)
@@ -158,6 +196,8 @@ class Qwen3Weights:
                 # the symmetric peer-memory heap of the fused collectives)
                 self.bufs[u] = (alloc(self.padded_numel(u), self.dtype) if alloc is not None else
                                 torch.empty(self.padded_numel(u), dtype=self.dtype, device=self.device))
+            for u, lay in self.expert_layouts.items():
+                self.expert_bufs[u] = torch.empty(lay.numel, dtype=self.dtype, device=self.device)
             if init:
                 self.init_random(seed, std)
 
@@ -166,7 +206,10 @@ class Qwen3Weights:
 
     # ------------------------------------------------------------------ views
     def views(self, u: int) -> Dict[str, torch.Tensor]:
-        return self.layouts[u].views(self.bufs[u])
+        v = self.layouts[u].views(self.bufs[u])
+        if u in self.expert_bufs:
+            v.update(self.expert_layouts[u].views(self.expert_bufs[u]))
+        return v
 
     @property
     def num_units(self) -> int:
@@ -186,11 +229,12 @@ class Qwen3Weights:
         """Random init like HF's ``_init_weights``: N(0, std) for matrices,
         ones for norm weights; segment padding is zeroed. Generated on the
         buffer's device (seeded per unit, so it is reproducible)."""
-        for u, lay in enumerate(self.layouts):
-            buf = self.bufs[u]
+        items = [(u, lay, self.bufs[u]) for u, lay in enumerate(self.layouts)]
+        items += [(1000 + u, lay, self.expert_bufs[u]) for u, lay in self.expert_layouts.items()]
+        for u, lay, buf in items:
             buf.zero_()
             g = torch.Generator(device=buf.device)
-            g.manual_seed(seed * 1000003 + u)
+            g.manual_seed(seed * 1000003 + u + (7919 * self.expert_lo if u >= 1000 else 0))
             for name, v in lay.views(buf).items():
                 init = lay.segments[name].init
                 if init == "ones":
@@ -217,14 +261,22 @@ class Qwen3Weights:
             if self.bufs[u] is None:
                 continue
             vs = lay.views(self.bufs[u])
-            for key, seg, rows, expert in hf_names(self.cfg, u, lay):
-                t = vs[seg]
-                if expert is not None:
-                    t = t[expert]
-                if rows is not None:
-                    t = t[rows[0]: rows[1]]
-                out[key] = t
+            pairs = [(lay, vs, 0)]
+            if u in self.expert_bufs:
+                el = self.expert_layouts[u]
+                pairs.append((el, el.views(self.expert_bufs[u]), self.expert_lo))
+            for lay_, vs_, base in pairs:
+                self._collect(out, u, lay_, vs_, base)
         return out
+
+    def _collect(self, out, u, lay, vs, base):
+        for key, seg, rows, expert in hf_names(self.cfg, u, lay, base):
+            t = vs[seg]
+            if expert is not None:
+                t = t[expert]
+            if rows is not None:
+                t = t[rows[0]: rows[1]]
+            out[key] = t
 
     @torch.no_grad()
     def load_hf_state_dict(self, sd: Dict[str, torch.Tensor], strict: bool = True) -> List[str]:
@@ -246,12 +298,14 @@ class Qwen3Weights:
 
     def to(self, device=None, dtype=None) -> "Qwen3Weights":
         w = Qwen3Weights(self.cfg, device or self.device, dtype or self.dtype, allocate=False,
-                         pad_multiple=self.pad_multiple)
+                         pad_multiple=self.pad_multiple, ep=self.ep)
         w.bufs = [b.to(device=w.device, dtype=w.dtype) if b is not None else None for b in self.bufs]
+        w.expert_bufs = {u: b.to(device=w.device, dtype=w.dtype) for u, b in self.expert_bufs.items()}
         return w
 
     def clone(self) -> "Qwen3Weights":
         w = Qwen3Weights(self.cfg, self.device, self.dtype, allocate=False,
-                         pad_multiple=self.pad_multiple)
+                         pad_multiple=self.pad_multiple, ep=self.ep)
         w.bufs = [b.clone() if b is not None else None for b in self.bufs]
+        w.expert_bufs = {u: b.clone() for u, b in self.expert_bufs.items()}
         return w

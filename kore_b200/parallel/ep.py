@@ -1,0 +1,245 @@
+"""Expert parallelism: MoE tokens are dispatched to the rank that owns their
+experts and the expert outputs are combined back.
+
+Each rank owns experts [lo, hi) (``Qwen3Weights(ep=(rank, world))``) and its
+own tokens. Forward of one MoE layer:
+
+  local route -> pairs sorted by global expert (so rows for each destination
+  rank are contiguous) -> exchange per-expert counts -> all-to-all of the
+  token rows -> expert-major permutation of the received rows -> grouped
+  tcgen05 GEMMs (SwiGLU experts) -> inverse permutation -> all-to-all back
+  -> weighted combine (+ residual) at the source.
+
+The backward mirrors it (combine bwd -> all-to-all -> expert backward with
+local weight gradients -> all-to-all -> un-permute sum). Data planes:
+``comm="nccl"`` uses ``all_to_all_single``; the counts are needed on the
+host anyway to size the grouped GEMM. Expert weights and their gradients
+never leave their rank; only the replicated parts go through ZeRO.
+"""
+from __future__ import annotations
+
+from typing import List, Tuple
+
+import torch
+import torch.distributed as dist
+
+from .. import ops
+from ..ops import moe
+
+
+class ExpertParallel:
+    def __init__(self, ctx, cfg, lo: int, hi: int):
+        self.ctx = ctx
+        self.cfg = cfg
+        self.lo, self.hi = lo, hi
+        self.W = ctx.world
+        self.E = cfg.num_experts
+        self.El = hi - lo
+
+    # ------------------------------------------------------------ plumbing
+    def _a2a(self, x: torch.Tensor, send: List[int], recv: List[int]) -> torch.Tensor:
+        out = torch.empty((sum(recv),) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
+        if self.ctx.backend == "nccl":
+            dist.all_to_all_single(out, x.contiguous(), recv, send, group=self.ctx.group)
+        else:  # gloo: no all_to_all_single on CPU for every dtype -> gather-based exchange
+            chunks = list(x.split(send))
+            gathered = [None] * self.W
+            dist.all_gather_object(gathered, [c.cpu() for c in chunks], group=self.ctx.group)
+            parts = [gathered[s][self.ctx.rank].to(x.device) for s in range(self.W)]
+            out = torch.cat(parts) if parts else out
+        return out
+
+    def _plan(self, idx: torch.Tensor):
+        """Send order (pairs sorted by global expert), per-dest row counts, and the
+        receive-side counts matrix [src, local expert]."""
+        T, k = idx.shape
+        flat = idx.reshape(-1).long()
+        order = torch.argsort(flat, stable=True)
+        counts = torch.bincount(flat, minlength=self.E)               # [E] on this rank
+        cm = torch.empty(self.W * self.El, dtype=counts.dtype, device=counts.device)
+        if self.ctx.backend == "nccl":
+            dist.all_to_all_single(cm, counts.contiguous(), group=self.ctx.group)
+        else:
+            g = [None] * self.W
+            dist.all_gather_object(g, counts.cpu(), group=self.ctx.group)
+            cm = torch.cat([g[s][self.lo:self.hi] for s in range(self.W)]).to(counts.device)
+        cnt = counts.view(self.W, self.El).sum(1).tolist()             # rows to each dest
+        recv_mat = cm.view(self.W, self.El).tolist()                   # [src][local expert]
+        return order, cnt, recv_mat
+
+    @staticmethod
+    def _expert_major(recv_mat) -> Tuple[torch.Tensor, List[int]]:
+        """Permutation from src-major receive order to expert-major order."""
+        W = len(recv_mat)
+        El = len(recv_mat[0]) if W else 0
+        src_off, o = [], 0
+        base = [[0] * El for _ in range(W)]
+        for s in range(W):
+            for e in range(El):
+                base[s][e] = o
+                o += recv_mat[s][e]
+        perm, offs = [], [0]
+        for e in range(El):
+            for s in range(W):
+                perm.extend(range(base[s][e], base[s][e] + recv_mat[s][e]))
+            offs.append(len(perm))
+        return torch.tensor(perm, dtype=torch.long), offs
+
+    # ------------------------------------------------------------ forward
+    def forward(self, eng, W, hn2, x2, probs, idx, wts):
+        T, k = idx.shape
+        order, send, recv_mat = self._plan(idx)
+        recv = [sum(r) for r in recv_mat]
+        rows = moe.gather_rows(hn2, order // k)                         # send buffer
+        xr = self._a2a(rows, send, recv)
+        perm, offs = self._expert_major(recv_mat)
+        perm = perm.to(hn2.device)
+        xp = moe.gather_rows(xr, perm)
+        gu = moe.grouped_mm(xp, W["experts_gate_up"], offs)
+        a = ops.swiglu_fwd(gu)
+        yp = moe.grouped_mm(a, W["experts_down"], offs)
+        yr = torch.empty_like(yp)
+        yr[perm] = yp                                                   # back to src-major
+        ys = self._a2a(yr, recv, send)                                  # rows in send order
+        pos = torch.empty(T * k, dtype=torch.int32, device=hn2.device)
+        pos[order] = torch.arange(T * k, dtype=torch.int32, device=hn2.device)
+        pos = pos.view(T, k)
+        x3 = moe.combine(ys, pos, wts, resid=x2)
+        ctx = dict(probs=probs, idx=idx, wts=wts, pos=pos, order=order, send=send, recv=recv, perm=perm,
+                   offs=offs, xp=xp, gu=gu, a=a, ys=ys)
+        return x3, ctx
+
+    # ------------------------------------------------------------ backward
+    def backward(self, eng, W, G, ctx, dx3):
+        dys, dw = moe.combine_bwd(dx3, ctx["ys"], ctx["pos"], ctx["wts"])
+        dyr = self._a2a(dys, ctx["send"], ctx["recv"])
+        dyp = moe.gather_rows(dyr, ctx["perm"])
+        offs = ctx["offs"]
+        da = moe.grouped_mm(dyp, W["experts_down"], offs, w_t=False)
+        eng._expert_wgrad(G["experts_down"], dyp, ctx["a"], offs)
+        dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])
+        dxp = moe.grouped_mm(dgu, W["experts_gate_up"], offs, w_t=False)
+        eng._expert_wgrad(G["experts_gate_up"], dgu, ctx["xp"], offs)
+        dxr = torch.empty_like(dxp)
+        dxr[ctx["perm"]] = dxp
+        dxs = self._a2a(dxr, ctx["recv"], ctx["send"])                 # send order
+        dhn2 = moe.combine(dxs, ctx["pos"], None)
+        return dhn2, dw
+
+
+class FusedExpertParallel(ExpertParallel):
+    """Expert parallelism on the symmetric peer-memory heap (path d).
+
+    Dispatch: every rank stores its token rows straight into the owner
+    rank's receive buffer, already in the owner's expert-major order, with
+    NVLink P2P stores (one kernel; no all-to-all and no receive-side
+    permutation). The owner runs the grouped tcgen05 expert GEMMs in place.
+    Combine: each source rank pulls its pairs' expert outputs from the
+    owners' heaps with P2P loads and reduces them with the routing weights
+    and the residual in the same kernel. The backward pushes w * dy rows to
+    the owners (scaled P2P stores), pulls dot products for the routing-weight
+    gradient, and pulls the input gradients back. Device barriers (epoch
+    flags) order the phases; only the per-expert counts (E ints) cross NCCL.
+    """
+
+    def __init__(self, ctx, cfg, lo, hi, heap, cap_rows: int):
+        super().__init__(ctx, cfg, lo, hi)
+        H = cfg.hidden_size
+        I = cfg.moe_intermediate_size
+        self.heap = heap
+        self.cap = int(cap_rows)
+        self.o_recv, self.recv = heap.alloc(self.cap * H)
+        self.o_y, self.ybuf = heap.alloc(self.cap * H)
+        self.o_dy, self.dybuf = heap.alloc(self.cap * H)
+        self.o_dx, self.dxbuf = heap.alloc(self.cap * H)
+        self.H, self.I = H, I
+
+    def _counts(self, idx):
+        flat = idx.reshape(-1).long()
+        counts = torch.bincount(flat, minlength=self.E).to(torch.int64)
+        allc = torch.empty(self.W * self.E, dtype=torch.int64, device=counts.device)
+        dist.all_gather_into_tensor(allc, counts, group=self.ctx.group)
+        return flat, counts, allc.view(self.W, self.E)
+
+    def _route_rows(self, idx):
+        """Destination rank/row of every local pair, and this rank's receive plan."""
+        T, k = idx.shape
+        flat, counts, C = self._counts(idx)
+        Ch = C.tolist()
+        W, El, r = self.W, self.El, self.ctx.rank
+        base = [0] * self.E          # first row of expert e in its owner's buffer
+        for d in range(W):
+            acc = 0
+            for e in range(d * El, (d + 1) * El):
+                base[e] = acc
+                acc += sum(Ch[s][e] for s in range(W))
+        off_me = torch.tensor([base[e] + sum(Ch[s][e] for s in range(r)) for e in range(self.E)],
+                              dtype=torch.long, device=idx.device)
+        order = torch.argsort(flat, stable=True)
+        start = torch.cumsum(counts, 0) - counts                       # my first sorted index per expert
+        e_sorted = flat[order]
+        p = torch.arange(order.numel(), device=idx.device)
+        dst_row_sorted = off_me[e_sorted] + (p - start[e_sorted])
+        dst_row = torch.empty_like(dst_row_sorted)
+        dst_row[order] = dst_row_sorted
+        dst_rank = (flat // El).to(torch.int32)
+        offs = [0]
+        for e in range(self.lo, self.hi):
+            offs.append(offs[-1] + sum(Ch[s][e] for s in range(W)))
+        rmax = max(sum(Ch[s][e] for s in range(W) for e in range(d * El, (d + 1) * El)) for d in range(W))
+        return dst_rank, dst_row, offs, rmax
+
+    def forward(self, eng, W, hn2, x2, probs, idx, wts):
+        T, k = idx.shape
+        dst_rank, dst_row, offs, rmax = self._route_rows(idx)
+        if rmax > self.cap:
+            return super().forward(eng, W, hn2, x2, probs, idx, wts)
+        C = ops.native()
+        src_row = torch.arange(T * k, device=hn2.device) // k
+        C.symm_ep_scatter(self.heap.id, self.o_recv, hn2, src_row, dst_rank, dst_row, None)
+        self.heap.barrier()                                   # all rows delivered
+        R = offs[-1]
+        H = self.H
+        xp = self.recv[: R * H].view(R, H).clone()            # kept for the weight gradient
+        gu = moe.grouped_mm(xp, W["experts_gate_up"], offs)
+        a = ops.swiglu_fwd(gu)
+        yp = self.ybuf[: R * H].view(R, H)
+        moe.grouped_mm(a, W["experts_down"], offs, out=yp)
+        self.heap.barrier()                                   # expert outputs ready
+        y = torch.empty_like(x2)
+        C.symm_ep_gather(self.heap.id, self.o_y, dst_rank.view(T, k), dst_row.view(T, k), wts.float().contiguous(),
+                         x2, y, None, None, H)
+        ctx = dict(probs=probs, idx=idx, wts=wts, fused=True, dst_rank=dst_rank, dst_row=dst_row, offs=offs,
+                   xp=xp, gu=gu, a=a)
+        return y, ctx
+
+    def backward(self, eng, W, G, ctx, dx3):
+        if not ctx.get("fused"):
+            return super().backward(eng, W, G, ctx, dx3)
+        C = ops.native()
+        T, k = ctx["idx"].shape
+        H = self.H
+        offs = ctx["offs"]
+        R = offs[-1]
+        dev = dx3.device
+        dw = torch.empty(T, k, dtype=torch.float32, device=dev)
+        # routing-weight gradient: <dy[t], y_expert> pulled from the owners (outputs still in their heaps)
+        C.symm_ep_gather(self.heap.id, self.o_y, ctx["dst_rank"].view(T, k), ctx["dst_row"].view(T, k), None, None,
+                         dx3, dx3, dw, H)
+        src_row = torch.arange(T * k, device=dev) // k
+        C.symm_ep_scatter(self.heap.id, self.o_dy, dx3, src_row, ctx["dst_rank"], ctx["dst_row"],
+                          ctx["wts"].reshape(-1).float().contiguous())
+        self.heap.barrier()                                   # w * dy rows delivered; y reads done
+        dyp = self.dybuf[: R * H].view(R, H)
+        da = moe.grouped_mm(dyp, W["experts_down"], offs, w_t=False)
+        eng._expert_wgrad(G["experts_down"], dyp, ctx["a"], offs)
+        dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])
+        dxp = self.dxbuf[: R * H].view(R, H)
+        moe.grouped_mm(dgu, W["experts_gate_up"], offs, w_t=False, out=dxp)
+        eng._expert_wgrad(G["experts_gate_up"], dgu, ctx["xp"], offs)
+        self.heap.barrier()                                   # input grads ready
+        dhn2 = torch.empty(T, H, dtype=dx3.dtype, device=dev)
+        C.symm_ep_gather(self.heap.id, self.o_dx, ctx["dst_rank"].view(T, k), ctx["dst_row"].view(T, k), None, None,
+                         dhn2, None, None, H)
+        self.heap.barrier()                                   # pulls done before buffers are reused
+        return dhn2, dw

@@ -52,8 +52,30 @@ def main(argv=None):
         print(json.dumps({"check": "zero2_fused_vs_nccl", "world": ctx.world, "ok": ok and same and err == 0,
                           "loss_nccl": res["nccl"][0], "loss_fused": res["fused"][0],
                           "replicas_identical": same, "device_error": err}), flush=True)
+    # expert parallelism: NCCL all-to-all vs fused peer-memory dispatch/combine
+    mcfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                       num_attention_heads=4, num_key_value_heads=2, head_dim=128, model_type="qwen3_moe",
+                       num_experts=8 * ctx.world, num_experts_per_tok=4, moe_intermediate_size=256,
+                       max_position_embeddings=2048)
+    ids_m = torch.randint(0, mcfg.vocab_size, (ctx.world * 2, 256), generator=g)[ctx.rank * 2:(ctx.rank + 1) * 2].cuda()
+    mres = {}
+    for comm in ("nccl", "fused"):
+        tr = CausalLMTrainer(mcfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm=comm, master="fp32",
+                             micro_tokens_hint=512)
+        losses = [tr.train_step_device(ids_m) for _ in range(3)]
+        torch.cuda.synchronize()
+        mres[comm] = ([float(l) for l in losses], [b.float().clone() for b in tr.w.expert_bufs.values()])
+        del tr
+    mok = all(abs(a - b) < 2e-2 * max(1.0, abs(a)) for a, b in zip(mres["nccl"][0], mres["fused"][0]))
+    for a, b in zip(mres["nccl"][1], mres["fused"][1]):
+        mok = mok and torch.allclose(a, b, atol=2e-2, rtol=0)
+    err2 = check_device_error()
+    if ctx.is_main:
+        print(json.dumps({"check": "ep_fused_vs_nccl", "world": ctx.world, "ok": mok and err2 == 0,
+                          "loss_nccl": mres["nccl"][0], "loss_fused": mres["fused"][0], "device_error": err2}),
+              flush=True)
     torch.distributed.barrier()
-    return 0 if (ok and same and err == 0) else 1
+    return 0 if (ok and same and err == 0 and mok and err2 == 0) else 1
 
 
 if __name__ == "__main__":

@@ -61,6 +61,7 @@ class ShardedAdamW:
                 self.gshard[u] = torch.empty(s, dtype=engine.grad_dtype, device=dev)
         self._sumsq = torch.zeros(1, dtype=torch.float32, device=dev)
         self.last_sumsq: Optional[torch.Tensor] = None
+        self.local = None      # ListAdamW over expert-parallel expert weights, if any
 
     def current_lr(self) -> float:
         return self.lr * self.lr_fn(self.step_count)
@@ -98,9 +99,13 @@ class ShardedAdamW:
             self._sumsq.zero_()
             for u in range(self.w.num_units):
                 ops.sumsq(self.gshard[u], self._sumsq)
+            if self.local is not None:        # disjoint across ranks: add before the reduce
+                self.local.add_sumsq(self._sumsq)
             dist.all_reduce(self._sumsq, group=self.ctx.group)
             sq = self._sumsq
             self.last_sumsq = sq
+        if self.local is not None:
+            self.local.step(sq, float(self.max_grad_norm or 0.0))
         lr = self.current_lr()
         self.step_count += 1
         for u in range(self.w.num_units):
@@ -150,6 +155,8 @@ class FusedShardedAdamW(ShardedAdamW):
             self._local.zero_()
             for u in range(self.w.num_units):
                 C.symm_rs_sumsq(h.id, self.g_off[u], self.shard_len[u], None, self._local, float(grad_scale))
+            if self.local is not None:
+                self.local.add_sumsq(self._local)
             C.symm_scalar_allreduce(h.id, 0, h.next_epoch(), self._local, self._sumsq)
             sq = self._sumsq
             self.last_sumsq = sq
@@ -161,4 +168,6 @@ class FusedShardedAdamW(ShardedAdamW):
                                self.m[u], self.v[u], lr, self.b1, self.b2, self.eps, self.wd,
                                self.step_count, sq, float(self.max_grad_norm or 0.0),
                                self.seed * 7919 + self.step_count * 104729 + u * 31 + self.ctx.rank)
+        if self.local is not None:
+            self.local.step(sq, float(self.max_grad_norm or 0.0))
         h.barrier()                                   # every rank received all parameter shards

@@ -102,3 +102,31 @@ def test_zero2_sft_matches_single_rank():
         assert torch.allclose(torch.tensor(a), torch.tensor(b), atol=1e-6)
     for a, b in zip(two[0]["w"], two[1]["w"]):
         assert a == b
+
+
+def _moe_ep(ctx):
+    from kore_b200.engine.trainer import CausalLMTrainer
+    from kore_b200.models import Qwen3Weights
+    from tests.test_moe_cpu import tiny_moe
+    cfg = tiny_moe()
+    full = Qwen3Weights(cfg, dtype=torch.float32, seed=5)
+    ep = (ctx.rank, ctx.world) if ctx.world > 1 else None
+    w = Qwen3Weights(cfg, dtype=torch.float32, init=False, pad_multiple=128 * ctx.world, ep=ep)
+    for b in w.bufs:
+        b.zero_()
+    w.load_hf_state_dict(full.hf_state_dict())
+    tr = CausalLMTrainer(cfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, dtype=torch.float32, weights=w)
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, 256, (4, 24), generator=g)
+    mine = ids[ctx.rank * 2:(ctx.rank + 1) * 2] if ctx.world > 1 else ids
+    loss = tr.train_step(mine)
+    return {"loss": loss, "sd": {k: v.flatten()[:64].tolist() for k, v in w.hf_state_dict().items()}}
+
+
+def test_expert_parallel_matches_single_rank():
+    two = _run(_moe_ep, 2)
+    one = _run(_moe_ep, 1)
+    assert two[0]["loss"] == pytest.approx(one[0]["loss"], rel=1e-5)
+    for r in (0, 1):
+        for k, v in two[r]["sd"].items():
+            assert torch.allclose(torch.tensor(v), torch.tensor(one[0]["sd"][k]), atol=1e-6), k
