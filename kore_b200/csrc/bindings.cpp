@@ -78,6 +78,12 @@ void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, cons
                     const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& resid,
                     at::Tensor& y, const c10::optional<at::Tensor>& g, const c10::optional<at::Tensor>& dw,
                     int64_t H);
+void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<int64_t>& a_peers, int64_t lda,
+                  int64_t M, const at::Tensor& b, const c10::optional<at::Tensor>& out,
+                  const std::vector<int64_t>& rs_peers, int64_t ldc, int64_t rows, int64_t rank);
+void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x, const c10::optional<at::Tensor>& g,
+                    const c10::optional<at::Tensor>& hn, double eps);
+std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -115,5 +121,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &kore::moe_combine_bwd);
   m.def("symm_ep_scatter", &kore::symm_ep_scatter);
   m.def("symm_ep_gather", &kore::symm_ep_gather);
+  m.def("gemm_tp_bf16", &kore::gemm_tp_bf16, "tensor-parallel AG->GEMM / GEMM->RS over peer memory");
+  m.def("tp_reduce_norm", &kore::tp_reduce_norm);
+  m.def("symm_peer_addrs", &kore::symm_peer_addrs);
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

@@ -49,6 +49,19 @@ struct Params {
   // B is a 3-D tensor map indexed by expert; rows >= limit are not stored.
   const int4* tiles;
   void* C_write;  // output base for the masked direct-store epilogue (grouped mode)
+  // tensor-parallel all-gather->GEMM: A rows [i*ag_rows, (i+1)*ag_rows) live on
+  // peer i and are loaded by TMA straight from that peer (tensor map pm.a[i]).
+  int ag_rows;
+  // tensor-parallel GEMM->reduce-scatter: output row r is stored (P2P) into
+  // peer r / rs_rows, slot rs_rank, i.e. rs_out[peer] + (rs_rank*rs_rows + r%rs_rows)*ldc.
+  int rs_rows;
+  int rs_rank;
+  void* rs_out[8];
+};
+
+// Per-peer tensor maps for the all-gather->GEMM mode (kernel parameter, 1 KB).
+struct PeerMaps {
+  CUtensorMap a[8];
 };
 
 template <int BN, int STAGES>
@@ -75,7 +88,7 @@ KORE_DEV void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, Params p) {
+                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ PeerMaps pm, Params p) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -135,7 +148,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sB = sA + S::A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], S::STAGE_BYTES);
           const int k0 = kb * BK;
-          if (!A_MN) {
+          if (p.ag_rows > 0) {  // rows of this tile come from their owner peers (64-row boxes)
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) {
+              const int r = m0 + 64 * j;
+              const int np = p.M / p.ag_rows;
+              int pi = r / p.ag_rows, lr = r % p.ag_rows;
+              if (pi >= np) { pi = np - 1; lr = 0; }  // past M: any valid rows (outputs are clipped)
+              tma_load_2d(sA + j * 8192, &pm.a[pi], &full_bar[stage], k0, lr);
+            }
+          } else if (!A_MN) {
             tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
           } else {
 #pragma unroll
@@ -275,19 +297,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (p.tiles != nullptr) {
-          // grouped: masked direct stores (a tile may end inside another expert's rows)
+        if (p.tiles != nullptr || p.rs_rows > 0) {
+          // grouped: masked direct stores (a tile may end inside another expert's rows);
+          // reduce-scatter: the row goes to its owner peer's slot (P2P store)
           const int ncols = min(CH, p.N - (n0 + c0));
+          size_t orow = (size_t)row;
+          void* obase = p.C_write;
+          if (p.rs_rows > 0) {
+            obase = p.rs_out[row / p.rs_rows];
+            orow = (size_t)p.rs_rank * p.rs_rows + row % p.rs_rows;
+          }
           if (row_ok) {
             if (p.out_f32) {
-              float* cp = reinterpret_cast<float*>(p.C_write) + (size_t)row * p.ldc + n0 + c0;
+              float* cp = reinterpret_cast<float*>(obase) + orow * p.ldc + n0 + c0;
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
                 if (j >= ncols) break;
                 *reinterpret_cast<float4*>(cp + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
               }
             } else {
-              __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(p.C_write) + (size_t)row * p.ldc + n0 + c0;
+              __nv_bfloat16* cp = reinterpret_cast<__nv_bfloat16*>(obase) + orow * p.ldc + n0 + c0;
 #pragma unroll
               for (int j = 0; j < 64; j += 8) {
                 if (j >= ncols) break;
@@ -346,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
-            int grid, cudaStream_t stream) {
+            int grid, cudaStream_t stream, const PeerMaps* pmp = nullptr) {
   auto k = gemm_kernel<BN, STAGES, A_MN, B_MN>;
   constexpr int smem = Smem<BN, STAGES>::TOTAL;
   static bool attr_set = false;  // per template instance; device attributes are per-function
@@ -355,7 +384,8 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                "cudaFuncSetAttribute(gemm smem)");
     attr_set = true;
   }
-  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, p);
+  static PeerMaps empty_maps{};
+  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, pmp ? *pmp : empty_maps, p);
   check_cuda(cudaGetLastError(), "gemm launch");
 }
 
@@ -404,6 +434,9 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
   p.ldr = 0;
   p.tiles = nullptr;
   p.C_write = out.data_ptr();
+  p.ag_rows = 0;
+  p.rs_rows = 0;
+  p.rs_rank = 0;
   if (residual) {
     TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1 &&
                     residual->size(0) == M && residual->size(1) == N,
@@ -438,6 +471,63 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
 #undef KORE_GEMM_DISPATCH
 }
 
+
+// Tensor-parallel GEMMs over peer memory (sequence-parallel layout: the M
+// rows are split in W blocks of ``rows`` rows, block i owned by rank i).
+//  * all-gather->GEMM (``a_peers`` given): out[M, N] = A . B^T where A's row
+//    block i is read by TMA directly from peer i's buffer at a_peers[i]
+//    (row stride lda). No gathered copy of A is ever materialised.
+//  * GEMM->reduce-scatter (``rs_peers`` given): out rows are stored into the
+//    owner peer's slot buffer (P2P stores): rs_peers[r/rows] +
+//    (rank*rows + r%rows) * ldc; the owner then sums its W slots.
+void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<int64_t>& a_peers, int64_t lda,
+                  int64_t M, const at::Tensor& b, const c10::optional<at::Tensor>& out,
+                  const std::vector<int64_t>& rs_peers, int64_t ldc, int64_t rows, int64_t rank) {
+  TORCH_CHECK(b.scalar_type() == at::kBFloat16 && b.dim() == 2 && b.stride(1) == 1, "b: bf16 [N, K]");
+  const int N = b.size(0), K = b.size(1);
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && rows % 64 == 0 && rows > 0, "tp gemm: N, K % 8 and rows % 64");
+  const bool ag = !a_peers.empty();
+  const bool rs = !rs_peers.empty();
+  TORCH_CHECK(ag || a_local.has_value(), "tp gemm: need a_local or a_peers");
+  TORCH_CHECK(rs || out.has_value(), "tp gemm: need out or rs_peers");
+  TORCH_CHECK(a_peers.size() <= 8 && rs_peers.size() <= 8, "tp gemm: at most 8 peers");
+  c10::cuda::CUDAGuard guard(b.device());
+  gemm::Params p;
+  p.M = (int)M; p.N = N; p.K = K;
+  p.alpha = 1.f;
+  p.accumulate = 0;
+  p.out_f32 = 0;
+  p.R = nullptr; p.ldr = 0;
+  p.tiles = nullptr;
+  p.C_read = out ? out->data_ptr() : nullptr;
+  p.C_write = out ? out->data_ptr() : nullptr;
+  p.ldc = rs ? (int)ldc : (int)out->stride(0);
+  p.ag_rows = ag ? (int)rows : 0;
+  p.rs_rows = rs ? (int)rows : 0;
+  p.rs_rank = (int)rank;
+  for (int i = 0; i < 8; ++i) p.rs_out[i] = nullptr;
+  for (size_t i = 0; i < rs_peers.size(); ++i) p.rs_out[i] = reinterpret_cast<void*>(rs_peers[i]);
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  const int BN = use256 ? 256 : 128;
+  gemm::PeerMaps pm{};
+  CUtensorMap ta;
+  if (ag) {
+    for (size_t i = 0; i < a_peers.size(); ++i)
+      pm.a[i] = make_tmap_2d(reinterpret_cast<void*>(a_peers[i]), bf, 2, K, rows, lda, 64, 64);
+    ta = pm.a[0];
+  } else {
+    TORCH_CHECK(a_local->stride(1) == 1 && a_local->size(1) == K, "a_local: [M, K]");
+    ta = make_tmap_2d(a_local->data_ptr(), bf, 2, K, M, a_local->stride(0), 64, 128);
+  }
+  CUtensorMap tb = make_tmap_2d(b.data_ptr(), bf, 2, K, N, b.stride(0), 64, BN);
+  CUtensorMap tc = rs ? tb : make_tmap_2d(out->data_ptr(), bf, 2, N, M, out->stride(0), 64, 32);
+  const int tiles = (int)((M + 127) / 128) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms(b.get_device()));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (use256) gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, &pm);
+  else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, &pm);
+}
 
 // Grouped GEMM over experts (MoE): rows of ``a`` are grouped by expert with
 // boundaries ``offsets`` (host int64 list, length E+1). For expert e:
@@ -481,6 +571,9 @@ void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
   p.R = nullptr;
   p.ldr = 0;
   p.tiles = reinterpret_cast<const int4*>(tt.data_ptr<int>());
+  p.ag_rows = 0;
+  p.rs_rows = 0;
+  p.rs_rank = 0;
   const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
   const int BN = use256 ? 256 : 128;
   auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;

@@ -486,3 +486,85 @@ void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, cons
 }
 
 }  // namespace kore
+
+// ============================================================== TP reduce + residual + RMSNorm
+namespace kore {
+namespace symm {
+
+// x[r] += sum_w slots[w][r] (the reduce of GEMM->reduce-scatter), then
+// hn[r] = rmsnorm(x[r]) * g. One CTA (128 threads) per local row; H <= 8192.
+__global__ void tp_reduce_norm_kernel(const __nv_bfloat16* __restrict__ slots, int W, int R, int H,
+                                      __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ g,
+                                      __nv_bfloat16* __restrict__ hn, float eps) {
+  const int r = blockIdx.x;
+  __shared__ float red[4];
+  float v[8][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = (threadIdx.x + i * 128) * 8;
+    if (c < H) {
+      float a[8];
+      const uint4 u = *reinterpret_cast<const uint4*>(x + (size_t)r * H + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) { float2 f = __bfloat1622float2(h[e]); a[2 * e] = f.x; a[2 * e + 1] = f.y; }
+      for (int w = 0; w < W; ++w) {
+        const uint4 q = *reinterpret_cast<const uint4*>(slots + ((size_t)w * R + r) * H + c);
+        const __nv_bfloat162* hq = reinterpret_cast<const __nv_bfloat162*>(&q);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) { float2 f = __bfloat1622float2(hq[e]); a[2 * e] += f.x; a[2 * e + 1] += f.y; }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { v[i][e] = a[e]; ss += a[e] * a[e]; }
+      *reinterpret_cast<uint4*>(x + (size_t)r * H + c) =
+          make_uint4(pack_bf16(a[0], a[1]), pack_bf16(a[2], a[3]), pack_bf16(a[4], a[5]), pack_bf16(a[6], a[7]));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffff, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  const float rs = rsqrtf((red[0] + red[1] + red[2] + red[3]) / H + eps);
+  if (hn == nullptr) return;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int c = (threadIdx.x + i * 128) * 8;
+    if (c < H) {
+      const uint4 u = *reinterpret_cast<const uint4*>(g + c);
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+      float o[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float2 f = __bfloat1622float2(h[e]);
+        o[2 * e] = v[i][2 * e] * rs * f.x;
+        o[2 * e + 1] = v[i][2 * e + 1] * rs * f.y;
+      }
+      *reinterpret_cast<uint4*>(hn + (size_t)r * H + c) =
+          make_uint4(pack_bf16(o[0], o[1]), pack_bf16(o[2], o[3]), pack_bf16(o[4], o[5]), pack_bf16(o[6], o[7]));
+    }
+  }
+}
+
+}  // namespace symm
+
+void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x, const c10::optional<at::Tensor>& g,
+                    const c10::optional<at::Tensor>& hn, double eps) {
+  const int H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 8192 && x.is_contiguous(), "tp_reduce_norm: H % 8, H <= 8192");
+  if (R == 0) return;
+  symm::tp_reduce_norm_kernel<<<(int)R, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const __nv_bfloat16*)slots.data_ptr(), (int)W, (int)R, H, (__nv_bfloat16*)x.data_ptr(),
+      g ? (const __nv_bfloat16*)g->data_ptr() : nullptr, hn ? (__nv_bfloat16*)hn->data_ptr() : nullptr, (float)eps);
+  check_cuda(cudaGetLastError(), "tp_reduce_norm");
+}
+
+// Device addresses of every peer's mapping of this heap at a byte offset.
+std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset) {
+  auto& h = *g_heaps.at(id);
+  std::vector<int64_t> out;
+  for (int p = 0; p < h.world; ++p) out.push_back(reinterpret_cast<int64_t>(h.peers[p] + offset));
+  return out;
+}
+
+}  // namespace kore

@@ -74,8 +74,32 @@ def main(argv=None):
         print(json.dumps({"check": "ep_fused_vs_nccl", "world": ctx.world, "ok": mok and err2 == 0,
                           "loss_nccl": mres["nccl"][0], "loss_fused": mres["fused"][0], "device_error": err2}),
               flush=True)
+    # tensor-parallel rollout (AG->GEMM / GEMM->RS over peer memory) vs the 1-GPU engine
+    from ..engine.rollout import GenRequest, RolloutEngine
+    from ..models import Qwen3Weights
+    from .tp import TPRolloutEngine
+    tcfg = Qwen3Config(vocab_size=4096, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                       num_attention_heads=2 * ctx.world, num_key_value_heads=ctx.world, head_dim=128,
+                       max_position_embeddings=2048)
+    w = Qwen3Weights(tcfg, device="cuda", dtype=torch.bfloat16, seed=3)
+    gp = torch.Generator().manual_seed(100 + ctx.rank)
+    prompts = [torch.randint(0, tcfg.vocab_size, (n,), generator=gp).tolist() for n in (70, 33, 150)]
+    tp = TPRolloutEngine(w, ctx, max_rows=1024, max_seqs=8, max_seq_len=512)
+    toks, lps = tp.generate_static(prompts, 16, temperature=0.0)
+    one = RolloutEngine(w, max_batch=8, page_size=64, num_pages=64, max_seq_len=512)
+    ref_out = one.generate([GenRequest(p, 16, rid=i) for i, p in enumerate(prompts)], temperature=0.0)
+    agree = sum(a == b for t, o in zip(toks, ref_out) for a, b in zip(t, o.tokens)) / max(1, sum(len(t) for t in toks))
+    first = all(t[:4] == o.tokens[:4] for t, o in zip(toks, ref_out))
+    lp_err = max(abs(a - b) for l, o in zip(lps, ref_out) for a, b in zip(l[:4], o.logps[:4]))
+    err3 = check_device_error()
+    tok_ok = first and agree > 0.8 and err3 == 0
+    res_all = ctx.all_gather_object({"agree": agree, "first": first, "lp_err": lp_err})
+    if ctx.is_main:
+        print(json.dumps({"check": "tp_rollout_vs_single_gpu", "world": ctx.world,
+                          "ok": all(r["first"] and r["agree"] > 0.8 for r in res_all), "ranks": res_all,
+                          "device_error": err3}), flush=True)
     torch.distributed.barrier()
-    return 0 if (ok and same and err == 0 and mok and err2 == 0) else 1
+    return 0 if (ok and same and err == 0 and mok and err2 == 0 and tok_ok) else 1
 
 
 if __name__ == "__main__":
