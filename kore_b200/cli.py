@@ -10,6 +10,8 @@ kore/cli.py:187-259, plus midtrain / soup / bench / launch).
     kore eval ...
     kore bench [--gpus N ...]
     kore launch <stage> <config.json> [--gpus N] [--dry-run]
+    kore campaign --out DIR --base-model M [--stages ...]
+    kore supervise -- <cmd ...>
 """
 from __future__ import annotations
 
@@ -120,6 +122,8 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("kind", choices=["sft", "dpo", "rft"])
     sub.add_parser("value-train", help="train the kernel value model")
     sub.add_parser("eval", help="evaluation suite")
+    sub.add_parser("campaign", help="staged campaign with a resumable manifest")
+    sub.add_parser("supervise", help="relaunch-with-resume supervisor / monitor")
     return ap
 
 
@@ -132,7 +136,9 @@ def main(argv: Optional[List[str]] = None) -> int:
     return {"launch": lambda: cmd_launch(args), "tasks": lambda: cmd_tasks(args),
             "soup": lambda: cmd_soup(args), "bench": lambda: cmd_bench(args, rest),
             "datagen": lambda: cmd_datagen(args, rest), "build-datasets": lambda: cmd_build(args, rest),
-            "value-train": lambda: cmd_value(args, rest), "eval": lambda: cmd_eval(args, rest)}[args.cmd]()
+            "value-train": lambda: cmd_value(args, rest), "eval": lambda: cmd_eval(args, rest),
+            "campaign": lambda: __import__("kore_b200.campaign.orchestrator", fromlist=["main"]).main(rest),
+            "supervise": lambda: __import__("kore_b200.campaign.supervise", fromlist=["main"]).main(rest)}[args.cmd]()
 
 
 if __name__ == "__main__":

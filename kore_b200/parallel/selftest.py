@@ -89,14 +89,24 @@ def main(argv=None):
     one = RolloutEngine(w, max_batch=8, page_size=64, num_pages=64, max_seq_len=512)
     ref_out = one.generate([GenRequest(p, 16, rid=i) for i, p in enumerate(prompts)], temperature=0.0)
     agree = sum(a == b for t, o in zip(toks, ref_out) for a, b in zip(t, o.tokens)) / max(1, sum(len(t) for t in toks))
-    first = all(t[:4] == o.tokens[:4] for t, o in zip(toks, ref_out))
-    lp_err = max(abs(a - b) for l, o in zip(lps, ref_out) for a, b in zip(l[:4], o.logps[:4]))
+    # teacher-forced: the fp32 reference scores the TP engine's own tokens (robust to greedy near-ties)
+    from ..engine.qwen3_engine import Batch
+    from ..models.reference_forward import forward_logprobs, leaf_buffers
+    seqs = [torch.tensor(list(p) + t) for p, t in zip(prompts, toks)]
+    b = Batch.from_sequences(seqs, device="cuda")
+    with torch.no_grad():
+        rlp, _ = forward_logprobs(w, [x.detach() for x in leaf_buffers(w)], b)
+    lp_err, off = 0.0, 0
+    for p, t, l in zip(prompts, toks, lps):
+        ref_l = rlp[off + len(p) - 1: off + len(p) - 1 + len(t)].float().cpu().tolist()
+        lp_err = max([lp_err] + [abs(a - c) for a, c in zip(l, ref_l)])
+        off += len(p) + len(t)
     err3 = check_device_error()
-    tok_ok = first and agree > 0.8 and err3 == 0
-    res_all = ctx.all_gather_object({"agree": agree, "first": first, "lp_err": lp_err})
+    tok_ok = lp_err < 5e-2 and err3 == 0
+    res_all = ctx.all_gather_object({"agree_greedy_1gpu": agree, "lp_err_teacher_forced": lp_err})
     if ctx.is_main:
-        print(json.dumps({"check": "tp_rollout_vs_single_gpu", "world": ctx.world,
-                          "ok": all(r["first"] and r["agree"] > 0.8 for r in res_all), "ranks": res_all,
+        print(json.dumps({"check": "tp_rollout_vs_fp32_reference", "world": ctx.world,
+                          "ok": all(r["lp_err_teacher_forced"] < 5e-2 for r in res_all), "ranks": res_all,
                           "device_error": err3}), flush=True)
     torch.distributed.barrier()
     return 0 if (ok and same and err == 0 and mok and err2 == 0 and tok_ok) else 1
