@@ -126,6 +126,8 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="data plane of the sharded optimizer (N > 1)")
+    ap.add_argument("--zero", type=int, default=2, choices=[2, 3],
+                    help="2: resident params, sharded grads/optimizer; 3: decoder layers fully sharded")
     args = ap.parse_args(argv)
     if args.impl == "reference":
         return reference_arm(args)
@@ -145,7 +147,8 @@ def main(argv=None):
         cfg.num_hidden_layers = args.layers
     ops.native()  # fail loudly if the extension is missing
     trainer = CausalLMTrainer(cfg, ctx, lr=1e-5, max_grad_norm=1.0, seed=0,
-                              micro_batch_size=args.micro_batch, comm=args.comm)
+                              micro_batch_size=args.micro_batch,
+                              comm=args.comm if args.zero == 2 else "nccl", zero_stage=args.zero)
     B, S = args.seqs_per_gpu, args.seq
     g = torch.Generator().manual_seed(1234 + ctx.rank)
     ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
@@ -213,7 +216,8 @@ def main(argv=None):
             "config": {"model": "qwen3-14b-arch (dense)" if args.model == "qwen3-14b" else args.model,
                        "layers": cfg.num_hidden_layers,
                        "global_batch": B * ctx.world, "seq_len": S,
-                       "parallelism": f"dp{ctx.world}" + (f"-zero2-{args.comm}" if ctx.world > 1 else ""),
+                       "parallelism": f"dp{ctx.world}" + (
+                           (f"-zero2-{args.comm}" if args.zero == 2 else "-zero3-nccl") if ctx.world > 1 else ""),
                        "loss": "last 50% of each sequence", "micro_batch": args.micro_batch,
                        "optimizer": f"AdamW fp32 moments, master={trainer.master_mode}",
                        "l2": "inputs larger than L2 (29.5 GB of weights streamed per step)"},

@@ -113,6 +113,7 @@ class Qwen3Engine:
         # bf16 + lse per layer) so the backward recomputes only the GEMMs
         self.save_attention = save_attention
         self.ep = None          # expert-parallel dispatcher (kore_b200.parallel.ep) when attached
+        self.param_hook = None  # full-sharding provider (kore_b200.parallel.fsdp.FullShard) when attached
         self.temperature = temperature
         c = self.cfg
         self.hq, self.hkv, self.D = c.num_attention_heads, c.num_key_value_heads, c.head_dim
@@ -137,6 +138,8 @@ class Qwen3Engine:
     def zero_grad(self) -> None:
         """Mark gradients stale: the next backward overwrites instead of adding."""
         self._fresh = [True] * self.w.num_units
+        if self.param_hook is not None:
+            self.param_hook.zero_grad()
         for g in self.grads:
             if g is not None:
                 g.zero_()
@@ -356,9 +359,13 @@ class Qwen3Engine:
         layer's attention output and logsumexp so the backward does not
         recompute attention."""
         x = ops.embed_fwd(b.ids, self.w.views(0)["embed"])
+        hook = self.param_hook
+        last = self.w.num_units - 2
         for u in range(1, self.w.num_units - 1):
             if checkpoints is not None:
                 checkpoints.append(x)
+            if hook is not None:
+                hook.acquire(u, u + 1 if u < last else None)
             x, _ = self._layer_fwd(u, x, b, keep=False, save_attn=attn_saves)
         return x
 
@@ -423,8 +430,13 @@ class Qwen3Engine:
         for u in range(self.w.num_units - 2, 0, -1):
             xin = ckpts[u - 1]
             saved = asaves[u - 1] if asaves is not None else None
+            if self.param_hook is not None:
+                self.param_hook.acquire(u, u - 1 if u > 1 else None)
+                self.param_hook.begin_bwd(u)
             _, ctx = self._layer_fwd(u, xin, b, keep=True, attn_saved=saved)
             dx = self._layer_bwd(u, xin, dx, ctx, b)
+            if self.param_hook is not None:
+                self.param_hook.end_bwd(u)
             del ctx, saved
             ckpts[u - 1] = None
             if asaves is not None:

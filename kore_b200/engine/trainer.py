@@ -42,7 +42,7 @@ class CausalLMTrainer:
                  micro_batch_size: int = 1, logits_chunk: int = 4096, schedule: str = "constant",
                  warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
                  weights: Optional[Qwen3Weights] = None, micro_tokens_hint: int = 8192,
-                 ep_capacity: float = 2.0):
+                 ep_capacity: float = 2.0, zero_stage: int = 2):
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device
@@ -50,6 +50,9 @@ class CausalLMTrainer:
         grad_alloc = None
         ep = (self.ctx.rank, self.ctx.world) if (cfg.is_moe and self.ctx.world > 1) else None
         fused = comm == "fused" and self.ctx.world > 1 and dev.type == "cuda"
+        self.zero_stage = zero_stage if self.ctx.world > 1 else 0
+        if self.zero_stage == 3 and fused:
+            raise ValueError("zero_stage=3 runs on NCCL collectives (comm='nccl')")
         if fused:
             from ..parallel.symmetric import SymmetricHeap
             per = 128 * self.ctx.world
@@ -91,6 +94,14 @@ class CausalLMTrainer:
                                          weight_decay=weight_decay, max_grad_norm=max_grad_norm,
                                          master=master, schedule=schedule, warmup_steps=warmup_steps,
                                          total_steps=total_steps, seed=seed)
+        elif self.zero_stage == 3:
+            from ..parallel.fsdp import FullShard, FullShardAdamW
+            self.fs = FullShard(self.w, self.eng, self.ctx)
+            self.eng.param_hook = self.fs
+            self.opt = FullShardAdamW(self.w, self.eng, self.ctx, self.fs, lr=lr, betas=betas,
+                                      weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                                      master=master, schedule=schedule, warmup_steps=warmup_steps,
+                                      total_steps=total_steps, seed=seed)
         elif self.ctx.world > 1:
             from ..parallel.zero import ShardedAdamW
             self.opt = ShardedAdamW(self.w, self.eng, self.ctx, lr=lr, betas=betas,
@@ -166,6 +177,18 @@ class CausalLMTrainer:
         self.opt.step()
         self.ctx.all_reduce(loss)
         return float(loss.item())
+
+    @torch.no_grad()
+    def full_weights(self) -> Qwen3Weights:
+        """The model with every unit materialised (gathers ZeRO-3 shards; for saving)."""
+        if getattr(self, "fs", None) is None:
+            return self.w
+        full = Qwen3Weights(self.cfg, device=self.w.device, dtype=self.w.dtype, allocate=False,
+                            pad_multiple=self.w.pad_multiple, ep=self.w.ep)
+        full.bufs = [self.fs.full_unit(u).clone() if u in self.fs.pshard else self.w.bufs[u]
+                     for u in range(self.w.num_units)]
+        full.expert_bufs = self.w.expert_bufs
+        return full
 
     def train_step(self, ids_host: torch.Tensor, loss_mask_host: Optional[torch.Tensor] = None
                    ) -> float:

@@ -52,6 +52,20 @@ def main(argv=None):
         print(json.dumps({"check": "zero2_fused_vs_nccl", "world": ctx.world, "ok": ok and same and err == 0,
                           "loss_nccl": res["nccl"][0], "loss_fused": res["fused"][0],
                           "replicas_identical": same, "device_error": err}), flush=True)
+    # full sharding (ZeRO-3 layers: per-use gathers, per-micro-batch reduce-scatter on a comm stream)
+    tr = CausalLMTrainer(cfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm="nccl", master="fp32",
+                         zero_stage=3, micro_batch_size=1)
+    l3 = [float(tr.train_step_device(mine)) for _ in range(3)]
+    full = tr.full_weights()
+    torch.cuda.synchronize()
+    z3ok = all(abs(a - b) < 2e-2 * max(1.0, abs(a)) for a, b in zip(res["nccl"][0], l3))
+    for a, b in zip(res["nccl"][1], full.bufs):
+        z3ok = z3ok and torch.allclose(a, b.float(), atol=2e-2, rtol=0)
+    del tr, full
+    if ctx.is_main:
+        print(json.dumps({"check": "zero3_vs_zero2", "world": ctx.world, "ok": z3ok, "loss_zero2": res["nccl"][0],
+                          "loss_zero3": l3}), flush=True)
+    ok = ok and z3ok
     # expert parallelism: NCCL all-to-all vs fused peer-memory dispatch/combine
     mcfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
                        num_attention_heads=4, num_key_value_heads=2, head_dim=128, model_type="qwen3_moe",
