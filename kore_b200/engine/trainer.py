@@ -190,6 +190,28 @@ class CausalLMTrainer:
         full.expert_bufs = self.w.expert_bufs
         return full
 
+    @torch.no_grad()
+    def load_checkpoint(self, path: str) -> None:
+        """Load HF weights (re-sharding ZeRO-3 layer units)."""
+        from ..models.hf_io import load_weights
+        if getattr(self, "fs", None) is None:
+            load_weights(self.w, path)
+            return
+        full = Qwen3Weights(self.cfg, device=self.w.device, dtype=self.w.dtype, init=False,
+                            pad_multiple=self.w.pad_multiple, ep=self.w.ep)
+        load_weights(full, path)
+        r, s = self.ctx.rank, self.fs.s
+        for u in range(self.w.num_units):
+            if u in self.fs.pshard:
+                self.fs.pshard[u].copy_(full.bufs[u][r * s:(r + 1) * s])
+                if u in self.opt.master:
+                    self.opt.master[u].copy_(self.fs.pshard[u].float())
+            else:
+                self.w.bufs[u].copy_(full.bufs[u])
+        for u, b in full.expert_bufs.items():
+            self.w.expert_bufs[u].copy_(b)
+        self.fs.owner = [-1, -1]
+
     def train_step(self, ids_host: torch.Tensor, loss_mask_host: Optional[torch.Tensor] = None
                    ) -> float:
         """Host inputs in, host loss out (the end-to-end call)."""

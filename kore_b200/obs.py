@@ -168,3 +168,49 @@ def gpu_mem_snapshot() -> dict:
                 for i in range(torch.cuda.device_count())}
     except Exception:  # noqa: BLE001 - best effort only
         return {}
+
+
+class PhaseTimer:
+    """Per-phase device time of a training step (rollout / logp / fwd-bwd /
+    optimizer / sync): each phase is an NVTX range (visible in any CUDA
+    profiler timeline) bracketed by CUDA events on the current stream.
+    ``summary(ctx)`` synchronises once and returns milliseconds per phase,
+    max over ranks. On CPU it falls back to wall time."""
+
+    def __init__(self, enabled: bool = True):
+        import torch
+        self.cuda = enabled and torch.cuda.is_available()
+        self.spans = []
+
+    @contextmanager
+    def phase(self, name: str):
+        import torch
+        if self.cuda:
+            torch.cuda.nvtx.range_push(name)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            try:
+                yield
+            finally:
+                e.record()
+                torch.cuda.nvtx.range_pop()
+                self.spans.append((name, s, e))
+        else:
+            t0 = time.time()
+            try:
+                yield
+            finally:
+                self.spans.append((name, t0, time.time()))
+
+    def summary(self, ctx=None) -> dict:
+        import torch
+        out: dict = {}
+        if self.cuda:
+            torch.cuda.synchronize()
+        for name, s, e in self.spans:
+            ms = s.elapsed_time(e) if self.cuda else (e - s) * 1e3
+            out[name] = out.get(name, 0.0) + ms
+        if ctx is not None and getattr(ctx, "enabled", False):
+            out = {k: ctx.max_over_ranks(v) for k, v in sorted(out.items())}
+        self.spans = []
+        return out

@@ -121,6 +121,25 @@ class ShardedAdamW:
     def grad_norm(self) -> float:
         return float(self.last_sumsq.sqrt()) if self.last_sumsq is not None else float("nan")
 
+    def state_dict(self) -> dict:
+        """This rank's optimizer shard (moments, master, step, expert-local state)."""
+        sd = {"step": self.step_count, "rank": self.ctx.rank, "world": self.ctx.world,
+              "m": {u: t.cpu() for u, t in self.m.items()}, "v": {u: t.cpu() for u, t in self.v.items()},
+              "master": {u: t.cpu() for u, t in self.master.items()}}
+        if self.local is not None and hasattr(self.local, "state_dict"):
+            sd["local"] = self.local.state_dict()
+        return sd
+
+    def load_state_dict(self, sd: dict) -> None:
+        if sd.get("world", self.ctx.world) != self.ctx.world:
+            raise ValueError(f"optimizer shard saved at world {sd['world']}, loading at {self.ctx.world}")
+        self.step_count = int(sd["step"])
+        for k in ("m", "v", "master"):
+            for u, t in sd.get(k, {}).items():
+                getattr(self, k)[int(u)].copy_(t)
+        if "local" in sd and self.local is not None:
+            self.local.load_state_dict(sd["local"])
+
 
 class FusedShardedAdamW(ShardedAdamW):
     """ZeRO-2 step on the symmetric peer-memory heap with fused kernels:

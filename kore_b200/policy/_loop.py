@@ -41,7 +41,10 @@ def run_loop(name: str, examples: Sequence, step_fn: Callable[[List], float], *,
     if ck is not None:
         import json
         from ..models.hf_io import load_weights
-        load_weights(trainer.w, ck)
+        if hasattr(trainer, "load_checkpoint"):
+            trainer.load_checkpoint(ck)
+        else:
+            load_weights(trainer.w, ck)
         start = json.load(open(os.path.join(ck, "trainer_state.json"))).get("global_step", 0)
         opt_f = os.path.join(ck, f"optimizer-rank{ctx.rank}.pt")
         if os.path.exists(opt_f):
@@ -50,7 +53,15 @@ def run_loop(name: str, examples: Sequence, step_fn: Callable[[List], float], *,
     order = list(range(n))
     per_rank_step = per_device * accum
     history = []
+    hb = None
+    if ctx.world > 1:
+        from ..parallel.health import Heartbeat
+        store = _default_store()
+        if store is not None:
+            hb = Heartbeat(store, ctx.rank, ctx.world, timeout_s=float(os.environ.get("KORE_HEARTBEAT_S", "600")))
     for step in range(start, total):
+        if hb is not None and step > start:
+            hb.wait_peers(step - 1)              # a lost peer stops us between steps, not inside a collective
         epoch = (step * per_rank_step * ctx.world) // max(1, n)
         rng = random.Random(seed + epoch)
         perm = order[:]
@@ -59,17 +70,32 @@ def run_loop(name: str, examples: Sequence, step_fn: Callable[[List], float], *,
         idx = [perm[(base + ctx.rank + ctx.world * j) % n] for j in range(per_rank_step)]
         loss = step_fn([examples[i] for i in idx])
         history.append(loss)
+        if hb is not None:
+            hb.beat(step)
         if ctx.is_main and ((step + 1) % max(1, logging_steps) == 0 or step == total - 1):
             log.event(f"{name}_step", step=step + 1, loss=round(loss, 5), lr=trainer.opt.current_lr(),
                       epoch=epoch)
         if save_steps and (step + 1) % save_steps == 0 and step + 1 < total:
             d = os.path.join(output_dir, f"checkpoint-{step + 1}")
+            full = trainer.full_weights() if hasattr(trainer, "full_weights") else trainer.w   # collective
             if ctx.is_main:
-                save_pretrained(trainer.w, d, tokenizer, keep_last=save_total_limit,
+                save_pretrained(full, d, tokenizer, keep_last=save_total_limit,
                                 trainer_state={"global_step": step + 1})
             ctx.barrier()
             torch.save(trainer.opt.state_dict(), os.path.join(d, f"optimizer-rank{ctx.rank}.pt"))
+    full = trainer.full_weights() if hasattr(trainer, "full_weights") else trainer.w
     if ctx.is_main:
-        save_pretrained(trainer.w, output_dir, tokenizer)
+        save_pretrained(full, output_dir, tokenizer)
+    if hb is not None:
+        hb.leave()
     ctx.barrier()
     return {"output_dir": output_dir, "steps": total, "history": history}
+
+
+def _default_store():
+    try:
+        import torch.distributed as dist
+        from torch.distributed import distributed_c10d as c10d
+        return c10d._get_default_store() if dist.is_initialized() else None
+    except Exception:  # noqa: BLE001 - no store: run without heartbeats
+        return None

@@ -302,6 +302,15 @@ def sharding_plan(config, world: int) -> dict:
     return {"zero": zero, "offload": bool(getattr(config, "fsdp_cpu_offload", False))}
 
 
+def parallel_kwargs(config, world: int) -> dict:
+    """CausalLMTrainer arguments of this config: ZeRO-3 (full_shard) runs on
+    NCCL collectives, ZeRO-2 on the configured data plane."""
+    z = sharding_plan(config, world)["zero"]
+    if z == 3:
+        return {"zero_stage": 3, "comm": "nccl"}
+    return {"zero_stage": 2, "comm": getattr(config, "comm", "nccl")}
+
+
 def build_fsdp_kwargs(config) -> dict:
     """The reference's HF-Trainer FSDP kwargs for this config ({} when not
     distributed). Kept so tools that inspect them keep working; the engine

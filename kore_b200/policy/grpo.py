@@ -312,7 +312,11 @@ class GRPOTrainer:
             return self.samples_from_group(trajs), [M.kevin_trajectory_score(
                 [r.reward for r in t.results], [r.correct for r in t.results]) for t in trajs]
 
+        from ..obs import PhaseTimer
+        pt = PhaseTimer()
         target = cfg.target_groups or len(tasks)
+        ph = pt.phase("rollout")
+        ph.__enter__()
         if cfg.dynamic_sampling and W == 1:
             kept, attempts = M.dynamic_sampling_refill(
                 roll, target, min_std=cfg.starpo_min_std,
@@ -323,11 +327,14 @@ class GRPOTrainer:
         for g, scores in kept:
             groups.append(g)
             rewards_all.extend(scores)
+        ph.__exit__(None, None, None)
         groups = self.assign_advantages(groups)
         samples = [s for g in groups for s in g]
-        self.fill_ref_logps(samples, micro_batch_tokens)
+        with pt.phase("ref_logp"):
+            self.fill_ref_logps(samples, micro_batch_tokens)
         t_roll = time.time() - t0
-        stats = self.update(samples, micro_batch_tokens)
+        with pt.phase("update"):
+            stats = self.update(samples, micro_batch_tokens)
         self.step_idx += 1
         stats.update({"step": self.step_idx, "reward_mean": sum(rewards_all) / max(1, len(rewards_all)),
                       "reward_std": M.group_reward_std(rewards_all), "groups": len(groups),
@@ -335,6 +342,7 @@ class GRPOTrainer:
                       "adv_absmean": sum(abs(s.adv) for s in samples) / max(1, len(samples)),
                       "rollout_s": t_roll, "step_s": time.time() - t0,
                       "grad_norm": self.trainer.opt.grad_norm()})
+        stats.update({f"ms_{k}": v for k, v in pt.summary(self.ctx).items()})
         if self.ctx.is_main and (self.step_idx % max(1, cfg.logging_steps) == 0):
             log.event("grpo_step", **{k: (round(v, 5) if isinstance(v, float) else v) for k, v in stats.items()})
         return stats
@@ -357,14 +365,14 @@ def train_grpo(config: GRPOConfig, tasks: Optional[List[str]] = None, backend: s
     tr = GRPOTrainer(config, weights=weights, env=env, ctx=ctx, tokenizer=tok)
     tasks = list(tasks or ["synthetic-0"])
     history = []
-    for step in range(config.total_steps):
+    start = resume_grpo(tr, config.output_dir, ctx)
+    for step in range(start, config.total_steps):
         k = config.tasks_per_step
         batch = [tasks[(step * k + i) % len(tasks)] for i in range(k)]
         st = tr.train_step(batch)
         history.append(st)
-        if config.save_steps and (step + 1) % config.save_steps == 0 and ctx.is_main:
-            save_pretrained(weights, os.path.join(config.output_dir, f"checkpoint-{step + 1}"), tok,
-                            keep_last=1, trainer_state={"global_step": step + 1})
+        if config.save_steps and (step + 1) % config.save_steps == 0:
+            save_grpo_checkpoint(tr, weights, tok, config.output_dir, step + 1, ctx)
         if tr.controller is not None and tr.controller.update(step, st["reward_mean"]):
             log.info("adaptive stop", reason=tr.controller.stopped_reason)
             break
@@ -372,6 +380,50 @@ def train_grpo(config: GRPOConfig, tasks: Optional[List[str]] = None, backend: s
         save_pretrained(weights, config.output_dir, tok)
     ctx.barrier()
     return {"output_dir": config.output_dir, "history": history}
+
+
+def save_grpo_checkpoint(tr, weights, tok, output_dir: str, step: int, ctx) -> str:
+    """``checkpoint-<step>``: HF weights + trainer_state (rank 0), and per rank
+    the optimizer shard plus RNG states, so a GRPO run resumes mid-stage
+    (the reference keeps weights only: kore/policy/grpo.py:906-928)."""
+    import random as _random
+    from ..models.hf_io import save_pretrained
+    d = os.path.join(output_dir, f"checkpoint-{step}")
+    if ctx.is_main:
+        save_pretrained(weights, d, tok, keep_last=1, trainer_state={"global_step": step,
+                                                                     "grpo_step_idx": tr.step_idx})
+    ctx.barrier()
+    state = {"opt": tr.trainer.opt.state_dict(), "py_rng": _random.getstate(),
+             "torch_rng": torch.get_rng_state(), "step_idx": tr.step_idx,
+             "cuda_rng": torch.cuda.get_rng_state() if torch.cuda.is_available() else None}
+    torch.save(state, os.path.join(d, f"grpo_state-rank{ctx.rank}.pt"))
+    ctx.barrier()
+    return d
+
+
+def resume_grpo(tr, output_dir: str, ctx) -> int:
+    """Restore the latest checkpoint (weights, optimizer shard, RNG); returns the next step."""
+    import random as _random
+    from ..models.hf_io import load_weights
+    from .configs import latest_checkpoint
+    ck = latest_checkpoint(output_dir)
+    if ck is None:
+        return 0
+    load_weights(tr.trainer.w, ck)
+    step = json.load(open(os.path.join(ck, "trainer_state.json"))).get("global_step", 0)
+    f = os.path.join(ck, f"grpo_state-rank{ctx.rank}.pt")
+    if os.path.exists(f):
+        st = torch.load(f, map_location="cpu", weights_only=False)
+        tr.trainer.opt.load_state_dict(st["opt"])
+        _random.setstate(st["py_rng"])
+        torch.set_rng_state(st["torch_rng"])
+        if st.get("cuda_rng") is not None and torch.cuda.is_available():
+            torch.cuda.set_rng_state(st["cuda_rng"])
+        tr.step_idx = st["step_idx"]
+    if hasattr(tr, "sync_rollout_weights"):
+        tr.sync_rollout_weights()
+    log.info("grpo resumed", checkpoint=ck, step=step)
+    return step
 
 
 def _kernel_env(config: GRPOConfig):

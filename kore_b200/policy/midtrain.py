@@ -18,6 +18,7 @@ from ..models.hf_io import load_pretrained_or_init
 from ..obs import configure, get_logger
 from ..parallel.dist import init_distributed
 from ._loop import plan_steps, run_loop
+from .configs import parallel_kwargs as _parallel_kwargs
 from .configs import MidTrainConfig, midtrain_config_from_dict
 
 log = get_logger("policy.midtrain")
@@ -55,7 +56,7 @@ def train_midtrain(config: MidTrainConfig, corpus_path=None, *, model_cfg=None, 
     tr = CausalLMTrainer(w.cfg, ctx, lr=config.learning_rate, weight_decay=config.weight_decay,
                          max_grad_norm=config.max_grad_norm, seed=config.seed,
                          schedule=config.lr_scheduler_type, warmup_steps=int(config.warmup_ratio * total),
-                         total_steps=total, weights=w, comm=config.comm)
+                         total_steps=total, weights=w, **_parallel_kwargs(config, ctx.world))
 
     def step_fn(wins):
         seqs = [d for win in wins for d in win]

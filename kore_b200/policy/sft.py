@@ -24,6 +24,7 @@ from ..models.hf_io import load_pretrained_or_init
 from ..obs import configure, get_logger
 from ..parallel.dist import init_distributed
 from ._loop import plan_steps, run_loop
+from .configs import parallel_kwargs as _parallel_kwargs
 from .configs import SFTConfig, sft_config_from_dict
 
 log = get_logger("policy.sft")
@@ -60,7 +61,7 @@ def train_sft(config: SFTConfig, dataset_path: Optional[str] = None, *, model_cf
     tr = CausalLMTrainer(w.cfg, ctx, lr=config.learning_rate, weight_decay=config.weight_decay,
                          max_grad_norm=config.max_grad_norm, seed=config.seed,
                          schedule=config.lr_scheduler_type, warmup_steps=int(config.warmup_ratio * total),
-                         total_steps=total, weights=w, comm=config.comm)
+                         total_steps=total, weights=w, **_parallel_kwargs(config, ctx.world))
     tr.eng.save_attention = config.save_attention
     budget = config.micro_batch_tokens or max(config.max_seq_length, 8192)
     step_fn = lambda exs: tr.train_step_sequences([e[0] for e in exs], [e[1] for e in exs],

@@ -159,3 +159,61 @@ def test_zero3_sft_matches_single_rank():
         assert torch.allclose(torch.tensor(a), torch.tensor(b), atol=1e-5)
     for a, b in zip(two[0]["w"], two[1]["w"]):
         assert a == b
+
+
+def _hb_worker(rank, world, path, die_rank, q):
+    import torch.distributed as dist
+    from kore_b200.parallel.health import Heartbeat, PeerFailure
+    store = dist.FileStore(path, world)
+    hb = Heartbeat(store, rank, world, timeout_s=2.0)
+    done = 0
+    try:
+        for step in range(4):
+            if step > 0:
+                hb.wait_peers(step - 1)
+            if rank == die_rank and step == 2:
+                import os
+                os._exit(0)                     # the rank vanishes between steps
+            done = step
+            hb.beat(step)
+        q.put((rank, "ok", done))
+    except PeerFailure as e:
+        q.put((rank, "peer_failure", e.ranks))
+
+
+def test_heartbeat_detects_dead_rank(tmp_path):
+    """A rank that exits between steps is reported to every survivor on the
+    host, within the heartbeat timeout, before their next step."""
+    import multiprocessing as mp
+    ctxm = mp.get_context("spawn")
+    q = ctxm.Queue()
+    world = 3
+    path = str(tmp_path / "store")
+    ps = [ctxm.Process(target=_hb_worker, args=(r, world, path, 1, q)) for r in range(world)]
+    t0 = __import__("time").time()
+    for p in ps:
+        p.start()
+    res = {}
+    for _ in range(world - 1):
+        r, kind, v = q.get(timeout=60)
+        res[r] = (kind, v)
+    for p in ps:
+        p.join(timeout=30)
+    assert res[0] == ("peer_failure", [1]) and res[2] == ("peer_failure", [1])
+    assert __import__("time").time() - t0 < 45
+
+
+def test_heartbeat_leave_and_classify():
+    import torch.distributed as dist
+    from kore_b200.parallel.health import Heartbeat, PeerFailure, classify_exception
+    store = dist.HashStore()
+    a, b = Heartbeat(store, 0, 2, timeout_s=0.2), Heartbeat(store, 1, 2, timeout_s=0.2)
+    a.beat(0)
+    b.beat(0)
+    a.wait_peers(0)
+    b.leave()
+    with pytest.raises(PeerFailure):
+        a.wait_peers(1)
+    assert classify_exception(RuntimeError("CUDA out of memory")) == "infra"
+    assert classify_exception(RuntimeError("NCCL error: unhandled system error")) == "infra"
+    assert classify_exception(ValueError("bad shape")) == "program"

@@ -98,3 +98,21 @@ def test_hf_checkpoint_roundtrip(tmp_path):
     keys = set(w.hf_state_dict())
     assert "model.layers.0.self_attn.q_proj.weight" in keys and "lm_head.weight" in keys
     assert "model.layers.1.mlp.down_proj.weight" in keys
+
+
+def test_grpo_resume_restores_optimizer_and_rng(tmp_path):
+    """A GRPO run checkpoints weights, optimizer shard and RNG; a restarted run
+    resumes at the saved step with the same optimizer step count."""
+    from kore_b200.policy.grpo import train_grpo
+    cfg, _ = _tiny()
+    out = str(tmp_path / "run")
+    kw = dict(num_trajectories=2, num_turns=1, tasks_per_step=1, max_response_length=4, max_prompt_length=64,
+              learning_rate=1e-3, dynamic_sampling=False, starpo_s=False, bf16=False, overlong_mask=False,
+              save_steps=1, output_dir=out, model_id="tiny-test")
+    env = SyntheticRewardEnv(seed=0, prompt_len=8, feedback_len=2, vocab_size=cfg.vocab_size)
+    r1 = train_grpo(GRPOConfig(total_steps=2, **kw), env=env, model_cfg=cfg)
+    assert len(r1["history"]) == 2
+    st = torch.load(f"{out}/checkpoint-2/grpo_state-rank0.pt", weights_only=False)
+    assert st["opt"]["step"] == 2
+    r2 = train_grpo(GRPOConfig(total_steps=3, **kw), env=env, model_cfg=cfg)
+    assert len(r2["history"]) == 1                       # resumed at step 2, ran step 3 only
