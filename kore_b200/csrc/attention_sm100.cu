@@ -354,17 +354,25 @@ struct BwdParams {
   int T;
 };
 
+// Backward tiling: one CTA per (128-row key block, kv head); per iteration a
+// 64-row query block of one query head of the GQA group.
+constexpr int BQB = 64;                           // query rows per backward iteration
+constexpr int QTILE_BYTES = BQB * D * 2;          // 16 KB: 64 rows as two 8 KB swizzle atoms
+constexpr int PTILE_BYTES = BKV * BQB * 2;        // 16 KB: 128 kv rows x 64 q cols, one atom
+constexpr int kBwdThreads = 320;                  // producer, MMA, 4 softmax, 4 dQ warps
+
 struct BwdSmem {
-  static constexpr int K_OFF = 0;
-  static constexpr int V_OFF = TILE_BYTES;
-  static constexpr int Q_OFF = 2 * TILE_BYTES;
-  static constexpr int DO_OFF = 3 * TILE_BYTES;
-  static constexpr int PT_OFF = 4 * TILE_BYTES;
-  static constexpr int DS_OFF = 5 * TILE_BYTES;
-  static constexpr int VEC_OFF = 6 * TILE_BYTES;           // lse2[128], delta[128]
+  static constexpr int K_OFF = 0;                             // 32 KB
+  static constexpr int V_OFF = TILE_BYTES;                    // 32 KB
+  static constexpr int Q_OFF = 2 * TILE_BYTES;                // 2 stages x 16 KB
+  static constexpr int DO_OFF = Q_OFF + 2 * QTILE_BYTES;      // 2 stages x 16 KB
+  static constexpr int PT_OFF = DO_OFF + 2 * QTILE_BYTES;     // 2 buffers x 16 KB
+  static constexpr int DS_OFF = PT_OFF + 2 * PTILE_BYTES;     // 2 buffers x 16 KB
+  static constexpr int VEC_OFF = DS_OFF + 2 * PTILE_BYTES;    // [2][lse2 64 | delta 64]
   static constexpr int BAR_OFF = VEC_OFF + 1024;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
+static_assert(BwdSmem::TOTAL <= 227 * 1024, "backward shared memory");
 
 KORE_DEV void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n)); }
 
@@ -383,7 +391,32 @@ KORE_DEV void store_row32_sw128(uint8_t* tile, int row, int c, const float* v) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// 64-row, 128-column tile (two 8 KB atoms): K-major operand at K-step kk.
+KORE_DEV uint64_t kmajor64_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+}
+// Same 64-row tile as an MN-major operand (rows = K, N = 128 in two 64-wide
+// blocks 8 KB apart) at K-step kk.
+KORE_DEV uint64_t mnmajor64_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 2048, 8192, 1024); }
+// 128-row x 64-column tile (one atom): K-major at K-step kk / MN-major (N = 64) at K-step kk.
+KORE_DEV uint64_t kmajor_narrow_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 32, 16, 1024); }
+KORE_DEV uint64_t mnmajor_narrow_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 2048, 16384, 1024); }
+
+// Work item of a CTA: heaviest key blocks (kb = 0) of every kv head first.
+struct BwdItem {
+  int seq, kb, kvh;
+};
+KORE_DEV BwdItem bwd_item(const BwdParams& p) {
+  const int x = blockIdx.x;
+  BwdItem it;
+  it.kvh = x % p.Hkv;
+  const int rest = x / p.Hkv;
+  it.kb = rest / p.nseq;
+  it.seq = rest % p.nseq;
+  return it;
+}
+
+__global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                     BwdParams p) {
@@ -393,37 +426,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* st_full = bars + 3;
-  uint64_t* p_full = bars + 4;
-  uint64_t* dq_full = bars + 5;
-  uint64_t* dq_empty = bars + 6;
-  uint64_t* all_done = bars + 7;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  uint64_t* qdo_full = bars + 1;   // [2]
+  uint64_t* qdo_empty = bars + 3;  // [2]
+  uint64_t* s_full = bars + 5;     // S^T, dP^T of this iteration in TMEM
+  uint64_t* s_free = bars + 6;     // softmax warps have read them
+  uint64_t* p_full = bars + 7;     // [2] P^T, dS^T in shared memory
+  uint64_t* p_empty = bars + 9;    // [2] the gradient MMAs that read them completed
+  uint64_t* dq_full = bars + 11;
+  uint64_t* dq_empty = bars + 12;
+  uint64_t* all_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  float* s_lse = reinterpret_cast<float*>(smem + S::VEC_OFF);
-  float* s_delta = s_lse + 128;
+  float* s_vec = reinterpret_cast<float*>(smem + S::VEC_OFF);  // [2][128]: lse2[64], delta[64]
 
-  const int seq = blockIdx.x / p.nkblk;
-  const int kb = blockIdx.x % p.nkblk;
-  const int kvh = blockIdx.y;
+  const BwdItem item = bwd_item(p);
+  const int seq = item.seq, kb = item.kb, kvh = item.kvh;
   const int G = p.Hq / p.Hkv;
   const int s0 = p.cu_seqlens[seq];
   const int len = p.cu_seqlens[seq + 1] - s0;
   const int k0 = kb * BKV;
   if (k0 >= len) return;
-  const int nqb = (len + BQ - 1) / BQ;
-  const int per_head = nqb - kb;
+  const int nqb = (len + BQB - 1) / BQB;
+  const int qb0 = k0 / BQB;           // first causal query block (2 * kb)
+  const int per_head = nqb - qb0;
   const int iters = G * per_head;
   const int warp = threadIdx.x / 32;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(qdo_full, 1);
-    mbar_init(qdo_empty, 1);
-    mbar_init(st_full, 1);
-    mbar_init(p_full, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&qdo_full[i], 1);
+      mbar_init(&qdo_empty[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_empty[i], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(s_free, 4);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(all_done, 1);
@@ -435,7 +473,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: [0,128) S^T then dQ partial, [128,256) dP^T, [256,384) dV, [384,512) dK
+  // TMEM columns: [0,64) S^T, [64,128) dP^T, [128,192) dQ^T (lanes = head dim), [256,384) dV, [384,512) dK
+  constexpr uint32_t T_S = 0, T_DP = 64, T_DQ = 128, T_DV = 256, T_DK = 384;
 
   if (warp == 0) {
     if (elect_one()) {
@@ -445,126 +484,132 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d(smem + S::V_OFF, &tmV, kv_full, kvh * D, s0 + k0);
       tma_load_2d(smem + S::V_OFF + 16384, &tmV, kv_full, kvh * D + 64, s0 + k0);
       for (int i = 0; i < iters && !*abort_flag; ++i) {
+        const int st = i & 1;
         const int h = kvh * G + i / per_head;
-        const int qb = kb + i % per_head;
-        if (!mbar_wait(qdo_empty, (i & 1) ^ 1)) { *abort_flag = 1; break; }
-        mbar_arrive_expect_tx(qdo_full, 2 * TILE_BYTES);
-        tma_load_2d(smem + S::Q_OFF, &tmQ, qdo_full, h * D, s0 + qb * BQ);
-        tma_load_2d(smem + S::Q_OFF + 16384, &tmQ, qdo_full, h * D + 64, s0 + qb * BQ);
-        tma_load_2d(smem + S::DO_OFF, &tmDO, qdo_full, h * D, s0 + qb * BQ);
-        tma_load_2d(smem + S::DO_OFF + 16384, &tmDO, qdo_full, h * D + 64, s0 + qb * BQ);
+        const int q0 = (qb0 + i % per_head) * BQB;
+        if (!mbar_wait(&qdo_empty[st], ((i >> 1) & 1) ^ 1)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * QTILE_BYTES);
+        uint8_t* qs = smem + S::Q_OFF + st * QTILE_BYTES;
+        uint8_t* ds = smem + S::DO_OFF + st * QTILE_BYTES;
+        tma_load_2d(qs, &tmQ, &qdo_full[st], h * D, s0 + q0);
+        tma_load_2d(qs + 8192, &tmQ, &qdo_full[st], h * D + 64, s0 + q0);
+        tma_load_2d(ds, &tmDO, &qdo_full[st], h * D, s0 + q0);
+        tma_load_2d(ds + 8192, &tmDO, &qdo_full[st], h * D + 64, s0 + q0);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    constexpr uint32_t id_s = make_idesc_bf16(128, 128, false, false);   // K Q^T, V dO^T
+    constexpr uint32_t id_s = make_idesc_bf16(128, BQB, false, false);   // K Q^T, V dO^T
     constexpr uint32_t id_dv = make_idesc_bf16(128, 128, false, true);   // P^T dO, dS^T Q
-    constexpr uint32_t id_dq = make_idesc_bf16(128, 128, true, true);    // dS K
+    constexpr uint32_t id_dq = make_idesc_bf16(128, BQB, true, true);    // K^T dS^T = dQ^T
     if (elect_one()) {
       const uint32_t ka = smem_u32(smem + S::K_OFF), va = smem_u32(smem + S::V_OFF);
-      const uint32_t qa = smem_u32(smem + S::Q_OFF), da = smem_u32(smem + S::DO_OFF);
-      const uint32_t pa = smem_u32(smem + S::PT_OFF), sa = smem_u32(smem + S::DS_OFF);
       bool ok = mbar_wait(kv_full, 0);
-      for (int i = 0; i < iters && ok; ++i) {
-        const uint32_t ph = i & 1;
-        if (!mbar_wait(qdo_full, ph)) { ok = false; break; }
-        if (i > 0 && !mbar_wait(dq_empty, ph ^ 1)) { ok = false; break; }
+      // gradient MMAs of iteration j (reads P^T/dS^T buffer j%2 and Q/dO stage j%2)
+      auto grads = [&](int j) -> bool {
+        const int st = j & 1;
+        if (!mbar_wait(&p_full[st], (j >> 1) & 1)) return false;
+        if (j > 0 && !mbar_wait(dq_empty, (j - 1) & 1)) return false;
         tc_fence_after();
+        const uint32_t qa = smem_u32(smem + S::Q_OFF + st * QTILE_BYTES);
+        const uint32_t da = smem_u32(smem + S::DO_OFF + st * QTILE_BYTES);
+        const uint32_t pa = smem_u32(smem + S::PT_OFF + st * PTILE_BYTES);
+        const uint32_t sa = smem_u32(smem + S::DS_OFF + st * PTILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          umma_f16_ss(tmem + 0, kmajor_desc(ka, kk), kmajor_desc(qa, kk), id_s, kk > 0);
-          umma_f16_ss(tmem + 128, kmajor_desc(va, kk), kmajor_desc(da, kk), id_s, kk > 0);
-        }
-        umma_commit(st_full);
-        if (!mbar_wait(p_full, ph)) { ok = false; break; }
-        tc_fence_after();
-#pragma unroll
-        for (int kk = 0; kk < BQ / 16; ++kk) {
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          umma_f16_ss(tmem + 256, kmajor_desc(pa, kk), mnmajor_desc(da, kk), id_dv, acc);
-          umma_f16_ss(tmem + 384, kmajor_desc(sa, kk), mnmajor_desc(qa, kk), id_dv, acc);
+        for (int kk = 0; kk < BQB / 16; ++kk) {
+          const uint32_t acc = (j > 0 || kk > 0) ? 1u : 0u;
+          umma_f16_ss(tmem + T_DV, kmajor_narrow_desc(pa, kk), mnmajor64_desc(da, kk), id_dv, acc);
+          umma_f16_ss(tmem + T_DK, kmajor_narrow_desc(sa, kk), mnmajor64_desc(qa, kk), id_dv, acc);
         }
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_f16_ss(tmem + 0, mnmajor_desc(sa, kk), mnmajor_desc(ka, kk), id_dq, kk > 0);
-        umma_commit(qdo_empty);
+          umma_f16_ss(tmem + T_DQ, mnmajor_desc(ka, kk), mnmajor_narrow_desc(sa, kk), id_dq, kk > 0);
+        umma_commit(&qdo_empty[st]);
+        umma_commit(&p_empty[st]);
         umma_commit(dq_full);
+        return true;
+      };
+      for (int i = 0; i < iters && ok; ++i) {
+        const int st = i & 1;
+        if (!mbar_wait(&qdo_full[st], (i >> 1) & 1)) { ok = false; break; }
+        if (i > 0 && !mbar_wait(s_free, (i - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t qa = smem_u32(smem + S::Q_OFF + st * QTILE_BYTES);
+        const uint32_t da = smem_u32(smem + S::DO_OFF + st * QTILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          umma_f16_ss(tmem + T_S, kmajor_desc(ka, kk), kmajor64_desc(qa, kk), id_s, kk > 0);
+          umma_f16_ss(tmem + T_DP, kmajor_desc(va, kk), kmajor64_desc(da, kk), id_s, kk > 0);
+        }
+        umma_commit(s_full);
+        if (i > 0 && !grads(i - 1)) { ok = false; break; }
       }
+      if (ok && iters > 0 && !grads(iters - 1)) ok = false;
       if (ok) umma_commit(all_done);
       else *abort_flag = 1;
     }
     __syncwarp();
-  } else {
+  } else if (warp < 6) {
+    // ---- softmax warps: one kv row per thread
     const int q4 = warp & 3;
     const int lane = threadIdx.x & 31;
-    const int row = q4 * 32 + lane;    // kv row for S^T/dP^T/dV/dK; q row for dQ
+    const int row = q4 * 32 + lane;
     const int tid = threadIdx.x - 64;  // 0..127
     const int kvi = k0 + row;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     bool ok = true;
-    for (int i = 0; i < iters; ++i) {
+    auto vec_load = [&](int i) -> float {  // lse2 (tid < 64) or delta (tid >= 64) of iteration i
       const int h = kvh * G + i / per_head;
-      const int qb = kb + i % per_head;
-      const int q0 = qb * BQ;
-      const uint32_t ph = i & 1;
-      // per-query-row softmax statistics for this block
-      {
-        const int qi = q0 + tid;
-        const bool in = qi < len;
-        s_lse[tid] = in ? p.lse[(size_t)h * p.T + s0 + qi] * kLog2e : INFINITY;
-        s_delta[tid] = in ? p.delta[(size_t)h * p.T + s0 + qi] : 0.f;
-      }
+      const int qi = (qb0 + i % per_head) * BQB + (tid & 63);
+      if (qi >= len) return tid < 64 ? INFINITY : 0.f;
+      return tid < 64 ? p.lse[(size_t)h * p.T + s0 + qi] * kLog2e : p.delta[(size_t)h * p.T + s0 + qi];
+    };
+    if (iters > 0) s_vec[tid] = vec_load(0);
+    // after a failed wait the loop keeps running (no waits, no work) so every
+    // softmax thread still reaches each named barrier
+    for (int i = 0; i < iters; ++i) {
+      const int q0 = (qb0 + i % per_head) * BQB;
+      const int st = i & 1;
+      const float nxt = (i + 1 < iters) ? vec_load(i + 1) : 0.f;   // prefetch next iteration's statistics
       named_bar_sync(1, 128);
-      if (!mbar_wait(st_full, ph)) { ok = false; break; }
+      if (!ok) continue;
+      const float* lse2 = s_vec + st * 128;
+      const float* dlt = lse2 + 64;
+      if (!mbar_wait(s_full, i & 1)) { ok = false; *abort_flag = 1; continue; }
       tc_fence_after();
-      const bool diag = (qb == kb);
+      uint32_t rs[2][32], rp[2][32];
+      tmem_ld32(tmem + lane_base + T_S, rs[0]);
+      tmem_ld32(tmem + lane_base + T_S + 32, rs[1]);
+      tmem_ld32(tmem + lane_base + T_DP, rp[0]);
+      tmem_ld32(tmem + lane_base + T_DP + 32, rp[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_free);
+      if (!mbar_wait(&p_empty[st], ((i >> 1) & 1) ^ 1)) { ok = false; *abort_flag = 1; continue; }
+      const bool diag = q0 < k0 + BKV;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t rs[32], rp[32];
-        tmem_ld32(tmem + lane_base + c * 32, rs);
-        tmem_ld32(tmem + lane_base + 128 + c * 32, rp);
-        tmem_wait_ld();
-        float pv[32], dv[32];
+      for (int c = 0; c < 2; ++c) {
+        // P and dS overwrite the raw registers in place (no extra live arrays)
+        float* pv = reinterpret_cast<float*>(rs[c]);
+        float* dv = reinterpret_cast<float*>(rp[c]);
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int qc = c * 32 + e;
-          float pr = exp2f(__uint_as_float(rs[e]) * p.scale_log2 - s_lse[qc]);
+          float pr = exp2f(__uint_as_float(rs[c][e]) * p.scale_log2 - lse2[qc]);
           if ((diag && q0 + qc < kvi) || kvi >= len) pr = 0.f;
+          dv[e] = pr * (__uint_as_float(rp[c][e]) - dlt[qc]);
           pv[e] = pr;
-          dv[e] = pr * (__uint_as_float(rp[e]) - s_delta[qc]);
         }
-        store_row32_sw128(smem + S::PT_OFF, row, c, pv);
-        store_row32_sw128(smem + S::DS_OFF, row, c, dv);
+        store_row32_sw128(smem + S::PT_OFF + st * PTILE_BYTES, row, c, pv);
+        store_row32_sw128(smem + S::DS_OFF + st * PTILE_BYTES, row, c, dv);
       }
       fence_proxy_async_smem();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      // dQ partial for query rows of this block
-      if (!mbar_wait(dq_full, ph)) { ok = false; break; }
-      tc_fence_after();
-      const int qi = q0 + row;
-      float* dst = p.dq_acc + ((size_t)(s0 + qi) * p.Hq + h) * D;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + c * 32, r);
-        tmem_wait_ld();
-        if (qi < len) {
-#pragma unroll
-          for (int e = 0; e < 32; e += 4) {
-            float4 v4 = make_float4(__uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
-                                    __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
-            atomicAdd(reinterpret_cast<float4*>(dst + c * 32 + e), v4);
-          }
-        }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      named_bar_sync(1, 128);  // s_lse / s_delta reuse
+      if (lane == 0) mbar_arrive(&p_full[st]);
+      s_vec[(st ^ 1) * 128 + tid] = nxt;   // buffer st^1 was last read in iteration i-1
     }
-    if (ok && mbar_wait(all_done, 0)) {
+    if (ok && iters > 0 && mbar_wait(all_done, 0)) {
       tc_fence_after();
       const bool valid = kvi < len;
       __nv_bfloat16* dvrow = p.dv + (size_t)(s0 + kvi) * p.ld_dv + kvh * D;
@@ -576,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem + lane_base + 256 + part * 128 + c * 32, r);
+          tmem_ld32(tmem + lane_base + (part == 0 ? T_DV : T_DK) + c * 32, r);
           tmem_wait_ld();
           if (valid) {
 #pragma unroll
@@ -591,8 +636,37 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-    } else {
+    } else if (iters > 0) {
       *abort_flag = 1;
+    }
+  } else {
+    // ---- dQ warps: one head-dim lane per thread; dQ^T columns are query rows
+    const int q4 = warp & 3;
+    const int lane = threadIdx.x & 31;
+    const int d = q4 * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    for (int j = 0; j < iters; ++j) {
+      const int h = kvh * G + j / per_head;
+      const int q0 = (qb0 + j % per_head) * BQB;
+      if (!mbar_wait(dq_full, j & 1)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      uint32_t r[2][32];
+      tmem_ld32(tmem + lane_base + T_DQ, r[0]);
+      tmem_ld32(tmem + lane_base + T_DQ + 32, r[1]);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_empty);
+      float* dst = p.dq_acc + ((size_t)(s0 + q0) * p.Hq + h) * D + d;
+      const size_t rstride = (size_t)p.Hq * D;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int qc = c * 32 + e;
+          if (q0 + qc < len) atomicAdd(dst + qc * rstride, __uint_as_float(r[c][e]) * p.scale);
+        }
+      }
     }
   }
   tc_fence_before();
@@ -601,6 +675,24 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// Host launch shared by the allocating and the allocation-free entry points.
+// tmQ / tmDO: 64-row boxes; tmK / tmV: 128-row boxes.
+inline cudaError_t launch_bwd_main(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
+                                   const CUtensorMap& tdo, const BwdParams& p, cudaStream_t st) {
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr[dev]) {   // the attribute is per device
+    e = cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BwdSmem::TOTAL);
+    if (e != cudaSuccess) return e;
+    attr[dev] = true;
+  }
+  attn_bwd_kernel<<<p.nseq * p.nkblk * p.Hkv, kBwdThreads, BwdSmem::TOTAL, st>>>(tq, tk, tv, tdo, p);
+  return cudaGetLastError();
 }
 
 void check_qkv(const at::Tensor& t, const char* n) {
@@ -686,10 +778,10 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
     check_cuda(cudaGetLastError(), "attn_bwd_prep");
   }
   auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-  CUtensorMap tq = make_tmap_2d(q.data_ptr(), bf, 2, (uint64_t)Hq * D, T, q.stride(0), 64, 128);
+  CUtensorMap tq = make_tmap_2d(q.data_ptr(), bf, 2, (uint64_t)Hq * D, T, q.stride(0), 64, BQB);
   CUtensorMap tk = make_tmap_2d(k.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, k.stride(0), 64, 128);
   CUtensorMap tv = make_tmap_2d(v.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, v.stride(0), 64, 128);
-  CUtensorMap tdo = make_tmap_2d(dout.data_ptr(), bf, 2, (uint64_t)Hq * D, T, dout.stride(0), 64, 128);
+  CUtensorMap tdo = make_tmap_2d(dout.data_ptr(), bf, 2, (uint64_t)Hq * D, T, dout.stride(0), 64, BQB);
   BwdParams p;
   p.cu_seqlens = cu_seqlens.data_ptr<int>();
   p.nseq = nseq;
@@ -706,16 +798,7 @@ void attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
   p.ld_dk = dk.stride(0);
   p.ld_dv = dv.stride(0);
   p.T = T;
-  constexpr int smem = BwdSmem::TOTAL;
-  static bool attr = false;
-  if (!attr) {
-    check_cuda(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-               "attn_bwd smem attr");
-    attr = true;
-  }
-  dim3 grid(nseq * p.nkblk, Hkv);
-  attn_bwd_kernel<<<grid, kThreads, smem, st>>>(tq, tk, tv, tdo, p);
-  check_cuda(cudaGetLastError(), "attn_bwd launch");
+  check_cuda(launch_bwd_main(tq, tk, tv, tdo, p, st), "attn_bwd launch");
   const long n8 = (long)T * Hq * (D / 8);
   attn_dq_convert_kernel<<<(int)((n8 + 255) / 256), 256, 0, st>>>(
       dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), dq.stride(0), Hq, T);
@@ -755,12 +838,6 @@ static int noalloc_setup(int dev, NoallocDeviceState** out) {
       return KORE_NOALLOC_ERR_SETUP;
     s.scratch = ptr;
   }
-  if (!s.smem_attr) {
-    if (cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             BwdSmem::TOTAL) != cudaSuccess)
-      return KORE_NOALLOC_ERR_SETUP;
-    s.smem_attr = true;
-  }
   *out = &s;
   return KORE_NOALLOC_OK;
 }
@@ -798,10 +875,10 @@ extern "C" int kore_attn_bwd_noalloc(const void* dout, int64_t ld_dout, const vo
   CUtensorMap tq, tk, tv, tdo;
   try {
     auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    tq = make_tmap_2d(q, bf, 2, (uint64_t)Hq * D, T, ld_q, 64, 128);
+    tq = make_tmap_2d(q, bf, 2, (uint64_t)Hq * D, T, ld_q, 64, BQB);
     tk = make_tmap_2d(k, bf, 2, (uint64_t)Hkv * D, T, ld_k, 64, 128);
     tv = make_tmap_2d(v, bf, 2, (uint64_t)Hkv * D, T, ld_v, 64, 128);
-    tdo = make_tmap_2d(dout, bf, 2, (uint64_t)Hq * D, T, ld_dout, 64, 128);
+    tdo = make_tmap_2d(dout, bf, 2, (uint64_t)Hq * D, T, ld_dout, 64, BQB);
   } catch (...) {
     return KORE_NOALLOC_ERR_ARGS;
   }
@@ -829,9 +906,7 @@ extern "C" int kore_attn_bwd_noalloc(const void* dout, int64_t ld_dout, const vo
   p.ld_dk = (int)ld_dk;
   p.ld_dv = (int)ld_dv;
   p.T = T;
-  dim3 grid(nseq * p.nkblk, Hkv);
-  attn_bwd_kernel<<<grid, kThreads, BwdSmem::TOTAL, stream>>>(tq, tk, tv, tdo, p);
-  if (cudaGetLastError() != cudaSuccess) return KORE_NOALLOC_ERR_LAUNCH;
+  if (launch_bwd_main(tq, tk, tv, tdo, p, stream) != cudaSuccess) return KORE_NOALLOC_ERR_LAUNCH;
   const long n8 = (long)T * Hq * (D / 8);
   attn_dq_convert_kernel<<<(int)((n8 + 255) / 256), 256, 0, stream>>>(
       dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), (int)ld_dq, Hq, T);

@@ -84,6 +84,7 @@ void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<in
 void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x, const c10::optional<at::Tensor>& g,
                     const c10::optional<at::Tensor>& hn, double eps);
 std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset);
+int64_t device_wait_flag(const at::Tensor& flag, int64_t want, double timeout_s);
 int read_and_clear_device_error();
 }  // namespace kore
 
@@ -111,6 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_heap_open", &kore::symm_heap_open);
   m.def("symm_heap_tensor", &kore::symm_heap_tensor);
   m.def("symm_barrier", &kore::symm_barrier);
+  m.def("device_wait_flag", &kore::device_wait_flag, "bounded wait on a device flag; 0 seen, 2 timed out");
   m.def("symm_rs_sumsq", &kore::symm_rs_sumsq);
   m.def("symm_scalar_allreduce", &kore::symm_scalar_allreduce);
   m.def("symm_adamw_bcast", &kore::symm_adamw_bcast);

@@ -568,3 +568,38 @@ std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset) {
 }
 
 }  // namespace kore
+
+// ============================================================== bounded flag wait (health check)
+namespace kore {
+namespace symm {
+
+// Wait until *flag >= want or timeout_ns elapse; status 0 = seen, 2 = timed
+// out. The same bounded-spin discipline as every peer wait in this file: the
+// kernel always returns, the context stays usable and the host reads status.
+__global__ void wait_flag_kernel(const unsigned long long* flag, unsigned long long want, unsigned long long timeout_ns,
+                                 int* status) {
+  if (threadIdx.x != 0) return;
+  const uint64_t t0 = globaltimer();
+  for (;;) {
+    if (ld_acquire_sys(flag) >= want) { *status = 0; return; }
+    if (globaltimer() - t0 > timeout_ns) { *status = 2; return; }
+    __nanosleep(1000);
+  }
+}
+
+}  // namespace symm
+
+// Host: returns the wait status (0 seen, 2 timed out). ``flag`` is a uint64
+// (int64 tensor) in device memory, local or a peer's mapping.
+int64_t device_wait_flag(const at::Tensor& flag, int64_t want, double timeout_s) {
+  TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kLong && flag.numel() >= 1, "device_wait_flag: int64 cuda");
+  TORCH_CHECK(timeout_s > 0 && timeout_s <= 10.0, "device_wait_flag: timeout in (0, 10] s");
+  auto st = at::full({1}, -1, flag.options().dtype(at::kInt));
+  symm::wait_flag_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
+      (const unsigned long long*)flag.data_ptr(), (unsigned long long)want,
+      (unsigned long long)(timeout_s * 1e9), st.data_ptr<int>());
+  check_cuda(cudaGetLastError(), "device_wait_flag");
+  return st.item<int>();
+}
+
+}  // namespace kore
