@@ -146,12 +146,16 @@ def flops_bytes(operation: str, dims: Dict[str, int], dtype: str) -> Optional[Tu
             M, N = dims["M"], dims["N"]
             return 5.0 * M * N, float(2 * M * N * e)
         if "rope" in op:
-            S, B, H, D = dims["S"], dims["B"], dims["H"], dims["D"]
+            S, B, H, D = dims["S"], get("B", default=1), dims["H"], dims["D"]
             n = S * B * H * D
             return 6.0 * n, float(2 * n * e + S * D * e)
         if "quant" in op:
             M, N = dims["M"], dims["N"]
             return 2.0 * M * N, float(M * N * 3 + M * 4)
+        if op in ("moe_permute", "moe_combine"):
+            M, D, k = dims["M"], dims["D"], get("K", "topk", default=1)
+            moved = M * k * D
+            return float(moved if op == "moe_combine" else 0) * 2.0, float((moved + (M * D if op == "moe_combine" else M * D)) * e)
         if "moe" in op:
             M = dims["M"]
             E, k = get("E", "n_experts", default=8), get("topk", "k", default=2)

@@ -53,6 +53,11 @@ def snr_db(out, ref) -> float:
     return 20 * math.log10(sig / noise) if sig > 0 else -999.0
 
 
+def task_torch_dtype(dtype: str):
+    """Input dtype of a task (fp8 tasks take bf16 inputs and quantise inside)."""
+    return {"fp16": torch.float16, "fp32": torch.float32}.get(dtype, torch.bfloat16)
+
+
 def load_candidate(path: str, entry: str):
     spec = importlib.util.spec_from_file_location("candidate_kernel", path)
     mod = importlib.util.module_from_spec(spec)
@@ -85,7 +90,7 @@ def adversarial(inputs, kind: int):
 
 def run_correctness(task, fn, dims, trials: int, atol: float, rtol: float, adv: bool) -> float:
     spec = SPECS[task.spec]
-    dt = torch.bfloat16 if task.dtype in ("bf16", "fp8") else torch.float32
+    dt = task_torch_dtype(task.dtype)
     worst, maxd, ok = 999.0, 0.0, True
     cases = [(s, None) for s in range(trials)] + ([(100 + k, k) for k in range(5)] if adv else [])
     for seed, kind in cases:
@@ -135,7 +140,7 @@ def time_events(fn, warmup: int, iters: int):
 
 def run_bench(task, fn, shapes, warmup, iters):
     spec = SPECS[task.spec]
-    dt = torch.bfloat16 if task.dtype in ("bf16", "fp8") else torch.float32
+    dt = task_torch_dtype(task.dtype)
     rng = random.Random()
     for name in shapes:
         sh = task.shape(name)

@@ -382,3 +382,13 @@ for _n, (_e, _r) in _BINARY.items():
                 (lambda r: lambda a, b: r(a, b))(_r), _elem(_n, f"y = {_e}"),
                 {"minimal": {"M": 16, "N": 1024}, "primary": {"M": 4096, "N": 4096}, "validation": []},
                 "binary"))
+
+
+# generated breadth families (kore_b200.tasks.breadth)
+def _register_breadth():
+    from .breadth import build
+    for _s in build():
+        _add(_s)
+
+
+_register_breadth()

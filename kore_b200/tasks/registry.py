@@ -15,8 +15,11 @@ from typing import List, Optional, Tuple
 from .base import Task
 from .ops_library import SPECS
 
-HELDOUT_FAMILIES = {"quant"}
+HELDOUT_FAMILIES = {"quant", "ssm", "sort_sparse"}
 HELDOUT_TASKS = {"flash_attn_prefill_bf16", "gen_max_bf16"}
+# held-out operator variants: every dtype / shape of these never appears in training
+HELDOUT_PATTERNS = ("_sliding", "_softcap", "genb_unary_mish_", "genb_binary_hypot_", "genb_reduce_entropy_",
+                    "genb_norm_rmsnorm_gated_", "genb_gemm_relu2_", "genb_train_lion_", "genb_sample_minp_")
 
 
 def _discover_dirs() -> List[Task]:
@@ -43,7 +46,8 @@ def get_task(task_id: str) -> Task:
 def split_tasks(seed: int = 0, heldout_frac: float = 0.0) -> Tuple[List[str], List[str]]:
     ids = sorted(t.task_id for t in all_tasks())
     fam = {t.task_id: t.family for t in all_tasks()}
-    held = {i for i in ids if fam[i] in HELDOUT_FAMILIES or i in HELDOUT_TASKS}
+    held = {i for i in ids if fam[i] in HELDOUT_FAMILIES or i in HELDOUT_TASKS
+            or any(p in i for p in HELDOUT_PATTERNS)}
     rest = [i for i in ids if i not in held]
     rng = random.Random(seed)
     extra = set(rng.sample(rest, int(round(heldout_frac * len(rest))))) if heldout_frac > 0 else set()

@@ -1,0 +1,38 @@
+"""Every generated breadth task is well formed: its seed is correct against its
+fp32 oracle on the minimal shape, the baseline runs, the roofline model has
+numbers for it, and held-out families never leak into the training split."""
+import pytest
+import torch
+
+from kore_b200.tasks.ops_library import SPECS
+from kore_b200.tasks.registry import split_tasks
+
+BREADTH = sorted(n for n in SPECS if n.startswith("genb_"))
+
+
+def test_breadth_size_and_split():
+    assert len(BREADTH) >= 450
+    tr, ho = split_tasks()
+    assert not set(tr) & set(ho)
+    assert any("genb_quant_" in h for h in ho) and any("_sliding" in h for h in ho)
+    assert len(ho) >= 20
+
+
+@pytest.mark.parametrize("name", BREADTH[::7])
+def test_seed_matches_oracle(name):
+    s = SPECS[name]
+    x = s.make_inputs(s.shapes["minimal"], 0, "cpu", torch.float32)
+    ref = s.reference(*x)
+    ns = {}
+    exec(s.seed_src, ns)
+    out = ns[s.entry](*x)
+    assert tuple(out.shape) == tuple(ref.shape)
+    r = ref.float().nan_to_num(0, 0, 0)
+    assert (out.float().nan_to_num(0, 0, 0) - r).abs().max() <= 1e-2 * max(1.0, r.abs().max().item())
+    s.baseline(*x)
+
+
+def test_rooflines_cover_breadth():
+    from kore_b200.analysis.rooflines import flops_bytes
+    missing = [n for n in BREADTH if flops_bytes(SPECS[n].operation, SPECS[n].shapes["primary"], SPECS[n].dtype) is None]
+    assert not missing, missing[:5]
