@@ -56,19 +56,6 @@ KORE_DEV uint64_t mnmajor_desc(uint32_t base, int kk) {
   return make_sw128_desc(base + kk * 2048, 16384, 1024);
 }
 
-// 2^x for x <= 0 on the FMA pipe: x = n + f with n = floor(x), f in [0, 1);
-// 2^f from a cubic fitted here to 2^f on [0, 1) by iteratively reweighted
-// least squares on the relative error (max relative error 7.6e-5, far below
-// the bf16 rounding of P); 2^n is added to the exponent field.
-KORE_DEV float exp2_poly(float x) {
-  if (x < -126.f) return 0.f;
-  const float n = floorf(x);
-  const float f = x - n;
-  const float p = fmaf(fmaf(fmaf(0.07802251590192465f, f, 0.22606561149419213f), f, 0.6958365057812748f), f,
-                       0.9999246655491744f);
-  return __int_as_float(__float_as_int(p) + (int)n * (1 << 23));
-}
-
 // Write a thread's 128 fp32 values (one tile row) as bf16 into a K-major SW128 tile.
 KORE_DEV void store_row_sw128(uint8_t* tile, int row, const float* v) {
 #pragma unroll
@@ -220,36 +207,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q * 32 + lane;  // row within the query block
     const int qi = q0 + row;        // query position within the sequence
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    float m = -INFINITY, l = 0.f;   // running max (log2 domain, scaled) and sum
+    float m = -INFINITY, l = 0.f;
     float sv[128];
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int st = j & 1;
       if (!mbar_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
-      {
-        uint32_t r[4][32];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + st * 128 + c * 32, r[c]);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + st * 128 + c * 32, r);
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 4; ++c)
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]);   // raw scores
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
       }
       const int kv0 = j * BKV;
+      float mx = -INFINITY;
       const bool edge = (j == nkv - 1) || (kv0 + BKV > len);
-      // row max with 8 independent chains (a single chain is latency bound)
-      float mx8[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) mx8[a] = -INFINITY;
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
         if (edge && (kv0 + i > qi || kv0 + i >= len)) sv[i] = -INFINITY;
-        mx8[i & 7] = fmaxf(mx8[i & 7], sv[i]);
+        mx = fmaxf(mx, sv[i]);
       }
-      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * p.scale_log2;
       float m_new = fmaxf(m, mx);
       const bool need = (m == -INFINITY) ? true : (m_new > m + 8.f);
       if (j > 0) {
@@ -273,18 +253,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (need) m = m_new;
       const float mref = (m == -INFINITY) ? 0.f : m;
-      // p = 2^(s * scale_log2 - m): three of every four on the MUFU unit, the
-      // fourth on the FMA pipe (exp2_poly) so neither unit alone bounds the row
-      float rs8[8];
-#pragma unroll
-      for (int a = 0; a < 8; ++a) rs8[a] = 0.f;
+      float rs = 0.f;
 #pragma unroll
       for (int i = 0; i < 128; ++i) {
-        const float x = fmaf(sv[i], p.scale_log2, -mref);
-        sv[i] = (i & 3) == 3 ? exp2_poly(x) : exp2f(x);
-        rs8[i & 7] += sv[i];
+        sv[i] = exp2f(sv[i] - mref);
+        rs += sv[i];
       }
-      l += ((rs8[0] + rs8[1]) + (rs8[2] + rs8[3])) + ((rs8[4] + rs8[5]) + (rs8[6] + rs8[7]));
+      l += rs;
       store_row_sw128(smem + S::P_OFF + st * TILE_BYTES, row, sv);
       fence_proxy_async_smem();
       tc_fence_before();
