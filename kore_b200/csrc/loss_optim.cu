@@ -214,6 +214,78 @@ __global__ void adamw_kernel(__nv_bfloat16* __restrict__ p, float* __restrict__ 
   }
 }
 
+// Same update, 8 elements per thread with 16-byte accesses (bf16 grads,
+// n % 8 == 0 and 16-byte aligned buffers; checked on the host).
+__global__ void adamw_vec8_kernel(__nv_bfloat16* __restrict__ p, float* __restrict__ master,
+                                  const __nv_bfloat16* __restrict__ g, float* __restrict__ m,
+                                  float* __restrict__ v, long n, float lr, float b1, float b2,
+                                  float eps, float wd, float bc1, float bc2, float grad_scale,
+                                  const float* __restrict__ sumsq, float max_norm, uint32_t seed) {
+  float scale = grad_scale;
+  if (sumsq != nullptr && max_norm > 0.f) {
+    float norm = sqrtf(*sumsq) * grad_scale;
+    scale *= fminf(1.f, max_norm / (norm + 1e-6f));
+  }
+  const long nv = n / 8;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < nv; i += (long)gridDim.x * blockDim.x) {
+    const uint4 gu = reinterpret_cast<const uint4*>(g)[i];
+    const uint4 pu = reinterpret_cast<const uint4*>(p)[i];
+    const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gu);
+    const __nv_bfloat162* ph = reinterpret_cast<const __nv_bfloat162*>(&pu);
+    float4* m4 = reinterpret_cast<float4*>(m) + 2 * i;
+    float4* v4 = reinterpret_cast<float4*>(v) + 2 * i;
+    float4* w4 = master ? reinterpret_cast<float4*>(master) + 2 * i : nullptr;
+    float gv[8], mv[8], vv[8], wv[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 a = __bfloat1622float2(gh[e]);
+      gv[2 * e] = a.x * scale;
+      gv[2 * e + 1] = a.y * scale;
+    }
+    {
+      const float4 a = m4[0], b = m4[1], c = v4[0], d = v4[1];
+      mv[0] = a.x; mv[1] = a.y; mv[2] = a.z; mv[3] = a.w; mv[4] = b.x; mv[5] = b.y; mv[6] = b.z; mv[7] = b.w;
+      vv[0] = c.x; vv[1] = c.y; vv[2] = c.z; vv[3] = c.w; vv[4] = d.x; vv[5] = d.y; vv[6] = d.z; vv[7] = d.w;
+    }
+    if (w4) {
+      const float4 a = w4[0], b = w4[1];
+      wv[0] = a.x; wv[1] = a.y; wv[2] = a.z; wv[3] = a.w; wv[4] = b.x; wv[5] = b.y; wv[6] = b.z; wv[7] = b.w;
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 a = __bfloat1622float2(ph[e]);
+        wv[2 * e] = a.x;
+        wv[2 * e + 1] = a.y;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      mv[k] = b1 * mv[k] + (1.f - b1) * gv[k];
+      vv[k] = b2 * vv[k] + (1.f - b2) * gv[k] * gv[k];
+      wv[k] = wv[k] * (1.f - lr * wd) - lr * (mv[k] / bc1) / (sqrtf(vv[k] / bc2) + eps);
+    }
+    m4[0] = make_float4(mv[0], mv[1], mv[2], mv[3]);
+    m4[1] = make_float4(mv[4], mv[5], mv[6], mv[7]);
+    v4[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    v4[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+    uint32_t out[4];
+    if (w4) {
+      w4[0] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+      w4[1] = make_float4(wv[4], wv[5], wv[6], wv[7]);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) out[e] = pack_bf16(wv[2 * e], wv[2 * e + 1]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const __nv_bfloat16 lo = bf16_stochastic(wv[2 * e], hash32((uint32_t)(8 * i + 2 * e) * 0x9E3779B9u ^ seed));
+        const __nv_bfloat16 hi = bf16_stochastic(wv[2 * e + 1], hash32((uint32_t)(8 * i + 2 * e + 1) * 0x9E3779B9u ^ seed));
+        out[e] = (uint32_t)__bfloat16_as_ushort(lo) | ((uint32_t)__bfloat16_as_ushort(hi) << 16);
+      }
+    }
+    reinterpret_cast<uint4*>(p)[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
 }  // namespace
 
 // logits: [T, V] bf16 (row stride ld). Returns nothing; fills the given outputs.
@@ -275,7 +347,16 @@ void adamw_step(at::Tensor& p, const c10::optional<at::Tensor>& master, const at
         (__nv_bfloat16*)p.data_ptr(), mp, g.data_ptr<float>(), m.data_ptr<float>(),
         v.data_ptr<float>(), n, lr, b1, b2, eps, wd, bc1, bc2, grad_scale, sq, max_norm,
         (uint32_t)seed);
-  else
+  else if (n % 8 == 0 && g.is_contiguous() && m.is_contiguous() && v.is_contiguous() &&
+           (!master || master->is_contiguous()) &&
+           ((reinterpret_cast<uintptr_t>(p.data_ptr()) | reinterpret_cast<uintptr_t>(g.data_ptr()) |
+             reinterpret_cast<uintptr_t>(m.data_ptr()) | reinterpret_cast<uintptr_t>(v.data_ptr()) |
+             reinterpret_cast<uintptr_t>(mp)) % 16) == 0) {
+    const int gv = (int)std::min<long>((n / 8 + 255) / 256, (long)num_sms(p.get_device()) * 8);
+    adamw_vec8_kernel<<<gv, 256, 0, st>>>(
+        (__nv_bfloat16*)p.data_ptr(), mp, (const __nv_bfloat16*)g.data_ptr(), m.data_ptr<float>(),
+        v.data_ptr<float>(), n, lr, b1, b2, eps, wd, bc1, bc2, grad_scale, sq, max_norm, (uint32_t)seed);
+  } else
     adamw_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
         (__nv_bfloat16*)p.data_ptr(), mp, (const __nv_bfloat16*)g.data_ptr(), m.data_ptr<float>(),
         v.data_ptr<float>(), n, lr, b1, b2, eps, wd, bc1, bc2, grad_scale, sq, max_norm,

@@ -177,27 +177,52 @@ __global__ void adamw_bcast_kernel(PeerPtrs grads, float gscale, float* __restri
     }
     const uint4 cur = *reinterpret_cast<const uint4*>(own + shard_off + i * 8);
     const __nv_bfloat162* ch = reinterpret_cast<const __nv_bfloat162*>(&cur);
+    // fp32 state as two 16-byte vectors per thread (8 consecutive elements)
+    float4* m4 = reinterpret_cast<float4*>(m + i * 8);
+    float4* v4 = reinterpret_cast<float4*>(v + i * 8);
+    float4* w4 = master ? reinterpret_cast<float4*>(master + i * 8) : nullptr;
+    float mv[8], vv[8], wv[8];
+    {
+      const float4 a = m4[0], b = m4[1], c = v4[0], d = v4[1];
+      mv[0] = a.x; mv[1] = a.y; mv[2] = a.z; mv[3] = a.w; mv[4] = b.x; mv[5] = b.y; mv[6] = b.z; mv[7] = b.w;
+      vv[0] = c.x; vv[1] = c.y; vv[2] = c.z; vv[3] = c.w; vv[4] = d.x; vv[5] = d.y; vv[6] = d.z; vv[7] = d.w;
+      if (w4) {
+        const float4 e = w4[0], f = w4[1];
+        wv[0] = e.x; wv[1] = e.y; wv[2] = e.z; wv[3] = e.w; wv[4] = f.x; wv[5] = f.y; wv[6] = f.z; wv[7] = f.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 cf = __bfloat1622float2(ch[e]);
+          wv[2 * e] = cf.x;
+          wv[2 * e + 1] = cf.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float gi = gs[k] * gscale * scale;
+      mv[k] = b1 * mv[k] + (1.f - b1) * gi;
+      vv[k] = b2 * vv[k] + (1.f - b2) * gi * gi;
+      wv[k] = wv[k] * (1.f - lr * wd) - lr * (mv[k] / bc1) / (sqrtf(vv[k] / bc2) + eps);
+    }
+    m4[0] = make_float4(mv[0], mv[1], mv[2], mv[3]);
+    m4[1] = make_float4(mv[4], mv[5], mv[6], mv[7]);
+    v4[0] = make_float4(vv[0], vv[1], vv[2], vv[3]);
+    v4[1] = make_float4(vv[4], vv[5], vv[6], vv[7]);
+    if (w4) {
+      w4[0] = make_float4(wv[0], wv[1], wv[2], wv[3]);
+      w4[1] = make_float4(wv[4], wv[5], wv[6], wv[7]);
+    }
 #pragma unroll
     for (int e = 0; e < 8; e += 2) {
       float w2[2];
-      float2 cf = __bfloat1622float2(ch[e / 2]);
-      w2[0] = cf.x;
-      w2[1] = cf.y;
 #pragma unroll
       for (int k = 0; k < 2; ++k) {
         const long j = i * 8 + e + k;
-        const float gi = gs[e + k] * gscale * scale;
-        const float mi = b1 * m[j] + (1.f - b1) * gi;
-        const float vi = b2 * v[j] + (1.f - b2) * gi * gi;
-        m[j] = mi;
-        v[j] = vi;
-        float w = master ? master[j] : w2[k];
-        w = w * (1.f - lr * wd) - lr * (mi / bc1) / (sqrtf(vi / bc2) + eps);
-        if (master) {
-          master[j] = w;
-          w2[k] = w;
+        if (w4) {
+          w2[k] = wv[e + k];
         } else {  // stochastic rounding to bf16 (unbiased)
-          uint32_t b = __float_as_uint(w);
+          uint32_t b = __float_as_uint(wv[e + k]);
           b += hash32((uint32_t)(shard_off + j) * 0x9E3779B9u ^ seed) & 0xffffu;
           w2[k] = __uint_as_float(b & 0xffff0000u);
         }
@@ -338,6 +363,13 @@ void symm_adamw_bcast(int64_t id, int64_t param_offset, int64_t grad_offset, int
                       const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed) {
   auto& h = *g_heaps.at(id);
   TORCH_CHECK(n % 8 == 0, "shard length must be a multiple of 8");
+  auto vec_ok = [&](const at::Tensor& t) {
+    return t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous() && t.numel() >= n &&
+           reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0;
+  };
+  TORCH_CHECK(vec_ok(m) && vec_ok(v) && (!master || vec_ok(*master)),
+              "symm_adamw_bcast: m / v / master must be contiguous fp32, >= n elements, 16-byte aligned");
+  TORCH_CHECK((param_offset % 16 == 0) && (grad_offset % 16 == 0), "symm_adamw_bcast: 16-byte aligned offsets");
   symm::PeerPtrs prm = peer_ptrs(h, param_offset, true);  // slot 0 = own buffer
   symm::PeerPtrs grd = peer_ptrs(h, grad_offset, false);
   const long shard_off = (long)h.rank * n;
