@@ -80,7 +80,8 @@ void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, cons
                     int64_t H);
 void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<int64_t>& a_peers, int64_t lda,
                   int64_t M, const at::Tensor& b, const c10::optional<at::Tensor>& out,
-                  const std::vector<int64_t>& rs_peers, int64_t ldc, int64_t rows, int64_t rank);
+                  const std::vector<int64_t>& rs_peers, int64_t ldc, int64_t rows, int64_t rank,
+                  const c10::optional<at::Tensor>& stage, const c10::optional<at::Tensor>& flags, int64_t epoch);
 void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x, const c10::optional<at::Tensor>& g,
                     const c10::optional<at::Tensor>& hn, double eps);
 std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset);
@@ -123,7 +124,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_combine_bwd", &kore::moe_combine_bwd);
   m.def("symm_ep_scatter", &kore::symm_ep_scatter);
   m.def("symm_ep_gather", &kore::symm_ep_gather);
-  m.def("gemm_tp_bf16", &kore::gemm_tp_bf16, "tensor-parallel AG->GEMM / GEMM->RS over peer memory");
+  m.def("gemm_tp_bf16", &kore::gemm_tp_bf16, "tensor-parallel AG->GEMM / GEMM->RS over peer memory",
+        py::arg("a_local"), py::arg("a_peers"), py::arg("lda"), py::arg("M"), py::arg("b"), py::arg("out"),
+        py::arg("rs_peers"), py::arg("ldc"), py::arg("rows"), py::arg("rank"), py::arg("stage") = py::none(),
+        py::arg("flags") = py::none(), py::arg("epoch") = 0);
   m.def("tp_reduce_norm", &kore::tp_reduce_norm);
   m.def("symm_peer_addrs", &kore::symm_peer_addrs);
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);

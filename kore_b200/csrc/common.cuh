@@ -146,6 +146,31 @@ KORE_DEV void tma_store_wait_all() {
 KORE_DEV void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
+// Order this thread's generic-proxy global accesses with later async-proxy (TMA) ones.
+KORE_DEV void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+KORE_DEV void st_release_gpu_s32(int* a, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(a), "r"(v) : "memory");
+}
+KORE_DEV int ld_acquire_gpu_s32(const int* a) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(a) : "memory");
+  return v;
+}
+// Bounded wait until *flag >= want (error code 4 after kWaitTimeoutNs).
+KORE_DEV bool wait_flag_ge(const int* flag, int want) {
+  if (ld_acquire_gpu_s32(flag) >= want) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_gpu_s32(flag) >= want) return true;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      atomicExch(&g_error, 4);
+      return false;
+    }
+  }
+}
 
 // ---------------------------------------------------------------- tcgen05
 // Allocate `ncols` TMEM columns (power of two >= 32); whole warp must call.

@@ -50,8 +50,17 @@ struct Params {
   const int4* tiles;
   void* C_write;  // output base for the masked direct-store epilogue (grouped mode)
   // tensor-parallel all-gather->GEMM: A rows [i*ag_rows, (i+1)*ag_rows) live on
-  // peer i and are loaded by TMA straight from that peer (tensor map pm.a[i]).
+  // peer i (ag_src[i], row stride ag_lda). At kernel start every CTA copies
+  // its share of 64-row groups into the local staging buffer ag_stage [M, K]
+  // (each remote row crosses NVLink once) and publishes ag_flags[g] = ag_epoch;
+  // a tile's producer waits for its groups, then TMA-loads A from ag_stage.
   int ag_rows;
+  const void* ag_src[8] = {};
+  void* ag_stage = nullptr;
+  int* ag_flags = nullptr;
+  int ag_epoch = 0;
+  int ag_lda = 0;
+  int ag_rot = 0;   // M-block rotation so each rank starts on its own (local) rows
   // tensor-parallel GEMM->reduce-scatter: output row r is stored (P2P) into
   // peer r / rs_rows, slot rs_rank, i.e. rs_out[peer] + (rs_rank*rs_rows + r%rs_rows)*ldc.
   int rs_rows;
@@ -127,6 +136,42 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  if (p.ag_flags != nullptr) {
+    // ---------------------------------------------- staged all-gather copy
+    // 64-row groups round-robin over CTAs; 8 outstanding 16-byte loads per
+    // thread keep enough peer reads in flight to fill the NVLink pipe.
+    const int groups = p.M / 64;
+    const int vpr = p.K / 8;                 // 16-byte vectors per row
+    const int total = 64 * vpr;
+    for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+      const int owner = (g * 64) / p.ag_rows;
+      const int lr = g * 64 - owner * p.ag_rows;
+      const uint4* src = reinterpret_cast<const uint4*>(
+          reinterpret_cast<const __nv_bfloat16*>(p.ag_src[owner]) + (size_t)lr * p.ag_lda);
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ag_stage) + (size_t)g * 64 * p.K);
+      const int sstride = p.ag_lda / 8;
+      for (int base = threadIdx.x; base < total; base += kThreads * 8) {
+        uint4 buf[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * kThreads;
+          if (idx < total) buf[u] = src[(size_t)(idx / vpr) * sstride + idx % vpr];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * kThreads;
+          if (idx < total) dst[(size_t)(idx / vpr) * vpr + idx % vpr] = buf[u];
+        }
+      }
+      fence_proxy_async_global();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        st_release_gpu_s32(&p.ag_flags[g], p.ag_epoch);
+      }
+    }
+  }
+
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (elect_one()) {
@@ -135,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int tm, tn;
         tile_coords(t, num_m, num_n, tm, tn);
+        if (p.ag_rot) tm = (tm + p.ag_rot) % num_m;
         int m0 = tm * BM, ex = 0;
         const int n0 = tn * BN;
         if (p.tiles != nullptr) {
@@ -142,22 +188,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           ex = ti.x;
           m0 = ti.y;
         }
+        if (p.ag_flags != nullptr) {   // staged all-gather: this tile's row groups must be in ag_stage
+          bool ready = true;
+          for (int g = m0 / 64; g < min(m0 + BM, p.M) / 64 && ready; ++g)
+            ready = wait_flag_ge(&p.ag_flags[g], p.ag_epoch);
+          if (!ready) { *abort_flag = 1; break; }
+          fence_proxy_async_global();    // generic-proxy copies -> TMA reads
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
           uint8_t* sB = sA + S::A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], S::STAGE_BYTES);
           const int k0 = kb * BK;
-          if (p.ag_rows > 0) {  // rows of this tile come from their owner peers (64-row boxes)
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j) {
-              const int r = m0 + 64 * j;
-              const int np = p.M / p.ag_rows;
-              int pi = r / p.ag_rows, lr = r % p.ag_rows;
-              if (pi >= np) { pi = np - 1; lr = 0; }  // past M: any valid rows (outputs are clipped)
-              tma_load_2d(sA + j * 8192, &pm.a[pi], &full_bar[stage], k0, lr);
-            }
-          } else if (!A_MN) {
+          if (!A_MN) {
             tma_load_2d(sA, &tmA, &full_bar[stage], k0, m0);
           } else {
 #pragma unroll
@@ -230,6 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
       int tm, tn;
       tile_coords(t, num_m, num_n, tm, tn);
+      if (p.ag_rot) tm = (tm + p.ag_rot) % num_m;
       int m0 = tm * BM, m_lim = p.M;
       const int n0 = tn * BN;
       if (p.tiles != nullptr) {
@@ -375,17 +420,29 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
-            int grid, cudaStream_t stream, const PeerMaps* pmp = nullptr) {
+            int grid, cudaStream_t stream, const PeerMaps* pmp = nullptr, bool cooperative = false) {
   auto k = gemm_kernel<BN, STAGES, A_MN, B_MN>;
   constexpr int smem = Smem<BN, STAGES>::TOTAL;
-  static bool attr_set = false;  // per template instance; device attributes are per-function
-  if (!attr_set) {
+  static bool attr_set[64] = {};  // per template instance and device
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  TORCH_CHECK(dev >= 0 && dev < 64, "gemm: device index");
+  if (!attr_set[dev]) {
     check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                "cudaFuncSetAttribute(gemm smem)");
-    attr_set = true;
+    attr_set[dev] = true;
   }
   static PeerMaps empty_maps{};
-  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, pmp ? *pmp : empty_maps, p);
+  PeerMaps pm = pmp ? *pmp : empty_maps;
+  if (cooperative) {
+    CUtensorMap a = ta, b = tb, c = tc;
+    Params pp = p;
+    void* args[] = {&a, &b, &c, &pm, &pp};
+    check_cuda(cudaLaunchCooperativeKernel((const void*)k, dim3(grid), dim3(kThreads), args, smem, stream),
+               "gemm cooperative launch");
+    return;
+  }
+  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, pm, p);
   check_cuda(cudaGetLastError(), "gemm launch");
 }
 
@@ -482,7 +539,8 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
 //    (rank*rows + r%rows) * ldc; the owner then sums its W slots.
 void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<int64_t>& a_peers, int64_t lda,
                   int64_t M, const at::Tensor& b, const c10::optional<at::Tensor>& out,
-                  const std::vector<int64_t>& rs_peers, int64_t ldc, int64_t rows, int64_t rank) {
+                  const std::vector<int64_t>& rs_peers, int64_t ldc, int64_t rows, int64_t rank,
+                  const c10::optional<at::Tensor>& stage, const c10::optional<at::Tensor>& flags, int64_t epoch) {
   TORCH_CHECK(b.scalar_type() == at::kBFloat16 && b.dim() == 2 && b.stride(1) == 1, "b: bf16 [N, K]");
   const int N = b.size(0), K = b.size(1);
   TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && rows % 64 == 0 && rows > 0, "tp gemm: N, K % 8 and rows % 64");
@@ -505,17 +563,30 @@ void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<in
   p.ag_rows = ag ? (int)rows : 0;
   p.rs_rows = rs ? (int)rows : 0;
   p.rs_rank = (int)rank;
-  for (int i = 0; i < 8; ++i) p.rs_out[i] = nullptr;
+  for (int i = 0; i < 8; ++i) { p.rs_out[i] = nullptr; p.ag_src[i] = nullptr; }
   for (size_t i = 0; i < rs_peers.size(); ++i) p.rs_out[i] = reinterpret_cast<void*>(rs_peers[i]);
+  p.ag_stage = nullptr; p.ag_flags = nullptr; p.ag_epoch = 0; p.ag_lda = 0; p.ag_rot = 0;
   auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
   const int BN = use256 ? 256 : 128;
-  gemm::PeerMaps pm{};
   CUtensorMap ta;
   if (ag) {
-    for (size_t i = 0; i < a_peers.size(); ++i)
-      pm.a[i] = make_tmap_2d(reinterpret_cast<void*>(a_peers[i]), bf, 2, K, rows, lda, 64, 64);
-    ta = pm.a[0];
+    TORCH_CHECK(stage && flags, "tp gemm: all-gather mode needs a staging buffer and flags");
+    TORCH_CHECK(stage->is_cuda() && stage->scalar_type() == at::kBFloat16 && stage->is_contiguous() &&
+                    stage->numel() >= M * K, "tp gemm: stage must be contiguous bf16 with >= M*K elements");
+    TORCH_CHECK(flags->is_cuda() && flags->scalar_type() == at::kInt && flags->numel() >= M / 64,
+                "tp gemm: flags must be int32 with >= M/64 entries");
+    TORCH_CHECK(epoch > 0 && lda % 8 == 0 && lda >= K && (int64_t)a_peers.size() * rows == M,
+                "tp gemm: epoch > 0, lda % 8, peers * rows == M");
+    for (int64_t a : a_peers) TORCH_CHECK(a % 16 == 0, "tp gemm: peer rows must be 16-byte aligned");
+    for (size_t i = 0; i < a_peers.size(); ++i) p.ag_src[i] = reinterpret_cast<const void*>(a_peers[i]);
+    p.ag_stage = stage->data_ptr();
+    p.ag_flags = flags->data_ptr<int>();
+    p.ag_epoch = (int)epoch;
+    p.ag_lda = (int)lda;
+    const int num_m = (int)((M + 127) / 128);
+    p.ag_rot = (rows % 128 == 0) ? (int)((rank * rows / 128) % num_m) : 0;
+    ta = make_tmap_2d(stage->data_ptr(), bf, 2, K, M, K, 64, 128);
   } else {
     TORCH_CHECK(a_local->stride(1) == 1 && a_local->size(1) == K, "a_local: [M, K]");
     ta = make_tmap_2d(a_local->data_ptr(), bf, 2, K, M, a_local->stride(0), 64, 128);
@@ -525,8 +596,9 @@ void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<in
   const int tiles = (int)((M + 127) / 128) * ((N + BN - 1) / BN);
   const int grid = std::min(tiles, num_sms(b.get_device()));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (use256) gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, &pm);
-  else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, &pm);
+  // all-gather mode: CTAs wait on each other's copies, so they must be co-resident
+  if (use256) gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, nullptr, ag);
+  else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, nullptr, ag);
 }
 
 // Grouped GEMM over experts (MoE): rows of ``a`` are grouped by expert with

@@ -9,8 +9,9 @@ baselines, each reported against its roofline (run under torchrun, >= 2 GPUs):
     parameters into every peer. Roofline: the slower of the NVLink bytes per
     direction per GPU (2 P (N-1)/N each way) at the measured peer bandwidth
     and the local HBM bytes at the measured copy bandwidth.
-(c) tensor-parallel all-gather -> GEMM (TMA loads of the activation rows
-    straight from their owners) versus NCCL all-gather + GEMM, and GEMM ->
+(c) tensor-parallel all-gather -> GEMM (the GEMM's CTAs stage each peer's
+    row blocks into local memory once and flag them; tiles start on local
+    rows) versus NCCL all-gather + GEMM, and GEMM ->
     reduce-scatter (P2P-store epilogue + fused reduce) versus GEMM + NCCL
     reduce-scatter. Roofline: max(FLOPs / measured bf16 peak, NVLink bytes /
     link bandwidth).
@@ -115,12 +116,17 @@ def bench_tp(ctx, rows: int, K: int, N_local: int) -> list:
     gathered = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
     x_full = torch.randn(M, N_local, device="cuda", dtype=torch.bfloat16)
     rs_out = torch.empty(rows, K, device="cuda", dtype=torch.bfloat16)
+    stage = torch.empty(M * K, device="cuda", dtype=torch.bfloat16)
+    flags = torch.zeros(M // 64, device="cuda", dtype=torch.int32)
+    epoch = [0]
     full = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
     x_res = torch.zeros(rows, K, device="cuda", dtype=torch.bfloat16)
 
     def ag_fused():
         heap.barrier()
-        C.gemm_tp_bf16(None, a_peers, K, M, w_col, out, [], 0, rows, r)
+        epoch[0] += 1
+        C.gemm_tp_bf16(None, a_peers, K, M, w_col, out, [], 0, rows, r, stage, flags, epoch[0])
+        heap.barrier()            # peers finished reading my rows before they change
 
     def ag_nccl():
         dist.all_gather_into_tensor(gathered, a_loc.view(rows, K), group=ctx.group)

@@ -6,9 +6,11 @@ and lm_head are replicated, so sampling and the residual stream stay local.
 Per decoder layer:
 
   reduce(+residual)+RMSNorm of my rows -> heap       (fused kernel)
-  QKV   = all-gather->GEMM: the tcgen05 GEMM TMA-loads each 64-row block of
-          the normed activations straight from its owner's heap (no gathered
-          copy), computing my heads for ALL rows
+  QKV   = all-gather->GEMM: at kernel start the GEMM's CTAs copy each peer's
+          64-row blocks of normed activations into a local staging buffer
+          (every row crosses NVLink once) and flag them; a tile waits for its
+          blocks and TMA-loads them locally, starting on this rank's own rows,
+          so the copies overlap the first tiles. Computes my heads for ALL rows
   attention on my heads for all sequences (KV cache holds my kv heads only)
   O     = GEMM->reduce-scatter: the epilogue stores each output row into its
           owner's slot buffer with P2P stores; the owner sums the W slots in
@@ -94,6 +96,10 @@ class TPRolloutEngine:
         self.o_slots, self.slots = self.heap.alloc(self.W * self.R * H)
         C = ops.native()
         self.hn_peers = C.symm_peer_addrs(self.heap.id, self.o_hn)
+        # all-gather staging: each peer row block is copied here once per GEMM
+        self.stage = torch.empty(self.W * self.R * H, dtype=weights.dtype, device=weights.device)
+        self.flags = torch.zeros(self.W * self.R // 64, dtype=torch.int32, device=weights.device)
+        self.ag_epoch = 0
         self.slot_peers = C.symm_peer_addrs(self.heap.id, self.o_slots)
         self.max_pages = (max_seq_len + page_size - 1) // page_size
         n_pages = self.W * self.S * self.max_pages + 1
@@ -120,7 +126,7 @@ class TPRolloutEngine:
         for li, L in enumerate(self.shard.layers):
             self.heap.barrier()                                    # every rank's normed rows ready
             qkv = torch.empty(M, (hq + 2 * hkv) * D, dtype=x.dtype, device=x.device)
-            C.gemm_tp_bf16(None, self.hn_peers, H, M, L["qkv"], qkv, [], 0, rows, r)
+            C.gemm_tp_bf16(None, self.hn_peers, H, M, L["qkv"], qkv, [], 0, rows, r, *self._ag())
             qk = ops.qk_norm_rope_fwd(qkv, L["q_norm"], L["k_norm"], pos, self.cos, self.sin, hq, hkv, self.eps)
             q = qk[:, : hq * D].view(M, hq, D)
             k = qk[:, hq * D:].view(M, hkv, D)
@@ -133,7 +139,7 @@ class TPRolloutEngine:
             C.tp_reduce_norm(self.slots, W, rows, x, L["ln2"], hn, self.eps)
             self.heap.barrier()
             gu = torch.empty(M, 2 * self.shard.F, dtype=x.dtype, device=x.device)
-            C.gemm_tp_bf16(None, self.hn_peers, H, M, L["gate_up"], gu, [], 0, rows, r)
+            C.gemm_tp_bf16(None, self.hn_peers, H, M, L["gate_up"], gu, [], 0, rows, r, *self._ag())
             a = ops.swiglu_fwd(gu)
             self.heap.barrier()
             C.gemm_tp_bf16(a, [], 0, M, L["down"], None, self.slot_peers, H, rows, r)
@@ -141,6 +147,10 @@ class TPRolloutEngine:
             nxt = self.shard.layers[li + 1]["ln1"] if li + 1 < len(self.shard.layers) else self.shard.norm
             C.tp_reduce_norm(self.slots, W, rows, x, nxt, hn, self.eps)
         return hn                                                  # final-normed rows
+
+    def _ag(self):
+        self.ag_epoch += 1
+        return self.stage, self.flags, self.ag_epoch
 
     def _logits(self, h_rows):
         return ops.mm(h_rows, self.shard.lm_head)
