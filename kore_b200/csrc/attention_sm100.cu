@@ -56,20 +56,6 @@ KORE_DEV uint64_t mnmajor_desc(uint32_t base, int kk) {
   return make_sw128_desc(base + kk * 2048, 16384, 1024);
 }
 
-// Write a thread's 128 fp32 values (one tile row) as bf16 into a K-major SW128 tile.
-KORE_DEV void store_row_sw128(uint8_t* tile, int row, const float* v) {
-#pragma unroll
-  for (int c = 0; c < 16; ++c) {  // 16 chunks of 8 values
-    uint4 u;
-    u.x = pack_bf16(v[8 * c + 0], v[8 * c + 1]);
-    u.y = pack_bf16(v[8 * c + 2], v[8 * c + 3]);
-    u.z = pack_bf16(v[8 * c + 4], v[8 * c + 5]);
-    u.w = pack_bf16(v[8 * c + 6], v[8 * c + 7]);
-    uint8_t* atom = tile + (c >> 3) * 16384;
-    *reinterpret_cast<uint4*>(atom + row * 128 + (((c & 7) ^ (row & 7)) * 16)) = u;
-  }
-}
-
 struct FwdParams {
   const int* cu_seqlens;
   int nseq;
@@ -81,14 +67,17 @@ struct FwdParams {
   int T;
 };
 
+// P lives in TMEM (aliasing its S buffer) and feeds the PV product as the
+// TMEM operand, which frees shared memory for three K and V stages.
+constexpr int kFwdStages = 3;
 struct FwdSmem {
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE_BYTES;             // 2 stages
-  static constexpr int V_OFF = K_OFF + 2 * TILE_BYTES;  // 2 stages
-  static constexpr int P_OFF = V_OFF + 2 * TILE_BYTES;  // 2 buffers
-  static constexpr int BAR_OFF = P_OFF + 2 * TILE_BYTES;
+  static constexpr int K_OFF = TILE_BYTES;                       // kFwdStages stages
+  static constexpr int V_OFF = K_OFF + kFwdStages * TILE_BYTES;  // kFwdStages stages
+  static constexpr int BAR_OFF = V_OFF + kFwdStages * TILE_BYTES;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
+static_assert(FwdSmem::TOTAL <= 227 * 1024, "fwd smem");
 
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -99,14 +88,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* p_full = bars + 11;  // [2]
-  uint64_t* o_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* k_full = bars + 1;    // [kFwdStages]
+  uint64_t* k_empty = bars + 4;   // [kFwdStages]
+  uint64_t* v_full = bars + 7;    // [kFwdStages]
+  uint64_t* v_empty = bars + 10;  // [kFwdStages]
+  uint64_t* s_full = bars + 13;   // [2]
+  uint64_t* p_full = bars + 15;   // [2]
+  uint64_t* o_done = bars + 17;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   // ---- work item: longest (latest) query blocks first
@@ -124,11 +113,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kFwdStages; ++i) {
       mbar_init(&k_full[i], 1);
       mbar_init(&k_empty[i], 1);
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&p_full[i], 4);
     }
@@ -148,8 +139,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_load_2d(smem + S::Q_OFF, &tmQ, q_full, h * D, s0 + q0);
       tma_load_2d(smem + S::Q_OFF + 16384, &tmQ, q_full, h * D + 64, s0 + q0);
       for (int j = 0; j < nkv && !*abort_flag; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
+        const int st = j % kFwdStages;
+        const uint32_t ph = (j / kFwdStages) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1)) { *abort_flag = 1; break; }
         uint8_t* kt = smem + S::K_OFF + st * TILE_BYTES;
         mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
@@ -165,36 +156,37 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else if (warp == 1) {
     constexpr uint32_t idesc_qk = make_idesc_bf16(BQ, BKV, false, false);
-    constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, false, true);
+    constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, false, true);   // A = P from TMEM (K-major)
     if (elect_one()) {
       const uint32_t qa = smem_u32(smem + S::Q_OFF);
       bool ok = mbar_wait(q_full, 0);
       auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&k_full[st], (j >> 1) & 1)) return false;
+        const int ks = j % kFwdStages;
+        if (!mbar_wait(&k_full[ks], (j / kFwdStages) & 1)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(smem + S::K_OFF + st * TILE_BYTES);
+        const uint32_t ka = smem_u32(smem + S::K_OFF + ks * TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem + st * 128, kmajor_desc(qa, kk), kmajor_desc(ka, kk), idesc_qk, kk > 0);
-        umma_commit(&k_empty[st]);
-        umma_commit(&s_full[st]);
+          umma_f16_ss(tmem + (j & 1) * 128, kmajor_desc(qa, kk), kmajor_desc(ka, kk), idesc_qk, kk > 0);
+        umma_commit(&k_empty[ks]);
+        umma_commit(&s_full[j & 1]);
         return true;
       };
       if (ok) ok = issue_s(0);
       for (int j = 0; j < nkv && ok; ++j) {
+        // S_{j+1} goes into the buffer whose P_{j-1} the already-issued PV_{j-1} reads (in-order pipe)
         if (j + 1 < nkv && !issue_s(j + 1)) { ok = false; break; }
         const int st = j & 1;
+        const int vs = j % kFwdStages;
         if (!mbar_wait(&p_full[st], (j >> 1) & 1)) { ok = false; break; }
-        if (!mbar_wait(&v_full[st], (j >> 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(&v_full[vs], (j / kFwdStages) & 1)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t pa = smem_u32(smem + S::P_OFF + st * TILE_BYTES);
-        const uint32_t va = smem_u32(smem + S::V_OFF + st * TILE_BYTES);
+        const uint32_t va = smem_u32(smem + S::V_OFF + vs * TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)
-          umma_f16_ss(tmem + 256, kmajor_desc(pa, kk), mnmajor_desc(va, kk), idesc_pv,
+        for (int kk = 0; kk < BKV / 16; ++kk)   // P_j: 64 TMEM columns of packed bf16 pairs, 8 per K-step
+          umma_f16_ts(tmem + 256, tmem + st * 128 + kk * 8, mnmajor_desc(va, kk), idesc_pv,
                       (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&v_empty[st]);
+        umma_commit(&v_empty[vs]);
         umma_commit(o_done);
       }
       if (!ok) *abort_flag = 1;
@@ -260,8 +252,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         rs += sv[i];
       }
       l += rs;
-      store_row_sw128(smem + S::P_OFF + st * TILE_BYTES, row, sv);
-      fence_proxy_async_smem();
+      {   // P_j as packed bf16 pairs over the first 64 columns of its S buffer
+        uint32_t pk[2][32];
+#pragma unroll
+        for (int i = 0; i < 64; ++i) pk[i >> 5][i & 31] = pack_bf16(sv[2 * i], sv[2 * i + 1]);
+        tmem_st32(tmem + lane_base + st * 128, pk[0]);
+        tmem_st32(tmem + lane_base + st * 128 + 32, pk[1]);
+        tmem_wait_st();
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[st]);
