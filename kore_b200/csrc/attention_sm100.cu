@@ -357,7 +357,7 @@ struct BwdParams {
 constexpr int BQB = 64;                           // query rows per backward iteration
 constexpr int QTILE_BYTES = BQB * D * 2;          // 16 KB: 64 rows as two 8 KB swizzle atoms
 constexpr int PTILE_BYTES = BKV * BQB * 2;        // 16 KB: 128 kv rows x 64 q cols, one atom
-constexpr int kBwdThreads = 320;                  // producer, MMA, 4 softmax, 4 dQ warps
+constexpr int kBwdThreads = 448;                  // producer, MMA, 8 softmax (two per kv row), 4 dQ warps
 
 struct BwdSmem {
   static constexpr int K_OFF = 0;                             // 32 KB
@@ -366,7 +366,8 @@ struct BwdSmem {
   static constexpr int DO_OFF = Q_OFF + 2 * QTILE_BYTES;      // 2 stages x 16 KB
   static constexpr int PT_OFF = DO_OFF + 2 * QTILE_BYTES;     // 2 buffers x 16 KB
   static constexpr int DS_OFF = PT_OFF + 2 * PTILE_BYTES;     // 2 buffers x 16 KB
-  static constexpr int VEC_OFF = DS_OFF + 2 * PTILE_BYTES;    // [2][lse2 64 | delta 64]
+  static constexpr int DQ_OFF = DS_OFF + 2 * PTILE_BYTES;     // [64 q][128 d] fp32 dQ staging, 32 KB
+  static constexpr int VEC_OFF = DQ_OFF + BQB * D * 4;         // [2][lse2 64 | delta 64]
   static constexpr int BAR_OFF = VEC_OFF + 1024;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
@@ -417,7 +418,7 @@ KORE_DEV BwdItem bwd_item(const BwdParams& p) {
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    BwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, BwdParams p) {
   using S = BwdSmem;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -455,11 +456,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&qdo_full[i], 1);
       mbar_init(&qdo_empty[i], 1);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&p_full[i], 8);
       mbar_init(&p_empty[i], 1);
     }
     mbar_init(s_full, 1);
-    mbar_init(s_free, 4);
+    mbar_init(s_free, 8);
     mbar_init(dq_full, 1);
     mbar_init(dq_empty, 4);
     mbar_init(all_done, 1);
@@ -547,65 +548,62 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       else *abort_flag = 1;
     }
     __syncwarp();
-  } else if (warp < 6) {
-    // ---- softmax warps: one kv row per thread
+  } else if (warp < 10) {
+    // ---- softmax warps: two per kv row, each on 32 of the 64 query columns
     const int q4 = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int lane = threadIdx.x & 31;
     const int row = q4 * 32 + lane;
-    const int tid = threadIdx.x - 64;  // 0..127
+    const int tid = threadIdx.x - 64;  // 0..255; 0..127 also stage lse2 / delta
     const int kvi = k0 + row;
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     bool ok = true;
-    auto vec_load = [&](int i) -> float {  // lse2 (tid < 64) or delta (tid >= 64) of iteration i
+    auto vec_load = [&](int i) -> float {  // lse2 (tid < 64) or delta (64 <= tid < 128) of iteration i
+      if (tid >= 128) return 0.f;
       const int h = kvh * G + i / per_head;
       const int qi = (qb0 + i % per_head) * BQB + (tid & 63);
       if (qi >= len) return tid < 64 ? INFINITY : 0.f;
       return tid < 64 ? p.lse[(size_t)h * p.T + s0 + qi] * kLog2e : p.delta[(size_t)h * p.T + s0 + qi];
     };
-    if (iters > 0) s_vec[tid] = vec_load(0);
+    if (iters > 0 && tid < 128) s_vec[tid] = vec_load(0);
     // after a failed wait the loop keeps running (no waits, no work) so every
     // softmax thread still reaches each named barrier
     for (int i = 0; i < iters; ++i) {
       const int q0 = (qb0 + i % per_head) * BQB;
       const int st = i & 1;
       const float nxt = (i + 1 < iters) ? vec_load(i + 1) : 0.f;   // prefetch next iteration's statistics
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       if (!ok) continue;
-      const float* lse2 = s_vec + st * 128;
-      const float* dlt = lse2 + 64;
+      const float* lse2 = s_vec + st * 128 + half * 32;
+      const float* dlt = s_vec + st * 128 + 64 + half * 32;
       if (!mbar_wait(s_full, i & 1)) { ok = false; *abort_flag = 1; continue; }
       tc_fence_after();
-      uint32_t rs[2][32], rp[2][32];
-      tmem_ld32(tmem + lane_base + T_S, rs[0]);
-      tmem_ld32(tmem + lane_base + T_S + 32, rs[1]);
-      tmem_ld32(tmem + lane_base + T_DP, rp[0]);
-      tmem_ld32(tmem + lane_base + T_DP + 32, rp[1]);
+      uint32_t rs[32], rp[32];
+      tmem_ld32(tmem + lane_base + T_S + half * 32, rs);
+      tmem_ld32(tmem + lane_base + T_DP + half * 32, rp);
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
       if (!mbar_wait(&p_empty[st], ((i >> 1) & 1) ^ 1)) { ok = false; *abort_flag = 1; continue; }
       const bool diag = q0 < k0 + BKV;
+      // P and dS overwrite the raw registers in place (no extra live arrays)
+      float* pv = reinterpret_cast<float*>(rs);
+      float* dv = reinterpret_cast<float*>(rp);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        // P and dS overwrite the raw registers in place (no extra live arrays)
-        float* pv = reinterpret_cast<float*>(rs[c]);
-        float* dv = reinterpret_cast<float*>(rp[c]);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int qc = c * 32 + e;
-          float pr = exp2f(__uint_as_float(rs[c][e]) * p.scale_log2 - lse2[qc]);
-          if ((diag && q0 + qc < kvi) || kvi >= len) pr = 0.f;
-          dv[e] = pr * (__uint_as_float(rp[c][e]) - dlt[qc]);
-          pv[e] = pr;
-        }
-        store_row32_sw128(smem + S::PT_OFF + st * PTILE_BYTES, row, c, pv);
-        store_row32_sw128(smem + S::DS_OFF + st * PTILE_BYTES, row, c, dv);
+      for (int e = 0; e < 32; ++e) {
+        const int qc = half * 32 + e;
+        float pr = exp2f(__uint_as_float(rs[e]) * p.scale_log2 - lse2[e]);
+        if ((diag && q0 + qc < kvi) || kvi >= len) pr = 0.f;
+        dv[e] = pr * (__uint_as_float(rp[e]) - dlt[e]);
+        pv[e] = pr;
       }
+      store_row32_sw128(smem + S::PT_OFF + st * PTILE_BYTES, row, half, pv);
+      store_row32_sw128(smem + S::DS_OFF + st * PTILE_BYTES, row, half, dv);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[st]);
-      s_vec[(st ^ 1) * 128 + tid] = nxt;   // buffer st^1 was last read in iteration i-1
+      if (tid < 128) s_vec[(st ^ 1) * 128 + tid] = nxt;   // buffer st^1 was last read in iteration i-1
     }
     if (ok && iters > 0 && mbar_wait(all_done, 0)) {
       tc_fence_after();
@@ -617,7 +615,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         __nv_bfloat16* out = part == 0 ? dvrow : dkrow;
         const float mul = part == 0 ? 1.f : p.scale;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int cc = 0; cc < 2; ++cc) {
+          const int c = half * 2 + cc;   // this warp's 64 of the 128 head-dim columns
           uint32_t r[32];
           tmem_ld32(tmem + lane_base + (part == 0 ? T_DV : T_DK) + c * 32, r);
           tmem_wait_ld();
@@ -638,34 +637,48 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       *abort_flag = 1;
     }
   } else {
-    // ---- dQ warps: one head-dim lane per thread; dQ^T columns are query rows
+    // ---- dQ warps: one head-dim lane per thread; dQ^T columns are query rows.
+    // The 64 x 128 fp32 partial goes through shared memory into one TMA
+    // reduce-add per iteration (whole 512-byte rows, no per-element atomics).
     const int q4 = warp & 3;
     const int lane = threadIdx.x & 31;
     const int d = q4 * 32 + lane;
+    const bool leader = threadIdx.x == 10 * 32;
+    float* stage = reinterpret_cast<float*>(smem + S::DQ_OFF);
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+    bool ok = true;
     for (int j = 0; j < iters; ++j) {
       const int h = kvh * G + j / per_head;
       const int q0 = (qb0 + j % per_head) * BQB;
-      if (!mbar_wait(dq_full, j & 1)) { *abort_flag = 1; break; }
-      tc_fence_after();
       uint32_t r[2][32];
-      tmem_ld32(tmem + lane_base + T_DQ, r[0]);
-      tmem_ld32(tmem + lane_base + T_DQ + 32, r[1]);
-      tmem_wait_ld();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_empty);
-      float* dst = p.dq_acc + ((size_t)(s0 + q0) * p.Hq + h) * D + d;
-      const size_t rstride = (size_t)p.Hq * D;
+      if (ok && !mbar_wait(dq_full, j & 1)) { ok = false; *abort_flag = 1; }
+      if (ok) {
+        tc_fence_after();
+        tmem_ld32(tmem + lane_base + T_DQ, r[0]);
+        tmem_ld32(tmem + lane_base + T_DQ + 32, r[1]);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(dq_empty);
+      }
+      if (leader) tma_store_wait_read<0>();   // the previous reduce has read the staging buffer
+      named_bar_sync(2, 128);
+      if (ok) {
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int qc = c * 32 + e;
-          if (q0 + qc < len) atomicAdd(dst + qc * rstride, __uint_as_float(r[c][e]) * p.scale);
-        }
+          for (int e = 0; e < 32; ++e) stage[(c * 32 + e) * D + d] = __uint_as_float(r[c][e]) * p.scale;
+      }
+      fence_proxy_async_smem();
+      named_bar_sync(2, 128);
+      // rows past the sequence hold exact zeros (their dS is zero), so adding
+      // them into the next sequence's rows changes nothing; rows past T are clipped
+      if (ok && leader) {
+        tma_reduce_add_3d(&tmDQ, stage, 0, h, s0 + q0);
+        tma_store_commit();
       }
     }
+    if (leader) tma_store_wait_all<0>();
   }
   tc_fence_before();
   __syncthreads();
@@ -679,6 +692,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // tmQ / tmDO: 64-row boxes; tmK / tmV: 128-row boxes.
 inline cudaError_t launch_bwd_main(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv,
                                    const CUtensorMap& tdo, const BwdParams& p, cudaStream_t st) {
+  // dQ accumulator [T, Hq, 128] fp32 as a 3-D map (d, head, token) for the reduce-add boxes
+  CUtensorMap tdq;
+  try {
+    tdq = make_tmap_3d(p.dq_acc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, D, p.Hq, p.T, D, (uint64_t)p.Hq * D, D, 1, BQB,
+                       CU_TENSOR_MAP_SWIZZLE_NONE);
+  } catch (...) {   // callers include a C entry point: no exceptions across it
+    return cudaErrorInvalidValue;
+  }
   static bool attr[64] = {};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -689,7 +710,7 @@ inline cudaError_t launch_bwd_main(const CUtensorMap& tq, const CUtensorMap& tk,
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  attn_bwd_kernel<<<p.nseq * p.nkblk * p.Hkv, kBwdThreads, BwdSmem::TOTAL, st>>>(tq, tk, tv, tdo, p);
+  attn_bwd_kernel<<<p.nseq * p.nkblk * p.Hkv, kBwdThreads, BwdSmem::TOTAL, st>>>(tq, tk, tv, tdo, tdq, p);
   return cudaGetLastError();
 }
 

@@ -134,6 +134,14 @@ KORE_DEV void tma_store_2d(const CUtensorMap* d, const void* smem_src, int x, in
                "r"(smem_u32(smem_src)), "r"(x), "r"(y)
                : "memory");
 }
+// Element-wise atomic add of a shared-memory box into global memory (TMA reduce).
+KORE_DEV void tma_reduce_add_3d(const CUtensorMap* d, const void* smem_src, int x, int y, int z) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(d)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y), "r"(z)
+      : "memory");
+}
 KORE_DEV void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 template <int N>
 KORE_DEV void tma_store_wait_read() {
