@@ -178,6 +178,12 @@ def main(argv=None):
     ctx.barrier()
     clocks = clk.stop()
     launches = ops.launch_count()
+    mstats = torch.cuda.memory_stats()
+    memory = {"peak_allocated_gb": round(torch.cuda.max_memory_allocated() / 1e9, 2),
+              "reserved_gb": round(torch.cuda.memory_reserved() / 1e9, 2),
+              "alloc_retries": int(mstats.get("num_alloc_retries", 0)),
+              "device_mallocs": int(mstats.get("num_device_alloc", 0)),
+              "device_frees": int(mstats.get("num_device_free", 0))}
     dev_ms = e0.elapsed_time(e1) / args.steps
     ms = ctx.max_over_ranks(dev_ms)
     loss_v = float(loss.item())
@@ -221,7 +227,7 @@ def main(argv=None):
                        "loss": "last 50% of each sequence", "micro_batch": args.micro_batch,
                        "optimizer": f"AdamW fp32 moments, master={trainer.master_mode}",
                        "l2": "inputs larger than L2 (29.5 GB of weights streamed per step)"},
-            "loss": loss_v, "clocks": clocks, "gpu_launches": launches, "e2e": e2e,
+            "loss": loss_v, "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "memory": memory,
             "impl": "kore",
         }
         print(json.dumps(out), flush=True)

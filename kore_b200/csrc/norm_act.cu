@@ -62,30 +62,33 @@ constexpr int kNormThreads = 128;
 constexpr int kMaxVecPerThread = 8;  // H <= 128 * 8 * 8 = 8192
 
 // ---------------------------------------------------------------- RMSNorm fwd
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(
+// THREADS x VPT 8-element vectors cover a row (H <= THREADS * VPT * 8); the
+// template keeps the per-thread arrays exactly as large as the row needs.
+template <int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS) rmsnorm_fwd_kernel(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
     __nv_bfloat16* __restrict__ y, float* __restrict__ rstd_out, int rows, int H, float eps) {
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[THREADS / 32];
   const int nvec = H / 8;
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const __nv_bfloat16* xr = x + (size_t)r * H;
-    float v[kMaxVecPerThread][8];
+    float v[VPT][8];
     float ss = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxVecPerThread; ++i) {
-      int j = threadIdx.x + i * kNormThreads;
+    for (int i = 0; i < VPT; ++i) {
+      int j = threadIdx.x + i * THREADS;
       if (j < nvec) {
         load8(xr + j * 8, v[i]);
 #pragma unroll
         for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
       }
     }
-    ss = block_sum<kNormThreads>(ss, red);
+    ss = block_sum<THREADS>(ss, red);
     const float rs = rsqrtf(ss / H + eps);
     if (rstd_out && threadIdx.x == 0) rstd_out[r] = rs;
 #pragma unroll
-    for (int i = 0; i < kMaxVecPerThread; ++i) {
-      int j = threadIdx.x + i * kNormThreads;
+    for (int i = 0; i < VPT; ++i) {
+      int j = threadIdx.x + i * THREADS;
       if (j < nvec) {
         float wv[8];
         load8(w + j * 8, wv);
@@ -99,25 +102,26 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(
 
 // ---------------------------------------------------------------- RMSNorm bwd
 // dx = rstd * (w*dy - xhat * mean(xhat*w*dy)) (+ dres);  dw += sum_rows dy*xhat
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
+template <int THREADS, int VPT>
+__global__ void __launch_bounds__(THREADS) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
     const __nv_bfloat16* __restrict__ w, const float* __restrict__ rstd,
     const __nv_bfloat16* __restrict__ dres, __nv_bfloat16* __restrict__ dx,
     float* __restrict__ dw, int rows, int H) {
-  __shared__ float red[kNormThreads / 32];
+  __shared__ float red[THREADS / 32];
   const int nvec = H / 8;
-  float dwacc[kMaxVecPerThread][8];
+  float dwacc[VPT][8];
 #pragma unroll
-  for (int i = 0; i < kMaxVecPerThread; ++i)
+  for (int i = 0; i < VPT; ++i)
 #pragma unroll
     for (int e = 0; e < 8; ++e) dwacc[i][e] = 0.f;
   for (int r = blockIdx.x; r < rows; r += gridDim.x) {
     const float rs = rstd[r];
-    float xv[kMaxVecPerThread][8], g[kMaxVecPerThread][8];
+    float xv[VPT][8], g[VPT][8];
     float dot = 0.f;
 #pragma unroll
-    for (int i = 0; i < kMaxVecPerThread; ++i) {
-      int j = threadIdx.x + i * kNormThreads;
+    for (int i = 0; i < VPT; ++i) {
+      int j = threadIdx.x + i * THREADS;
       if (j < nvec) {
         float wv[8];
         load8(x + (size_t)r * H + j * 8, xv[i]);
@@ -133,10 +137,10 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
         }
       }
     }
-    dot = block_sum<kNormThreads>(dot, red) / H;
+    dot = block_sum<THREADS>(dot, red) / H;
 #pragma unroll
-    for (int i = 0; i < kMaxVecPerThread; ++i) {
-      int j = threadIdx.x + i * kNormThreads;
+    for (int i = 0; i < VPT; ++i) {
+      int j = threadIdx.x + i * THREADS;
       if (j < nvec) {
         float o[8];
 #pragma unroll
@@ -153,8 +157,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(
   }
   if (dw) {
 #pragma unroll
-    for (int i = 0; i < kMaxVecPerThread; ++i) {
-      int j = threadIdx.x + i * kNormThreads;
+    for (int i = 0; i < VPT; ++i) {
+      int j = threadIdx.x + i * THREADS;
       if (j < nvec)
 #pragma unroll
         for (int e = 0; e < 8; ++e) atomicAdd(dw + j * 8 + e, dwacc[i][e]);
@@ -399,10 +403,19 @@ void rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, at::Tensor& y,
   TORCH_CHECK(H % 8 == 0 && H <= kNormThreads * kMaxVecPerThread * 8, "rmsnorm: unsupported H");
   if (rows == 0) return;
   c10::cuda::CUDAGuard g(x.device());
-  int grid = (int)std::min<long>(rows, (long)num_sms(x.get_device()) * 8);
-  rmsnorm_fwd_kernel<<<grid, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
-      (__nv_bfloat16*)y.data_ptr(), rstd ? rstd->data_ptr<float>() : nullptr, rows, H, (float)eps);
+  const int nvec = H / 8;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int sms = num_sms(x.get_device());
+#define KORE_RMS_FWD(T, V)                                                                           \
+  rmsnorm_fwd_kernel<T, V><<<(int)std::min<long>(rows, (long)sms * (2048 / T)), T, 0, st>>>(          \
+      (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(), \
+      rstd ? rstd->data_ptr<float>() : nullptr, rows, H, (float)eps)
+  if (nvec <= 256) KORE_RMS_FWD(256, 1);
+  else if (nvec <= 512) KORE_RMS_FWD(256, 2);
+  else if (nvec <= 768) KORE_RMS_FWD(256, 3);
+  else if (nvec <= 1024) KORE_RMS_FWD(256, 4);
+  else KORE_RMS_FWD(128, 8);
+#undef KORE_RMS_FWD
   check_cuda(cudaGetLastError(), "rmsnorm_fwd");
 }
 
@@ -417,12 +430,22 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   if (rows == 0) return;
   if (dw) TORCH_CHECK(dw->scalar_type() == at::kFloat && dw->numel() == H, "dw must be fp32 [H]");
   c10::cuda::CUDAGuard g(x.device());
-  int grid = (int)std::min<long>(rows, (long)num_sms(x.get_device()) * 4);
-  rmsnorm_bwd_kernel<<<grid, kNormThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
-      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(),
-      (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(),
-      dres ? (const __nv_bfloat16*)dres->data_ptr() : nullptr, (__nv_bfloat16*)dx.data_ptr(),
-      dw ? dw->data_ptr<float>() : nullptr, rows, H);
+  const int nvec = H / 8;
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int sms = num_sms(x.get_device());
+  // persistent blocks (two 256-thread blocks per SM) accumulate dw over their rows
+#define KORE_RMS_BWD(T, V)                                                                           \
+  rmsnorm_bwd_kernel<T, V><<<(int)std::min<long>(rows, (long)sms * (512 / T)), T, 0, st>>>(           \
+      (const __nv_bfloat16*)dy.data_ptr(), (const __nv_bfloat16*)x.data_ptr(),                         \
+      (const __nv_bfloat16*)w.data_ptr(), rstd.data_ptr<float>(),                                     \
+      dres ? (const __nv_bfloat16*)dres->data_ptr() : nullptr, (__nv_bfloat16*)dx.data_ptr(),         \
+      dw ? dw->data_ptr<float>() : nullptr, rows, H)
+  if (nvec <= 256) KORE_RMS_BWD(256, 1);
+  else if (nvec <= 512) KORE_RMS_BWD(256, 2);
+  else if (nvec <= 768) KORE_RMS_BWD(256, 3);
+  else if (nvec <= 1024) KORE_RMS_BWD(256, 4);
+  else KORE_RMS_BWD(128, 8);
+#undef KORE_RMS_BWD
   check_cuda(cudaGetLastError(), "rmsnorm_bwd");
 }
 
