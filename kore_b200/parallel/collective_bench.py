@@ -15,6 +15,9 @@ baselines, each reported against its roofline (run under torchrun, >= 2 GPUs):
     reduce-scatter (P2P-store epilogue + fused reduce) versus GEMM + NCCL
     reduce-scatter. Roofline: max(FLOPs / measured bf16 peak, NVLink bytes /
     link bandwidth).
+(d) MoE dispatch and combine (P2P scatter into the owners' expert-major
+    buffers; pull-combine with routing weights and residual) versus permute +
+    NCCL all-to-all. Roofline: the token rows crossing NVLink at link bandwidth.
 
 Every number is CUDA-event time on the launching stream after warm-up, max
 over ranks. Prints one JSON line per path from rank 0.
@@ -155,18 +158,85 @@ def bench_tp(ctx, rows: int, K: int, N_local: int) -> list:
     return res
 
 
+def bench_ep(ctx, tokens: int) -> list:
+    """(d) MoE dispatch / combine for the Qwen3-Coder-30B-A3B shape (H 2048,
+    128 experts, top-8): fused P2P scatter into the owners' expert-major
+    buffers vs permute + NCCL all-to-all; fused pull-combine with the routing
+    weights and residual vs NCCL all-to-all back + weighted sum."""
+    from .. import ops
+    from ..models.config import qwen3_coder_30b_a3b
+    from .ep import FusedExpertParallel
+    from .symmetric import SymmetricHeap
+    C = ops.native()
+    cfg = qwen3_coder_30b_a3b()
+    W, r = ctx.world, ctx.rank
+    E, k, H = cfg.num_experts, cfg.num_experts_per_tok, cfg.hidden_size
+    El = E // W
+    cap = int(2.0 * tokens * k)
+    heap = SymmetricHeap(ctx, 4 * cap * H * 2 + (1 << 20))
+    fep = FusedExpertParallel(ctx, cfg, r * El, (r + 1) * El, heap, cap)
+    g = torch.Generator(device="cuda").manual_seed(11 + r)
+    logits = torch.randn(tokens, E, device="cuda", generator=g)
+    wts, idx = torch.softmax(logits, -1).topk(k, -1)
+    wts = (wts / wts.sum(-1, keepdim=True)).float().contiguous()
+    x = torch.randn(tokens, H, device="cuda", dtype=torch.bfloat16)
+    dst_rank, dst_row, offs, rmax = fep._route_rows(idx)
+    fep.ybuf.zero_()
+    src_row = torch.arange(tokens * k, device="cuda") // k
+    y = torch.empty_like(x)
+    # NCCL arm: rows grouped by destination rank; split sizes exchanged once, outside the timing
+    order = torch.argsort(dst_rank.long(), stable=True)
+    send = torch.bincount(dst_rank.long(), minlength=W)
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send, group=ctx.group)
+    ss, rs_ = send.tolist(), recv.tolist()
+    rbuf = torch.empty(sum(rs_), H, device="cuda", dtype=torch.bfloat16)
+    back = torch.empty(tokens * k, H, device="cuda", dtype=torch.bfloat16)
+
+    def disp_fused():
+        C.symm_ep_scatter(heap.id, fep.o_recv, x, src_row, dst_rank, dst_row, None)
+        heap.barrier()
+
+    def disp_nccl():
+        sbuf = x.index_select(0, src_row[order])
+        dist.all_to_all_single(rbuf, sbuf, rs_, ss, group=ctx.group)
+
+    def comb_fused():
+        heap.barrier()
+        C.symm_ep_gather(heap.id, fep.o_y, dst_rank.view(tokens, k), dst_row.view(tokens, k), wts, x, y, None,
+                         None, H)
+
+    def comb_nccl():
+        dist.all_to_all_single(back, rbuf, ss, rs_, group=ctx.group)
+        rows = torch.empty_like(back)
+        rows[order] = back
+        torch.add(x, (rows.view(tokens, k, H).float() * wts[..., None]).sum(1).to(x.dtype), out=y)
+
+    link = 2.0 * tokens * k * H * (W - 1) / W
+    res = []
+    for name, ff, fn in (("d_moe_dispatch", disp_fused, disp_nccl), ("d_moe_combine", comb_fused, comb_nccl)):
+        tf, tn = _time(ff, ctx), _time(fn, ctx)
+        roof = link / LINK_BPS * 1e3
+        res.append({"path": name, "world": W, "tokens": tokens, "H": H, "topk": k, "fused_ms": tf, "nccl_ms": tn,
+                    "roofline_ms": roof, "fused_frac_of_roofline": roof / tf, "nccl_frac_of_roofline": roof / tn,
+                    "speedup_vs_nccl": tn / tf})
+    return res
+
+
 def main(argv=None) -> int:
     from .dist import init_distributed
     ap = argparse.ArgumentParser()
     ap.add_argument("--params", type=int, default=2_000_000_000)
     ap.add_argument("--units", type=int, default=8)
     ap.add_argument("--rows", type=int, default=2048, help="TP rows per rank")
+    ap.add_argument("--ep-tokens", type=int, default=8192, help="MoE tokens per rank")
     a = ap.parse_args(argv)
     ctx = init_distributed()
     out = [bench_optimizer(ctx, a.params, a.units)]
     W = ctx.world
     out += bench_tp(ctx, a.rows, 5120, (40 + 16) * 128 // W)    # QKV projection of the 14B model
     out += bench_tp(ctx, a.rows, 5120, 2 * 17408 // W)          # gate|up projection
+    out += bench_ep(ctx, a.ep_tokens)
     if ctx.is_main:
         for r in out:
             print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}), flush=True)
