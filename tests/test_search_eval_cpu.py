@@ -120,3 +120,32 @@ def test_agent_tool_call_parsing():
     calls = parse_tool_calls(txt)
     assert calls and calls[0]["name"] == "test" and calls[0]["arguments"]["source"] == "x"
     assert "test" in format_tool_result("test", {"correct": True})
+
+
+def test_eval_suites(tmp_path):
+    import types
+    from kore_b200.data.schemas import WinRecord
+    from kore_b200.eval.suite import KOREBENCH_V1, champion_reeval, head_to_head, korebench, write_report
+    from kore_b200.tasks.ops_library import SPECS
+    from kore_b200.tasks.registry import get_task
+    assert all(t in SPECS for t in KOREBENCH_V1)
+
+    class Env:
+        def __init__(self, t):
+            self.t = t
+
+        def step(self, src):
+            fast = "fast" in src
+            return types.SimpleNamespace(validation_passed=True, compiled=True, wall_ms=1.0,
+                                         wall_by_shape={"primary": 1.0 if fast else 2.0},
+                                         baseline_by_shape={"primary": 1.5}, cv_by_shape=None)
+    tasks = [get_task(t) for t in KOREBENCH_V1[:3]]
+    h = head_to_head(lambda t: ["fast"], lambda t: ["slow"], tasks, Env)
+    assert h["a_win_rate"] == 1.0
+    kb = korebench(lambda t: ["fast"], Env, KOREBENCH_V1[:4])
+    assert kb["fast_1.0"] == 1.0 and kb["fast_1.5"] == 1.0
+    ch = champion_reeval([WinRecord(KOREBENCH_V1[0], [], 1, 1, 3.0, final_kernel="slow")],
+                         {t.task_id: t for t in tasks}, Env, min_speedup=1.0)
+    assert ch[0]["kept"] is False and ch[0]["claimed"] == 3.0
+    txt = write_report(str(tmp_path / "r.md"), "eval", {"korebench": kb})
+    assert "fast_1.0" in txt
