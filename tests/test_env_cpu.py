@@ -67,3 +67,21 @@ def test_equivalence_oracle_and_coevolution():
     pop = coevolve_tests(mk, lambda x: torch.clamp(x, max=5.0), lambda x: x,
                          lambda a, b: float((a - b).abs().max()), population=6, generations=3)
     assert pop[0][1] > 0
+
+
+def test_adversarial_hook_registry_and_replay(tmp_path):
+    import torch
+    from kore_b200.verify.adversarial_hook import AdversarialHook, AdversarialRegistry
+    reg = AdversarialRegistry(str(tmp_path / "reg.json"))
+    hook = AdversarialHook(reg, every=2, tol=1e-3, population=24, generations=3)
+    make = lambda s: (torch.randn(64, 64, generator=torch.Generator().manual_seed(s)),)
+    oracle = lambda x: torch.softmax(x.double(), -1).float()
+    naive = lambda x: torch.exp(x) / torch.exp(x).sum(-1, keepdim=True)      # overflows on large inputs
+    assert hook.on_accepted("softmax", "fp32", make, naive, oracle) == 0     # throttled: 1st of every 2
+    added = hook.on_accepted("softmax", "fp32", make, naive, oracle)
+    assert added > 0 and reg.genomes("softmax", "fp32")
+    ok, _ = hook.replay("softmax", "fp32", make, naive, oracle)
+    assert not ok
+    ok, _ = hook.replay("softmax", "fp32", make, lambda x: torch.softmax(x, -1), oracle)
+    assert ok
+    assert AdversarialRegistry(str(tmp_path / "reg.json")).genomes("softmax", "fp32")
