@@ -87,3 +87,38 @@ def mint(n: int = 4, seed: int = 0) -> List[str]:
                             "minted")
         made.append(tid)
     return made
+
+
+def materialize(task_id: str, root: str) -> str:
+    """Write a registered (e.g. minted) spec to ``root/<task_id>/`` in the task
+    ABI (task.yaml, reference.py, seed kernel) and self-check that the
+    directory loads back with the same shapes (reference parity:
+    kore/openended/materialize.py:232)."""
+    import inspect
+    import os
+
+    import yaml
+
+    from ..tasks.base import Task
+    spec = SPECS[task_id]
+    d = os.path.join(root, task_id)
+    os.makedirs(d, exist_ok=True)
+    shapes = {k: spec.shapes[k] for k in ("minimal", "primary") if k in spec.shapes}
+    shapes["validation"] = list(spec.shapes.get("validation", []) or [])
+    y = {"task_id": task_id, "operation": spec.operation, "dtype": spec.dtype, "backend": "triton",
+         "gpu_target": "sm_100a", "seed_kernel_name": "seed_kernel.py", "entry": spec.entry, "spec": task_id,
+         "snr_threshold": spec.snr_threshold, "family": spec.family, "shapes": shapes,
+         "targets": {"comparison_baseline": "torch eager in the task dtype"}}
+    with open(os.path.join(d, "task.yaml"), "w") as f:
+        yaml.safe_dump(y, f, sort_keys=False)
+    with open(os.path.join(d, "seed_kernel.py"), "w") as f:
+        f.write(spec.seed_src)
+    try:
+        ref = inspect.getsource(spec.reference)
+    except (OSError, TypeError):
+        ref = f"# reference: {task_id} (generated expression)\n"
+    with open(os.path.join(d, "reference.py"), "w") as f:
+        f.write(ref)
+    t = Task.from_dir(d)
+    assert t.task_id == task_id and [s.dims for s in t.shapes][:1] == [shapes["minimal"]], "materialize self-check"
+    return d

@@ -149,3 +149,12 @@ def test_eval_suites(tmp_path):
     assert ch[0]["kept"] is False and ch[0]["claimed"] == 3.0
     txt = write_report(str(tmp_path / "r.md"), "eval", {"korebench": kb})
     assert "fast_1.0" in txt
+
+
+def test_minted_task_materializes(tmp_path):
+    from kore_b200.openended.minter import materialize, mint
+    tid = mint(1, seed=5)[0]
+    d = materialize(tid, str(tmp_path))
+    from kore_b200.tasks.base import Task
+    t = Task.from_dir(d)
+    assert t.task_id == tid and t.shape("primary").dims == {"M": 4096, "N": 4096}
