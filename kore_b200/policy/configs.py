@@ -331,8 +331,30 @@ def build_fsdp_kwargs(config) -> dict:
     return {"fsdp": s, "fsdp_config": cfg}
 
 
+def checkpoint_intact(path: str) -> bool:
+    """Every safetensors file in ``path`` has a readable header and exactly the
+    bytes its header declares (catches files truncated by a crash mid-save)."""
+    import json as _json
+    import struct
+    for f in glob.glob(os.path.join(path, "*.safetensors")):
+        try:
+            size = os.path.getsize(f)
+            with open(f, "rb") as fh:
+                n = struct.unpack("<Q", fh.read(8))[0]
+                if n <= 0 or 8 + n > size:
+                    return False
+                hdr = _json.loads(fh.read(n))
+            end = max((v["data_offsets"][1] for k, v in hdr.items() if k != "__metadata__"), default=0)
+            if 8 + n + end != size:
+                return False
+        except (OSError, ValueError, KeyError, struct.error):
+            return False
+    return True
+
+
 def latest_checkpoint(output_dir) -> Optional[str]:
-    """Newest ``checkpoint-<step>`` directory that has ``trainer_state.json``."""
+    """Newest intact ``checkpoint-<step>`` directory that has ``trainer_state.json``
+    (a checkpoint left corrupt by a crash is skipped for the previous one)."""
     cands = [c for c in glob.glob(os.path.join(str(output_dir), "checkpoint-*")) if os.path.isdir(c)]
 
     def step(p):
@@ -343,7 +365,7 @@ def latest_checkpoint(output_dir) -> Optional[str]:
 
     cands.sort(key=step)
     for c in reversed(cands):
-        if os.path.exists(os.path.join(c, "trainer_state.json")):
+        if os.path.exists(os.path.join(c, "trainer_state.json")) and checkpoint_intact(c):
             return c
     return None
 

@@ -74,3 +74,43 @@ def test_sft_step_reduces_loss():
         opt.step()
     after = -eng.token_logprobs(b)[0][valid].mean().item()
     assert after < before - 0.05
+
+
+def test_microbatch_grads_equal_global_token_mean():
+    """Two micro-batches with coefficients -1/N_total accumulate exactly the
+    gradient of one global token-mean backward over both."""
+    import torch
+    from kore_b200.engine.qwen3_engine import Batch, Qwen3Engine
+    from kore_b200.models import Qwen3Weights, qwen3_tiny
+    cfg = qwen3_tiny(vocab=256)
+    w = Qwen3Weights(cfg, dtype=torch.float32, seed=1)
+    g = torch.Generator().manual_seed(3)
+    seqs = [torch.randint(0, 256, (n,), generator=g) for n in (20, 33, 7)]
+    eng = Qwen3Engine(w)
+    full = Batch.from_sequences(seqs)
+    ntok = float((full.targets >= 0).sum())
+    eng.zero_grad()
+    eng.forward_backward(full, coef=torch.where(full.targets >= 0, -1.0 / ntok, 0.0))
+    ref = [x.clone() for x in eng.grads]
+    eng.zero_grad()
+    for part in (seqs[:1], seqs[1:]):
+        b = Batch.from_sequences(part)
+        eng.forward_backward(b, coef=torch.where(b.targets >= 0, -1.0 / ntok, 0.0))
+    for a, b in zip(ref, eng.grads):
+        assert torch.allclose(a, b, atol=1e-6, rtol=1e-4)
+
+
+def test_corrupt_checkpoint_is_skipped(tmp_path):
+    import json
+    import torch
+    from kore_b200.models import Qwen3Weights, qwen3_tiny
+    from kore_b200.models.hf_io import save_pretrained
+    from kore_b200.policy.configs import latest_checkpoint
+    w = Qwen3Weights(qwen3_tiny(vocab=256), dtype=torch.float32, seed=1)
+    for step in (1, 2):
+        save_pretrained(w, str(tmp_path / f"checkpoint-{step}"), trainer_state={"global_step": step})
+    assert latest_checkpoint(str(tmp_path)).endswith("checkpoint-2")
+    f = next((tmp_path / "checkpoint-2").glob("*.safetensors"))
+    data = f.read_bytes()
+    f.write_bytes(data[: len(data) // 2])                    # a crash mid-save
+    assert latest_checkpoint(str(tmp_path)).endswith("checkpoint-1")
