@@ -67,19 +67,36 @@ struct FwdParams {
   int T;
 };
 
-// P lives in TMEM (aliasing its S buffer) and feeds the PV product as the
-// TMEM operand, which frees shared memory for three K and V stages.
-constexpr int kFwdStages = 3;
+// 64-row, 128-column tile (two 8 KB atoms): K-major operand at K-step kk.
+KORE_DEV uint64_t kmajor64_desc(uint32_t base, int kk) {
+  return make_sw128_desc(base + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+}
+// Same 64-row tile as an MN-major operand (rows = K, N = 128 in two 64-wide
+// blocks 8 KB apart) at K-step kk.
+KORE_DEV uint64_t mnmajor64_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 2048, 8192, 1024); }
+// 128-row x 64-column tile (one atom): K-major at K-step kk / MN-major (N = 64) at K-step kk.
+KORE_DEV uint64_t kmajor_narrow_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 32, 16, 1024); }
+KORE_DEV uint64_t mnmajor_narrow_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 2048, 16384, 1024); }
+
+// Forward tiling: 128 query rows x 64-key blocks. P lives in TMEM (aliasing
+// its S buffer) and feeds the PV product as the TMEM operand. Shared memory
+// (Q + two K and two V stages, 96 KB) and TMEM (two 64-column S buffers +
+// 128-column O = 256 columns) are sized so that two CTAs share an SM: while
+// one CTA's softmax warps work, the other's products keep the tensor pipe busy.
+constexpr int FBKV = 64;
+constexpr int KV_TILE_BYTES = FBKV * D * 2;   // 16 KB: 64 rows as two 8 KB swizzle atoms
+constexpr int kFwdStages = 2;
+constexpr int kFwdTmemCols = 256;
 struct FwdSmem {
   static constexpr int Q_OFF = 0;
-  static constexpr int K_OFF = TILE_BYTES;                       // kFwdStages stages
-  static constexpr int V_OFF = K_OFF + kFwdStages * TILE_BYTES;  // kFwdStages stages
-  static constexpr int BAR_OFF = V_OFF + kFwdStages * TILE_BYTES;
+  static constexpr int K_OFF = TILE_BYTES;                          // kFwdStages stages
+  static constexpr int V_OFF = K_OFF + kFwdStages * KV_TILE_BYTES;  // kFwdStages stages
+  static constexpr int BAR_OFF = V_OFF + kFwdStages * KV_TILE_BYTES;
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
-static_assert(FwdSmem::TOTAL <= 227 * 1024, "fwd smem");
+static_assert(2 * (FwdSmem::TOTAL + 1024) <= 228 * 1024, "fwd smem: two CTAs per SM");
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 2)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, FwdParams p) {
   using S = FwdSmem;
@@ -89,13 +106,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* q_full = bars + 0;
   uint64_t* k_full = bars + 1;    // [kFwdStages]
-  uint64_t* k_empty = bars + 4;   // [kFwdStages]
-  uint64_t* v_full = bars + 7;    // [kFwdStages]
-  uint64_t* v_empty = bars + 10;  // [kFwdStages]
-  uint64_t* s_full = bars + 13;   // [2]
-  uint64_t* p_full = bars + 15;   // [2]
-  uint64_t* o_done = bars + 17;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 18);
+  uint64_t* k_empty = bars + 3;   // [kFwdStages]
+  uint64_t* v_full = bars + 5;    // [kFwdStages]
+  uint64_t* v_empty = bars + 7;   // [kFwdStages]
+  uint64_t* s_full = bars + 9;    // [2]
+  uint64_t* p_full = bars + 11;   // [2]
+  uint64_t* o_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   // ---- work item: longest (latest) query blocks first
@@ -108,7 +125,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int len = p.cu_seqlens[seq + 1] - s0;
   const int q0 = qb * BQ;
   if (q0 >= len) return;  // whole CTA exits before any barrier / TMEM use
-  const int nkv = qb + 1;  // causal: kv tiles 0..qb
+  const int nkv = (min(q0 + BQ, len) + FBKV - 1) / FBKV;   // causal: key blocks up to the last query row
   const int warp = threadIdx.x / 32;
 
   if (threadIdx.x == 0) {
@@ -127,11 +144,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 1) tmem_alloc(tmem_slot, 512);
+  if (warp == 1) tmem_alloc(tmem_slot, kFwdTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // TMEM columns: [0,64) S/P buffer 0, [64,128) S/P buffer 1, [128,256) O
+  constexpr uint32_t T_O = 128;
 
   if (warp == 0) {
     if (elect_one()) {
@@ -142,20 +161,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int st = j % kFwdStages;
         const uint32_t ph = (j / kFwdStages) & 1;
         if (!mbar_wait(&k_empty[st], ph ^ 1)) { *abort_flag = 1; break; }
-        uint8_t* kt = smem + S::K_OFF + st * TILE_BYTES;
-        mbar_arrive_expect_tx(&k_full[st], TILE_BYTES);
-        tma_load_2d(kt, &tmK, &k_full[st], kvh * D, s0 + j * BKV);
-        tma_load_2d(kt + 16384, &tmK, &k_full[st], kvh * D + 64, s0 + j * BKV);
+        uint8_t* kt = smem + S::K_OFF + st * KV_TILE_BYTES;
+        mbar_arrive_expect_tx(&k_full[st], KV_TILE_BYTES);
+        tma_load_2d(kt, &tmK, &k_full[st], kvh * D, s0 + j * FBKV);
+        tma_load_2d(kt + 8192, &tmK, &k_full[st], kvh * D + 64, s0 + j * FBKV);
         if (!mbar_wait(&v_empty[st], ph ^ 1)) { *abort_flag = 1; break; }
-        uint8_t* vt = smem + S::V_OFF + st * TILE_BYTES;
-        mbar_arrive_expect_tx(&v_full[st], TILE_BYTES);
-        tma_load_2d(vt, &tmV, &v_full[st], kvh * D, s0 + j * BKV);
-        tma_load_2d(vt + 16384, &tmV, &v_full[st], kvh * D + 64, s0 + j * BKV);
+        uint8_t* vt = smem + S::V_OFF + st * KV_TILE_BYTES;
+        mbar_arrive_expect_tx(&v_full[st], KV_TILE_BYTES);
+        tma_load_2d(vt, &tmV, &v_full[st], kvh * D, s0 + j * FBKV);
+        tma_load_2d(vt + 8192, &tmV, &v_full[st], kvh * D + 64, s0 + j * FBKV);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    constexpr uint32_t idesc_qk = make_idesc_bf16(BQ, BKV, false, false);
+    constexpr uint32_t idesc_qk = make_idesc_bf16(BQ, FBKV, false, false);
     constexpr uint32_t idesc_pv = make_idesc_bf16(BQ, D, false, true);   // A = P from TMEM (K-major)
     if (elect_one()) {
       const uint32_t qa = smem_u32(smem + S::Q_OFF);
@@ -164,10 +183,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ks = j % kFwdStages;
         if (!mbar_wait(&k_full[ks], (j / kFwdStages) & 1)) return false;
         tc_fence_after();
-        const uint32_t ka = smem_u32(smem + S::K_OFF + ks * TILE_BYTES);
+        const uint32_t ka = smem_u32(smem + S::K_OFF + ks * KV_TILE_BYTES);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem + (j & 1) * 128, kmajor_desc(qa, kk), kmajor_desc(ka, kk), idesc_qk, kk > 0);
+          umma_f16_ss(tmem + (j & 1) * FBKV, kmajor_desc(qa, kk), kmajor64_desc(ka, kk), idesc_qk, kk > 0);
         umma_commit(&k_empty[ks]);
         umma_commit(&s_full[j & 1]);
         return true;
@@ -181,10 +200,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!mbar_wait(&p_full[st], (j >> 1) & 1)) { ok = false; break; }
         if (!mbar_wait(&v_full[vs], (j / kFwdStages) & 1)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t va = smem_u32(smem + S::V_OFF + vs * TILE_BYTES);
+        const uint32_t va = smem_u32(smem + S::V_OFF + vs * KV_TILE_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; ++kk)   // P_j: 64 TMEM columns of packed bf16 pairs, 8 per K-step
-          umma_f16_ts(tmem + 256, tmem + st * 128 + kk * 8, mnmajor_desc(va, kk), idesc_pv,
+        for (int kk = 0; kk < FBKV / 16; ++kk)   // P_j: 32 TMEM columns of packed bf16 pairs, 8 per K-step
+          umma_f16_ts(tmem + T_O, tmem + st * FBKV + kk * 8, mnmajor64_desc(va, kk), idesc_pv,
                       (j > 0 || kk > 0) ? 1u : 0u);
         umma_commit(&v_empty[vs]);
         umma_commit(o_done);
@@ -200,28 +219,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qi = q0 + row;        // query position within the sequence
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     float m = -INFINITY, l = 0.f;
-    float sv[128];
+    float sv[FBKV];
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       const int st = j & 1;
       if (!mbar_wait(&s_full[st], (j >> 1) & 1)) { ok = false; break; }
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + st * 128 + c * 32, r);
+      {
+        uint32_t r[2][32];
+        tmem_ld32(tmem + lane_base + st * FBKV, r[0]);
+        tmem_ld32(tmem + lane_base + st * FBKV + 32, r[1]);
         tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[i]) * p.scale_log2;
-      }
-      const int kv0 = j * BKV;
-      float mx = -INFINITY;
-      const bool edge = (j == nkv - 1) || (kv0 + BKV > len);
+        for (int c = 0; c < 2; ++c)
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        if (edge && (kv0 + i > qi || kv0 + i >= len)) sv[i] = -INFINITY;
-        mx = fmaxf(mx, sv[i]);
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]) * p.scale_log2;
       }
+      const int kv0 = j * FBKV;
+      const bool edge = (kv0 + FBKV > q0) || (kv0 + FBKV > len);
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < FBKV; ++i) {
+        if (edge && (kv0 + i > qi || kv0 + i >= len)) sv[i] = -INFINITY;
+        mx4[i & 3] = fmaxf(mx4[i & 3], sv[i]);
+      }
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       float m_new = fmaxf(m, mx);
       const bool need = (m == -INFINITY) ? true : (m_new > m + 8.f);
       if (j > 0) {
@@ -232,7 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
-            const uint32_t a = tmem + lane_base + 256 + c * 32;
+            const uint32_t a = tmem + lane_base + T_O + c * 32;
             tmem_ld32(a, r);
             tmem_wait_ld();
 #pragma unroll
@@ -245,19 +267,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (need) m = m_new;
       const float mref = (m == -INFINITY) ? 0.f : m;
-      float rs = 0.f;
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < 128; ++i) {
+      for (int i = 0; i < FBKV; ++i) {
         sv[i] = exp2f(sv[i] - mref);
-        rs += sv[i];
+        rs4[i & 3] += sv[i];
       }
-      l += rs;
-      {   // P_j as packed bf16 pairs over the first 64 columns of its S buffer
-        uint32_t pk[2][32];
+      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      {   // P_j as packed bf16 pairs over the first 32 columns of its S buffer
+        uint32_t pk[32];
 #pragma unroll
-        for (int i = 0; i < 64; ++i) pk[i >> 5][i & 31] = pack_bf16(sv[2 * i], sv[2 * i + 1]);
-        tmem_st32(tmem + lane_base + st * 128, pk[0]);
-        tmem_st32(tmem + lane_base + st * 128 + 32, pk[1]);
+        for (int i = 0; i < 32; ++i) pk[i] = pack_bf16(sv[2 * i], sv[2 * i + 1]);
+        tmem_st32(tmem + lane_base + st * FBKV, pk);
         tmem_wait_st();
       }
       tc_fence_before();
@@ -272,7 +293,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + 256 + c * 32, r);
+        tmem_ld32(tmem + lane_base + T_O + c * 32, r);
         tmem_wait_ld();
         if (valid) {
 #pragma unroll
@@ -295,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, kFwdTmemCols);
   }
 }
 
@@ -389,17 +410,6 @@ KORE_DEV void store_row32_sw128(uint8_t* tile, int row, int c, const float* v) {
     *reinterpret_cast<uint4*>(atom + row * 128 + (((chunk & 7) ^ (row & 7)) * 16)) = u;
   }
 }
-
-// 64-row, 128-column tile (two 8 KB atoms): K-major operand at K-step kk.
-KORE_DEV uint64_t kmajor64_desc(uint32_t base, int kk) {
-  return make_sw128_desc(base + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-}
-// Same 64-row tile as an MN-major operand (rows = K, N = 128 in two 64-wide
-// blocks 8 KB apart) at K-step kk.
-KORE_DEV uint64_t mnmajor64_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 2048, 8192, 1024); }
-// 128-row x 64-column tile (one atom): K-major at K-step kk / MN-major (N = 64) at K-step kk.
-KORE_DEV uint64_t kmajor_narrow_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 32, 16, 1024); }
-KORE_DEV uint64_t mnmajor_narrow_desc(uint32_t base, int kk) { return make_sw128_desc(base + kk * 2048, 16384, 1024); }
 
 // Work item of a CTA: heaviest key blocks (kb = 0) of every kv head first.
 struct BwdItem {
@@ -740,8 +750,8 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
   c10::cuda::CUDAGuard g(q.device());
   auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tq = make_tmap_2d(q.data_ptr(), bf, 2, (uint64_t)Hq * D, T, q.stride(0), 64, 128);
-  CUtensorMap tk = make_tmap_2d(k.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, k.stride(0), 64, 128);
-  CUtensorMap tv = make_tmap_2d(v.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, v.stride(0), 64, 128);
+  CUtensorMap tk = make_tmap_2d(k.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, k.stride(0), 64, FBKV);
+  CUtensorMap tv = make_tmap_2d(v.data_ptr(), bf, 2, (uint64_t)Hkv * D, T, v.stride(0), 64, FBKV);
   FwdParams p;
   p.cu_seqlens = cu_seqlens.data_ptr<int>();
   p.nseq = nseq;
@@ -753,11 +763,16 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
   p.lse = lse.data_ptr<float>();
   p.T = T;
   constexpr int smem = FwdSmem::TOTAL;
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64] = {};
+  const int dev = q.get_device();
+  TORCH_CHECK(dev >= 0 && dev < 64, "attn_fwd: device index");
+  if (!attr[dev]) {
     check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                "attn_fwd smem attr");
-    attr = true;
+    // two CTAs per SM: ask for the full shared-memory carveout
+    check_cuda(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100),
+               "attn_fwd carveout");
+    attr[dev] = true;
   }
   dim3 grid(nseq * p.nqblk, Hq);
   attn_fwd_kernel<<<grid, kThreads, smem, at::cuda::getCurrentCUDAStream()>>>(tq, tk, tv, p);
