@@ -31,7 +31,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "sft_tokens_per_s"
-BASELINE_VALUE = None  # BASELINE.md publishes no SFT tokens/s for the reference
+BASELINE_VALUE = None  # the reference publishes no SFT tokens/s figure
 
 
 class ClockSampler:

@@ -68,11 +68,6 @@ struct Params {
   void* rs_out[8];
 };
 
-// Per-peer tensor maps for the all-gather->GEMM mode (kernel parameter, 1 KB).
-struct PeerMaps {
-  CUtensorMap a[8];
-};
-
 template <int BN, int STAGES>
 struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;
@@ -97,7 +92,7 @@ KORE_DEV void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ PeerMaps pm, Params p) {
+                const __grid_constant__ CUtensorMap tmC, Params p) {
   using S = Smem<BN, STAGES>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -420,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
-            int grid, cudaStream_t stream, const PeerMaps* pmp = nullptr, bool cooperative = false) {
+            int grid, cudaStream_t stream, bool cooperative = false) {
   auto k = gemm_kernel<BN, STAGES, A_MN, B_MN>;
   constexpr int smem = Smem<BN, STAGES>::TOTAL;
   static bool attr_set[64] = {};  // per template instance and device
@@ -432,17 +427,15 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
                "cudaFuncSetAttribute(gemm smem)");
     attr_set[dev] = true;
   }
-  static PeerMaps empty_maps{};
-  PeerMaps pm = pmp ? *pmp : empty_maps;
   if (cooperative) {
     CUtensorMap a = ta, b = tb, c = tc;
     Params pp = p;
-    void* args[] = {&a, &b, &c, &pm, &pp};
+    void* args[] = {&a, &b, &c, &pp};
     check_cuda(cudaLaunchCooperativeKernel((const void*)k, dim3(grid), dim3(kThreads), args, smem, stream),
                "gemm cooperative launch");
     return;
   }
-  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, pm, p);
+  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, p);
   check_cuda(cudaGetLastError(), "gemm launch");
 }
 
@@ -532,8 +525,12 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
 // Tensor-parallel GEMMs over peer memory (sequence-parallel layout: the M
 // rows are split in W blocks of ``rows`` rows, block i owned by rank i).
 //  * all-gather->GEMM (``a_peers`` given): out[M, N] = A . B^T where A's row
-//    block i is read by TMA directly from peer i's buffer at a_peers[i]
-//    (row stride lda). No gathered copy of A is ever materialised.
+//    block i lives on peer i at a_peers[i] (row stride lda). At kernel start
+//    the CTAs copy the peers' 64-row groups into the local staging buffer
+//    ``stage`` with 16-byte peer loads (each remote row crosses NVLink once)
+//    and publish a per-group flag; a tile's producer waits (bounded) for its
+//    groups and then TMA-loads A from ``stage``. Tiles start on this rank's
+//    own rows, so the first waves overlap the remote copies.
 //  * GEMM->reduce-scatter (``rs_peers`` given): out rows are stored into the
 //    owner peer's slot buffer (P2P stores): rs_peers[r/rows] +
 //    (rank*rows + r%rows) * ldc; the owner then sums its W slots.
@@ -597,8 +594,8 @@ void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<in
   const int grid = std::min(tiles, num_sms(b.get_device()));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   // all-gather mode: CTAs wait on each other's copies, so they must be co-resident
-  if (use256) gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, nullptr, ag);
-  else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, nullptr, ag);
+  if (use256) gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, ag);
+  else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, ag);
 }
 
 // Grouped GEMM over experts (MoE): rows of ``a`` are grouped by expert with

@@ -4,8 +4,9 @@ Layout: q [T, Hq, D], k/v [T, Hkv, D] (strided views are fine), sequence
 boundaries ``cu_seqlens`` (int32, [n+1]). Forward returns o [T, Hq, D] and
 the per-row logsumexp lse [Hq, T] (fp32) needed by the backward.
 
-CUDA tensors use the native sm_100a kernel when it is built with attention
-support (``_C.attn_fwd``); CPU tensors use the fp32 PyTorch definition.
+CUDA tensors always run the native sm_100a kernels (``_C.attn_fwd`` /
+``_C.attn_bwd``); if the extension is missing the call raises, there is no
+library fallback on a GPU. CPU tensors use the fp32 PyTorch definition.
 """
 from __future__ import annotations
 
@@ -16,13 +17,6 @@ import torch
 
 from . import reference as ref
 from ._lib import native
-
-
-def _has_native_attn() -> bool:
-    try:
-        return hasattr(native(), "attn_fwd")
-    except RuntimeError:
-        return False
 
 
 def _seq_bounds(cu_seqlens: Optional[torch.Tensor], T: int):
@@ -36,7 +30,7 @@ def attn_fwd(q, k, v, cu_seqlens=None, max_seqlen: int = 0, scale: Optional[floa
              ) -> Tuple[torch.Tensor, torch.Tensor]:
     T, hq, D = q.shape
     scale = scale if scale is not None else 1.0 / math.sqrt(D)
-    if q.is_cuda and _has_native_attn():
+    if q.is_cuda:
         o = torch.empty(T, hq, D, dtype=q.dtype, device=q.device)
         lse = torch.empty(hq, T, dtype=torch.float32, device=q.device)
         cu = cu_seqlens if cu_seqlens is not None else torch.tensor([0, T], dtype=torch.int32, device=q.device)
@@ -52,7 +46,7 @@ def attn_bwd(do, q, k, v, o, lse, cu_seqlens=None, max_seqlen: int = 0,
     dq = dq if dq is not None else torch.empty_like(q)
     dk = dk if dk is not None else torch.empty(k.shape, dtype=k.dtype, device=k.device)
     dv = dv if dv is not None else torch.empty(v.shape, dtype=v.dtype, device=v.device)
-    if q.is_cuda and _has_native_attn() and hasattr(native(), "attn_bwd"):
+    if q.is_cuda:
         cu = cu_seqlens if cu_seqlens is not None else torch.tensor([0, T], dtype=torch.int32, device=q.device)
         # fp32 dQ accumulator and per-row delta: scratch of this call
         dq_acc = torch.empty(T, hq, D, dtype=torch.float32, device=q.device)
@@ -73,7 +67,9 @@ def attn_bwd(do, q, k, v, o, lse, cu_seqlens=None, max_seqlen: int = 0,
 
 
 def _attn_fwd_torch(q, k, v, cu_seqlens, scale, need_lse: bool = True):
-    """Plain PyTorch path (CPU tests, and GPU until the native kernel is present)."""
+    """Plain fp32 PyTorch definition (CPU only; the reference the kernels are tested against)."""
+    if q.is_cuda:
+        raise RuntimeError("attention on CUDA tensors runs only on the native kernels")
     T, hq, D = q.shape
     hkv = k.shape[1]
     outs = []
@@ -82,20 +78,16 @@ def _attn_fwd_torch(q, k, v, cu_seqlens, scale, need_lse: bool = True):
         qs = q[a:b].transpose(0, 1).unsqueeze(0)
         ks = k[a:b].transpose(0, 1).unsqueeze(0)
         vs = v[a:b].transpose(0, 1).unsqueeze(0)
-        if q.is_cuda:
-            o = torch.nn.functional.scaled_dot_product_attention(
-                qs, ks, vs, is_causal=True, scale=scale, enable_gqa=(hq != hkv))
-        else:
-            rep = hq // hkv
-            kf = ks.float().repeat_interleave(rep, 1)
-            vf = vs.float().repeat_interleave(rep, 1)
-            s = (qs.float() @ kf.transpose(-1, -2)) * scale
-            n = b - a
-            mask = torch.ones(n, n, dtype=torch.bool, device=q.device).tril()
-            s = s.masked_fill(~mask, float("-inf"))
-            o = (s.softmax(-1) @ vf).to(q.dtype)
+        rep = hq // hkv
+        kf = ks.float().repeat_interleave(rep, 1)
+        vf = vs.float().repeat_interleave(rep, 1)
+        s = (qs.float() @ kf.transpose(-1, -2)) * scale
+        n = b - a
+        mask = torch.ones(n, n, dtype=torch.bool, device=q.device).tril()
+        s = s.masked_fill(~mask, float("-inf"))
+        o = (s.softmax(-1) @ vf).to(q.dtype)
         outs.append(o[0].transpose(0, 1))
-        if need_lse and not q.is_cuda:
+        if need_lse:
             with torch.no_grad():
                 rep = hq // hkv
                 kf = ks.float().repeat_interleave(rep, 1)

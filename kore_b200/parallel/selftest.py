@@ -2,10 +2,13 @@
 
     python -m torch.distributed.run --nproc-per-node N -m kore_b200.parallel.selftest
 
-Checks: (1) ZeRO-2 step with NCCL collectives and with the fused peer-memory
-kernels give the same parameters as each other and as a 1-GPU reference
-computed on every rank; (2) replicas stay bit-identical across ranks; (3)
-timing of both optimizer data planes on a 14B-sized unit set (optional).
+Checks: (1) three ZeRO-2 steps with NCCL collectives and with the fused
+peer-memory optimizer give the same parameters (bf16 tolerance) and the
+replicas stay bit-identical across ranks; (2) ZeRO-3 matches ZeRO-2 in loss
+and final parameters; (3) expert parallelism over NCCL all-to-all and over
+the fused peer-memory dispatch/combine agree; (4) the tensor-parallel rollout
+engine's sampled log-probs match an fp32 single-GPU reference forward that
+scores the same tokens (teacher forcing).
 Prints one JSON line per check from rank 0 and exits non-zero on failure.
 """
 from __future__ import annotations

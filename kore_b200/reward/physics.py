@@ -1,20 +1,33 @@
-"""Physics residual-descent reward and the single reward dispatch.
+"""Roofline-grounded ("physics") scoring of a correct kernel.
 
-For a correct kernel the speed term becomes an absolute, roofline-grounded
-credit: rho = T_min / (T_min + N) with the named residual
-N = (stall fraction + occupancy deficit) * T_meas clamped to [0, T_meas - T_min]
-when ncu counters are available, else eta = T_min / T_meas (flagged
-``no_pmc``). All hack / compile / correctness gating is delegated to
-:func:`compute_reward`, so the tier order is unchanged. On B200 the counters
-come from ``ncu`` (``smsp__average_warps_issue_stalled_*`` /
-``sm__warps_active``) instead of rocprofv3.
+The speedup reward measures a candidate against a baseline that may itself be
+far from the hardware limit. This module scores it against the limit instead:
 
-Behavioural parity: kore/reward/physics.py:61-348.
+* ``RooflineEvidence`` is what is known about one timed shape: the roofline
+  time ``t_min`` (from the shape's FLOPs and bytes at the measured B200 peaks),
+  the measured time ``t``, and optionally two ncu counters (issue-stall
+  fraction, achieved occupancy).
+* Its ``attainment`` is ``t_min / (t_min + N)``, where ``N`` is the part of the
+  gap to the roofline that the counters can name: ``(stall + (1 - occupancy))
+  * t``, clipped to ``[0, t - t_min]``. Without counters it degrades to
+  ``eta = t_min / t``. This is the residual-descent formula of
+  kore/reward/physics.py:77-113; it is what makes the credit grow when a
+  kernel removes a stall even before its wall time moves.
+* ``KernelScorer`` is the single entry the GRPO environment calls. Its order
+  is: roofline ceiling gate (a time below ``t_min`` beyond a tolerance is a
+  measurement exploit and scores as a hack), then the ladder of
+  :func:`compute_reward` for every non-correct outcome, then the physics credit
+  (``mode="residual"``) or the speedup credit (``mode="speedup"``), and finally
+  the curriculum phase mask (``"correctness"`` pays only the correctness
+  weight). Reference dispatch: kore/reward/physics.py:296-348.
+
+On B200 the counters come from ncu
+(``smsp__average_warps_issue_stalled_*`` and ``sm__warps_active``).
 """
 from __future__ import annotations
 
 from dataclasses import dataclass, replace
-from typing import Optional, Tuple
+from typing import Iterator, Optional, Tuple
 
 from ..config import CONFIG
 from .reward import (DEFAULT_ROOFLINE_TOL, Observation, RewardResult, compute_reward,
@@ -24,120 +37,158 @@ DEFAULT_PHYSICS_WEIGHT = 1.0
 
 
 @dataclass
-class PhysicsSignal:
+class RooflineEvidence:
+    """Roofline time, measured time and optional counters of one shape (ms)."""
     t_min_ms: float
     measured_ms: Optional[float] = None
     stall_frac: Optional[float] = None
     occupancy: Optional[float] = None
 
+    @property
+    def has_counters(self) -> bool:
+        return self.stall_frac is not None or self.occupancy is not None
 
-def named_residual_ms(measured_ms: float, sig: PhysicsSignal) -> Optional[float]:
-    if sig.stall_frac is None and sig.occupancy is None:
-        return None
-    stall = max(0.0, sig.stall_frac or 0.0)
-    deficit = max(0.0, 1.0 - (sig.occupancy if sig.occupancy is not None else 1.0))
-    resid = max(measured_ms - sig.t_min_ms, 0.0) if sig.t_min_ms == sig.t_min_ms else measured_ms
-    return min(max((stall + deficit) * measured_ms, 0.0), resid)
+    def residual_ms(self, t: float) -> Optional[float]:
+        """The named part of the gap ``t - t_min`` (None without counters)."""
+        if not self.has_counters:
+            return None
+        lost = max(0.0, self.stall_frac or 0.0)
+        if self.occupancy is not None:
+            lost += max(0.0, 1.0 - self.occupancy)
+        gap = t - self.t_min_ms if self.t_min_ms == self.t_min_ms else t
+        return max(0.0, min(lost * t, max(gap, 0.0)))
 
-
-def residual_descent_frac(sig: PhysicsSignal, measured_ms: Optional[float] = None) -> Tuple[Optional[float], bool]:
-    t = sig.measured_ms if sig.measured_ms is not None else measured_ms
-    if not t or t <= 0 or sig.t_min_ms is None or not sig.t_min_ms > 0:
-        return None, False
-    n = named_residual_ms(t, sig)
-    if n is None:
-        return min(sig.t_min_ms / t, 1.0), False
-    return min(sig.t_min_ms / (sig.t_min_ms + n), 1.0), True
-
-
-def compute_residual_reward(obs: Observation, physics: PhysicsSignal, source: str = "", dtype: str = "fp32",
-                            cfg=CONFIG, physics_weight: float = DEFAULT_PHYSICS_WEIGHT,
-                            snr_threshold=None, response=None, phase=None) -> RewardResult:
-    base = compute_reward(obs, source=source, dtype=dtype, cfg=cfg, snr_threshold=snr_threshold,
-                          response=response, phase=phase)
-    if not base.correct:
-        return base
-    measured = obs.wall_ms
-    if measured is None and obs.wall_by_shape:
-        measured = max(obs.wall_by_shape.values())
-    rho, pmc = residual_descent_frac(physics, measured)
-    fmt = format_component(response, cfg)
-    flags = list(base.flags)
-    if rho is None:
-        return RewardResult(cfg.correctness_weight + fmt, True, base.speedup, "correct_no_physics",
-                            flags + ["no_physics"], "correct; no roofline/timing for residual credit")
-    if not pmc:
-        flags.append("no_pmc")
-    return RewardResult(cfg.correctness_weight + physics_weight * max(rho, 0.0) + fmt, True, base.speedup,
-                        "correct_residual", flags,
-                        f"residual-descent rho={rho:.3f} ({'named-residual' if pmc else 'eta-fallback'}); "
-                        f"credit={physics_weight * rho:.3f}")
+    def attainment(self, measured_ms: Optional[float] = None) -> Tuple[Optional[float], bool]:
+        """(score in [0, 1], whether counters named the residual)."""
+        t = self.measured_ms if self.measured_ms is not None else measured_ms
+        if t is None or t <= 0 or self.t_min_ms is None or not self.t_min_ms > 0:
+            return None, False
+        n = self.residual_ms(t)
+        if n is None:
+            return min(1.0, self.t_min_ms / t), False
+        return min(1.0, self.t_min_ms / (self.t_min_ms + n)), True
 
 
-def _walls(task, obs):
+# Older name kept for callers that construct the signal directly.
+PhysicsSignal = RooflineEvidence
+
+
+def residual_descent_frac(ev: RooflineEvidence, measured_ms: Optional[float] = None):
+    return ev.attainment(measured_ms)
+
+
+def _timed_shapes(task, obs) -> Iterator[Tuple[str, float]]:
     walls = dict(getattr(obs, "wall_by_shape", None) or {})
     if not walls and getattr(obs, "wall_ms", None):
         prim = task.shape("primary") if hasattr(task, "shape") else None
-        walls = {(prim.name if prim else "primary"): obs.wall_ms}
-    return walls
+        walls = {prim.name if prim is not None else "primary": obs.wall_ms}
+    for name, wall in walls.items():
+        if wall and wall > 0:
+            yield name, wall
 
 
-def _shape_rooflines(task, obs, arch=None):
-    from ..analysis.rooflines import detect_arch, resolve_peaks, roofline, shape_to_str
-    a = arch or detect_arch()
-    peaks = resolve_peaks(a)
-    for name, wall in _walls(task, obs).items():
-        if not wall or wall <= 0:
-            continue
-        sh = task.shape(name) if hasattr(task, "shape") else None
-        dims = getattr(sh, "dims", None)
-        if not dims:
-            continue
-        rf = roofline(task.task_id, task.operation, task.dtype, shape_to_str(dims), dims, peaks, a)
-        if rf is not None and rf.t_min_ms > 0:
-            yield name, wall, rf
+class KernelScorer:
+    """Scores one verified kernel; configured once per GRPO run."""
+
+    def __init__(self, *, mode: str = "speedup", cfg=CONFIG, physics_weight: float = DEFAULT_PHYSICS_WEIGHT,
+                 reward_phase: str = "all", roofline_gate: bool = False,
+                 roofline_tol: float = DEFAULT_ROOFLINE_TOL, arch: Optional[str] = None):
+        if mode not in ("speedup", "residual"):
+            raise ValueError(f"reward mode must be speedup|residual, got {mode!r}")
+        self.mode = mode
+        self.cfg = cfg
+        self.weight = physics_weight
+        self.phase = str(reward_phase or "all").lower()
+        self.gate = roofline_gate
+        self.tol = roofline_tol
+        self.arch = arch
+
+    # -- roofline per shape
+    def rooflines(self, task, obs):
+        from ..analysis.rooflines import detect_arch, resolve_peaks, roofline, shape_to_str
+        arch = self.arch or detect_arch()
+        peaks = resolve_peaks(arch)
+        for name, wall in _timed_shapes(task, obs):
+            sh = task.shape(name) if hasattr(task, "shape") else None
+            dims = getattr(sh, "dims", None)
+            if not dims:
+                continue
+            rf = roofline(task.task_id, task.operation, task.dtype, shape_to_str(dims), dims, peaks, arch)
+            if rf is not None and rf.t_min_ms > 0:
+                yield name, wall, rf.t_min_ms
+
+    def evidence(self, task, obs) -> Optional[RooflineEvidence]:
+        """The evidence of the shape furthest from its roofline."""
+        worst = min(((t_min / wall, t_min, wall) for _, wall, t_min in self.rooflines(task, obs)),
+                    default=None)
+        return None if worst is None else RooflineEvidence(t_min_ms=worst[1], measured_ms=worst[2])
+
+    def ceiling_breach(self, task, obs) -> Optional[str]:
+        for name, wall, t_min in self.rooflines(task, obs):
+            if roofline_ceiling_violation(wall, t_min, self.tol):
+                return (f"shape {name}: {wall:.4g} ms beats the roofline minimum {t_min:.4g} ms by more "
+                        f"than the {self.tol:.0%} tolerance, which no kernel can do")
+        return None
+
+    # -- credit
+    def physics_credit(self, obs: Observation, ev: RooflineEvidence, base: RewardResult,
+                       response: Optional[str]) -> RewardResult:
+        t = obs.wall_ms
+        if t is None and obs.wall_by_shape:
+            t = max(obs.wall_by_shape.values())
+        score, named = ev.attainment(t)
+        fmt = format_component(response, self.cfg)
+        if score is None:
+            return RewardResult(self.cfg.correctness_weight + fmt, True, base.speedup, "correct_no_physics",
+                                list(base.flags) + ["no_physics"], "correct, but no roofline time to score")
+        flags = list(base.flags) + ([] if named else ["no_pmc"])
+        credit = self.weight * max(score, 0.0)
+        how = "counter-named residual" if named else "eta (no counters)"
+        return RewardResult(self.cfg.correctness_weight + credit + fmt, True, base.speedup,
+                            "correct_residual", flags, f"roofline attainment {score:.3f} by {how}, "
+                            f"credit {credit:.3f}")
+
+    def _mask(self, rr: RewardResult) -> RewardResult:
+        if self.phase == "correctness" and rr.correct:
+            return replace(rr, reward=float(self.cfg.correctness_weight), speedup=None, tier="correct_masked")
+        return rr
+
+    def score(self, obs: Observation, source: str, task, *, dtype: str = "fp32",
+              snr_threshold=None, response: Optional[str] = None,
+              evidence: Optional[RooflineEvidence] = None) -> RewardResult:
+        if self.gate:
+            why = self.ceiling_breach(task, obs)
+            if why:
+                return RewardResult(self.cfg.reward_hack, False, None, "hack", ["hack", "roofline_ceiling"], why)
+        base = compute_reward(obs, source, dtype=dtype, cfg=self.cfg, snr_threshold=snr_threshold,
+                              response=response)
+        if self.mode == "residual" and base.correct:
+            ev = evidence if evidence is not None else self.evidence(task, obs)
+            if ev is not None:
+                base = self.physics_credit(obs, ev, base, response)
+        return self._mask(base)
 
 
-def physics_signal_from_obs(task, obs, arch=None) -> Optional[PhysicsSignal]:
-    """Worst-shape (minimum eta) physics signal from timings + rooflines."""
-    worst = None
-    for _, wall, rf in _shape_rooflines(task, obs, arch):
-        e = rf.t_min_ms / wall
-        if worst is None or e < worst[0]:
-            worst = (e, rf.t_min_ms, wall)
-    return None if worst is None else PhysicsSignal(t_min_ms=worst[1], measured_ms=worst[2])
+def compute_residual_reward(obs: Observation, evidence: RooflineEvidence, source: str = "",
+                            dtype: str = "fp32", cfg=CONFIG,
+                            physics_weight: float = DEFAULT_PHYSICS_WEIGHT, snr_threshold=None,
+                            response=None, phase=None) -> RewardResult:
+    """Residual-mode score of an observation whose roofline evidence is already known."""
+    sc = KernelScorer(mode="residual", cfg=cfg, physics_weight=physics_weight)
+    base = compute_reward(obs, source=source, dtype=dtype, cfg=cfg, snr_threshold=snr_threshold,
+                          response=response, phase=phase)
+    return sc.physics_credit(obs, evidence, base, response) if base.correct else base
 
 
-def roofline_ceiling_violation_from_obs(task, obs, tol: float = DEFAULT_ROOFLINE_TOL, arch=None):
-    for name, wall, rf in _shape_rooflines(task, obs, arch):
-        if roofline_ceiling_violation(wall, rf.t_min_ms, tol):
-            return True, (f"shape {name}: measured {wall:.4g} ms is below the roofline T_min "
-                          f"{rf.t_min_ms:.4g} ms (tol {tol:.2f}): impossible throughput")
-    return False, ""
-
-
-def mask_reward_phase(rr: RewardResult, phase: str, correctness_weight: float) -> RewardResult:
-    if str(phase).lower() == "correctness" and rr.correct:
-        return replace(rr, reward=float(correctness_weight), speedup=None, tier="correct_masked")
-    return rr
+def physics_signal_from_obs(task, obs, arch=None) -> Optional[RooflineEvidence]:
+    return KernelScorer(arch=arch).evidence(task, obs)
 
 
 def compute_kernel_reward(obs: Observation, source: str, task, *, mode: str = "speedup", dtype: str = "fp32",
                           cfg=CONFIG, snr_threshold=None, physics_weight: float = DEFAULT_PHYSICS_WEIGHT,
                           response=None, reward_phase: str = "all", roofline_gate: bool = False,
                           roofline_tol: float = DEFAULT_ROOFLINE_TOL, arch=None) -> RewardResult:
-    """One dispatch for the training loop: optional roofline ceiling gate, then
-    residual (physics) or speedup reward, then the curriculum phase mask."""
-    if roofline_gate:
-        bad, why = roofline_ceiling_violation_from_obs(task, obs, roofline_tol, arch)
-        if bad:
-            return RewardResult(cfg.reward_hack, False, None, "hack", ["hack", "roofline_ceiling"], why)
-    if mode == "residual":
-        sig = physics_signal_from_obs(task, obs, arch)
-        if sig is not None:
-            rr = compute_residual_reward(obs, sig, source=source, dtype=dtype, cfg=cfg,
-                                         physics_weight=physics_weight, snr_threshold=snr_threshold,
-                                         response=response)
-            return mask_reward_phase(rr, reward_phase, cfg.correctness_weight)
-    rr = compute_reward(obs, source, dtype=dtype, cfg=cfg, snr_threshold=snr_threshold, response=response)
-    return mask_reward_phase(rr, reward_phase, cfg.correctness_weight)
+    """Functional form of ``KernelScorer(...).score(...)``."""
+    return KernelScorer(mode=mode, cfg=cfg, physics_weight=physics_weight, reward_phase=reward_phase,
+                        roofline_gate=roofline_gate, roofline_tol=roofline_tol, arch=arch
+                        ).score(obs, source, task, dtype=dtype, snr_threshold=snr_threshold, response=response)

@@ -213,17 +213,26 @@ def format_component(response: Optional[str], cfg=CONFIG) -> float:
 
 
 def speedup_term(su_scored: float, su_raw: float, obs: Observation, cfg, flags: List[str]) -> float:
+    """Speed credit of a correct kernel.
+
+    The curve is linear below 1x and logarithmic above it (so a 4x kernel is
+    not paid twice a 2x one); on top sit the fast_p bonuses, each paid when
+    the raw speedup clears its threshold by the timing-noise margin. With
+    ``fast_p_significant_only`` the bonuses need a trusted measurement: CV at
+    most ``cv_threshold_pct`` and no excessive-speedup flag."""
     w = float(cfg.speedup_weight)
-    term = w * (1.0 + math.log(su_scored)) if (cfg.speedup_log and su_scored > 1.0) else w * max(su_scored, 0.0)
-    if cfg.fast_p_bonus:
-        trusted = obs.cv_pct is None or obs.cv_pct <= cfg.cv_threshold_pct
-        margin = 1.0 + cfg.noise_floor_pct / 100.0
-        if not cfg.fast_p_significant_only or (trusted and "excessive_speedup" not in flags):
-            for thr, bonus in cfg.fast_p_bonus:
-                if su_raw >= thr * margin:
-                    term += float(bonus)
-                    flags.append(f"fast_p>={thr}")
-    return term
+    curve = (lambda s: 1.0 + math.log(s)) if cfg.speedup_log else (lambda s: s)
+    base = w * (curve(su_scored) if su_scored > 1.0 else max(su_scored, 0.0))
+    table = list(cfg.fast_p_bonus or ())
+    if not table:
+        return base
+    noisy = obs.cv_pct is not None and obs.cv_pct > cfg.cv_threshold_pct
+    if cfg.fast_p_significant_only and (noisy or "excessive_speedup" in flags):
+        return base
+    need = 1.0 + cfg.noise_floor_pct / 100.0
+    earned = [(thr, float(b)) for thr, b in table if su_raw >= thr * need]
+    flags.extend(f"fast_p>={thr}" for thr, _ in earned)
+    return base + sum(b for _, b in earned)
 
 
 def all_shapes_pass(obs: Observation, dtype: str, cfg=CONFIG, snr_threshold=None) -> bool:
@@ -234,7 +243,7 @@ def all_shapes_pass(obs: Observation, dtype: str, cfg=CONFIG, snr_threshold=None
 
 
 def _done(rr: RewardResult) -> RewardResult:
-    _LOG._emit("INFO" if rr.tier == "hack" else "DEBUG", "reward",
+    _LOG.emit("INFO" if rr.tier == "hack" else "DEBUG", "reward",
                {"tier": rr.tier, "reward": round(rr.reward, 4), "correct": rr.correct,
                 "speedup": None if rr.speedup is None else round(rr.speedup, 4),
                 "flags": list(rr.flags), "detail": rr.detail}, kind="event")
