@@ -90,11 +90,17 @@ class ClockSampler:
 
 
 def reference_arm(args) -> None:
-    """Run the unmodified reference (baseline/_ref) through its own SFT API."""
+    """The reference's SFT step on its own stack.
+
+    The reference's entry point (TRL SFTTrainer over accelerate FSDP) needs
+    ``trl`` and ``accelerate``; when they are missing, the reference-equivalent
+    arm in ``baseline/reference_arm.py`` runs the same model class, FSDP
+    settings, precision, checkpointing and loss on plain torch + transformers
+    (none of kore_b200 is imported on that path)."""
     ref = os.path.join(ROOT, "baseline", "_ref")
-    reason = None
+    why = None
     if not os.path.isdir(os.path.join(ref, "kore")):
-        reason = "reference not installed at baseline/_ref"
+        why = "reference not installed at baseline/_ref"
     else:
         probe = subprocess.run(
             [sys.executable, "-c",
@@ -103,13 +109,16 @@ def reference_arm(args) -> None:
             capture_output=True, text=True)
         if probe.returncode != 0:
             last = (probe.stderr.strip().splitlines() or ["import failed"])[-1]
-            reason = ("reference SFT trainer needs trl + accelerate (TRL SFTTrainer over "
-                      "accelerate FSDP), which are not installed in this offline image: " + last)
-    if reason is not None:
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps({"impl": "reference", "unavailable": reason}))
-        return
-    raise SystemExit("reference arm: dependencies present but no runner implemented")
+            why = "TRL SFTTrainer over accelerate FSDP cannot run offline: " + last
+    if why is None:
+        raise SystemExit("reference arm: trl + accelerate importable; run the reference's "
+                         "kore.policy.sft entry point directly")
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    import reference_arm as ra
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "note": "unmodified entry point unavailable (" + why
+                          + "); running the reference-equivalent arm"}), file=sys.stderr, flush=True)
+    ra.run(args, ClockSampler)
 
 
 def main(argv=None):
@@ -126,6 +135,8 @@ def main(argv=None):
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="data plane of the sharded optimizer (N > 1)")
+    ap.add_argument("--recompute", default="auto", choices=["auto", "full", "none"],
+                    help="activation recompute: auto keeps whole layers' contexts while HBM allows")
     ap.add_argument("--zero", type=int, default=2, choices=[2, 3],
                     help="2: resident params, sharded grads/optimizer; 3: decoder layers fully sharded")
     args = ap.parse_args(argv)
@@ -148,18 +159,22 @@ def main(argv=None):
     ops.native()  # fail loudly if the extension is missing
     trainer = CausalLMTrainer(cfg, ctx, lr=1e-5, max_grad_norm=1.0, seed=0,
                               micro_batch_size=args.micro_batch,
-                              comm=args.comm if args.zero == 2 else "nccl", zero_stage=args.zero)
+                              comm=args.comm if args.zero == 2 else "nccl", zero_stage=args.zero,
+                              recompute=args.recompute)
     B, S = args.seqs_per_gpu, args.seq
     g = torch.Generator().manual_seed(1234 + ctx.rank)
-    ids_host = torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory()
+    # a fresh token block every step (cycled over NB distinct blocks)
+    NB = max(2, min(8, args.steps + args.warmup))
+    ids_hosts = [torch.randint(0, cfg.vocab_size, (B, S), generator=g).pin_memory() for _ in range(NB)]
     mask_host = torch.zeros(B, S, dtype=torch.bool)
     mask_host[:, S // 2:] = True  # loss on the last 50% of each sequence
     mask_host = mask_host.pin_memory()
-    ids = ids_host.cuda()
+    ids_devs = [h.cuda() for h in ids_hosts]
+    ids_host = ids_hosts[0]
     mask = mask_host.cuda()
 
-    for _ in range(args.warmup):
-        trainer.train_step_device(ids, mask)
+    for i in range(args.warmup):
+        trainer.train_step_device(ids_devs[i % NB], mask)
     torch.cuda.synchronize()
     ctx.barrier()
 
@@ -171,8 +186,8 @@ def main(argv=None):
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
-        loss = trainer.train_step_device(ids, mask)
+    for i in range(args.steps):
+        loss = trainer.train_step_device(ids_devs[(args.warmup + i) % NB], mask)
     e1.record()
     torch.cuda.synchronize()
     ctx.barrier()
@@ -197,8 +212,8 @@ def main(argv=None):
         s0 = torch.cuda.Event(enable_timing=True)
         s1 = torch.cuda.Event(enable_timing=True)
         s0.record()
-        for _ in range(args.steps):
-            trainer.train_step(ids_host, mask_host)
+        for i in range(args.steps):
+            trainer.train_step(ids_hosts[i % NB], mask_host)
         s1.record()
         torch.cuda.synchronize()
         e2e_ms = ctx.max_over_ranks(s0.elapsed_time(s1) / args.steps)
@@ -218,7 +233,7 @@ def main(argv=None):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None,
-            "dtype": "bf16", "data": "synthetic uniform-random token ids, random-init weights",
+            "dtype": "bf16", "data": f"synthetic uniform-random token ids ({NB} distinct blocks cycled), random-init weights",
             "config": {"model": "qwen3-14b-arch (dense)" if args.model == "qwen3-14b" else args.model,
                        "layers": cfg.num_hidden_layers,
                        "global_batch": B * ctx.world, "seq_len": S,
@@ -226,6 +241,8 @@ def main(argv=None):
                            (f"-zero2-{args.comm}" if args.zero == 2 else "-zero3-nccl") if ctx.world > 1 else ""),
                        "loss": "last 50% of each sequence", "micro_batch": args.micro_batch,
                        "optimizer": f"AdamW fp32 moments, master={trainer.master_mode}",
+                       "activation_recompute": f"{cfg.num_hidden_layers - trainer.eng.keep_layers} of "
+                                               f"{cfg.num_hidden_layers} layers recompute their GEMMs",
                        "l2": "inputs larger than L2 (29.5 GB of weights streamed per step)"},
             "loss": loss_v, "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "memory": memory,
             "impl": "kore",

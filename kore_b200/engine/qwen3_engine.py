@@ -112,6 +112,10 @@ class Qwen3Engine:
         # selective activation checkpointing: keep attention outputs (T x Hq*D
         # bf16 + lse per layer) so the backward recomputes only the GEMMs
         self.save_attention = save_attention
+        # decoder layers (counted from the last one) whose whole forward context
+        # is kept during forward_backward, so their backward recomputes nothing;
+        # set by the trainer from the free HBM (0 = full activation checkpointing)
+        self.keep_layers = 0
         self.ep = None          # expert-parallel dispatcher (kore_b200.parallel.ep) when attached
         self.param_hook = None  # full-sharding provider (kore_b200.parallel.fsdp.FullShard) when attached
         self.temperature = temperature
@@ -351,13 +355,27 @@ class Qwen3Engine:
         return dhn
 
     # ------------------------------------------------------------------ public
+    def activation_bytes_per_layer(self, tokens: int) -> int:
+        """HBM a dense layer's kept forward context takes for ``tokens`` tokens
+        beyond what selective checkpointing keeps anyway (input, attention
+        output and logsumexp)."""
+        c = self.cfg
+        qd, kd = self.hq * self.D, self.hkv * self.D
+        H, F = c.hidden_size, c.intermediate_size
+        elems = H + (qd + 2 * kd) + (qd + kd) + H + H + 2 * F + F   # hn qkv qk x2 hn2 gu a
+        return tokens * (elems * self.w.dtype.itemsize + 8)           # + two fp32 rstd
+
+    def _kept(self, u: int) -> bool:
+        return self.keep_layers > 0 and u > self.w.num_units - 2 - self.keep_layers
+
     @torch.no_grad()
     def forward_hidden(self, b: Batch, checkpoints: Optional[list] = None,
-                       attn_saves: Optional[list] = None) -> torch.Tensor:
+                       attn_saves: Optional[list] = None, contexts: Optional[dict] = None) -> torch.Tensor:
         """Forward to the last hidden state. ``checkpoints`` collects each
         layer's input; ``attn_saves`` (selective checkpointing) also keeps each
         layer's attention output and logsumexp so the backward does not
-        recompute attention."""
+        recompute attention; ``contexts`` receives the whole forward context of
+        the layers selected by ``keep_layers`` (no recompute at all)."""
         x = ops.embed_fwd(b.ids, self.w.views(0)["embed"])
         hook = self.param_hook
         last = self.w.num_units - 2
@@ -366,7 +384,14 @@ class Qwen3Engine:
                 checkpoints.append(x)
             if hook is not None:
                 hook.acquire(u, u + 1 if u < last else None)
-            x, _ = self._layer_fwd(u, x, b, keep=False, save_attn=attn_saves)
+            if contexts is not None and self._kept(u) and self.w.layouts[u].kind != "moe_layer":
+                xin = x
+                x, contexts[u] = self._layer_fwd(u, x, b, keep=True)
+                if attn_saves is not None:
+                    attn_saves.append(None)
+                del xin
+            else:
+                x, _ = self._layer_fwd(u, x, b, keep=False, save_attn=attn_saves)
         return x
 
     @torch.no_grad()
@@ -398,7 +423,8 @@ class Qwen3Engine:
         assert (coef is None) != (coef_fn is None), "pass exactly one of coef / coef_fn"
         ckpts: list = []
         asaves: Optional[list] = [] if self.save_attention else None
-        x = self.forward_hidden(b, ckpts, asaves)
+        kept: dict = {}
+        x = self.forward_hidden(b, ckpts, asaves, kept)
         uh = self.w.num_units - 1
         Wn = self.w.views(uh)["norm"]
         T = b.num_tokens
@@ -433,7 +459,9 @@ class Qwen3Engine:
             if self.param_hook is not None:
                 self.param_hook.acquire(u, u - 1 if u > 1 else None)
                 self.param_hook.begin_bwd(u)
-            _, ctx = self._layer_fwd(u, xin, b, keep=True, attn_saved=saved)
+            ctx = kept.pop(u, None)
+            if ctx is None:
+                _, ctx = self._layer_fwd(u, xin, b, keep=True, attn_saved=saved)
             dx = self._layer_bwd(u, xin, dx, ctx, b)
             if self.param_hook is not None:
                 self.param_hook.end_bwd(u)

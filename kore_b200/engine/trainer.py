@@ -42,7 +42,8 @@ class CausalLMTrainer:
                  micro_batch_size: int = 1, logits_chunk: int = 4096, schedule: str = "constant",
                  warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
                  weights: Optional[Qwen3Weights] = None, micro_tokens_hint: int = 8192,
-                 ep_capacity: float = 2.0, zero_stage: int = 2):
+                 ep_capacity: float = 2.0, zero_stage: int = 2, recompute: str = "auto",
+                 activation_reserve_gb: float = 12.0):
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device
@@ -118,12 +119,49 @@ class CausalLMTrainer:
                              max_grad_norm=max_grad_norm, master=master, schedule=schedule,
                              warmup_steps=warmup_steps, total_steps=total_steps, seed=seed)
         self._count = torch.zeros(1, dtype=torch.float32, device=dev)
+        if recompute not in ("auto", "full", "none"):
+            raise ValueError("recompute must be auto|full|none")
+        self.recompute = recompute
+        self.reserve_bytes = int(activation_reserve_gb * 1e9)
+        self._planned_tokens = None
+
+    def plan_activations(self, micro_tokens: int) -> int:
+        """Choose how many decoder layers keep their whole forward context
+        (no recompute in the backward) for micro-batches of ``micro_tokens``.
+
+        ``full``: none (every layer recomputes its GEMMs from its checkpointed
+        input); ``none``: all; ``auto``: as many as fit in the HBM left after
+        weights, gradients and optimizer state, minus a reserve for the head
+        chunks and one recomputed layer. The choice is agreed as the minimum
+        over ranks so every rank runs the same schedule."""
+        L = self.cfg.num_hidden_layers
+        if self.recompute == "full" or self.cfg.is_moe:
+            keep = 0
+        elif self.recompute == "none":
+            keep = L
+        elif self.ctx.device.type != "cuda":
+            keep = 0
+        else:
+            free, _ = torch.cuda.mem_get_info(self.ctx.device)
+            free += torch.cuda.memory_reserved(self.ctx.device) - torch.cuda.memory_allocated(self.ctx.device)
+            per = self.eng.activation_bytes_per_layer(micro_tokens)
+            budget = free - self.reserve_bytes - per
+            keep = int(max(0, min(L, budget // per)))
+        if self.ctx.world > 1:
+            t = torch.tensor([float(keep)], device=self.ctx.device)
+            self.ctx.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            keep = int(t.item())
+        self.eng.keep_layers = keep
+        self._planned_tokens = micro_tokens
+        return keep
 
     @torch.no_grad()
     def train_step_device(self, ids: torch.Tensor, loss_mask: Optional[torch.Tensor] = None
                           ) -> torch.Tensor:
         """ids/loss_mask: [B, S] on the device. Returns the global mean loss (device)."""
         B, S = ids.shape
+        if self._planned_tokens != min(self.mbs, B) * S:
+            self.plan_activations(min(self.mbs, B) * S)
         lab = torch.zeros_like(ids, dtype=torch.bool)
         lab[:, :-1] = True if loss_mask is None else loss_mask[:, 1:].bool()
         self._count.fill_(0)

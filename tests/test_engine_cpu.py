@@ -114,3 +114,20 @@ def test_corrupt_checkpoint_is_skipped(tmp_path):
     data = f.read_bytes()
     f.write_bytes(data[: len(data) // 2])                    # a crash mid-save
     assert latest_checkpoint(str(tmp_path)).endswith("checkpoint-1")
+
+
+def test_kept_layer_contexts_match_recompute():
+    """Keeping whole layer contexts (no recompute) gives the same gradients."""
+    cfg, w, b = _setup(3)
+    eng = Qwen3Engine(w)
+    coef = eng.sft_coef(b)
+    eng.zero_grad()
+    eng.forward_backward(b, coef=coef)
+    g_full = [g.clone() for g in eng.grads]
+    for keep in (1, cfg.num_hidden_layers):
+        eng.keep_layers = keep
+        eng.zero_grad()
+        eng.forward_backward(b, coef=coef)
+        for a, c in zip(g_full, eng.grads):
+            assert torch.allclose(a, c, atol=1e-6, rtol=1e-5)
+    assert eng.activation_bytes_per_layer(10) > 0
