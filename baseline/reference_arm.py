@@ -106,7 +106,12 @@ def run(args, clock_sampler_cls) -> None:
         module.to_empty(device=dev, recurse=False)
         with torch.no_grad():
             if isinstance(module, Qwen3RotaryEmbedding):
-                inv, _ = module.rope_init_fn(module.config, dev)
+                fn = getattr(module, "rope_init_fn", None)
+                if fn is None:
+                    from transformers.modeling_rope_utils import ROPE_INIT_FUNCTIONS
+                    fn = (module.compute_default_rope_parameters if module.rope_type == "default"
+                          else ROPE_INIT_FUNCTIONS[module.rope_type])
+                inv, _ = fn(module.config, dev)
                 module.inv_freq.copy_(inv)
                 module.original_inv_freq.copy_(inv)
                 return

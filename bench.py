@@ -121,6 +121,94 @@ def reference_arm(args) -> None:
     ra.run(args, ClockSampler)
 
 
+def grpo_main(args) -> None:
+    """GRPO-step tokens/s (BASELINE GRPO row): multi-turn rollout + reference
+    log-probs + update + weight sync, one optimizer step per GRPO step.
+
+    Weak scaling: every GPU rolls 8 prompts x group 8 = 64 trajectories (at
+    N = 8 that is the 64 x 8 of the BASELINE config), 1024-token prompts, 3
+    turns of up to 2048 sampled tokens (temperature 1.0) with 32 feedback
+    tokens between turns, synthetic per-turn rewards {0, 0.1, 0.3} + 0.9 Phi' -
+    Phi, clip 0.2, KL beta 0.01 against a frozen reference copy. Tokens counted
+    = every trajectory's final transcript (prompt + generations + feedback)."""
+    import torch
+
+    from kore_b200 import ops
+    from kore_b200.env.base import SyntheticRewardEnv
+    from kore_b200.models import PRESETS, Qwen3Weights
+    from kore_b200.parallel.dist import init_distributed
+    from kore_b200.policy.configs import GRPOConfig
+    from kore_b200.policy.grpo import GRPOTrainer
+
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    ctx = init_distributed()
+    cfg = PRESETS[args.model]()
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
+    ops.native()
+    W = ctx.world
+    G = 8
+    gc = GRPOConfig(num_trajectories=G, num_turns=args.turns, tasks_per_step=8 * W,
+                    max_response_length=args.gen_len, max_prompt_length=16384, max_feedback_tokens=32,
+                    learning_rate=1e-6, temperature=1.0, top_p=1.0, clip_ratio_low=0.2, clip_ratio_high=0.2,
+                    ref_anchor_coef=0.01, dynamic_sampling=False, starpo_s=False, bf16=True,
+                    overlong_mask=False, total_steps=args.warmup + args.steps, kv_page_size=64,
+                    reward_env="synthetic", seed=0, offload_state=args.offload)
+    gc.comm = args.comm
+    env = SyntheticRewardEnv(seed=0, prompt_len=args.prompt_len, feedback_len=32, vocab_size=cfg.vocab_size)
+    w = Qwen3Weights(cfg, device=ctx.device, dtype=torch.bfloat16, seed=0, pad_multiple=128 * max(1, W))
+    tr = GRPOTrainer(gc, weights=w, env=env, ctx=ctx,
+                     rollout_kwargs=dict(max_batch=G * 8, page_size=64, max_seq_len=16384))
+    del w
+    tasks = [f"synthetic-{i}" for i in range(8 * W)]
+    for _ in range(args.warmup):
+        st = tr.train_step(tasks, micro_batch_tokens=args.micro_tokens)
+    torch.cuda.synchronize()
+    ctx.barrier()
+    ops.reset_launch_count()
+    clk = ClockSampler(ctx.local_rank).start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    toks, phases = 0, {}
+    for _ in range(args.steps):
+        st = tr.train_step(tasks, micro_batch_tokens=args.micro_tokens)
+        toks += st["traj_tokens"]
+        for k, v in st.items():
+            if k.startswith("ms_"):
+                phases[k[3:]] = phases.get(k[3:], 0.0) + v / args.steps
+    e1.record()
+    torch.cuda.synchronize()
+    wall = (time.perf_counter() - t0) * 1000 / args.steps
+    clocks = clk.stop()
+    ms = ctx.max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    wall_ms = ctx.max_over_ranks(wall)
+    t = torch.tensor([float(toks) / args.steps], device=ctx.device)
+    ctx.all_reduce(t)
+    tokens = float(t.item())
+    if ctx.is_main:
+        print(json.dumps({
+            "metric": "grpo_step_tokens_per_s", "value": tokens / (ms / 1000.0), "unit": "tokens/s",
+            "n_gpus": W, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic uniform-random prompts and feedback, synthetic rewards, random-init weights",
+            "config": {"model": "qwen3-14b-arch (dense)" if args.model == "qwen3-14b" else args.model,
+                       "layers": cfg.num_hidden_layers, "prompts": 8 * W, "group": G,
+                       "trajectories_per_gpu": 8 * G, "prompt_len": args.prompt_len, "turns": args.turns,
+                       "max_new_per_turn": args.gen_len, "feedback_tokens": 32,
+                       "tokens_per_step": tokens, "gen_tokens_per_step_rank0": st["gen_tokens"],
+                       "parallelism": f"dp{W} replicated rollout" + (f", zero2-{args.comm}" if W > 1 else ""),
+                       "clip": 0.2, "kl_beta": 0.01, "temperature": 1.0,
+                       "offload": {"optimizer_state": st.get("offload_opt"), "ref_model": st.get("offload_ref")},
+                       "l2": "inputs larger than L2 (weights and KV cache streamed every decode step)"},
+            "phases_ms": phases, "clocks": clocks, "gpu_launches": ops.launch_count(),
+            "e2e": {"value": tokens / (wall_ms / 1000.0), "unit": "tokens/s", "ms_per_step": wall_ms,
+                    "h2d_bytes_per_step": int(8 * W * G * (args.prompt_len + 32 * (args.turns - 1)) * 8 / W),
+                    "d2h_bytes_per_step": int(8 * G * (args.turns * args.gen_len) * 12)},
+            "memory": {"peak_allocated_gb": round(torch.cuda.max_memory_allocated() / 1e9, 2)},
+            "impl": "kore"}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -133,6 +221,13 @@ def main(argv=None):
     ap.add_argument("--micro-batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--metric", default="sft", choices=["sft", "grpo"])
+    ap.add_argument("--turns", type=int, default=3, help="grpo: turns per trajectory")
+    ap.add_argument("--gen-len", type=int, default=2048, help="grpo: max sampled tokens per turn")
+    ap.add_argument("--prompt-len", type=int, default=1024, help="grpo: prompt tokens")
+    ap.add_argument("--micro-tokens", type=int, default=8192, help="grpo: tokens per update micro-batch")
+    ap.add_argument("--offload", default="auto", choices=["auto", "always", "never"],
+                    help="grpo: park optimizer state / reference model in host memory between phases")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="data plane of the sharded optimizer (N > 1)")
     ap.add_argument("--recompute", default="auto", choices=["auto", "full", "none"],
@@ -141,7 +236,14 @@ def main(argv=None):
                     help="2: resident params, sharded grads/optimizer; 3: decoder layers fully sharded")
     args = ap.parse_args(argv)
     if args.impl == "reference":
+        if args.metric != "sft":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference's GRPO loop needs trl + "
+                                  "accelerate (not installable offline); only the SFT arm has an equivalent"}))
+            return None
         return reference_arm(args)
+    if args.metric == "grpo":
+        return grpo_main(args)
 
     import torch
 

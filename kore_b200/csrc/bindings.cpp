@@ -46,7 +46,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor
                      int64_t nsplit, at::Tensor& out, const c10::optional<at::Tensor>& part_o,
                      const c10::optional<at::Tensor>& part_ml);
 void sample_tokens(const at::Tensor& logits, double temperature, double top_p, int64_t seed,
-                   int64_t step, at::Tensor& tokens, at::Tensor& logprobs);
+                   int64_t step, at::Tensor& tokens, at::Tensor& logprobs,
+                   const c10::optional<at::Tensor>& step_dev);
 int64_t symm_heap_create(int64_t bytes, int64_t rank, int64_t world);
 at::Tensor symm_heap_handle(int64_t id);
 void symm_heap_open(int64_t id, const at::Tensor& handles);
@@ -107,7 +108,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd", &kore::attn_bwd, "tcgen05 causal GQA flash attention backward");
   m.def("kv_append", &kore::kv_append);
   m.def("paged_attention", &kore::paged_attention);
-  m.def("sample_tokens", &kore::sample_tokens);
+  m.def("sample_tokens", &kore::sample_tokens, "temperature / top-p sampler",
+        py::arg("logits"), py::arg("temperature"), py::arg("top_p"), py::arg("seed"), py::arg("step"),
+        py::arg("tokens"), py::arg("logprobs"), py::arg("step_dev") = py::none());
   m.def("symm_heap_create", &kore::symm_heap_create);
   m.def("symm_heap_handle", &kore::symm_heap_handle);
   m.def("symm_heap_open", &kore::symm_heap_open);

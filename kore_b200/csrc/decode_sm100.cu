@@ -177,6 +177,133 @@ __global__ void __launch_bounds__(kWarps * 32) paged_attn_kernel(AttnParams p, i
   }
 }
 
+// Decode (one query token per sequence), key-per-lane layout: every lane of a
+// warp owns one key of a 32-key chunk, reads that key's whole 256-byte K row
+// and scores it against the G query heads kept in shared memory, so the
+// softmax needs one warp max per chunk instead of a shuffle tree per key. The
+// P.V product then walks the chunk's V rows with lanes spread over D (coalesced
+// 256-byte rows). 32-key chunks never cross a page (page_size % 32 == 0).
+// Partial results use the layout of paged_attn_kernel, so paged_combine_kernel
+// merges the splits.
+template <int G>
+__global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(AttnParams p) {
+  const int seq = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int trow = p.q_start[seq];
+  const int nkeys = p.seq_lens[seq];
+  const int per = ((nkeys + p.nsplit - 1) / p.nsplit + 31) & ~31;
+  const int k_begin = split * per;
+  const int k_end = min(nkeys, k_begin + per);
+  __shared__ __align__(16) float sq[G][D];
+  __shared__ float sp[kWarps][G][32];
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    sq[g][d] = __bfloat162float(p.q[(size_t)trow * p.ldq + (kvh * G + g) * D + d]) * p.scale_log2;
+  }
+  __syncthreads();
+  float m[G], l[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+  }
+  const int* bt = p.block_table + (size_t)seq * p.max_pages;
+  const size_t hstride = (size_t)p.Hkv * D;
+  for (int c = k_begin + warp * 32; c < k_end; c += kWarps * 32) {
+    const int page = bt[c / p.page_size];
+    const size_t base = ((size_t)page * p.page_size + c % p.page_size) * hstride + (size_t)kvh * D;
+    const int key = c + lane;
+    const bool valid = key < k_end;
+    float s[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) s[g] = 0.f;
+    if (valid) {
+      const uint4* kr = reinterpret_cast<const uint4*>(p.kc + base + (size_t)lane * hstride);
+#pragma unroll 4
+      for (int j = 0; j < D / 8; ++j) {
+        const uint4 u = kr[j];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const float2 k0 = __bfloat1622float2(h[0]), k1 = __bfloat1622float2(h[1]);
+        const float2 k2 = __bfloat1622float2(h[2]), k3 = __bfloat1622float2(h[3]);
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(&sq[g][j * 8]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sq[g][j * 8 + 4]);
+          s[g] += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y +
+                  qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float cm = valid ? s[g] : -INFINITY;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffff, cm, o));
+      const float mn = fmaxf(m[g], cm);
+      const float corr = exp2f(m[g] - mn);
+      const float e = valid ? exp2f(s[g] - mn) : 0.f;
+      l[g] = l[g] * corr + e;                 // per-lane partial of the row sum
+      acc[g][0] *= corr; acc[g][1] *= corr; acc[g][2] *= corr; acc[g][3] *= corr;
+      m[g] = mn;
+      sp[warp][g][lane] = e;
+    }
+    __syncwarp();
+    const int nk = min(32, k_end - c);
+    const __nv_bfloat16* vr = p.vc + base + lane * 4;
+#pragma unroll 8
+    for (int kk = 0; kk < nk; ++kk) {
+      const uint2 vu = *reinterpret_cast<const uint2*>(vr + (size_t)kk * hstride);
+      const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.x));
+      const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.y));
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float pe = sp[warp][g][kk];
+        acc[g][0] += pe * va.x; acc[g][1] += pe * va.y; acc[g][2] += pe * vb.x; acc[g][3] += pe * vb.y;
+      }
+    }
+    __syncwarp();
+  }
+  // row sums across lanes, then merge the warps through shared memory
+  __shared__ float sm_m[kWarps][G], sm_l[kWarps][G];
+  __shared__ float sm_acc[kWarps][G][D];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float t = l[g];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
+    if (lane == 0) { sm_m[warp][g] = m[g]; sm_l[warp][g] = t; }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sm_acc[warp][g][lane * 4 + e] = acc[g][e];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int g = idx / D, d = idx % D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, sm_m[w][g]);
+    float ll = 0.f, aa = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      if (sm_m[w][g] == -INFINITY) continue;
+      const float c = exp2f(sm_m[w][g] - mm);
+      ll += sm_l[w][g] * c;
+      aa += sm_acc[w][g][d] * c;
+    }
+    const int h = kvh * G + g;
+    if (p.nsplit == 1) {
+      p.out[((size_t)trow * p.Hq + h) * D + d] = __float2bfloat16(ll > 0.f ? aa / ll : 0.f);
+    } else {
+      const size_t tq = (size_t)p.q_start[gridDim.x];
+      const size_t o = ((size_t)split * tq + trow) * p.Hq + h;
+      p.part_o[o * D + d] = aa;
+      if (d == 0) {
+        p.part_ml[o * 2 + 0] = mm;
+        p.part_ml[o * 2 + 1] = ll;
+      }
+    }
+  }
+}
+
 __global__ void paged_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                      __nv_bfloat16* __restrict__ out, int Tq, int Hq, int nsplit) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // over Tq * Hq * D
@@ -234,7 +361,9 @@ KORE_DEV float blk_reduce(float v, float* red, bool is_max) {
 // the temperature-scaled full distribution.
 __global__ void __launch_bounds__(kSampThreads) sample_kernel(
     const __nv_bfloat16* __restrict__ logits, int ld, int V, float inv_temp, float top_p,
-    uint32_t seed, uint32_t step, int greedy, long* __restrict__ out_tok, float* __restrict__ out_lp) {
+    uint32_t seed, uint32_t step, const int* __restrict__ step_ptr, int greedy, long* __restrict__ out_tok,
+    float* __restrict__ out_lp) {
+  if (step_ptr != nullptr) step = (uint32_t)*step_ptr;
   __shared__ float red[32];
   __shared__ float s_best[32];
   __shared__ int s_bidx[32];
@@ -349,9 +478,23 @@ void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor
   p.part_ml = nsplit > 1 ? part_ml->data_ptr<float>() : nullptr;
   p.out = (__nv_bfloat16*)out.data_ptr();
   auto st = at::cuda::getCurrentCUDAStream();
-  dim3 grid(nseq * max_q, Hkv, nsplit);
-  paged_attn_kernel<<<grid, kWarps * 32, 0, st>>>(p, (int)max_q);
-  check_cuda(cudaGetLastError(), "paged_attn");
+  const int G = Hq / Hkv;
+  if (max_q == 1 && page_size % 32 == 0 && Tq == nseq) {
+    dim3 grid(nseq, Hkv, nsplit);
+    switch (G) {
+      case 1: paged_decode_kernel<1><<<grid, kWarps * 32, 0, st>>>(p); break;
+      case 2: paged_decode_kernel<2><<<grid, kWarps * 32, 0, st>>>(p); break;
+      case 4: paged_decode_kernel<4><<<grid, kWarps * 32, 0, st>>>(p); break;
+      case 5: paged_decode_kernel<5><<<grid, kWarps * 32, 0, st>>>(p); break;
+      case 8: paged_decode_kernel<8><<<grid, kWarps * 32, 0, st>>>(p); break;
+      default: paged_attn_kernel<<<dim3(nseq, Hkv, nsplit), kWarps * 32, 0, st>>>(p, 1);
+    }
+    check_cuda(cudaGetLastError(), "paged_decode");
+  } else {
+    dim3 grid(nseq * max_q, Hkv, nsplit);
+    paged_attn_kernel<<<grid, kWarps * 32, 0, st>>>(p, (int)max_q);
+    check_cuda(cudaGetLastError(), "paged_attn");
+  }
   if (nsplit > 1) {
     const long n = (long)Tq * Hq * D;
     paged_combine_kernel<<<(int)((n + 255) / 256), 256, 0, st>>>(p.part_o, p.part_ml, p.out, Tq, Hq, nsplit);
@@ -360,7 +503,8 @@ void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor
 }
 
 void sample_tokens(const at::Tensor& logits, double temperature, double top_p, int64_t seed,
-                   int64_t step, at::Tensor& tokens, at::Tensor& logprobs) {
+                   int64_t step, at::Tensor& tokens, at::Tensor& logprobs,
+                   const c10::optional<at::Tensor>& step_dev) {
   using namespace dec;
   TORCH_CHECK(logits.scalar_type() == at::kBFloat16 && logits.stride(1) == 1, "logits bf16 rows");
   const int B = logits.size(0), V = logits.size(1);
@@ -370,7 +514,8 @@ void sample_tokens(const at::Tensor& logits, double temperature, double top_p, i
   sample_kernel<<<B, kSampThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)logits.data_ptr(), logits.stride(0), V,
       greedy ? 1.f : (float)(1.0 / temperature), greedy ? 1.f : (float)top_p, (uint32_t)seed,
-      (uint32_t)step, greedy ? 1 : 0, tokens.data_ptr<long>(), logprobs.data_ptr<float>());
+      (uint32_t)step, step_dev ? step_dev->data_ptr<int>() : nullptr, greedy ? 1 : 0, tokens.data_ptr<long>(),
+      logprobs.data_ptr<float>());
   check_cuda(cudaGetLastError(), "sample_tokens");
 }
 

@@ -66,7 +66,18 @@ struct Params {
   int rs_rows;
   int rs_rank;
   void* rs_out[8];
+  // split-K (skinny problems such as decode, M <= a few hundred rows): work unit
+  // t covers output tile t % (num_m*num_n) over K blocks of split t / (num_m*num_n);
+  // the fp32 partial tile goes to rows split*ws_rows + m of the workspace map tmC
+  int splits = 1;
+  int ws_rows = 0;
 };
+
+// K blocks [kb0, kb1) of split s when `kblocks` are divided over `splits`.
+KORE_DEV void split_range(int s, int splits, int kblocks, int& kb0, int& kb1) {
+  kb0 = (int)(((long)s * kblocks) / splits);
+  kb1 = (int)(((long)(s + 1) * kblocks) / splits);
+}
 
 template <int BN, int STAGES>
 struct Smem {
@@ -107,7 +118,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  const int num_mn = num_m * num_n;
+  const int num_tiles = num_mn * p.splits;
   const int kblocks = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -173,8 +185,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
+        int tm, tn, kb0, kb1;
+        tile_coords(t % num_mn, num_m, num_n, tm, tn);
+        split_range(t / num_mn, p.splits, kblocks, kb0, kb1);
         if (p.ag_rot) tm = (tm + p.ag_rot) % num_m;
         int m0 = tm * BM, ex = 0;
         const int n0 = tn * BN;
@@ -190,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ready) { *abort_flag = 1; break; }
           fence_proxy_async_global();    // generic-proxy copies -> TMA reads
         }
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
           uint8_t* sB = sA + S::A_BYTES;
@@ -237,7 +250,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        int kb0, kb1;
+        split_range(t / num_mn, p.splits, kblocks, kb0, kb1);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(smem + stage * S::STAGE_BYTES);
@@ -248,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                : make_sw128_desc(a_addr + k * 32, 16, 1024);
             uint64_t bd = B_MN ? make_sw128_desc(b_addr + k * 2048, 8192, 1024)
                                : make_sw128_desc(b_addr + k * 32, 16, 1024);
-            umma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) != 0);
+            umma_f16_ss(d_tmem, ad, bd, idesc, (kb != kb0) || (k != 0));
           }
           umma_commit(&empty_bar[stage]);
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -268,7 +283,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int CH = p.out_f32 ? 32 : 64;  // output columns per 128-byte staging row
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
       int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
+      tile_coords(t % num_mn, num_m, num_n, tm, tn);
+      const int ws_row0 = (t / num_mn) * p.ws_rows;   // split-K: this split's workspace rows
       if (p.ag_rot) tm = (tm + p.ag_rot) % num_m;
       int m0 = tm * BM, m_lim = p.M;
       const int n0 = tn * BN;
@@ -391,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, stage_buf + buf * kStageBytesC, n0 + c0, m0 + q * 32);
+          tma_store_2d(&tmC, stage_buf + buf * kStageBytesC, n0 + c0, ws_row0 + m0 + q * 32);
           tma_store_commit();
         }
         buf ^= 1;
@@ -437,6 +453,55 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
   }
   k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, p);
   check_cuda(cudaGetLastError(), "gemm launch");
+}
+
+// Sum of the split-K partials (+ old C when accumulating, + residual) into C.
+// One thread per 4 consecutive columns; N % 8 == 0.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int ws_rows, int M, int N,
+                                     void* __restrict__ out, int ldc, int out_f32, int accumulate,
+                                     const __nv_bfloat16* __restrict__ R, int ldr) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int n4 = N / 4;
+  if (i >= (long)M * n4) return;
+  const int m = (int)(i / n4), n = (int)(i % n4) * 4;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s = 0; s < splits; ++s) {
+    const float4 v = *reinterpret_cast<const float4*>(ws + ((size_t)s * ws_rows + m) * N + n);
+    acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if (R != nullptr) {
+    const __nv_bfloat162* r = reinterpret_cast<const __nv_bfloat162*>(R + (size_t)m * ldr + n);
+    const float2 a = __bfloat1622float2(r[0]), b = __bfloat1622float2(r[1]);
+    acc.x += a.x; acc.y += a.y; acc.z += b.x; acc.w += b.y;
+  }
+  if (out_f32) {
+    float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)m * ldc + n);
+    if (accumulate) { const float4 c = *o; acc.x += c.x; acc.y += c.y; acc.z += c.z; acc.w += c.w; }
+    *o = acc;
+  } else {
+    __nv_bfloat162* o = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(out) +
+                                                          (size_t)m * ldc + n);
+    if (accumulate) {
+      const float2 a = __bfloat1622float2(o[0]), b = __bfloat1622float2(o[1]);
+      acc.x += a.x; acc.y += a.y; acc.z += b.x; acc.w += b.y;
+    }
+    o[0] = __floats2bfloat162_rn(acc.x, acc.y);
+    o[1] = __floats2bfloat162_rn(acc.z, acc.w);
+  }
+}
+
+// Number of K splits for a problem with `tiles` output tiles: minimises the
+// per-SM critical path ceil(tiles*s / sms) * ceil(kblocks / s); 1 when the
+// output tiles alone fill the GPU.
+int choose_splits(int tiles, int kblocks, int sms) {
+  if (tiles >= sms || kblocks < 8) return 1;
+  long best = -1;
+  int bs = 1;
+  for (int s = 1; s <= 16 && s <= kblocks / 4; ++s) {
+    const long cost = (long)((tiles * s + sms - 1) / sms) * ((kblocks + s - 1) / s);
+    if (best < 0 || cost < best) { best = cost; bs = s; }
+  }
+  return bs;
 }
 
 }  // namespace gemm
@@ -494,18 +559,42 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
     p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
     p.ldr = residual->stride(0);
   }
-  const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  const int sms = num_sms(a.get_device());
+  const int kblocks = (K + 63) / 64;
+  bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  int splits = 1;
+  if (max_ctas <= 0 && M <= 512) {   // skinny (decode-sized) problem: split K over the SMs
+    const int t128 = ((M + 127) / 128) * ((N + 127) / 128);
+    const int t = use256 ? ((M + 127) / 128) * ((N + 255) / 256) : t128;
+    if (t < sms) {
+      use256 = false;
+      splits = gemm::choose_splits(t128, kblocks, sms);
+    }
+  }
   const int BN = use256 ? 256 : 128;
   auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta = a_mn ? make_tmap_2d(a.data_ptr(), bf, 2, M, K, a.stride(0), 64, 64)
                         : make_tmap_2d(a.data_ptr(), bf, 2, K, M, a.stride(0), 64, 128);
   CUtensorMap tb = b_mn ? make_tmap_2d(b.data_ptr(), bf, 2, N, K, b.stride(0), 64, 64)
                         : make_tmap_2d(b.data_ptr(), bf, 2, K, N, b.stride(0), 64, BN);
-  CUtensorMap tc = f32 ? make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M,
-                                      out.stride(0), 32, 32)
-                       : make_tmap_2d(out.data_ptr(), bf, 2, N, M, out.stride(0), 64, 32);
-  const int tiles = ((M + 127) / 128) * ((N + BN - 1) / BN);
-  int grid = std::min(tiles, num_sms(a.get_device()));
+  at::Tensor ws;
+  CUtensorMap tc;
+  if (splits > 1) {
+    // fp32 partial tiles [splits, ws_rows, N]; the reduce kernel applies accumulate / residual
+    p.splits = splits;
+    p.ws_rows = ((M + 127) / 128) * 128;
+    ws = at::empty({(int64_t)splits * p.ws_rows, N}, a.options().dtype(at::kFloat));
+    p.out_f32 = 1;
+    p.accumulate = 0;
+    p.R = nullptr;
+    tc = make_tmap_2d(ws.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, (uint64_t)splits * p.ws_rows, N,
+                      32, 32);
+  } else {
+    tc = f32 ? make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M, out.stride(0), 32, 32)
+             : make_tmap_2d(out.data_ptr(), bf, 2, N, M, out.stride(0), 64, 32);
+  }
+  const int tiles = ((M + 127) / 128) * ((N + BN - 1) / BN) * splits;
+  int grid = std::min(tiles, sms);
   if (max_ctas > 0) grid = std::min<int>(grid, (int)max_ctas);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
 #define KORE_GEMM_DISPATCH(BN_, ST_)                                              \
@@ -519,6 +608,16 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
     KORE_GEMM_DISPATCH(128, 6)
   }
 #undef KORE_GEMM_DISPATCH
+  if (splits > 1) {
+    const long n = (long)M * (N / 4);
+    gemm::splitk_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(
+        ws.data_ptr<float>(), splits, p.ws_rows, M, N, out.data_ptr(), (int)out.stride(0), f32 ? 1 : 0,
+        accumulate ? 1 : 0,
+        residual ? reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr()) : nullptr,
+        residual ? (int)residual->stride(0) : 0);
+    check_cuda(cudaGetLastError(), "split-K reduce launch");
+    ws.record_stream(at::cuda::getCurrentCUDAStream());
+  }
 }
 
 

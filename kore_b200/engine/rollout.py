@@ -112,18 +112,48 @@ class RolloutEngine:
         self.page_size = page_size
         self.max_pages_per_seq = (max_seq_len + page_size - 1) // page_size
         self.split_kv_min = split_kv_min
-        if num_pages is None:
-            per = PagedKVCache.bytes_per_page(c.num_hidden_layers, page_size, self.hkv, self.D)
-            if self.dev.type == "cuda":
-                free, _ = torch.cuda.mem_get_info(self.dev)
-                num_pages = max(16, int(free * kv_fraction) // per)
-            else:
-                num_pages = max(16, (256 << 20) // per)
-        self.cache = PagedKVCache(c.num_hidden_layers, num_pages, page_size, self.hkv, self.D, self.dev,
-                                  weights.dtype)
+        self.kv_fraction = kv_fraction
+        self._num_pages = num_pages
+        self._cache: Optional[PagedKVCache] = None
         self.cos, self.sin = ref.rope_tables(c.max_position_embeddings, self.D, c.rope_theta, self.dev)
         self._step = 0
         self._prefix: Dict[object, tuple] = {}
+
+    # ------------------------------------------------------------------ KV pool
+    def kv_bytes_per_token(self) -> int:
+        return PagedKVCache.bytes_per_page(self.cfg.num_hidden_layers, 1, self.hkv, self.D,
+                                           self.w.dtype.itemsize)
+
+    @property
+    def cache(self) -> PagedKVCache:
+        """The paged KV pool, allocated on first use: ``num_pages`` when given,
+        else ``kv_fraction`` of the HBM free at that moment."""
+        if self._cache is None:
+            self.ensure_cache()
+        return self._cache
+
+    def ensure_cache(self, num_pages: Optional[int] = None) -> PagedKVCache:
+        c = self.cfg
+        want = num_pages or self._num_pages
+        if self._cache is not None and (want is None or self._cache.num_pages >= want):
+            return self._cache
+        self._cache = None
+        if want is None:
+            per = PagedKVCache.bytes_per_page(c.num_hidden_layers, self.page_size, self.hkv, self.D)
+            if self.dev.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(self.dev)
+                free += torch.cuda.memory_reserved(self.dev) - torch.cuda.memory_allocated(self.dev)
+                want = max(16, int(free * self.kv_fraction) // per)
+            else:
+                want = max(16, (256 << 20) // per)
+        self._cache = PagedKVCache(c.num_hidden_layers, want, self.page_size, self.hkv, self.D, self.dev,
+                                   self.w.dtype)
+        return self._cache
+
+    def release_cache(self) -> None:
+        """Free the KV pool (it is re-allocated on next use); for phases of a
+        training step that need the HBM back."""
+        self._cache = None
 
     # ------------------------------------------------------------------ model
     def _forward(self, seqs: List[_Seq], fresh: bool, want_logits: bool = True):

@@ -216,6 +216,11 @@ class GRPOConfig(DistributedMixin):
     kv_page_size: int = 128             # tokens per paged-KV page
     kv_cache_fraction: float = 0.35     # fraction of free HBM reserved for the KV pool
     reward_env: str = "kernel"          # "kernel" (KoreEnv) | "synthetic" (benchmark reward)
+    batched_rollout: bool = True        # all groups of a step in one multi-turn batch (CUDA-graph decode)
+    max_feedback_tokens: int = 1024     # per-turn feedback budget of the batched rollout
+    pack_trajectories: bool = True      # train all turns of a trajectory in one packed sequence
+    old_logp_source: str = "trainer"    # "trainer" (policy forward of the update) | "sampler"
+    offload_state: str = "auto"         # optimizer state / frozen ref to host between phases: auto|always|never
 
 
 @dataclass

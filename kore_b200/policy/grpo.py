@@ -65,6 +65,8 @@ class TrainSample:
     old_logp: Optional[float] = None
     ref_logp: Optional[float] = None
     overlong: bool = False
+    row: Optional[tuple] = None     # (group, trajectory): samples of one trajectory share a packed row
+    turn: int = 0
 
     @property
     def n_gen(self) -> int:
@@ -97,7 +99,9 @@ class GRPOTrainer:
                                        total_steps=config.total_steps, weights=weights,
                                        comm=getattr(config, "comm", "nccl"))
         self.trainer.eng.temperature = config.temperature
-        self.w = weights
+        # the trainer may have moved the weights (e.g. into the symmetric heap of
+        # the fused optimizer): rollout and reference read the trainer's copy
+        self.w = weights = self.trainer.w
         self.ref_w = ref_weights if ref_weights is not None else (
             weights.clone() if config.ref_anchor_coef else None)
         self.ref_eng = (Qwen3Engine(self.ref_w, allocate_grads=False, temperature=config.temperature)
@@ -163,8 +167,81 @@ class GRPOTrainer:
                 ctxs[i] = ctxs[i] + list(o.tokens) + self._feedback_ids(task, res, turn, tr.traj)
         return trajs
 
+    def rollout_batch(self, tasks: Sequence[Any], traj_ids: Sequence[int], *,
+                      max_new_tokens: Optional[int] = None) -> List[List[Trajectory]]:
+        """Every group of the step (``tasks`` x ``traj_ids``) in one multi-turn
+        batch on the CUDA-graph decode loop; groups share their prompt's KV pages.
+        Same transcripts as :meth:`rollout_group` while they fit ``max_prompt_length``."""
+        from ..engine.multiturn import MultiTurnRollout
+        cfg = self.cfg
+        max_new = max_new_tokens or cfg.max_response_length
+        G = len(traj_ids)
+        prompts, keys = [], []
+        for gi, task in enumerate(tasks):
+            base = self._initial_context(task)[-cfg.max_prompt_length:]
+            for _ in traj_ids:
+                prompts.append(list(base))
+                keys.append(gi)
+        groups = [[Trajectory(t) for t in traj_ids] for _ in tasks]
+        flat = [tr for g in groups for tr in g]
+
+        def on_turn(turn, outs):
+            for i, (o, tr) in enumerate(zip(outs, flat)):
+                tr.results.append(self.env.step(tasks[i // G], self._decode(o.gens[-1]), turn, tr.traj,
+                                                tr.results))
+
+        def feedback(turn, i, gen):
+            tr = flat[i]
+            return self._feedback_ids(tasks[i // G], tr.results[-1], turn, tr.traj)
+
+        outs = MultiTurnRollout(self.rollout).run(
+            prompts, num_turns=cfg.num_turns, max_new=max_new, feedback=feedback, share_keys=keys,
+            max_feedback=cfg.max_feedback_tokens, temperature=cfg.temperature, top_p=cfg.top_p,
+            eos_ids=self.eos, seed=cfg.seed * 1000003 + self.step_idx * 97, on_turn=on_turn)
+        for o, tr in zip(outs, flat):
+            tr.contexts, tr.gens, tr.gen_logps, tr.finish = o.contexts, o.gens, o.logps, o.finish
+        return groups
+
+    def memory_plan(self, trajectories: int, transcript: int) -> Dict[str, bool]:
+        """Which state to park in host memory during the phases of a step.
+
+        ``opt``: the optimizer moments / master leave HBM for the rollout and
+        the reference forward when the KV cache of ``trajectories`` transcripts
+        of ``transcript`` tokens would not fit next to them. ``ref``: the frozen
+        reference model leaves HBM for the update when the update's activations
+        would not fit next to everything else. Decided with every piece of
+        state resident; ``offload_state`` = always / never overrides."""
+        from ..engine.offload import optimizer_slots, slots_bytes, weight_slots
+        mode = self.cfg.offload_state
+        dev = self.ctx.device
+        if mode == "never" or dev.type != "cuda":
+            return {"opt": False, "ref": False}
+        if mode == "always":
+            return {"opt": True, "ref": self.ref_w is not None}
+        free, _ = torch.cuda.mem_get_info(dev)
+        free += torch.cuda.memory_reserved(dev) - torch.cuda.memory_allocated(dev)
+        kv = trajectories * transcript * self.rollout.kv_bytes_per_token()
+        margin = 10e9
+        opt_bytes = slots_bytes(optimizer_slots(self.trainer.opt))
+        need_opt = kv + margin > free
+        if need_opt and kv + margin > free + opt_bytes:
+            raise RuntimeError(f"rollout KV cache ({kv / 1e9:.1f} GB) does not fit even with the optimizer "
+                               f"state ({opt_bytes / 1e9:.1f} GB) parked in host memory")
+        act = 16e9 if self.trainer.eng.keep_layers == 0 else 16e9 + 40e9
+        need_ref = self.ref_w is not None and act > free
+        return {"opt": need_opt, "ref": need_ref}
+
+    def _batched_ok(self, max_new: int) -> bool:
+        cfg = self.cfg
+        synth = isinstance(self.env, SyntheticRewardEnv)
+        longest = self.env.prompt_len if synth else cfg.max_prompt_length
+        fb = min(self.env.feedback_len, cfg.max_feedback_tokens) if synth else cfg.max_feedback_tokens
+        transcript = longest + cfg.num_turns * (max_new + fb)
+        return (cfg.batched_rollout and transcript <= cfg.max_prompt_length + max_new
+                and transcript <= self.rollout.max_pages_per_seq * self.rollout.page_size)
+
     # ------------------------------------------------------------ credit
-    def samples_from_group(self, trajs: List[Trajectory]) -> List[TrainSample]:
+    def samples_from_group(self, trajs: List[Trajectory], group: int = 0) -> List[TrainSample]:
         cfg = self.cfg
         rewards = [[r.reward for r in t.results] for t in trajs]
         correct = [[r.correct for r in t.results] for t in trajs]
@@ -183,7 +260,8 @@ class GRPOTrainer:
             over = cfg.overlong_mask and M.is_overlong(n, cfg.max_response_length, cfg.overlong_buffer_len) \
                 and t.finish[tu] == "length"
             out.append(TrainSample(ids=t.contexts[tu] + t.gens[tu], n_ctx=len(t.contexts[tu]), ret=r,
-                                   old_logp=sum(gl) / max(1, len(gl)), overlong=over))
+                                   old_logp=sum(gl) / max(1, len(gl)), overlong=over,
+                                   row=(group, t.traj), turn=tu))
         return out
 
     def assign_advantages(self, groups: List[List[TrainSample]]) -> List[List[TrainSample]]:
@@ -204,51 +282,84 @@ class GRPOTrainer:
         return [groups[i] for i in kept_idx]
 
     # ------------------------------------------------------------ update
-    def _pack(self, samples: List[TrainSample], budget: int):
+    def _rows(self, samples: List[TrainSample]) -> List[List[TrainSample]]:
+        """Trajectory packing: the turn samples of one trajectory whose token
+        ids extend each other form one row (the longest sample's ids), each
+        turn's generated span labelled for its own sample. Causal attention
+        makes every span's log-probs identical to a forward of its own sample,
+        so all turns train in one forward over the transcript instead of one
+        forward per turn (the reference's per-sample backward,
+        kore/policy/grpo.py:613-701, recomputes each turn's whole context)."""
+        if not self.cfg.pack_trajectories:
+            return [[s] for s in samples]
+        keyed: Dict[Any, List[TrainSample]] = {}
+        order: List[Any] = []
+        for i, s in enumerate(samples):
+            k = s.row if s.row is not None else ("solo", i)
+            if k not in keyed:
+                keyed[k] = []
+                order.append(k)
+            keyed[k].append(s)
+        rows: List[List[TrainSample]] = []
+        for k in order:
+            chain: List[TrainSample] = []
+            for s in sorted(keyed[k], key=lambda x: len(x.ids)):
+                if chain and not (len(s.ids) >= len(chain[-1].ids) and s.ids[:len(chain[-1].ids)] == chain[-1].ids):
+                    rows.append(chain)
+                    chain = []
+                chain.append(s)
+            rows.append(chain)
+        return rows
+
+    def _pack(self, rows: List[List[TrainSample]], budget: int):
         cur, n = [], 0
-        for s in samples:
-            if cur and n + len(s.ids) > budget:
+        for r in rows:
+            L = len(r[-1].ids)
+            if cur and n + L > budget:
                 yield cur
                 cur, n = [], 0
-            cur.append(s)
-            n += len(s.ids)
+            cur.append(r)
+            n += L
         if cur:
             yield cur
 
-    def _batch(self, samples: List[TrainSample]):
+    def _batch(self, rows: List[List[TrainSample]]):
+        """Packed micro-batch of rows; returns (batch, samples in order, per-token sample index)."""
         from ..engine.qwen3_engine import Batch
         dev = self.ctx.device
-        seqs, masks = [], []
-        for s in samples:
-            seqs.append(torch.tensor(s.ids, dtype=torch.long))
-            m = torch.zeros(len(s.ids), dtype=torch.bool)
-            m[s.n_ctx:] = True
+        seqs, masks, flat = [], [], []
+        seg = []
+        for r in rows:
+            ids = r[-1].ids
+            seqs.append(torch.tensor(ids, dtype=torch.long))
+            m = torch.zeros(len(ids), dtype=torch.bool)
+            sg = torch.full((len(ids),), -1, dtype=torch.long)
+            for s in r:
+                m[s.n_ctx: len(s.ids)] = True
+                # label position j predicts token j + 1
+                sg[s.n_ctx - 1: len(s.ids) - 1] = len(flat)
+                flat.append(s)
             masks.append(m)
-        return Batch.from_sequences(seqs, masks, device=dev)
+            seg.append(sg)
+        b = Batch.from_sequences(seqs, masks, device=dev)
+        return b, flat, torch.cat(seg).to(dev)
 
     @staticmethod
-    def _segments(b, samples):
-        """Per-token sample index for label positions (target >= 0)."""
-        seg = torch.full((b.num_tokens,), -1, dtype=torch.long)
-        off = 0
-        for i, s in enumerate(samples):
-            L = len(s.ids)
-            seg[off + s.n_ctx - 1: off + L - 1] = i  # label positions predict generated tokens
-            off += L
-        return seg.to(b.ids.device)
+    def _sample_means(lp_full, seg, flat):
+        sums = torch.zeros(len(flat), dtype=torch.float64, device=lp_full.device)
+        sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, lp_full.double(),
+                                                         torch.zeros_like(lp_full, dtype=torch.float64)))
+        return [v / max(1, s.n_gen) for v, s in zip(sums.tolist(), flat)]
 
     @torch.no_grad()
     def fill_ref_logps(self, samples: List[TrainSample], budget: int):
         if self.ref_eng is None:
             return
-        for chunk in self._pack(samples, budget):
-            b = self._batch(chunk)
+        for chunk in self._pack(self._rows(samples), budget):
+            b, flat, seg = self._batch(chunk)
             lp, _ = self.ref_eng.token_logprobs(b)
-            seg = self._segments(b, chunk)
-            sums = torch.zeros(len(chunk), dtype=torch.float64, device=lp.device)
-            sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, lp.double(), torch.zeros_like(lp.double())))
-            for s, v in zip(chunk, sums.tolist()):
-                s.ref_logp = v / max(1, s.n_gen)
+            for s, v in zip(flat, self._sample_means(lp, seg, flat)):
+                s.ref_logp = v
 
     def update(self, samples: List[TrainSample], budget: int) -> Dict[str, float]:
         cfg = self.cfg
@@ -261,17 +372,16 @@ class GRPOTrainer:
         eng.zero_grad()
         loss_sum = 0.0
         kl_sum, kl_n = 0.0, 0
-        for chunk in self._pack(train, budget):
-            b = self._batch(chunk)
-            seg = self._segments(b, chunk)
-            gs = [M.GRPOSample(adv=s.adv, n_tokens=s.n_gen, old_logp=s.old_logp,
-                               ref_logp=s.ref_logp if cfg.ref_anchor_coef else None) for s in chunk]
+        trainer_old = cfg.old_logp_source == "trainer"
+        for chunk in self._pack(self._rows(train), budget):
+            b, flat, seg = self._batch(chunk)
 
-            def coef_fn(lp_full, seg=seg, chunk=chunk, gs=gs):
-                sums = torch.zeros(len(chunk), dtype=torch.float64, device=lp_full.device)
-                sums.index_add_(0, seg.clamp_min(0),
-                                torch.where(seg >= 0, lp_full.double(), torch.zeros_like(lp_full.double())))
-                lps = [v / max(1, s.n_gen) for v, s in zip(sums.tolist(), chunk)]
+            def coef_fn(lp_full, seg=seg, flat=flat):
+                lps = self._sample_means(lp_full, seg, flat)
+                gs = [M.GRPOSample(adv=s.adv, n_tokens=s.n_gen,
+                                   old_logp=lp if trainer_old else s.old_logp,
+                                   ref_logp=s.ref_logp if cfg.ref_anchor_coef else None)
+                      for s, lp in zip(flat, lps)]
                 loss, coefs = M.grpo_token_coefficients(gs, lps, clip_lo=cfg.clip_ratio_low,
                                                         clip_hi=cfg.clip_ratio_high,
                                                         ref_coef=cfg.ref_anchor_coef,
@@ -279,7 +389,9 @@ class GRPOTrainer:
                 cvec = torch.tensor(coefs, dtype=torch.float32, device=lp_full.device)
                 coef = torch.where(seg >= 0, cvec[seg.clamp_min(0)], torch.zeros_like(lp_full))
                 nonlocal kl_sum, kl_n
-                for s, lp in zip(chunk, lps):
+                for s, lp in zip(flat, lps):
+                    if trainer_old:
+                        s.old_logp = lp
                     if s.ref_logp is not None:
                         kl_sum += M.kl_k3(lp, s.ref_logp)
                         kl_n += 1
@@ -303,13 +415,14 @@ class GRPOTrainer:
         groups: List[List[TrainSample]] = []
         rewards_all: List[float] = []
         gen_tokens = 0
+        traj_tokens = 0
 
         def roll(attempt):
             task = tasks[attempt % len(tasks)]
             trajs = self.rollout_group(task, mine, max_new_tokens=max_new_tokens)
             nonlocal gen_tokens
             gen_tokens += sum(len(g) for t in trajs for g in t.gens)
-            return self.samples_from_group(trajs), [M.kevin_trajectory_score(
+            return self.samples_from_group(trajs, attempt), [M.kevin_trajectory_score(
                 [r.reward for r in t.results], [r.correct for r in t.results]) for t in trajs]
 
         from ..obs import PhaseTimer
@@ -317,7 +430,28 @@ class GRPOTrainer:
         target = cfg.target_groups or len(tasks)
         ph = pt.phase("rollout")
         ph.__enter__()
-        if cfg.dynamic_sampling and W == 1:
+        max_new = max_new_tokens or cfg.max_response_length
+        plan = {"opt": False, "ref": False}
+        batched = self._batched_ok(max_new) and not (cfg.dynamic_sampling and W == 1)
+        if batched:
+            from ..engine.offload import HostStash, optimizer_slots, weight_slots
+            plen = self.env.prompt_len if isinstance(self.env, SyntheticRewardEnv) else cfg.max_prompt_length
+            fb = getattr(self.env, "feedback_len", cfg.max_feedback_tokens)
+            plan = self.memory_plan(target * len(mine), plen + cfg.num_turns * (max_new + fb) + 1)
+            if not hasattr(self, "_opt_stash"):
+                self._opt_stash, self._ref_stash = HostStash(), HostStash()
+            if plan["opt"]:
+                self._opt_stash.park(optimizer_slots(self.trainer.opt))
+        if batched:
+            batch_tasks = [tasks[i % len(tasks)] for i in range(target)]
+            for gi, trajs in enumerate(self.rollout_batch(batch_tasks, mine, max_new_tokens=max_new)):
+                gen_tokens += sum(len(g) for t in trajs for g in t.gens)
+                traj_tokens += sum(len(t.contexts[-1]) + len(t.gens[-1]) for t in trajs if t.gens)
+                rewards_all.extend(M.kevin_trajectory_score([r.reward for r in t.results],
+                                                            [r.correct for r in t.results]) for t in trajs)
+                groups.append(self.samples_from_group(trajs, gi))
+            kept = []
+        elif cfg.dynamic_sampling and W == 1:
             kept, attempts = M.dynamic_sampling_refill(
                 roll, target, min_std=cfg.starpo_min_std,
                 max_attempts=cfg.max_sampling_attempts or 0,
@@ -328,19 +462,30 @@ class GRPOTrainer:
             groups.append(g)
             rewards_all.extend(scores)
         ph.__exit__(None, None, None)
+        if batched and self.rollout._num_pages is None:
+            self.rollout.release_cache()          # the KV pool is rebuilt at the next rollout
         groups = self.assign_advantages(groups)
         samples = [s for g in groups for s in g]
         with pt.phase("ref_logp"):
             self.fill_ref_logps(samples, micro_batch_tokens)
         t_roll = time.time() - t0
+        with pt.phase("offload"):
+            if plan["ref"]:
+                self._ref_stash.park(weight_slots(self.ref_w))
+            if plan["opt"]:
+                self._opt_stash.restore(optimizer_slots(self.trainer.opt), self.ctx.device)
         with pt.phase("update"):
             stats = self.update(samples, micro_batch_tokens)
+        if plan["ref"]:
+            with pt.phase("offload"):
+                self._ref_stash.restore(weight_slots(self.ref_w), self.ctx.device)
         self.step_idx += 1
         stats.update({"step": self.step_idx, "reward_mean": sum(rewards_all) / max(1, len(rewards_all)),
                       "reward_std": M.group_reward_std(rewards_all), "groups": len(groups),
-                      "samples": len(samples), "gen_tokens": gen_tokens,
+                      "samples": len(samples), "gen_tokens": gen_tokens, "traj_tokens": traj_tokens,
                       "adv_absmean": sum(abs(s.adv) for s in samples) / max(1, len(samples)),
                       "rollout_s": t_roll, "step_s": time.time() - t0,
+                      "offload_opt": plan["opt"], "offload_ref": plan["ref"],
                       "grad_norm": self.trainer.opt.grad_norm()})
         stats.update({f"ms_{k}": v for k, v in pt.summary(self.ctx).items()})
         if self.ctx.is_main and (self.step_idx % max(1, cfg.logging_steps) == 0):

@@ -47,6 +47,49 @@ def test_paged_attention_vs_reference(qlens, lens, nsplit):
     assert _rel(out, want) < 1e-2
 
 
+@pytest.mark.parametrize("hq,hkv", [(40, 8), (8, 8), (32, 4), (16, 8)])
+@pytest.mark.parametrize("nsplit", [1, 3])
+def test_paged_decode_groups(hq, hkv, nsplit):
+    """Decode path (one query per sequence) for every GQA group size it
+    specialises, including keys that end mid-chunk and empty splits."""
+    torch.manual_seed(3)
+    D, ps = 128, 64
+    lens = [1, 31, 33, 64, 1000, 2049]
+    npages = sum((L + ps - 1) // ps for L in lens) + 2
+    kc = torch.randn(npages * ps, hkv, D, device="cuda").bfloat16()
+    vc = torch.randn(npages * ps, hkv, D, device="cuda").bfloat16()
+    perm = torch.randperm(npages).tolist()
+    maxp = max((L + ps - 1) // ps for L in lens)
+    bt = torch.zeros(len(lens), maxp, dtype=torch.int32)
+    k = 0
+    for i, L in enumerate(lens):
+        n = (L + ps - 1) // ps
+        bt[i, :n] = torch.tensor(perm[k:k + n], dtype=torch.int32)
+        k += n
+    bt = bt.cuda()
+    T = len(lens)
+    qs = torch.arange(T + 1, dtype=torch.int32, device="cuda")
+    q = torch.randn(T, hq, D, device="cuda").bfloat16()
+    lens_t = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    out = torch.empty_like(q)
+    po = torch.empty(nsplit * T * hq * D, device="cuda")
+    pm = torch.empty(nsplit * T * hq * 2, device="cuda")
+    native().paged_attention(q, kc, vc, bt, lens_t, qs, 1, ps, 1 / math.sqrt(D), nsplit, out,
+                             po if nsplit > 1 else None, pm if nsplit > 1 else None)
+    want = paged_attention_reference(q, kc, vc, bt, lens_t, qs, ps, 1 / math.sqrt(D))
+    assert _rel(out, want) < 1e-2
+
+
+def test_sampler_device_step_matches_host_step():
+    torch.manual_seed(4)
+    logits = (3 * torch.randn(4, 5000, device="cuda")).bfloat16()
+    t1, l1 = torch.empty(4, dtype=torch.long, device="cuda"), torch.empty(4, device="cuda")
+    t2, l2 = torch.empty_like(t1), torch.empty_like(l1)
+    native().sample_tokens(logits, 1.0, 0.9, 11, 7, t1, l1)
+    native().sample_tokens(logits, 1.0, 0.9, 11, 0, t2, l2, torch.tensor([7], dtype=torch.int32, device="cuda"))
+    assert torch.equal(t1, t2) and torch.equal(l1, l2)
+
+
 def test_sampler_greedy_topp_and_logprob():
     torch.manual_seed(1)
     V = 151936

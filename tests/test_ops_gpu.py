@@ -50,6 +50,28 @@ def test_gemm_epilogues():
     assert ops.check_device_error() == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(64, 7168, 5120), (1, 5120, 17408), (200, 1024, 4096)])
+def test_gemm_split_k_epilogues(M, N, K):
+    """Skinny (decode-sized) GEMMs split K over the SMs; the reduce applies
+    alpha, the residual and accumulation."""
+    torch.manual_seed(2)
+    A = torch.randn(M, K, device="cuda").bfloat16()
+    B = (torch.randn(N, K, device="cuda") / math.sqrt(K)).bfloat16()
+    R = torch.randn(M, N, device="cuda").bfloat16()
+    want = A.float() @ B.float().t()
+    assert _rel(ops.mm(A, B), want) < 8e-3
+    assert _rel(ops.mm(A, B, residual=R), want + R.float()) < 8e-3
+    acc = torch.randn(M, N, device="cuda")
+    acc0 = acc.clone()
+    ops.mm(A, B, out=acc, accumulate=True, alpha=0.5)
+    assert _rel(acc, acc0 + 0.5 * want) < 5e-3
+    accb = torch.randn(M, N, device="cuda").bfloat16()
+    accb0 = accb.float().clone()
+    ops.mm(A, B, out=accb, accumulate=True)
+    assert _rel(accb, accb0 + want) < 8e-3
+    assert ops.check_device_error() == 0
+
+
 def test_rmsnorm_fwd_bwd():
     torch.manual_seed(2)
     T, H = 300, 5120
