@@ -56,10 +56,15 @@ class AgentHarness:
         return [{"role": "system", "content": sys_p}, {"role": "user", "content": user}]
 
     def run(self, policy) -> Episode:
+        """Drive the tool loop. ``turn_rewards`` / ``turn_correct`` / ``codes``
+        have one entry per assistant turn (the best evaluation among that
+        turn's test/bench/keep calls; 0 and incorrect for a turn without one),
+        so they align with the policy's recorded generations."""
         msgs = self.initial_messages()
         ep = Episode(messages=msgs)
         for _ in range(self.max_turns):
             resp = policy.generate(msgs)
+            turn_best = None
             msgs.append({"role": "assistant", "content": resp})
             calls = parse_tool_calls(resp)
             if not calls:
@@ -67,6 +72,9 @@ class AgentHarness:
                 k = parse_response(resp).get("kernel")
                 calls = [{"name": "keep", "arguments": {"source": k}}] if k else []
             if not calls:
+                ep.turn_correct.append(False)
+                ep.turn_rewards.append(0.0)
+                ep.codes.append(self.exec.current)
                 break
             stop = False
             for c in calls:
@@ -74,11 +82,15 @@ class AgentHarness:
                 msgs.append({"role": "tool", "content": format_tool_result(c["name"], res)})
                 if c["name"] in ("test", "bench", "keep"):
                     ok = bool(res.get("correct"))
-                    ep.turn_correct.append(ok)
-                    ep.codes.append(self.exec.current)
-                    ep.turn_rewards.append(self.reward_fn(res) if self.reward_fn else (0.3 if ok else 0.0))
+                    r = self.reward_fn(res) if self.reward_fn else (0.3 if ok else 0.0)
+                    if turn_best is None or (ok, r) > (turn_best[0], turn_best[1]):
+                        turn_best = (ok, r, self.exec.current)
                 if c["name"] == "keep":
                     stop = True
+            ok, r, code = turn_best if turn_best is not None else (False, 0.0, self.exec.current)
+            ep.turn_correct.append(ok)
+            ep.turn_rewards.append(r)
+            ep.codes.append(code)
             if stop:
                 break
         ep.best_correct = self.exec.kept or self.exec.best

@@ -30,14 +30,22 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, default=8192)
     ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--pair", type=int, default=-1, help="1: 2-CTA pair kernel, 0: one CTA per tile, -1: both")
     args = ap.parse_args(argv)
+    C = ops.native()
     torch.manual_seed(0)
     res = []
     for name, M, N, K, a_t, b_t in shapes(args.tokens):
         A = torch.randn((K, M) if a_t else (M, K), device="cuda").bfloat16()
         B = torch.randn((N, K) if b_t else (K, N), device="cuda").bfloat16()
         out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        ours = median_ms(time_cuda(lambda: ops.mm(A, B, a_t=a_t, b_t=b_t, out=out), args.iters))
+        modes = [0, 1] if args.pair < 0 else [args.pair]
+        per_mode = {}
+        for mode in modes:
+            old = C.gemm_set_pair_mode(mode)
+            per_mode[mode] = median_ms(time_cuda(lambda: ops.mm(A, B, a_t=a_t, b_t=b_t, out=out), args.iters))
+            C.gemm_set_pair_mode(old)
+        ours = min(per_mode.values())
         At = A.t() if a_t else A
         Bt = B.t() if b_t else B
         cub = median_ms(time_cuda(lambda: torch.matmul(At, Bt, out=out), args.iters))
@@ -47,7 +55,8 @@ def main(argv=None):
         err = ((out.float() - ref).norm() / ref.norm()).item()
         r = {"op": name, "M": M, "N": N, "K": K, "ours_ms": round(ours, 4),
              "cublas_ms": round(cub, 4), "ours_tflops": round(fl / ours / 1e9, 1),
-             "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": err}
+             "cublas_tflops": round(fl / cub / 1e9, 1), "rel_err": err,
+             "tflops_by_mode": {("pair" if m else "single"): round(fl / t / 1e9, 1) for m, t in per_mode.items()}}
         print(json.dumps(r), flush=True)
         res.append(r)
     return res

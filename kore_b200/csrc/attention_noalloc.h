@@ -23,10 +23,19 @@
 // (different streams, no ordering between them) race on it.
 //
 // Layouts (bf16, head_dim 128): dout/q/dq [T, Hq, 128] and k/v/dk/dv
-// [T, Hkv, 128], each with a row stride (elements between tokens) that is a
-// multiple of 8 and heads contiguous; o [T, Hq, 128] contiguous; lse [Hq, T]
-// fp32 (natural log, as written by the forward); cu_seqlens int32 [nseq+1] on
-// the device. Returns 0 on success or one of the error codes below.
+// [T, Hkv, 128], heads contiguous, each with a row stride (elements between
+// tokens) that is a multiple of 8, at least the row width (Hq*128 or
+// Hkv*128) and below 2^31; o [T, Hq, 128] contiguous; these eight pointers
+// must be 16-byte aligned. lse [Hq, T] fp32 (natural log, as written by the
+// forward) and cu_seqlens int32 [nseq+1] on the device need 4-byte alignment.
+// max_seqlen must not exceed T. dq/dk/dv rows are written in place: columns
+// between one row's end and the next row's start are left untouched.
+//
+// Return value: 0 means the arguments were valid and the kernels were
+// launched on `stream`, not that they finished. The kernels' waits are
+// bounded; if one gives up, the outputs are incomplete and the kernels record
+// an error that kore_attn_noalloc_read_error() returns (and clears) after
+// synchronizing the device.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -46,3 +55,7 @@ extern "C" __attribute__((visibility("default"))) int kore_attn_bwd_noalloc(
     const void* v, int64_t ld_v, const void* o, const float* lse, const int* cu_seqlens,
     int nseq, int max_seqlen, int T, int Hq, int Hkv, float scale, void* dq, int64_t ld_dq,
     void* dk, int64_t ld_dk, void* dv, int64_t ld_dv, cudaStream_t stream);
+
+// 0 = no kernel error since the last read, 1 = a bounded wait timed out,
+// -1 = the device could not be queried. Synchronizes the current device.
+extern "C" __attribute__((visibility("default"))) int kore_attn_noalloc_read_error(void);

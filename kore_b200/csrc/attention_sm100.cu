@@ -856,7 +856,6 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[KORE_ATTN_NOALL
 
 struct NoallocDeviceState {
   void* scratch = nullptr;  // device address of g_noalloc_scratch on this device
-  bool smem_attr = false;
 };
 
 static int noalloc_setup(int dev, NoallocDeviceState** out) {
@@ -888,14 +887,24 @@ extern "C" int kore_attn_bwd_noalloc(const void* dout, int64_t ld_dout, const vo
                                      cudaStream_t stream) {
   using namespace kore;
   using namespace kore::attn;
-  if (T <= 0 || nseq <= 0 || max_seqlen <= 0 || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
+  if (T <= 0 || nseq <= 0 || max_seqlen <= 0 || max_seqlen > T || Hq <= 0 || Hkv <= 0 || Hq % Hkv != 0)
     return KORE_NOALLOC_ERR_ARGS;
-  const int64_t ld[7] = {ld_dout, ld_q, ld_k, ld_v, ld_dq, ld_dk, ld_dv};
-  for (int64_t x : ld)
-    if (x <= 0 || x % 8 != 0) return KORE_NOALLOC_ERR_ARGS;
-  const void* ptrs[10] = {dout, q, k, v, o, lse, cu_seqlens, dq, dk, dv};
-  for (const void* ptr : ptrs)
+  // row strides: multiples of 8 elements, at least one row wide, and within int range
+  const int64_t wq = (int64_t)Hq * D, wk = (int64_t)Hkv * D;
+  const int64_t ld[7] = {ld_dout, ld_q, ld_dq, ld_k, ld_v, ld_dk, ld_dv};
+  const int64_t width[7] = {wq, wq, wq, wk, wk, wk, wk};
+  for (int i = 0; i < 7; ++i)
+    if (ld[i] % 8 != 0 || ld[i] < width[i] || ld[i] > INT32_MAX) return KORE_NOALLOC_ERR_ARGS;
+  // tensors read by TMA or 16-byte vectors need 16-byte alignment; lse and
+  // cu_seqlens are read element-wise and need 4
+  const void* ptrs16[8] = {dout, q, k, v, o, dq, dk, dv};
+  for (const void* ptr : ptrs16)
     if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15) != 0) return KORE_NOALLOC_ERR_ARGS;
+  const void* ptrs4[2] = {lse, cu_seqlens};
+  for (const void* ptr : ptrs4)
+    if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 3) != 0) return KORE_NOALLOC_ERR_ARGS;
+  // the backward grid is nseq * ceil(max_seqlen / 128) * Hkv CTAs
+  if ((int64_t)nseq * ((max_seqlen + BKV - 1) / BKV) * Hkv > INT32_MAX) return KORE_NOALLOC_ERR_ARGS;
   const uint64_t acc_bytes = (uint64_t)T * Hq * D * sizeof(float);
   const uint64_t delta_bytes = (uint64_t)T * Hq * sizeof(float);
   if (acc_bytes + delta_bytes > KORE_ATTN_NOALLOC_SCRATCH_BYTES) return KORE_NOALLOC_ERR_TOO_LARGE;
@@ -946,4 +955,15 @@ extern "C" int kore_attn_bwd_noalloc(const void* dout, int64_t ld_dout, const vo
       dq_acc, reinterpret_cast<__nv_bfloat16*>(dq), (int)ld_dq, Hq, T);
   if (cudaGetLastError() != cudaSuccess) return KORE_NOALLOC_ERR_LAUNCH;
   return KORE_NOALLOC_OK;
+}
+
+// Reads and clears the device-side error word of the attention kernels (0 =
+// no error, 1 = a bounded wait inside a kernel timed out and its outputs are
+// incomplete). Synchronizes the current device.
+extern "C" int kore_attn_noalloc_read_error(void) {
+  int v = 0, z = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess) return -1;
+  if (cudaMemcpyFromSymbol(&v, kore::g_error, sizeof(int)) != cudaSuccess) return -1;
+  if (cudaMemcpyToSymbol(kore::g_error, &z, sizeof(int)) != cudaSuccess) return -1;
+  return v;
 }

@@ -48,6 +48,7 @@ void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor
 void sample_tokens(const at::Tensor& logits, double temperature, double top_p, int64_t seed,
                    int64_t step, at::Tensor& tokens, at::Tensor& logprobs,
                    const c10::optional<at::Tensor>& step_dev);
+int64_t gemm_set_pair_mode(int64_t mode);
 int64_t symm_heap_create(int64_t bytes, int64_t rank, int64_t world);
 at::Tensor symm_heap_handle(int64_t id);
 void symm_heap_open(int64_t id, const at::Tensor& handles);
@@ -93,6 +94,8 @@ int read_and_clear_device_error();
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "kore_b200 sm_100a kernels";
   m.def("gemm_bf16", &kore::gemm_bf16, "tcgen05 bf16 GEMM");
+  m.def("gemm_set_pair_mode", &kore::gemm_set_pair_mode,
+        "large plain GEMMs on 2-CTA pairs (1) or one CTA per tile (0); returns the previous mode");
   m.def("rmsnorm_fwd", &kore::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &kore::rmsnorm_bwd);
   m.def("qk_norm_rope_fwd", &kore::qk_norm_rope_fwd);

@@ -455,6 +455,285 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
   check_cuda(cudaGetLastError(), "gemm launch");
 }
 
+// ---------------------------------------------------------------------------
+// 2-CTA variant (cta_group::2) for large plain GEMMs. A cluster of two CTAs
+// owns a 256 x BN output tile: CTA r loads A rows [m0 + 128 r, +128) and B rows
+// (output columns) [n0 + r BN/2, +BN/2) with its own plain TMA loads, both
+// counted on the leader's (rank 0) full barrier; the leader's MMA warp issues
+// 256 x BN x 16 UMMAs that read both CTAs' shared memory, and each CTA's TMEM
+// receives its own 128 accumulator rows. Per CTA, a stage holds half the B
+// tile of the one-CTA kernel, so the same shared memory keeps more stages in
+// flight and each operand byte feeds twice the MMA work.
+template <int BN, int STAGES>
+struct PairSmem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = EPI_OFF + kEpiWarps * 2 * kStageBytesC;
+  static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+};
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, Params p) {
+  using S = PairSmem<BN, STAGES>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* tfull_bar = empty_bar + STAGES;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;       // [2] (leader: both CTAs' epilogue warps arrive)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const uint32_t rank = cluster_ctarank();
+  const int pair = blockIdx.x / 2, npairs = gridDim.x / 2;
+  const int num_m = (p.M + 2 * BM - 1) / (2 * BM);
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int kblocks = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull_bar[b], 1);
+      mbar_init(&tempty_bar[b], 2 * kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, 2 * BN);
+  tc_fence_before();
+  cluster_sync();   // both CTAs' barriers initialised and TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
+        int tm, tn;
+        tile_coords(t, num_m, num_n, tm, tn);
+        const int m0 = tm * 2 * BM + (int)rank * BM;
+        const int n0 = tn * BN + (int)rank * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { *abort_flag = 1; break; }
+          uint8_t* sA = smem + stage * S::STAGE_BYTES;
+          uint8_t* sB = sA + S::A_BYTES;
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * S::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (!A_MN) {
+            tma_load_2d_pair(sA, &tmA, fb, k0, m0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(sA + j * 8192, &tmA, fb, m0 + 64 * j, k0);
+          }
+          if (!B_MN) {
+            tma_load_2d_pair(sB, &tmB, fb, k0, n0);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 128; ++j) tma_load_2d_pair(sB + j * 8192, &tmB, fb, n0 + 64 * j, k0);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    constexpr uint32_t idesc = make_idesc_bf16(2 * BM, BN, A_MN, B_MN);
+    if (rank == 0 && elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) { *abort_flag = 1; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * S::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + S::A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            uint64_t ad = A_MN ? make_sw128_desc(a_addr + k * 2048, 8192, 1024)
+                               : make_sw128_desc(a_addr + k * 32, 16, 1024);
+            uint64_t bd = B_MN ? make_sw128_desc(b_addr + k * 2048, 8192, 1024)
+                               : make_sw128_desc(b_addr + k * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, idesc, (kb | k) != 0);
+          }
+          umma_commit_pair(&empty_bar[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) { *abort_flag = 1; break; }
+        umma_commit_pair(&tfull_bar[acc], 0x3);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;
+    const int lane = threadIdx.x & 31;
+    uint8_t* stage_buf = smem + S::EPI_OFF + (warp - 2) * 2 * kStageBytesC;
+    const uint32_t tempty_leader[2] = {mapa_shared(smem_u32(&tempty_bar[0]), 0),
+                                       mapa_shared(smem_u32(&tempty_bar[1]), 0)};
+    int buf = 0, it = 0;
+    const int CH = p.out_f32 ? 32 : 64;
+    for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, ++it) {
+      int tm, tn;
+      tile_coords(t, num_m, num_n, tm, tn);
+      const int m0 = tm * 2 * BM + (int)rank * BM;
+      const int n0 = tn * BN;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
+      tc_fence_after();
+      const int row = m0 + q * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      for (int c0 = 0; c0 < BN; c0 += CH) {
+        if (n0 + c0 >= p.N) break;
+        float v[64];
+        {
+          uint32_t r[32];
+          tmem_ld32(t_row + c0, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * p.alpha;
+          if (!p.out_f32) {
+            tmem_ld32(t_row + c0 + 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[32 + i] = __uint_as_float(r[i]) * p.alpha;
+          }
+        }
+        if (row < p.M && (p.accumulate || p.R != nullptr)) {
+          const int ncols = min(CH, p.N - (n0 + c0));
+          if (p.R != nullptr) {
+            const __nv_bfloat16* rp = p.R + (size_t)row * p.ldr + n0 + c0;
+#pragma unroll
+            for (int j = 0; j < 64; j += 8) {
+              if (j >= ncols) break;
+              uint4 u = *reinterpret_cast<const uint4*>(rp + j);
+              const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+              for (int e = 0; e < 8; ++e) v[j + e] += __bfloat162float(h[e]);
+            }
+          }
+          if (p.accumulate) {
+            if (p.out_f32) {
+              const float* cp = reinterpret_cast<const float*>(p.C_read) + (size_t)row * p.ldc + n0 + c0;
+#pragma unroll
+              for (int j = 0; j < 32; j += 4) {
+                if (j >= ncols) break;
+                float4 u = *reinterpret_cast<const float4*>(cp + j);
+                v[j] += u.x; v[j + 1] += u.y; v[j + 2] += u.z; v[j + 3] += u.w;
+              }
+            } else {
+              const __nv_bfloat16* cp =
+                  reinterpret_cast<const __nv_bfloat16*>(p.C_read) + (size_t)row * p.ldc + n0 + c0;
+#pragma unroll
+              for (int j = 0; j < 64; j += 8) {
+                if (j >= ncols) break;
+                uint4 u = *reinterpret_cast<const uint4*>(cp + j);
+                const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&u);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) v[j + e] += __bfloat162float(h[e]);
+              }
+            }
+          }
+        }
+        if (lane == 0) tma_store_wait_read<1>();
+        __syncwarp();
+        uint8_t* sb = stage_buf + buf * kStageBytesC + lane * 128;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          uint4 u;
+          if (p.out_f32) {
+            u.x = __float_as_uint(v[4 * j]);
+            u.y = __float_as_uint(v[4 * j + 1]);
+            u.z = __float_as_uint(v[4 * j + 2]);
+            u.w = __float_as_uint(v[4 * j + 3]);
+          } else {
+            u.x = pack_bf16(v[8 * j], v[8 * j + 1]);
+            u.y = pack_bf16(v[8 * j + 2], v[8 * j + 3]);
+            u.z = pack_bf16(v[8 * j + 4], v[8 * j + 5]);
+            u.w = pack_bf16(v[8 * j + 6], v[8 * j + 7]);
+          }
+          *reinterpret_cast<uint4*>(sb + ((j ^ (lane & 7)) * 16)) = u;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, stage_buf + buf * kStageBytesC, n0 + c0, m0 + q * 32);
+          tma_store_commit();
+        }
+        buf ^= 1;
+      }
+      // this CTA's 128 accumulator rows are read: tell the leader's MMA warp
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader[acc]);
+    }
+    if (lane == 0) tma_store_wait_all<0>();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  cluster_sync();   // the peer's shared memory is no longer read by the leader's MMAs
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 2 * BN);
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN>
+void launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
+                 int grid, cudaStream_t stream) {
+  auto k = gemm_pair_kernel<BN, STAGES, A_MN, B_MN>;
+  constexpr int smem = PairSmem<BN, STAGES>::TOTAL;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+  TORCH_CHECK(dev >= 0 && dev < 64, "gemm: device index");
+  if (!attr_set[dev]) {
+    check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+               "cudaFuncSetAttribute(gemm pair smem)");
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CUtensorMap a = ta, b = tb, c = tc;
+  Params pp = p;
+  check_cuda(cudaLaunchKernelEx(&cfg, k, a, b, c, pp), "gemm pair launch");
+}
+
 // Sum of the split-K partials (+ old C when accumulating, + residual) into C.
 // One thread per 4 consecutive columns; N % 8 == 0.
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int ws_rows, int M, int N,
@@ -505,6 +784,14 @@ int choose_splits(int tiles, int kblocks, int sms) {
 }
 
 }  // namespace gemm
+
+// Which kernel large plain GEMMs use: 1 = 2-CTA pairs (cta_group::2), 0 = one CTA per tile.
+static int g_gemm_pair_mode = 0;
+int64_t gemm_set_pair_mode(int64_t mode) {
+  const int old = g_gemm_pair_mode;
+  g_gemm_pair_mode = (int)mode;
+  return old;
+}
 
 // out = alpha * op(a) @ op(b)^T (+ residual) (+ out if accumulate)
 //  a: [M,K] if !a_mn else [K,M];  b: [N,K] if !b_mn else [K,N];  out: [M,N] (row stride may exceed N)
@@ -575,6 +862,22 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
   auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap ta = a_mn ? make_tmap_2d(a.data_ptr(), bf, 2, M, K, a.stride(0), 64, 64)
                         : make_tmap_2d(a.data_ptr(), bf, 2, K, M, a.stride(0), 64, 128);
+  cudaStream_t st0 = at::cuda::getCurrentCUDAStream();
+  const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (g_gemm_pair_mode == 1 && splits == 1 && max_ctas <= 0 && use256 && pair_tiles >= sms) {
+    // 2-CTA pairs: each CTA loads half of the 256-column B tile
+    CUtensorMap tbp = b_mn ? make_tmap_2d(b.data_ptr(), bf, 2, N, K, b.stride(0), 64, 64)
+                           : make_tmap_2d(b.data_ptr(), bf, 2, K, N, b.stride(0), 64, 128);
+    CUtensorMap tcp = f32 ? make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, M,
+                                         out.stride(0), 32, 32)
+                          : make_tmap_2d(out.data_ptr(), bf, 2, N, M, out.stride(0), 64, 32);
+    const int grid = std::min(2 * pair_tiles, sms & ~1);
+    if (!a_mn && !b_mn) gemm::launch_pair<256, 6, false, false>(ta, tbp, tcp, p, grid, st0);
+    else if (!a_mn && b_mn) gemm::launch_pair<256, 6, false, true>(ta, tbp, tcp, p, grid, st0);
+    else if (a_mn && !b_mn) gemm::launch_pair<256, 6, true, false>(ta, tbp, tcp, p, grid, st0);
+    else gemm::launch_pair<256, 6, true, true>(ta, tbp, tcp, p, grid, st0);
+    return;
+  }
   CUtensorMap tb = b_mn ? make_tmap_2d(b.data_ptr(), bf, 2, N, K, b.stride(0), 64, 64)
                         : make_tmap_2d(b.data_ptr(), bf, 2, K, N, b.stride(0), 64, BN);
   at::Tensor ws;

@@ -114,6 +114,10 @@ class GRPOTrainer:
         self.controller = (M.DynamicStepController(config.min_steps, config.total_steps,
                                                    config.plateau_patience, config.plateau_min_delta)
                            if config.adaptive_steps else None)
+        from .grpo_hooks import CurriculumHook, SearchDistill, ValuePrefilter
+        self.curriculum = CurriculumHook(self) if config.coevolve else None
+        self.prefilter = ValuePrefilter(self) if config.value_prefilter else None
+        self.search_hook = SearchDistill(self) if config.use_search else None
         self.eos = []
         if tokenizer is not None:
             from ..data.tokenizer import eos_ids
@@ -147,22 +151,37 @@ class GRPOTrainer:
         base = self._initial_context(task)
         trajs = [Trajectory(t) for t in traj_ids]
         ctxs = [list(base) for _ in trajs]
+        ncand = self.prefilter.n if self.prefilter is not None else 1
         for turn in range(cfg.num_turns):
             from ..engine.rollout import GenRequest
             reqs = []
             for i, (tr, c) in enumerate(zip(trajs, ctxs)):
                 c = c[-cfg.max_prompt_length:]
                 ctxs[i] = c
-                reqs.append(GenRequest(prompt=c, max_new_tokens=max_new, rid=i,
-                                       share_key=(task, "t0") if turn == 0 else None))
+                key = (task, "t0") if (turn == 0 and ncand == 1) else ((task, turn, i) if ncand > 1 else None)
+                for j in range(ncand):
+                    reqs.append(GenRequest(prompt=c, max_new_tokens=max_new, rid=i * ncand + j, share_key=key))
             outs = self.rollout.generate(reqs, temperature=cfg.temperature, top_p=cfg.top_p,
                                          eos_ids=self.eos, seed=cfg.seed * 1000003 + self.step_idx * 97 + turn)
-            for i, (tr, o) in enumerate(zip(trajs, outs)):
+            for i, tr in enumerate(trajs):
+                cands = outs[i * ncand:(i + 1) * ncand]
+                if ncand == 1:
+                    o = cands[0]
+                    res = self.env.step(task, self._decode(o.tokens), turn, tr.traj, tr.results)
+                else:   # value prefilter: verify only the value model's top-k candidates
+                    from .format import parse_response
+                    texts = [self._decode(o.tokens) for o in cands]
+                    pick = self.prefilter.pick([parse_response(t).get("kernel", "") for t in texts])
+                    best = None
+                    for j in pick:
+                        r = self.env.step(task, texts[j], turn, tr.traj, tr.results)
+                        if best is None or (r.correct, r.reward) > (best[1].correct, best[1].reward):
+                            best = (j, r)
+                    o, res = cands[best[0]], best[1]
                 tr.contexts.append(list(ctxs[i]))
                 tr.gens.append(list(o.tokens))
                 tr.gen_logps.append(list(o.logps))
                 tr.finish.append(o.finish_reason)
-                res = self.env.step(task, self._decode(o.tokens), turn, tr.traj, tr.results)
                 tr.results.append(res)
                 ctxs[i] = ctxs[i] + list(o.tokens) + self._feedback_ids(task, res, turn, tr.traj)
         return trajs
@@ -194,9 +213,12 @@ class GRPOTrainer:
             tr = flat[i]
             return self._feedback_ids(tasks[i // G], tr.results[-1], turn, tr.traj)
 
+        fb_cap = cfg.max_feedback_tokens
+        if isinstance(self.env, SyntheticRewardEnv):
+            fb_cap = min(fb_cap, self.env.feedback_len)
         outs = MultiTurnRollout(self.rollout).run(
             prompts, num_turns=cfg.num_turns, max_new=max_new, feedback=feedback, share_keys=keys,
-            max_feedback=cfg.max_feedback_tokens, temperature=cfg.temperature, top_p=cfg.top_p,
+            max_feedback=fb_cap, temperature=cfg.temperature, top_p=cfg.top_p,
             eos_ids=self.eos, seed=cfg.seed * 1000003 + self.step_idx * 97, on_turn=on_turn)
         for o, tr in zip(outs, flat):
             tr.contexts, tr.gens, tr.gen_logps, tr.finish = o.contexts, o.gens, o.logps, o.finish
@@ -417,9 +439,18 @@ class GRPOTrainer:
         gen_tokens = 0
         traj_tokens = 0
 
+        if self.curriculum is not None:
+            tasks = self.curriculum.choose(tasks, cfg.target_groups or len(tasks))
+        traj_groups: List[tuple] = []
+
         def roll(attempt):
             task = tasks[attempt % len(tasks)]
-            trajs = self.rollout_group(task, mine, max_new_tokens=max_new_tokens)
+            if cfg.agentic:
+                from .grpo_hooks import rollout_agentic
+                trajs = rollout_agentic(self, task, mine, max_new_tokens or cfg.max_response_length)
+            else:
+                trajs = self.rollout_group(task, mine, max_new_tokens=max_new_tokens)
+            traj_groups.append((task, trajs))
             nonlocal gen_tokens
             gen_tokens += sum(len(g) for t in trajs for g in t.gens)
             return self.samples_from_group(trajs, attempt), [M.kevin_trajectory_score(
@@ -432,7 +463,8 @@ class GRPOTrainer:
         ph.__enter__()
         max_new = max_new_tokens or cfg.max_response_length
         plan = {"opt": False, "ref": False}
-        batched = self._batched_ok(max_new) and not (cfg.dynamic_sampling and W == 1)
+        batched = self._batched_ok(max_new) and not cfg.dynamic_sampling and not cfg.agentic \
+            and self.prefilter is None
         if batched:
             from ..engine.offload import HostStash, optimizer_slots, weight_slots
             plen = self.env.prompt_len if isinstance(self.env, SyntheticRewardEnv) else cfg.max_prompt_length
@@ -445,6 +477,7 @@ class GRPOTrainer:
         if batched:
             batch_tasks = [tasks[i % len(tasks)] for i in range(target)]
             for gi, trajs in enumerate(self.rollout_batch(batch_tasks, mine, max_new_tokens=max_new)):
+                traj_groups.append((batch_tasks[gi], trajs))
                 gen_tokens += sum(len(g) for t in trajs for g in t.gens)
                 traj_tokens += sum(len(t.contexts[-1]) + len(t.gens[-1]) for t in trajs if t.gens)
                 rewards_all.extend(M.kevin_trajectory_score([r.reward for r in t.results],
@@ -456,7 +489,11 @@ class GRPOTrainer:
                 roll, target, min_std=cfg.starpo_min_std,
                 max_attempts=cfg.max_sampling_attempts or 0,
                 std_key=lambda g: M.group_reward_std([s.ret for s in g[0]]))
-        else:  # ranks must roll identical group counts: no data-dependent refill
+        elif cfg.dynamic_sampling:   # several ranks: refill decided on the gathered returns
+            from .grpo_hooks import distributed_refill
+            kept, attempts = distributed_refill(self.ctx, roll, target, min_std=cfg.starpo_min_std,
+                                                max_attempts=cfg.max_sampling_attempts or 0)
+        else:
             kept = [roll(i) for i in range(target)]
         for g, scores in kept:
             groups.append(g)
@@ -480,6 +517,13 @@ class GRPOTrainer:
             with pt.phase("offload"):
                 self._ref_stash.restore(weight_slots(self.ref_w), self.ctx.device)
         self.step_idx += 1
+        if self.curriculum is not None:
+            self.curriculum.record([t for t, _ in traj_groups], [g for _, g in traj_groups])
+        if self.search_hook is not None:
+            rec = self.search_hook.maybe_run(self.step_idx, [t for t, _ in traj_groups],
+                                             [g for _, g in traj_groups])
+            if rec is not None:
+                stats["search"] = rec
         stats.update({"step": self.step_idx, "reward_mean": sum(rewards_all) / max(1, len(rewards_all)),
                       "reward_std": M.group_reward_std(rewards_all), "groups": len(groups),
                       "samples": len(samples), "gen_tokens": gen_tokens, "traj_tokens": traj_tokens,

@@ -217,3 +217,75 @@ def test_heartbeat_leave_and_classify():
     assert classify_exception(RuntimeError("CUDA out of memory")) == "infra"
     assert classify_exception(RuntimeError("NCCL error: unhandled system error")) == "infra"
     assert classify_exception(ValueError("bad shape")) == "program"
+
+
+class _FakeKernelTask:
+    def __init__(self, tid):
+        self.task_id, self.operation, self.seed_src, self.dtype = tid, "rmsnorm", "def k(x): return x", "fp32"
+
+
+class _FakeKernelEnv:
+    """Stands in for KoreEnv: correctness and timing depend on a hash of the source."""
+
+    def __init__(self, tid):
+        self.task = _FakeKernelTask(tid)
+
+    def step(self, src):
+        import zlib
+
+        from kore_b200.reward.reward import Observation
+        h = zlib.crc32(src.encode())
+        ok = h % 3 != 0
+        return Observation(compiled=True, validation_passed=ok, snr_db=60.0 if ok else 5.0,
+                           wall_ms=1.0 + (h % 7) / 10.0, baseline_ms=2.0)
+
+
+class _FakeRolloutEnv:
+    def __init__(self):
+        self.envs = {}
+
+    def _env(self, task):
+        return self.envs.setdefault(task, _FakeKernelEnv(task))
+
+    def prompt_messages(self, task):
+        return [{"role": "user", "content": f"optimize {task}"}]
+
+
+def _agentic_world2(ctx, out_dir):
+    import kore_b200.agent.harness as H
+    from kore_b200.data.tokenizer import ByteTokenizer
+    from kore_b200.models import Qwen3Weights, qwen3_tiny
+    from kore_b200.policy.configs import GRPOConfig
+    from kore_b200.policy.grpo import GRPOTrainer
+    calls = {"n": 0}
+
+    def scripted(resp):   # the tiny random model cannot write tool calls: script them
+        calls["n"] += 1
+        return [{"name": "test", "arguments": {"source": f"def k(x): return x * {calls['n'] % 5}"}}]
+
+    H.parse_tool_calls = scripted
+    cfg = qwen3_tiny(vocab=512)
+    w = Qwen3Weights(cfg, device="cpu", dtype=torch.float32, seed=0)
+    gc = GRPOConfig(num_trajectories=4, num_turns=1, tasks_per_step=2, max_response_length=4,
+                    max_prompt_length=512, learning_rate=1e-3, bf16=False, starpo_s=False, overlong_mask=False,
+                    agentic=True, max_tool_turns=1, coevolve=True, use_search=True, search_every=1,
+                    search_budget=4, coevolve_distill_path=os.path.join(out_dir, "wins.jsonl"),
+                    dynamic_sampling=True, max_sampling_attempts=6, target_groups=2)
+    tr = GRPOTrainer(gc, weights=w, env=_FakeRolloutEnv(), ctx=ctx, tokenizer=ByteTokenizer(512),
+                     rollout_kwargs=dict(num_pages=256, page_size=16, max_seq_len=1024))
+    st = tr.train_step(["t0", "t1"], max_new_tokens=4)
+    picked = [e.desc.task_id for e in tr.curriculum.ctrl.archive.entries.values() if e.attempts]
+    return {"samples": st["samples"], "groups": st["groups"], "picked": sorted(picked),
+            "search": st.get("search"), "checksum": float(sum(b.double().sum() for b in w.bufs))}
+
+
+def test_agentic_grpo_world2_with_curriculum_and_distill(tmp_path):
+    """Agentic GRPO step on gloo world 2: tasks from the curriculum controller
+    (same on both ranks), tool-using episodes, distributed dynamic sampling,
+    rank-0 search-then-distill, identical replicas after the update."""
+    out = _run(_agentic_world2, 2, str(tmp_path))
+    assert out[0]["picked"] == out[1]["picked"] and out[0]["picked"]
+    assert out[0]["groups"] >= 1 and out[0]["samples"] > 0
+    assert out[0]["checksum"] == out[1]["checksum"]
+    assert out[0]["search"] is not None and out[1]["search"] is None
+    assert os.path.exists(tmp_path / "wins.jsonl")

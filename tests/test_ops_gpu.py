@@ -50,6 +50,29 @@ def test_gemm_epilogues():
     assert ops.check_device_error() == 0
 
 
+@pytest.mark.parametrize("M,N,K", [(8192, 7168, 512), (4000, 5120, 1024), (5120, 34816, 256)])
+@pytest.mark.parametrize("a_t,b_t", [(False, True), (False, False), (True, False), (True, True)])
+def test_gemm_pair_kernel(M, N, K, a_t, b_t):
+    """2-CTA (cta_group::2) kernel: every operand layout, ragged M."""
+    C = ops.native()
+    torch.manual_seed(5)
+    A = (torch.randn(K, M) if a_t else torch.randn(M, K)).cuda().bfloat16()
+    B = (torch.randn(N, K) if b_t else torch.randn(K, N)).cuda().bfloat16()
+    R = torch.randn(M, N, device="cuda").bfloat16()
+    old = C.gemm_set_pair_mode(1)
+    try:
+        out = ops.mm(A, B, a_t=a_t, b_t=b_t, residual=R)
+        o32 = ops.mm(A, B, a_t=a_t, b_t=b_t, out_dtype=torch.float32)
+    finally:
+        C.gemm_set_pair_mode(old)
+    Af = A.float().t() if a_t else A.float()
+    Bf = B.float().t() if b_t else B.float()
+    want = Af @ Bf
+    assert ops.check_device_error() == 0
+    assert _rel(out, want + R.float()) < 8e-3
+    assert _rel(o32, want) < 2e-3
+
+
 @pytest.mark.parametrize("M,N,K", [(64, 7168, 5120), (1, 5120, 17408), (200, 1024, 4096)])
 def test_gemm_split_k_epilogues(M, N, K):
     """Skinny (decode-sized) GEMMs split K over the SMs; the reduce applies

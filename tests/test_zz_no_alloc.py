@@ -81,3 +81,41 @@ def test_noalloc_rejects_oversized_call():
             1 << 20, 2, 1, 0.088, q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
             v.data_ptr(), v.stride(0), torch.cuda.current_stream().cuda_stream)
     assert rc == 1
+
+
+def test_noalloc_strided_outputs_and_argument_checks():
+    """dq/dk/dv as row-strided views of wider buffers: the gaps between rows
+    stay untouched; a row stride that is not a multiple of 8, or narrower than
+    a row, is rejected with code 2; the error reader reports a clean run."""
+    fn = _lib()
+    import kore_b200._C  # noqa: F401
+    lib = ctypes.CDLL(glob.glob(os.path.join(_ROOT, "kore_b200", "_C*.so"))[0])
+    read_err = lib.kore_attn_noalloc_read_error
+    read_err.restype = ctypes.c_int
+    lens, hq, hkv = [200, 56], 4, 2
+    q, k, v, o, lse, do, cu, mx = _case(lens, hq, hkv, 7)
+    dq_ref, dk_ref, dv_ref = attn.attn_bwd(do, q, k, v, o, lse, cu, mx)
+    T, D = q.shape[0], 128
+    pad = 24
+    bq = torch.full((T, hq * D + pad), 7.0, device="cuda").bfloat16()
+    bk = torch.full((T, hkv * D + pad), 7.0, device="cuda").bfloat16()
+    bv = torch.full((T, hkv * D + pad), 7.0, device="cuda").bfloat16()
+    dq, dk, dv = bq[:, : hq * D], bk[:, : hkv * D], bv[:, : hkv * D]
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call(ld_dq, ld_dk):
+        return fn(do.data_ptr(), do.stride(0), q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0),
+                  v.data_ptr(), v.stride(0), o.data_ptr(), lse.data_ptr(), cu.data_ptr(), cu.numel() - 1, mx,
+                  T, hq, hkv, 1.0 / 128 ** 0.5, dq.data_ptr(), ld_dq, dk.data_ptr(), ld_dk,
+                  dv.data_ptr(), bv.stride(0), stream)
+
+    assert call(bq.stride(0), bk.stride(0)) == 0
+    torch.cuda.synchronize()
+    assert read_err() == 0
+    assert _rel(dq.reshape(T, hq, D), dq_ref) < 2e-2
+    assert _rel(dk.reshape(T, hkv, D), dk_ref) < 2e-2
+    assert _rel(dv.reshape(T, hkv, D), dv_ref) < 2e-2
+    for b, w in ((bq, hq * D), (bk, hkv * D), (bv, hkv * D)):
+        assert torch.all(b[:, w:] == 7.0)
+    assert call(bq.stride(0) - 4, bk.stride(0)) == 2          # not a multiple of 8
+    assert call(hq * D - 8, bk.stride(0)) == 2                  # narrower than a row
