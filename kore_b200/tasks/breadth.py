@@ -28,7 +28,7 @@ from typing import Callable, Dict, List, Tuple
 import torch
 import torch.nn.functional as F
 
-from .ops_library import OpSpec, _randn
+from .spec import OpSpec, _randn
 
 DT = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}
 

@@ -14,39 +14,12 @@ routing, fp8 quant), retargeted from gfx950 to sm_100a.
 from __future__ import annotations
 
 import math
-from dataclasses import dataclass, field
-from typing import Callable, Dict, List, Optional, Tuple
+from typing import Dict
 
 import torch
 import torch.nn.functional as F
 
-Inputs = Tuple[torch.Tensor, ...]
-
-
-def _gen(seed: int, device):
-    g = torch.Generator(device=device)
-    g.manual_seed(int(seed))
-    return g
-
-
-def _randn(shape, seed, device, dtype, scale=1.0):
-    g = _gen(seed, device)
-    return (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * scale).to(dtype)
-
-
-@dataclass
-class OpSpec:
-    name: str
-    operation: str                                   # roofline op name
-    entry: str                                       # function the candidate defines
-    make_inputs: Callable[[Dict[str, int], int, str, torch.dtype], Inputs]
-    reference: Callable[..., torch.Tensor]           # fp32 oracle
-    baseline: Callable[..., torch.Tensor]            # vendor bar on B200
-    seed_src: str
-    shapes: Dict[str, object] = field(default_factory=dict)
-    family: str = "core"
-    dtype: str = "bf16"
-    snr_threshold: Optional[float] = None
+from .spec import Inputs, OpSpec, _gen, _randn  # noqa: F401
 
 
 # ------------------------------------------------------------------ seeds
@@ -387,8 +360,13 @@ for _n, (_e, _r) in _BINARY.items():
 # generated breadth families (kore_b200.tasks.breadth)
 def _register_breadth():
     from .breadth import build
+    from .core_ext import build as build_core
+    from .genops import build as build_gen
     for _s in build():
         _add(_s)
+    for _n, _s in list(build_gen().items()) + list(build_core().items()):
+        if _n not in SPECS:          # the hand-written gen_* seeds above take precedence
+            _add(_s)
 
 
 _register_breadth()
