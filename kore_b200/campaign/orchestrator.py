@@ -196,14 +196,25 @@ class RetentionStop(RuntimeError):
 
 
 def retention_check(c: Campaign, m: dict, generate_factory: Optional[Callable[[str], Callable]] = None) -> None:
-    """Hard stop when the latest model regresses general capability."""
-    if not c.retention_suites or generate_factory is None:
+    """Hard stop when the latest model regresses general capability.
+
+    ``generate_factory(model) -> generate``: with ``retention_suites`` (name ->
+    JSONL of {"prompt", "answer"|"tests"}) the generate callable maps a prompt
+    string to text; without them the bundled six-benchmark suite
+    (kore_b200.eval.retention) is used and generate maps chat messages to text."""
+    if generate_factory is None:
         return
-    from ..eval.gates import retention_gate, run_retention_suite
+    from ..eval.gates import retention_gate
     cache = str(c.out_dir / "retention_cache.json")
-    base = run_retention_suite(generate_factory(c.base_model), c.retention_suites, cache, c.base_model)
     cur_model = _latest_model(c, m)
-    cur = run_retention_suite(generate_factory(cur_model), c.retention_suites, cache, cur_model)
+    if c.retention_suites:
+        from ..eval.gates import run_retention_suite
+        base = run_retention_suite(generate_factory(c.base_model), c.retention_suites, cache, c.base_model)
+        cur = run_retention_suite(generate_factory(cur_model), c.retention_suites, cache, cur_model)
+    else:
+        from ..eval.retention import run_retention_suite as run_bundled
+        base = run_bundled(generate_factory(c.base_model), cache_path=cache, model_key=c.base_model)
+        cur = run_bundled(generate_factory(cur_model), cache_path=cache, model_key=cur_model)
     g = retention_gate(base, cur, c.retention_epsilon)
     m["retention"] = {"base": base, "current": cur, "passed": g.passed}
     if not g.passed:

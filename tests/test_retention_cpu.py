@@ -60,3 +60,44 @@ def test_ifeval_checks_and_suite_cache(tmp_path):
     R.run_retention_suite(lambda m: calls.append(1) or "", ["ifeval", "mtbench"],
                           cache_path=str(tmp_path / "c.json"), model_key="m")
     assert len(calls) == n        # second run served from the cache
+
+
+def test_kernelbench_adapter_and_leakage():
+    import torch
+
+    from kore_b200.eval import kernelbench as KB
+    specs = KB.bundled_specs()
+    assert {s.level for s in specs} == {1, 2}
+    t = KB.spec_to_task(specs[0], "fp32")
+    from kore_b200.tasks.ops_library import SPECS
+    s = SPECS[t.task_id]
+    x = s.make_inputs({}, 0, "cpu", torch.float32)
+    ns = {}
+    exec(t.seed_src, ns)
+    assert torch.allclose(ns["kernel"](*x), s.reference(*x))
+    rep = KB.kernelbench_report([{"task_id": t.task_id, "correct": True, "speedup": 1.7}], specs)
+    assert rep["fast_1.0"] == 1.0 and rep["fast_2.0"] == 0.0 and "level1" in rep["levels"]
+    proto = KB.propose_heldout(families=("attention",))
+    KB.assert_no_leakage(proto)
+    assert proto.heldout_tasks and not set(proto.heldout_tasks) & set(proto.train_tasks)
+    proto.train_tasks.append(proto.heldout_tasks[0])
+    import pytest
+    with pytest.raises(AssertionError):
+        KB.assert_no_leakage(proto)
+
+
+def test_e2e_gate_on_engine_backend():
+    import torch
+
+    from kore_b200.data.tokenizer import ByteTokenizer
+    from kore_b200.eval.e2e_gate import Workload, e2e_gate, engine_backend
+    from kore_b200.models import Qwen3Weights, qwen3_tiny
+    cfg = qwen3_tiny(vocab=512)
+    w = Qwen3Weights(cfg, device="cpu", dtype=torch.float32, seed=0)
+    tok = ByteTokenizer(512)
+    be = engine_backend(w, tok, max_new_tokens=4, num_pages=128, page_size=16, max_seq_len=512)
+    wl = Workload(["hello", "what is 2+2"], answers=[None, "4"], max_new_tokens=4)
+    v = e2e_gate(be, be, wl, max_tput_drop=0.9)
+    assert v.candidate.n == 2 and v.candidate.tokens_per_s > 0
+    slow = lambda ps: (__import__("time").sleep(0.5), be(ps))[1]
+    assert not e2e_gate(slow, be, wl, max_tput_drop=0.1).passed
