@@ -31,7 +31,9 @@ from ..obs import get_logger
 
 log = get_logger("campaign")
 
-STAGES = ["reverify", "datagen", "evolve", "agentic", "build", "midtrain", "sft", "dpo", "grpo", "soup", "eval"]
+STAGES = ["reverify", "datagen", "evolve", "agentic", "build", "midtrain", "sft", "dpo", "dpo_iterative", "grpo",
+          "soup", "eval"]
+OPTIONAL_STAGES = {"dpo_iterative"}     # run only when configured or asked for by name
 TRAIN_STAGES = {"midtrain", "sft", "dpo", "grpo"}
 
 
@@ -72,7 +74,7 @@ def _digest(obj) -> str:
 
 # ------------------------------------------------------------------ stage bodies
 def _latest_model(c: Campaign, m: dict) -> str:
-    for st in ("soup", "grpo", "dpo", "sft", "midtrain"):
+    for st in ("soup", "grpo", "dpo_iterative", "dpo", "sft", "midtrain"):
         o = m["stages"].get(st, {}).get("outputs", {})
         if o.get("model"):
             return o["model"]
@@ -164,6 +166,50 @@ def _stage_build(c: Campaign, m: dict) -> dict:
     return out
 
 
+def _stage_dpo_iterative(c: Campaign, m: dict, policy_factory=None, env_factory=None) -> dict:
+    """On-policy iterative DPO (+ DAgger): each round samples the current model
+    on the training tasks, pairs its best verified response against worse ones,
+    and trains a DPO round (IPO + SFT loss) from that model. Reference:
+    scripts/run_campaign.py:1425 and kore/data/onpolicy.py:96."""
+    cfg = dict(c.configs.get("dpo_iterative", {}))
+    rounds = int(cfg.pop("rounds", 2))
+    n_tasks = int(cfg.pop("tasks", 64))
+    samples = int(cfg.pop("samples_per_task", 4))
+    model = _latest_model(c, m)
+    history = []
+    for r in range(rounds):
+        d = c.out_dir / "dpo_iterative" / f"round{r}"
+        d.mkdir(parents=True, exist_ok=True)
+        pairs_path = d / "pairs.jsonl"
+        if not c.dry_run:
+            from ..data.generators import onpolicy_pairs
+            from ..tasks.registry import get_task, split_tasks
+            train, _ = split_tasks()
+            tasks = [get_task(t) for t in train[:n_tasks]]
+            if policy_factory is None:
+                from ..policy.format import SYSTEM_PROMPT, build_task_prompt
+                from ..policy.serve import KorePolicy
+                pol = KorePolicy(model, temperature=1.0)
+                policy_factory = lambda _m: (lambda t: pol.chat(
+                    [[{"role": "system", "content": SYSTEM_PROMPT},
+                      {"role": "user", "content": build_task_prompt(t)}]] * samples))
+            if env_factory is None:
+                from ..env.kore_env import KoreEnv
+                env_factory = lambda t: KoreEnv(t.task_id)
+            pairs = onpolicy_pairs(tasks, policy_factory(model), env_factory)
+            with open(pairs_path, "w") as f:
+                for p in pairs:
+                    f.write(json.dumps(p) + "\n")
+        dcfg = {"model_name_or_path": model, "output_dir": str(d / "model"), "dataset_path": str(pairs_path),
+                "loss_type": ["ipo", "sft"]}
+        dcfg.update(cfg)
+        if launch_stage(c, "dpo", dcfg, port=29521 + r) != 0:
+            raise RuntimeError(f"iterative DPO round {r} failed")
+        model = dcfg["output_dir"]
+        history.append(model)
+    return {"model": model, "rounds": history}
+
+
 def _stage_soup(c: Campaign, m: dict) -> dict:
     from ..policy.configs import SoupConfig
     from ..policy.soup import build_soup
@@ -186,7 +232,8 @@ def _stage_eval(c: Campaign, m: dict) -> dict:
 STAGE_FNS: Dict[str, Callable[[Campaign, dict], dict]] = {
     "reverify": _stage_reverify, "datagen": _stage_datagen, "evolve": _datagen("evolve"),
     "agentic": _datagen("agentic"), "build": _stage_build, "midtrain": _train_stage("midtrain"),
-    "sft": _train_stage("sft"), "dpo": _train_stage("dpo"), "grpo": _train_stage("grpo"),
+    "sft": _train_stage("sft"), "dpo": _train_stage("dpo"), "dpo_iterative": _stage_dpo_iterative,
+    "grpo": _train_stage("grpo"),
     "soup": _stage_soup, "eval": _stage_eval,
 }
 
@@ -224,7 +271,8 @@ def retention_check(c: Campaign, m: dict, generate_factory: Optional[Callable[[s
 def run(c: Campaign, stages: Optional[List[str]] = None, force: Optional[List[str]] = None,
         generate_factory=None) -> dict:
     m = c.load_manifest()
-    todo = [s for s in STAGES if stages is None or s in stages]
+    todo = [s for s in STAGES if (stages is None and (s not in OPTIONAL_STAGES or s in c.configs))
+            or (stages is not None and s in stages)]
     for st in todo:
         inputs = {"cfg": c.configs.get(st, {}), "base": c.base_model,
                   "upstream": {k: v.get("outputs") for k, v in m["stages"].items() if STAGES.index(k) < STAGES.index(st)}}

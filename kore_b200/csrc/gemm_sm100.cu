@@ -786,7 +786,7 @@ int choose_splits(int tiles, int kblocks, int sms) {
 }  // namespace gemm
 
 // Which kernel large plain GEMMs use: 1 = 2-CTA pairs (cta_group::2), 0 = one CTA per tile.
-static int g_gemm_pair_mode = 0;
+static int g_gemm_pair_mode = 1;
 int64_t gemm_set_pair_mode(int64_t mode) {
   const int old = g_gemm_pair_mode;
   g_gemm_pair_mode = (int)mode;

@@ -27,7 +27,8 @@ def test_manifest_resume_and_force(tmp_path, monkeypatch):
     o, c, fns = _campaign(tmp_path, calls)
     monkeypatch.setattr(o, "STAGE_FNS", fns)
     m = o.run(c)
-    assert calls == o.STAGES and all(v["status"] == "done" for v in m["stages"].values())
+    assert calls == [s for s in o.STAGES if s not in o.OPTIONAL_STAGES]
+    assert all(v["status"] == "done" for v in m["stages"].values())
     calls.clear()
     o.run(c)
     assert calls == []                                   # everything resumed from the manifest
@@ -120,3 +121,14 @@ def test_distill_sink_dedup(tmp_path):
     assert s.flush() == 1
     s2 = DistillSink(p)
     assert len(s2.best) == 1 and list(s2.best.values())[0].speedup == 2.0
+
+
+def test_iterative_dpo_stage_dry_run(tmp_path):
+    from kore_b200.campaign.orchestrator import Campaign, run
+    c = Campaign(out_dir=tmp_path, base_model="base", dry_run=True, configs={"dpo_iterative": {"rounds": 2}})
+    m = run(c, stages=["dpo_iterative"])
+    st = m["stages"]["dpo_iterative"]
+    assert st["status"] == "done" and len(st["outputs"]["rounds"]) == 2
+    assert st["outputs"]["model"].endswith("round1/model")
+    cfg = (tmp_path / "dpo" / "config.json").read_text()
+    assert "round0/model" in cfg and "ipo" in cfg          # round 2 trains from round 1's model

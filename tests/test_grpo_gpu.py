@@ -45,20 +45,20 @@ def test_multiturn_graph_rollout_gpu():
                                               share_keys=[i // 4 for i in range(12)], max_feedback=9,
                                               temperature=0.0)
     assert check_device_error() == 0
-    ref_eng = RolloutEngine(w, max_batch=16, page_size=64, num_pages=256, max_seq_len=2048)
-    ctx = [list(p) for p in prompts]
-    agree = total = 0
-    lp_err = 0.0
-    for turn in range(3):
-        res = ref_eng.generate([GenRequest(c, 40, rid=i) for i, c in enumerate(ctx)], temperature=0.0)
-        for i, r in enumerate(res):
-            a, b = outs[i].gens[turn], r.tokens
-            n = 0
-            while n < min(len(a), len(b)) and a[n] == b[n]:
+    # teacher forcing: the training engine scores the transcripts the graph loop produced;
+    # greedy sampling reports log-probs of the untempered softmax
+    from kore_b200.engine.qwen3_engine import Batch, Qwen3Engine
+    scorer = Qwen3Engine(w, allocate_grads=False)
+    err, n = 0.0, 0
+    for o in outs:
+        full = o.contexts[-1] + o.gens[-1]
+        b = Batch.from_sequences([torch.tensor(full)], device="cuda")
+        lp, _ = scorer.token_logprobs(b)
+        lp = lp.float().cpu()
+        for t in range(3):
+            c0 = len(o.contexts[t])
+            for j, v in enumerate(o.logps[t]):
+                err = max(err, abs(v - float(lp[c0 - 1 + j])))
                 n += 1
-            agree += n
-            total += len(b)
-            lp_err = max([lp_err] + [abs(x - y) for x, y in zip(outs[i].logps[turn][:n], r.logps[:n])])
-            ctx[i] = outs[i].contexts[turn] + a + fb(turn, i, a)   # follow the graph's transcript
-    assert agree / total > 0.9 and lp_err < 5e-2, (agree / total, lp_err)
+    assert n == 12 * 3 * 40 and err < 6e-2, err
     assert len(eng.cache.free) == eng.cache.num_pages
