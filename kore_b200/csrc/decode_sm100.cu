@@ -304,6 +304,204 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(AttnParams p)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode attention with a TMA pipeline (one query token per sequence).
+// CTA = (sequence, kv head, split); warp 0 streams the split's pages of this
+// kv head's K and V through a STAGES-deep ring of shared-memory buffers with
+// plain (non-multicast) TMA tile loads (one 64-key page per stage, two 64-column
+// boxes per matrix so the 128-byte swizzle applies), warps 1..2 consume: each
+// owns 32 of a page's 64 keys (lane = key), scores them against the G query
+// heads kept in shared memory, keeps an online softmax per head, and
+// accumulates P.V with lanes spread over D. The loads run STAGES pages ahead of
+// the math, so HBM sees several 32 KB requests per CTA in flight.
+constexpr int kTmaStages = 3;
+constexpr int kPage = 64;                          // keys per stage (= cache page size)
+constexpr int kStageK = kPage * D * 2;             // 16 KB of K per stage
+constexpr int kTmaThreads = 96;                    // 1 producer + 2 consumer warps
+
+struct TmaDecodeSmem {
+  static constexpr int K_OFF = 0;
+  static constexpr int V_OFF = kTmaStages * kStageK;
+  static constexpr int BAR_OFF = 2 * kTmaStages * kStageK;
+  static constexpr int TOTAL = BAR_OFF + 64 + 1024;
+};
+
+// Element offset of (row, col) inside a 64-row x 64-column bf16 box written by
+// TMA with the 128-byte swizzle: 16-byte chunks of a row are XORed with row % 8.
+KORE_DEV int swz(int row, int col) {
+  return row * 64 + ((((col >> 3) ^ (row & 7)) << 3) | (col & 7));
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
+    const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p) {
+  extern __shared__ __align__(1024) uint8_t dsm_raw[];
+  uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
+  const __nv_bfloat16* sK = reinterpret_cast<const __nv_bfloat16*>(dsm + TmaDecodeSmem::K_OFF);
+  const __nv_bfloat16* sV = reinterpret_cast<const __nv_bfloat16*>(dsm + TmaDecodeSmem::V_OFF);
+  uint64_t* full = reinterpret_cast<uint64_t*>(dsm + TmaDecodeSmem::BAR_OFF);
+  uint64_t* empty = full + kTmaStages;
+  __shared__ __align__(16) float sq[G][D];
+  __shared__ float sp[2][G][32];
+  __shared__ float sm_m[2][G], sm_l[2][G];
+  __shared__ float sm_acc[2][G][D];
+  __shared__ int s_abort;
+
+  const int seq = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int trow = p.q_start[seq];
+  const int nkeys = p.seq_lens[seq];
+  const int npages = (nkeys + kPage - 1) / kPage;
+  const int per = (npages + p.nsplit - 1) / p.nsplit;       // pages per split
+  const int pg0 = split * per, pg1 = min(npages, pg0 + per);
+  const int* bt = p.block_table + (size_t)seq * p.max_pages;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTmaStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 2);
+    }
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) {
+    const int g = i / D, d = i % D;
+    sq[g][d] = __bfloat162float(p.q[(size_t)trow * p.ldq + (kvh * G + g) * D + d]) * p.scale_log2;
+  }
+  __syncthreads();
+
+  float m[G], l[G], acc[G][4];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    m[g] = -INFINITY; l[g] = 0.f;
+    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
+  }
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int pg = pg0; pg < pg1; ++pg) {
+        if (!mbar_wait(&empty[stage], phase ^ 1)) { s_abort = 1; break; }
+        const int y = bt[pg] * kPage;
+        uint8_t* kb = dsm + TmaDecodeSmem::K_OFF + stage * kStageK;
+        uint8_t* vb = dsm + TmaDecodeSmem::V_OFF + stage * kStageK;
+        mbar_arrive_expect_tx(&full[stage], 2 * kStageK);
+        tma_load_2d(kb, &tmK, &full[stage], kvh * D, y);
+        tma_load_2d(kb + kStageK / 2, &tmK, &full[stage], kvh * D + 64, y);
+        tma_load_2d(vb, &tmV, &full[stage], kvh * D, y);
+        tma_load_2d(vb + kStageK / 2, &tmV, &full[stage], kvh * D + 64, y);
+        if (++stage == kTmaStages) { stage = 0; phase ^= 1; }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---------------------------------------------------------- consumers
+    const int cw = warp - 1;                 // keys [32 cw, 32 cw + 32) of each page
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int pg = pg0; pg < pg1 && !s_abort; ++pg) {
+      if (!mbar_wait(&full[stage], phase)) { s_abort = 1; break; }
+      const __nv_bfloat16* Kp = sK + stage * (kStageK / 2);
+      const __nv_bfloat16* Vp = sV + stage * (kStageK / 2);
+      const int r = cw * 32 + lane;                          // this lane's key row in the page
+      const int key = pg * kPage + r;
+      const bool valid = key < nkeys;
+      float s[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) s[g] = 0.f;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const __nv_bfloat16* box = Kp + half * (kPage * 64);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {        // 8 chunks of 8 columns
+          const uint4 u = *reinterpret_cast<const uint4*>(box + swz(r, c * 8));
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+          const float2 k0 = __bfloat1622float2(h[0]), k1 = __bfloat1622float2(h[1]);
+          const float2 k2 = __bfloat1622float2(h[2]), k3 = __bfloat1622float2(h[3]);
+          const int d0 = half * 64 + c * 8;
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const float4 qa = *reinterpret_cast<const float4*>(&sq[g][d0]);
+            const float4 qb = *reinterpret_cast<const float4*>(&sq[g][d0 + 4]);
+            s[g] += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y +
+                    qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
+          }
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float cm = valid ? s[g] : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffff, cm, o));
+        const float mn = fmaxf(m[g], cm);
+        const float corr = mn == -INFINITY ? 1.f : exp2f(m[g] - mn);
+        const float e = valid ? exp2f(s[g] - mn) : 0.f;
+        l[g] = l[g] * corr + e;
+        acc[g][0] *= corr; acc[g][1] *= corr; acc[g][2] *= corr; acc[g][3] *= corr;
+        m[g] = mn;
+        sp[cw][g][lane] = e;
+      }
+      __syncwarp();
+      // P.V: lane owns columns [4 lane, 4 lane + 4) -> box lane / 16, column (4 lane) % 64
+      const __nv_bfloat16* vbox = Vp + (lane / 16) * (kPage * 64);
+      const int col = (lane * 4) & 63;
+      const int nk = min(32, nkeys - (pg * kPage + cw * 32));
+#pragma unroll 8
+      for (int kk = 0; kk < 32; ++kk) {
+        if (kk >= nk) break;
+        const int row = cw * 32 + kk;
+        const uint2 vu = *reinterpret_cast<const uint2*>(vbox + swz(row, col));
+        const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.x));
+        const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.y));
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float pe = sp[cw][g][kk];
+          acc[g][0] += pe * va.x; acc[g][1] += pe * va.y; acc[g][2] += pe * vb.x; acc[g][3] += pe * vb.y;
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == kTmaStages) { stage = 0; phase ^= 1; }
+    }
+    // per-warp row sums, then publish for the merge
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float t = l[g];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
+      if (lane == 0) { sm_m[cw][g] = m[g]; sm_l[cw][g] = t; }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sm_acc[cw][g][lane * 4 + e] = acc[g][e];
+    }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+    const int g = idx / D, d = idx % D;
+    const float mm = fmaxf(sm_m[0][g], sm_m[1][g]);
+    float ll = 0.f, aa = 0.f;
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      if (sm_m[w][g] == -INFINITY) continue;
+      const float c = exp2f(sm_m[w][g] - mm);
+      ll += sm_l[w][g] * c;
+      aa += sm_acc[w][g][d] * c;
+    }
+    const int h = kvh * G + g;
+    if (p.nsplit == 1) {
+      p.out[((size_t)trow * p.Hq + h) * D + d] = __float2bfloat16(ll > 0.f ? aa / ll : 0.f);
+    } else {
+      const size_t tq = (size_t)p.q_start[gridDim.x];
+      const size_t o = ((size_t)split * tq + trow) * p.Hq + h;
+      p.part_o[o * D + d] = aa;
+      if (d == 0) {
+        p.part_ml[o * 2 + 0] = mm;
+        p.part_ml[o * 2 + 1] = ll;
+      }
+    }
+  }
+}
+
 __global__ void paged_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml,
                                      __nv_bfloat16* __restrict__ out, int Tq, int Hq, int nsplit) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // over Tq * Hq * D
@@ -479,7 +677,36 @@ void paged_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor
   p.out = (__nv_bfloat16*)out.data_ptr();
   auto st = at::cuda::getCurrentCUDAStream();
   const int G = Hq / Hkv;
-  if (max_q == 1 && page_size % 32 == 0 && Tq == nseq) {
+  if (max_q == 1 && page_size == kPage && Tq == nseq && (G == 1 || G == 2 || G == 4 || G == 5 || G == 8)) {
+    // TMA-pipelined decode: tensor maps over the caches viewed as [slots, Hkv * 128]
+    auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const uint64_t slots = (uint64_t)kc.size(0);
+    CUtensorMap tk = make_tmap_2d(kc.data_ptr(), bf, 2, (uint64_t)Hkv * D, slots, (uint64_t)Hkv * D, 64, kPage);
+    CUtensorMap tv = make_tmap_2d(vc.data_ptr(), bf, 2, (uint64_t)Hkv * D, slots, (uint64_t)Hkv * D, 64, kPage);
+    dim3 grid(nseq, Hkv, nsplit);
+    const int smem = TmaDecodeSmem::TOTAL;
+    static bool attr[64][9] = {};
+    int dev = 0;
+    check_cuda(cudaGetDevice(&dev), "cudaGetDevice");
+#define KORE_DEC_TMA(GG)                                                                                   \
+  {                                                                                                        \
+    auto kfn = paged_decode_tma_kernel<GG>;                                                                \
+    if (!attr[dev][GG]) {                                                                                  \
+      check_cuda(cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), "decode smem"); \
+      attr[dev][GG] = true;                                                                                \
+    }                                                                                                      \
+    kfn<<<grid, kTmaThreads, smem, st>>>(tk, tv, p);                                                       \
+  }
+    switch (G) {
+      case 1: KORE_DEC_TMA(1) break;
+      case 2: KORE_DEC_TMA(2) break;
+      case 4: KORE_DEC_TMA(4) break;
+      case 5: KORE_DEC_TMA(5) break;
+      default: KORE_DEC_TMA(8) break;
+    }
+#undef KORE_DEC_TMA
+    check_cuda(cudaGetLastError(), "paged_decode_tma");
+  } else if (max_q == 1 && page_size % 32 == 0 && Tq == nseq) {
     dim3 grid(nseq, Hkv, nsplit);
     switch (G) {
       case 1: paged_decode_kernel<1><<<grid, kWarps * 32, 0, st>>>(p); break;

@@ -39,7 +39,11 @@ class HostStash:
                 continue
             h = self._host.get(i)
             if h is None or h.shape != t.shape or h.dtype != t.dtype:
-                h = torch.empty(t.shape, dtype=t.dtype, pin_memory=self.pin and t.is_cuda)
+                try:
+                    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=self.pin and t.is_cuda)
+                except RuntimeError:   # page-locking refused (host memory): pageable copies still work
+                    self.pin = False
+                    h = torch.empty(t.shape, dtype=t.dtype)
                 self._host[i] = h
             h.copy_(t, non_blocking=True)
             moved += t.numel() * t.element_size()
