@@ -209,6 +209,83 @@ def grpo_main(args) -> None:
             "impl": "kore"}), flush=True)
 
 
+def dpo_main(args) -> None:
+    """DPO tokens/s (BASELINE DPO row), weak-scaled: 4 chosen/rejected pairs per
+    GPU (32 on 8 GPUs), a shared 1024-token prompt + 3072-token responses of
+    uniform-random ids, beta 0.1, sigmoid loss; the frozen reference is
+    sharded over the ranks (streamed from host memory on one GPU)."""
+    import torch
+
+    from kore_b200 import ops
+    from kore_b200.models import PRESETS, Qwen3Weights
+    from kore_b200.parallel.dist import init_distributed
+    from kore_b200.policy.configs import DPOConfig
+    from kore_b200.policy.dpo import DPOTrainer
+
+    assert args.warmup >= 3, "at least 3 warm-up steps"
+    ctx = init_distributed()
+    cfg = PRESETS[args.model]()
+    if args.layers:
+        cfg.num_hidden_layers = args.layers
+    ops.native()
+    W = ctx.world
+    P, R = args.prompt_len, args.response_len
+    dc = DPOConfig(beta=0.1, learning_rate=1e-6, lr_scheduler_type="constant", warmup_ratio=0.0, bf16=True,
+                   use_lora=False, micro_pairs=1, ref_placement=args.ref_placement)
+    dc.comm = args.comm
+    w = Qwen3Weights(cfg, device=ctx.device, dtype=torch.bfloat16, seed=0, pad_multiple=128 * max(1, W))
+    dt = DPOTrainer(dc, ctx, w, total_steps=args.warmup + args.steps)   # reference = the policy at step 0
+    del w
+    g = torch.Generator().manual_seed(77 + ctx.rank)
+
+    def batch():
+        out = []
+        for _ in range(args.pairs_per_gpu):
+            prompt = torch.randint(0, cfg.vocab_size, (P,), generator=g).tolist()
+            pair = []
+            for _ in range(2):
+                pair.append((prompt + torch.randint(0, cfg.vocab_size, (R,), generator=g).tolist(), P))
+            out.append(pair)
+        return out
+
+    batches = [batch() for _ in range(min(4, args.warmup + args.steps))]
+    for i in range(args.warmup):
+        dt.step(batches[i % len(batches)])
+    torch.cuda.synchronize()
+    ctx.barrier()
+    ops.reset_launch_count()
+    clk = ClockSampler(ctx.local_rank).start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    e0.record()
+    for i in range(args.steps):
+        loss = dt.step(batches[(args.warmup + i) % len(batches)])
+    e1.record()
+    torch.cuda.synchronize()
+    wall_ms = ctx.max_over_ranks((time.perf_counter() - t0) * 1000 / args.steps)
+    clocks = clk.stop()
+    ms = ctx.max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    tokens = args.pairs_per_gpu * 2 * (P + R) * W
+    if ctx.is_main:
+        print(json.dumps({
+            "metric": "dpo_tokens_per_s", "value": tokens / (ms / 1000.0), "unit": "tokens/s", "n_gpus": W,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic uniform-random prompt/response ids, random-init weights",
+            "config": {"model": "qwen3-14b-arch (dense)" if args.model == "qwen3-14b" else args.model,
+                       "layers": cfg.num_hidden_layers, "pairs": args.pairs_per_gpu * W, "prompt_len": P,
+                       "response_len": R, "beta": 0.1, "loss": "sigmoid",
+                       "reference_model": dt.ref_placement,
+                       "parallelism": f"dp{W}" + (f"-zero2-{args.comm}" if W > 1 else ""),
+                       "l2": "inputs larger than L2 (weights streamed every micro-batch)"},
+            "loss": loss, "clocks": clocks, "gpu_launches": ops.launch_count(),
+            "e2e": {"value": tokens / (wall_ms / 1000.0), "unit": "tokens/s", "ms_per_step": wall_ms,
+                    "h2d_bytes_per_step": int(args.pairs_per_gpu * 2 * (P + R) * 8),
+                    "d2h_bytes_per_step": 8},
+            "memory": {"peak_allocated_gb": round(torch.cuda.max_memory_allocated() / 1e9, 2)},
+            "impl": "kore"}), flush=True)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -221,7 +298,11 @@ def main(argv=None):
     ap.add_argument("--micro-batch", type=int, default=1)
     ap.add_argument("--layers", type=int, default=0, help="debug only: override layer count")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--metric", default="sft", choices=["sft", "grpo"])
+    ap.add_argument("--metric", default="sft", choices=["sft", "grpo", "dpo"])
+    ap.add_argument("--pairs-per-gpu", type=int, default=4, help="dpo: chosen/rejected pairs per GPU")
+    ap.add_argument("--response-len", type=int, default=3072, help="dpo: response tokens")
+    ap.add_argument("--ref-placement", default="auto", choices=["auto", "resident", "host", "shard"],
+                    help="dpo: where the frozen reference's layers live")
     ap.add_argument("--turns", type=int, default=3, help="grpo: turns per trajectory")
     ap.add_argument("--gen-len", type=int, default=2048, help="grpo: max sampled tokens per turn")
     ap.add_argument("--prompt-len", type=int, default=1024, help="grpo: prompt tokens")
@@ -244,6 +325,8 @@ def main(argv=None):
         return reference_arm(args)
     if args.metric == "grpo":
         return grpo_main(args)
+    if args.metric == "dpo":
+        return dpo_main(args)
 
     import torch
 

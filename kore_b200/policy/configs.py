@@ -111,6 +111,9 @@ class DPOConfig(DistributedMixin):
     report_to: str = "none"
     max_steps: int = -1
     max_prompt_length: int = 4096
+    # --- B200 knobs (not in the reference)
+    ref_placement: str = "auto"         # frozen reference: resident | host (streamed) | shard (all-gathered) | auto
+    micro_pairs: int = 1                # pairs per forward/backward micro-batch
 
 
 @dataclass

@@ -97,8 +97,11 @@ class DPOTrainer:
                                   seed=config.seed, schedule=config.lr_scheduler_type,
                                   warmup_steps=int(config.warmup_ratio * total_steps), total_steps=total_steps,
                                   weights=weights, comm=config.comm)
-        self.ref = Qwen3Engine(ref_weights if ref_weights is not None else weights.clone(),
-                               allocate_grads=False)
+        self.ref_placement = self._choose_placement(getattr(config, "ref_placement", "auto"))
+        self.ref = Qwen3Engine(self._build_ref(ref_weights), allocate_grads=False)
+        if self.ref_placement != "resident":
+            self.ref.param_hook = self._ref_stream
+        self.micro_pairs = max(1, int(getattr(config, "micro_pairs", 1)))
         lt = getattr(config, "loss_type", "sigmoid")
         self.loss_types = lt if isinstance(lt, list) else [lt]
         lw = getattr(config, "loss_weights", None)
@@ -107,6 +110,37 @@ class DPOTrainer:
             raise ValueError("loss_weights must match loss_type in length")
         self.ld_alpha = getattr(config, "ld_alpha", None)
         self.eps = float(getattr(config, "label_smoothing", 0.0) or 0.0)
+
+    def _choose_placement(self, mode: str) -> str:
+        """Where the frozen reference's decoder layers live: resident in HBM,
+        streamed from pinned host memory, or sharded over ranks and
+        all-gathered layer by layer (the reference sharded alongside the policy).
+        ``auto``: sharded with several ranks; on one GPU streamed from host when a
+        second resident copy of the weights would not leave room for activations."""
+        if mode != "auto":
+            return mode
+        if self.ctx.world > 1:
+            return "shard"
+        w = self.tr.w
+        if w.device.type != "cuda":
+            return "resident"
+        free, _ = torch.cuda.mem_get_info(w.device)
+        need = sum(b.numel() * b.element_size() for b in w.bufs if b is not None)
+        return "host" if free < need + 24e9 else "resident"
+
+    def _build_ref(self, ref_weights):
+        from ..engine.frozen_stream import FrozenLayerStream
+        from ..models import Qwen3Weights
+        if self.ref_placement == "resident":
+            return ref_weights if ref_weights is not None else self.tr.w.clone()
+        src = ref_weights if ref_weights is not None else self.tr.w
+        ref = Qwen3Weights(src.cfg, device=src.device, dtype=src.dtype, allocate=False,
+                           pad_multiple=src.pad_multiple, ep=src.ep)
+        last = src.num_units - 1
+        ref.bufs = [src.bufs[u].clone() if u in (0, last) else None for u in range(src.num_units)]
+        self._ref_stream = FrozenLayerStream(ref, source=self.ref_placement, ctx=self.ctx, layers_from=src)
+        self._ref_hook = self._ref_stream
+        return ref
 
     def _batch(self, items):
         from ..engine.qwen3_engine import Batch
@@ -136,46 +170,52 @@ class DPOTrainer:
         return seg.to(b.ids.device), wt.to(b.ids.device)
 
     def step(self, pairs: List[list]) -> float:
-        """pairs: list of [(chosen_ids, n_ctx), (rejected_ids, n_ctx)]."""
+        """pairs: list of [(chosen_ids, n_ctx), (rejected_ids, n_ctx)]; one
+        optimizer step over micro-batches of ``micro_pairs`` pairs (a pair's
+        loss depends only on its own sums, so micro-batching is exact)."""
         cfg = self.cfg
-        items = [x for p in pairs for x in p]
-        b = self._batch(items)
-        seg, wt = self._token_weights(b, items)
-        lp_ref, _ = self.ref.token_logprobs(b)
-        n = len(items)
-        ref_sums = torch.zeros(n, dtype=torch.float64, device=lp_ref.device)
-        ref_sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, (lp_ref * wt).double(),
-                                                             torch.zeros_like(lp_ref.double())))
-        ref_s = ref_sums.tolist()
-        counts = [max(1, len(ids) - c) for ids, c in items]
         npairs_t = torch.tensor([float(len(pairs))], device=self.ctx.device)
         self.ctx.all_reduce(npairs_t)
         npairs_global = float(npairs_t.item())
         eng = self.tr.eng
         eng.zero_grad()
+        total = 0.0
+        for s0 in range(0, len(pairs), self.micro_pairs):
+            chunk = pairs[s0:s0 + self.micro_pairs]
+            items = [x for p in chunk for x in p]
+            b = self._batch(items)
+            seg, wt = self._token_weights(b, items)
+            lp_ref, _ = self.ref.token_logprobs(b)
+            n = len(items)
+            ref_sums = torch.zeros(n, dtype=torch.float64, device=lp_ref.device)
+            ref_sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, (lp_ref * wt).double(),
+                                                                 torch.zeros_like(lp_ref.double())))
+            ref_s = ref_sums.tolist()
+            counts = [max(1, len(ids) - c) for ids, c in items]
 
-        def coef_fn(lp_full):
-            sums = torch.zeros(n, dtype=torch.float64, device=lp_full.device)
-            sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, (lp_full * wt).double(),
-                                                             torch.zeros_like(lp_full.double())))
-            ps = sums.tolist()
-            d = [0.0] * n
-            loss = 0.0
-            for k in range(len(pairs)):
-                c, r = 2 * k, 2 * k + 1
-                l, dc, dr = dpo_pair_loss(ps[c], ps[r], ref_s[c], ref_s[r], counts[c], counts[r],
-                                          beta=cfg.beta, loss_types=self.loss_types,
-                                          loss_weights=self.loss_weights, label_smoothing=self.eps)
-                loss += l / npairs_global
-                d[c] = dc / npairs_global
-                d[r] = dr / npairs_global
-            dv = torch.tensor(d, dtype=torch.float32, device=lp_full.device)
-            coef = torch.where(seg >= 0, dv[seg.clamp_min(0)] * wt, torch.zeros_like(lp_full))
-            return coef, loss
+            def coef_fn(lp_full, seg=seg, wt=wt, n=n, ref_s=ref_s, counts=counts, np_=len(chunk)):
+                sums = torch.zeros(n, dtype=torch.float64, device=lp_full.device)
+                sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, (lp_full * wt).double(),
+                                                                 torch.zeros_like(lp_full.double())))
+                ps = sums.tolist()
+                d = [0.0] * n
+                loss = 0.0
+                for k in range(np_):
+                    c, r = 2 * k, 2 * k + 1
+                    l, dc, dr = dpo_pair_loss(ps[c], ps[r], ref_s[c], ref_s[r], counts[c], counts[r],
+                                              beta=cfg.beta, loss_types=self.loss_types,
+                                              loss_weights=self.loss_weights, label_smoothing=self.eps)
+                    loss += l / npairs_global
+                    d[c] = dc / npairs_global
+                    d[r] = dr / npairs_global
+                dv = torch.tensor(d, dtype=torch.float32, device=lp_full.device)
+                coef = torch.where(seg >= 0, dv[seg.clamp_min(0)] * wt, torch.zeros_like(lp_full))
+                return coef, loss
 
-        out = eng.forward_backward(b, coef_fn=coef_fn)
+            out = eng.forward_backward(b, coef_fn=coef_fn)
+            total += float(out["loss"])
         self.tr.opt.step()
-        loss = torch.tensor([float(out["loss"])], device=self.ctx.device)
+        loss = torch.tensor([total], device=self.ctx.device)
         self.ctx.all_reduce(loss)
         return float(loss.item())
 
