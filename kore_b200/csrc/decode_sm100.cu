@@ -309,15 +309,17 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(AttnParams p)
 // CTA = (sequence, kv head, split); warp 0 streams the split's pages of this
 // kv head's K and V through a STAGES-deep ring of shared-memory buffers with
 // plain (non-multicast) TMA tile loads (one 64-key page per stage, two 64-column
-// boxes per matrix so the 128-byte swizzle applies), warps 1..2 consume: each
-// owns 32 of a page's 64 keys (lane = key), scores them against the G query
-// heads kept in shared memory, keeps an online softmax per head, and
-// accumulates P.V with lanes spread over D. The loads run STAGES pages ahead of
-// the math, so HBM sees several 32 KB requests per CTA in flight.
+// boxes per matrix so the 128-byte swizzle applies); warps 1..4 consume a page
+// together, 16 keys each: for the scores, two lanes share a key (one half of D
+// each, combined with one shuffle); for P.V the lanes spread over D. Two CTAs
+// fit an SM, so eight consumer warps hide the arithmetic latency while the
+// loads run STAGES pages ahead.
 constexpr int kTmaStages = 3;
 constexpr int kPage = 64;                          // keys per stage (= cache page size)
 constexpr int kStageK = kPage * D * 2;             // 16 KB of K per stage
-constexpr int kTmaThreads = 96;                    // 1 producer + 2 consumer warps
+constexpr int kConsumers = 4;
+constexpr int kKeysPerWarp = kPage / kConsumers;   // 16
+constexpr int kTmaThreads = 32 * (1 + kConsumers);
 
 struct TmaDecodeSmem {
   static constexpr int K_OFF = 0;
@@ -342,10 +344,12 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + TmaDecodeSmem::BAR_OFF);
   uint64_t* empty = full + kTmaStages;
   __shared__ __align__(16) float sq[G][D];
-  __shared__ float sp[2][G][32];
-  __shared__ float sm_m[2][G], sm_l[2][G];
-  __shared__ float sm_acc[2][G][D];
+  __shared__ float sp[kConsumers][G][kKeysPerWarp];
+  __shared__ float sm_m[kConsumers][G], sm_l[kConsumers][G];
   __shared__ int s_abort;
+  // the merge buffer reuses the K stages once every page has been consumed
+  float (*sm_acc)[G][D] = reinterpret_cast<float (*)[G][D]>(dsm + TmaDecodeSmem::K_OFF);
+  static_assert(kConsumers * G * D * 4 <= kTmaStages * kStageK, "merge buffer fits the K stages");
 
   const int seq = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -359,7 +363,7 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
   if (threadIdx.x == 0) {
     for (int s = 0; s < kTmaStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 2);
+      mbar_init(&empty[s], kConsumers);
     }
     s_abort = 0;
     fence_barrier_init();
@@ -397,61 +401,58 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
     __syncwarp();
   } else {
     // ---------------------------------------------------------- consumers
-    const int cw = warp - 1;                 // keys [32 cw, 32 cw + 32) of each page
+    const int cw = warp - 1;
+    const int kl = lane >> 1;                  // this lane pair's key within the warp's 16
+    const int half = lane & 1;                 // which 64 columns of D this lane scores
+    const int r = cw * kKeysPerWarp + kl;      // key row within the page
+    const int col = (lane * 4) & 63;           // P.V: columns [4 lane, 4 lane + 4) of box lane / 16
     int stage = 0;
     uint32_t phase = 0;
     for (int pg = pg0; pg < pg1 && !s_abort; ++pg) {
       if (!mbar_wait(&full[stage], phase)) { s_abort = 1; break; }
-      const __nv_bfloat16* Kp = sK + stage * (kStageK / 2);
-      const __nv_bfloat16* Vp = sV + stage * (kStageK / 2);
-      const int r = cw * 32 + lane;                          // this lane's key row in the page
+      const __nv_bfloat16* Kp = sK + stage * (kStageK / 2) + half * (kPage * 64);
+      const __nv_bfloat16* Vp = sV + stage * (kStageK / 2) + (lane / 16) * (kPage * 64);
       const int key = pg * kPage + r;
       const bool valid = key < nkeys;
       float s[G];
 #pragma unroll
       for (int g = 0; g < G; ++g) s[g] = 0.f;
 #pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        const __nv_bfloat16* box = Kp + half * (kPage * 64);
+      for (int c = 0; c < 8; ++c) {
+        const uint4 u = *reinterpret_cast<const uint4*>(Kp + swz(r, c * 8));
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+        const float2 k0 = __bfloat1622float2(h[0]), k1 = __bfloat1622float2(h[1]);
+        const float2 k2 = __bfloat1622float2(h[2]), k3 = __bfloat1622float2(h[3]);
+        const int d0 = half * 64 + c * 8;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {        // 8 chunks of 8 columns
-          const uint4 u = *reinterpret_cast<const uint4*>(box + swz(r, c * 8));
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-          const float2 k0 = __bfloat1622float2(h[0]), k1 = __bfloat1622float2(h[1]);
-          const float2 k2 = __bfloat1622float2(h[2]), k3 = __bfloat1622float2(h[3]);
-          const int d0 = half * 64 + c * 8;
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float4 qa = *reinterpret_cast<const float4*>(&sq[g][d0]);
-            const float4 qb = *reinterpret_cast<const float4*>(&sq[g][d0 + 4]);
-            s[g] += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y +
-                    qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
-          }
+        for (int g = 0; g < G; ++g) {
+          const float4 qa = *reinterpret_cast<const float4*>(&sq[g][d0]);
+          const float4 qb = *reinterpret_cast<const float4*>(&sq[g][d0 + 4]);
+          s[g] += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y +
+                  qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
         }
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float cm = valid ? s[g] : -INFINITY;
+        const float full_s = s[g] + __shfl_xor_sync(0xffffffff, s[g], 1);
+        float cm = valid ? full_s : -INFINITY;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffff, cm, o));
+        for (int o = 16; o > 1; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffff, cm, o));
         const float mn = fmaxf(m[g], cm);
         const float corr = mn == -INFINITY ? 1.f : exp2f(m[g] - mn);
-        const float e = valid ? exp2f(s[g] - mn) : 0.f;
-        l[g] = l[g] * corr + e;
+        const float e = valid ? exp2f(full_s - mn) : 0.f;
+        l[g] = l[g] * corr + (half == 0 ? e : 0.f);     // each key counted once
         acc[g][0] *= corr; acc[g][1] *= corr; acc[g][2] *= corr; acc[g][3] *= corr;
         m[g] = mn;
-        sp[cw][g][lane] = e;
+        if (half == 0) sp[cw][g][kl] = e;
       }
       __syncwarp();
-      // P.V: lane owns columns [4 lane, 4 lane + 4) -> box lane / 16, column (4 lane) % 64
-      const __nv_bfloat16* vbox = Vp + (lane / 16) * (kPage * 64);
-      const int col = (lane * 4) & 63;
-      const int nk = min(32, nkeys - (pg * kPage + cw * 32));
-#pragma unroll 8
-      for (int kk = 0; kk < 32; ++kk) {
+      const int nk = min(kKeysPerWarp, nkeys - (pg * kPage + cw * kKeysPerWarp));
+#pragma unroll 4
+      for (int kk = 0; kk < kKeysPerWarp; ++kk) {
         if (kk >= nk) break;
-        const int row = cw * 32 + kk;
-        const uint2 vu = *reinterpret_cast<const uint2*>(vbox + swz(row, col));
+        const int row = cw * kKeysPerWarp + kk;
+        const uint2 vu = *reinterpret_cast<const uint2*>(Vp + swz(row, col));
         const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.x));
         const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.y));
 #pragma unroll
@@ -464,6 +465,8 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
       if (lane == 0) mbar_arrive(&empty[stage]);
       if (++stage == kTmaStages) { stage = 0; phase ^= 1; }
     }
+    // every consumer is done reading the K stages before any overwrites them
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumers) : "memory");
     // per-warp row sums, then publish for the merge
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -478,10 +481,12 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
     const int g = idx / D, d = idx % D;
-    const float mm = fmaxf(sm_m[0][g], sm_m[1][g]);
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumers; ++w) mm = fmaxf(mm, sm_m[w][g]);
     float ll = 0.f, aa = 0.f;
 #pragma unroll
-    for (int w = 0; w < 2; ++w) {
+    for (int w = 0; w < kConsumers; ++w) {
       if (sm_m[w][g] == -INFINITY) continue;
       const float c = exp2f(sm_m[w][g] - mm);
       ll += sm_l[w][g] * c;

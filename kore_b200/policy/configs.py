@@ -224,6 +224,7 @@ class GRPOConfig(DistributedMixin):
     pack_trajectories: bool = True      # train all turns of a trajectory in one packed sequence
     old_logp_source: str = "trainer"    # "trainer" (policy forward of the update) | "sampler"
     offload_state: str = "auto"         # optimizer state / frozen ref to host between phases: auto|always|never
+    ref_placement: str = "auto"         # frozen KL reference: resident | host (streamed) | shard (all-gathered) | auto
 
 
 @dataclass

@@ -102,10 +102,14 @@ class GRPOTrainer:
         # the trainer may have moved the weights (e.g. into the symmetric heap of
         # the fused optimizer): rollout and reference read the trainer's copy
         self.w = weights = self.trainer.w
-        self.ref_w = ref_weights if ref_weights is not None else (
-            weights.clone() if config.ref_anchor_coef else None)
+        self.ref_w, self.ref_stream = None, None
+        self.ref_placement = "none"
+        if ref_weights is not None or config.ref_anchor_coef:
+            self.ref_w, self.ref_placement = self._build_ref(ref_weights, getattr(config, "ref_placement", "auto"))
         self.ref_eng = (Qwen3Engine(self.ref_w, allocate_grads=False, temperature=config.temperature)
                         if self.ref_w is not None else None)
+        if self.ref_eng is not None and self.ref_stream is not None:
+            self.ref_eng.param_hook = self.ref_stream
         rk = dict(max_batch=config.rollout_max_batch, page_size=min(config.kv_page_size, 128),
                   kv_fraction=config.kv_cache_fraction)
         rk.update(rollout_kwargs or {})
@@ -122,6 +126,32 @@ class GRPOTrainer:
         if tokenizer is not None:
             from ..data.tokenizer import eos_ids
             self.eos = eos_ids(tokenizer)
+
+    def _build_ref(self, ref_weights, mode: str):
+        """The frozen KL reference: resident, or its decoder layers streamed
+        from pinned host memory (one GPU) / sharded and all-gathered per layer
+        (several ranks). ``auto`` keeps it resident only when a second copy of
+        the weights leaves 40 GB of HBM for the rollout and activations."""
+        from ..engine.frozen_stream import FrozenLayerStream
+        from ..models import Qwen3Weights
+        src = ref_weights if ref_weights is not None else self.w
+        if mode == "auto":
+            mode = "resident"
+            if self.ctx.world > 1:
+                mode = "shard"
+            elif src.device.type == "cuda":
+                free, _ = torch.cuda.mem_get_info(src.device)
+                need = sum(b.numel() * b.element_size() for b in src.bufs if b is not None)
+                mode = "host" if free < need + 40e9 else "resident"
+        if mode == "resident":
+            return (ref_weights if ref_weights is not None else self.w.clone()), mode
+        ref = Qwen3Weights(src.cfg, device=src.device, dtype=src.dtype, allocate=False,
+                           pad_multiple=src.pad_multiple, ep=src.ep)
+        last = src.num_units - 1
+        ref.bufs = [src.bufs[u].clone() if u in (0, last) else None for u in range(src.num_units)]
+        ref.expert_bufs = {u: b.clone() for u, b in src.expert_bufs.items()}
+        self.ref_stream = FrozenLayerStream(ref, source=mode, ctx=self.ctx, layers_from=src)
+        return ref, mode
 
     # ------------------------------------------------------------ rollout
     def _decode(self, ids: Sequence[int]) -> str:
@@ -239,7 +269,7 @@ class GRPOTrainer:
         if mode == "never" or dev.type != "cuda":
             return {"opt": False, "ref": False}
         if mode == "always":
-            return {"opt": True, "ref": self.ref_w is not None}
+            return {"opt": True, "ref": self.ref_w is not None and self.ref_stream is None}
         free, _ = torch.cuda.mem_get_info(dev)
         free += torch.cuda.memory_reserved(dev) - torch.cuda.memory_allocated(dev)
         kv = trajectories * transcript * self.rollout.kv_bytes_per_token()
@@ -250,7 +280,7 @@ class GRPOTrainer:
             raise RuntimeError(f"rollout KV cache ({kv / 1e9:.1f} GB) does not fit even with the optimizer "
                                f"state ({opt_bytes / 1e9:.1f} GB) parked in host memory")
         act = 16e9 if self.trainer.eng.keep_layers == 0 else 16e9 + 40e9
-        need_ref = self.ref_w is not None and act > free
+        need_ref = self.ref_w is not None and self.ref_stream is None and act > free
         return {"opt": need_opt, "ref": need_ref}
 
     def _batched_ok(self, max_new: int) -> bool:

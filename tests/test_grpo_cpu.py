@@ -1,4 +1,5 @@
 """GRPO trainer, rollout engine and HF checkpoints on a tiny fp32 model (CPU)."""
+import pytest
 import json
 import os
 
@@ -170,3 +171,22 @@ def test_grpo_trajectory_packing_same_gradient():
     for a, b in zip(grads[True], grads[False]):
         assert torch.allclose(a, b, atol=1e-6, rtol=1e-4)
     assert any(g.abs().sum() > 0 for g in grads[True])
+
+
+def test_grpo_streamed_reference_matches_resident():
+    """The frozen KL reference streamed layer by layer scores like a resident copy."""
+    cfg, w = _tiny()
+    env = SyntheticRewardEnv(seed=0, prompt_len=12, feedback_len=4, vocab_size=cfg.vocab_size)
+    base = dict(num_trajectories=2, num_turns=1, tasks_per_step=1, max_response_length=6, max_prompt_length=256,
+                max_feedback_tokens=4, learning_rate=1e-3, temperature=1.0, ref_anchor_coef=1e-2,
+                dynamic_sampling=False, starpo_s=False, bf16=False, overlong_mask=False)
+    res = {}
+    for place in ("resident", "host"):
+        tr = GRPOTrainer(GRPOConfig(ref_placement=place, **base), weights=w.clone(), env=env,
+                         rollout_kwargs=dict(num_pages=128, page_size=16, max_seq_len=512))
+        assert tr.ref_placement == place
+        groups = tr.rollout_batch(["a"], [0, 1], max_new_tokens=6)
+        samples = tr.samples_from_group(groups[0], 0)
+        tr.fill_ref_logps(samples, 4096)
+        res[place] = [s.ref_logp for s in samples]
+    assert res["resident"] == pytest.approx(res["host"], abs=1e-5)
