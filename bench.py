@@ -199,7 +199,9 @@ def grpo_main(args) -> None:
                        "tokens_per_step": tokens, "gen_tokens_per_step_rank0": st["gen_tokens"],
                        "parallelism": f"dp{W} replicated rollout" + (f", zero2-{args.comm}" if W > 1 else ""),
                        "clip": 0.2, "kl_beta": 0.01, "temperature": 1.0,
-                       "offload": {"optimizer_state": st.get("offload_opt"), "ref_model": st.get("offload_ref")},
+                       "offload": {"optimizer_state_gb_parked": st.get("offload_opt_gb"),
+                                   "gradients_dropped_during_rollout": st.get("dropped_grads"),
+                                   "reference_model": tr.ref_placement},
                        "l2": "inputs larger than L2 (weights and KV cache streamed every decode step)"},
             "phases_ms": phases, "clocks": clocks, "gpu_launches": ops.launch_count(),
             "e2e": {"value": tokens / (wall_ms / 1000.0), "unit": "tokens/s", "ms_per_step": wall_ms,

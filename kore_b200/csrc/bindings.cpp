@@ -49,6 +49,17 @@ void sample_tokens(const at::Tensor& logits, double temperature, double top_p, i
                    int64_t step, at::Tensor& tokens, at::Tensor& logprobs,
                    const c10::optional<at::Tensor>& step_dev);
 int64_t gemm_set_pair_mode(int64_t mode);
+void gemm_grouped_dev(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& tiles,
+                      const at::Tensor& ntiles, bool b_mn, bool accumulate);
+void gemm_grouped_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& out, const at::Tensor& offsets,
+                        bool accumulate);
+void moe_plan(const at::Tensor& idx, int64_t lo, int64_t hi, at::Tensor& pos, at::Tensor& src_row,
+              at::Tensor& offsets, at::Tensor& tiles, at::Tensor& ntiles, at::Tensor& counts);
+void moe_gather_rows(const at::Tensor& x, const at::Tensor& src_row, at::Tensor& out);
+void moe_ep_plan(const at::Tensor& idx, const at::Tensor& allc, int64_t W, int64_t rank, int64_t cap,
+                 at::Tensor& dst_rank, at::Tensor& dst_row, at::Tensor& loc_offsets, at::Tensor& loc_totals,
+                 at::Tensor& tiles, at::Tensor& ntiles, at::Tensor& overflow);
+void moe_zero_pad_rows(at::Tensor& buf, const at::Tensor& offsets, const at::Tensor& totals, int64_t H);
 int64_t symm_heap_create(int64_t bytes, int64_t rank, int64_t world);
 at::Tensor symm_heap_handle(int64_t id);
 void symm_heap_open(int64_t id, const at::Tensor& handles);
@@ -75,7 +86,7 @@ void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& src, const at::Tens
                      at::Tensor& dsrc, at::Tensor& dw);
 void symm_ep_scatter(int64_t id, int64_t buf_offset, const at::Tensor& x, const at::Tensor& src_row,
                      const at::Tensor& dst_rank, const at::Tensor& dst_row,
-                     const c10::optional<at::Tensor>& scale);
+                     const c10::optional<at::Tensor>& scale, int64_t cap);
 void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, const at::Tensor& row,
                     const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& resid,
                     at::Tensor& y, const c10::optional<at::Tensor>& g, const c10::optional<at::Tensor>& dw,
@@ -125,10 +136,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_adamw_bcast", &kore::symm_adamw_bcast);
   m.def("gemm_grouped_bf16", &kore::gemm_grouped_bf16, "grouped (MoE) tcgen05 GEMM");
   m.def("moe_route_fwd", &kore::moe_route_fwd);
+  m.def("moe_plan", &kore::moe_plan, "device routing plan: counts, padded offsets, positions, tiles");
+  m.def("moe_gather_rows", &kore::moe_gather_rows);
+  m.def("moe_ep_plan", &kore::moe_ep_plan, "expert-parallel plan from gathered counts (device)");
+  m.def("moe_zero_pad_rows", &kore::moe_zero_pad_rows);
+  m.def("gemm_grouped_dev", &kore::gemm_grouped_dev, "grouped GEMM over a device tile table");
+  m.def("gemm_grouped_wgrad", &kore::gemm_grouped_wgrad, "per-expert weight gradient, device offsets");
   m.def("moe_route_bwd", &kore::moe_route_bwd);
   m.def("moe_combine", &kore::moe_combine);
   m.def("moe_combine_bwd", &kore::moe_combine_bwd);
-  m.def("symm_ep_scatter", &kore::symm_ep_scatter);
+  m.def("symm_ep_scatter", &kore::symm_ep_scatter, "P2P scatter of rows into owners' buffers",
+        py::arg("id"), py::arg("buf_offset"), py::arg("x"), py::arg("src_row"), py::arg("dst_rank"),
+        py::arg("dst_row"), py::arg("scale") = py::none(), py::arg("cap") = 0);
   m.def("symm_ep_gather", &kore::symm_ep_gather);
   m.def("gemm_tp_bf16", &kore::gemm_tp_bf16, "tensor-parallel AG->GEMM / GEMM->RS over peer memory",
         py::arg("a_local"), py::arg("a_peers"), py::arg("lda"), py::arg("M"), py::arg("b"), py::arg("out"),

@@ -71,6 +71,14 @@ struct Params {
   // the fp32 partial tile goes to rows split*ws_rows + m of the workspace map tmC
   int splits = 1;
   int ws_rows = 0;
+  // grouped mode with a device-built tile table: the number of M tiles is read
+  // from device memory (no host round trip); p.M is the table's capacity
+  const int* ntiles_dev = nullptr;
+  // grouped weight-gradient mode (MoE experts): work item t covers expert
+  // t / (num_m*num_n); its K range is rows [wg_offs[e], wg_offs[e+1]) of the
+  // expert-major operands (multiples of 64); output rows are e * M + row
+  const int* wg_offs = nullptr;
+  int wg_E = 0;
 };
 
 // K blocks [kb0, kb1) of split s when `kblocks` are divided over `splits`.
@@ -116,10 +124,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
-  const int num_m = (p.M + BM - 1) / BM;
+  const int num_m = p.ntiles_dev != nullptr ? min(*p.ntiles_dev, (p.M + BM - 1) / BM) : (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_mn = num_m * num_n;
-  const int num_tiles = num_mn * p.splits;
+  const int num_tiles = p.wg_offs != nullptr ? num_mn * p.wg_E : num_mn * p.splits;
   const int kblocks = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -187,7 +195,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int tm, tn, kb0, kb1;
         tile_coords(t % num_mn, num_m, num_n, tm, tn);
-        split_range(t / num_mn, p.splits, kblocks, kb0, kb1);
+        if (p.wg_offs != nullptr) {
+          kb0 = p.wg_offs[t / num_mn] / BK;
+          kb1 = p.wg_offs[t / num_mn + 1] / BK;
+          if (kb0 >= kb1) continue;          // expert without rows: no loads, no MMA, no store
+        } else {
+          split_range(t / num_mn, p.splits, kblocks, kb0, kb1);
+        }
         if (p.ag_rot) tm = (tm + p.ag_rot) % num_m;
         int m0 = tm * BM, ex = 0;
         const int n0 = tn * BN;
@@ -243,15 +257,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+      for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
+        int kb0, kb1;
+        if (p.wg_offs != nullptr) {
+          kb0 = p.wg_offs[t / num_mn] / BK;
+          kb1 = p.wg_offs[t / num_mn + 1] / BK;
+          if (kb0 >= kb1) continue;
+        } else {
+          split_range(t / num_mn, p.splits, kblocks, kb0, kb1);
+        }
         const int acc = it & 1;
         const uint32_t acc_phase = (it >> 1) & 1;
+        ++it;
         if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1)) { *abort_flag = 1; break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
         bool ok = true;
-        int kb0, kb1;
-        split_range(t / num_mn, p.splits, kblocks, kb0, kb1);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase)) { ok = false; break; }
           tc_fence_after();
@@ -281,10 +302,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     int buf = 0;
     int it = 0;
     const int CH = p.out_f32 ? 32 : 64;  // output columns per 128-byte staging row
-    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x, ++it) {
+    for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
       int tm, tn;
       tile_coords(t % num_mn, num_m, num_n, tm, tn);
-      const int ws_row0 = (t / num_mn) * p.ws_rows;   // split-K: this split's workspace rows
+      int ws_row0 = (t / num_mn) * p.ws_rows;   // split-K: this split's workspace rows
+      if (p.wg_offs != nullptr) {
+        const int e = t / num_mn;
+        if (p.wg_offs[e] >= p.wg_offs[e + 1]) continue;
+        ws_row0 = e * p.M;                      // expert e's block of the [E * M, N] gradient
+      }
       if (p.ag_rot) tm = (tm + p.ag_rot) % num_m;
       int m0 = tm * BM, m_lim = p.M;
       const int n0 = tn * BN;
@@ -295,6 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      ++it;
       if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
@@ -332,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           if (p.accumulate) {
             if (p.out_f32) {
-              const float* cp = reinterpret_cast<const float*>(p.C_read) + (size_t)row * p.ldc + n0 + c0;
+              const float* cp = reinterpret_cast<const float*>(p.C_read) + (size_t)(row + (p.wg_offs ? ws_row0 : 0)) * p.ldc + n0 + c0;
 #pragma unroll
               for (int j = 0; j < 32; j += 4) {
                 if (j >= ncols) break;
@@ -341,7 +368,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             } else {
               const __nv_bfloat16* cp =
-                  reinterpret_cast<const __nv_bfloat16*>(p.C_read) + (size_t)row * p.ldc + n0 + c0;
+                  reinterpret_cast<const __nv_bfloat16*>(p.C_read) + (size_t)(row + (p.wg_offs ? ws_row0 : 0)) * p.ldc + n0 + c0;
 #pragma unroll
               for (int j = 0; j < 64; j += 8) {
                 if (j >= ncols) break;
@@ -603,6 +630,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n0 = tn * BN;
       const int acc = it & 1;
       const uint32_t acc_phase = (it >> 1) & 1;
+      ++it;
       if (!mbar_wait(&tfull_bar[acc], acc_phase)) { *abort_flag = 1; break; }
       tc_fence_after();
       const int row = m0 + q * 32 + lane;
@@ -1066,6 +1094,106 @@ void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
     else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st);
   }
   tt.record_stream(cst);
+}
+
+}  // namespace kore
+
+namespace kore {
+
+// Grouped GEMM whose tile table lives on the device (built by moe_plan): no
+// host round trip. tiles: int32 [cap * 4] of {expert, first row, row limit, 0};
+// ntiles: int32 [1] with the number of valid entries (<= cap).
+void gemm_grouped_dev(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& tiles,
+                      const at::Tensor& ntiles, bool b_mn, bool accumulate) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda() && a.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16, "grouped gemm: bf16 CUDA tensors");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 3 && out.dim() == 2 && a.stride(1) == 1 && b.is_contiguous() &&
+                  out.stride(1) == 1, "grouped gemm: a [M,K], b [E,..] contiguous, out [M,N]");
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && ntiles.scalar_type() == at::kInt && tiles.is_cuda() &&
+                  ntiles.is_cuda(), "grouped gemm: int32 device tile table");
+  const int E = b.size(0);
+  const int K = a.size(1);
+  const int N = b_mn ? b.size(2) : b.size(1);
+  TORCH_CHECK((b_mn ? b.size(1) : b.size(2)) == K, "grouped gemm: K mismatch");
+  TORCH_CHECK(out.size(1) == N && out.size(0) == a.size(0), "grouped gemm: out shape");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && a.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "alignment");
+  const int cap = (int)(tiles.numel() / 4);
+  if (cap == 0) return;
+  c10::cuda::CUDAGuard guard(a.device());
+  const bool f32 = out.scalar_type() == at::kFloat;
+  gemm::Params p;
+  p.M = cap * 128; p.N = N; p.K = K;
+  p.alpha = 1.f;
+  p.accumulate = accumulate ? 1 : 0;
+  p.out_f32 = f32 ? 1 : 0;
+  p.C_read = out.data_ptr();
+  p.C_write = out.data_ptr();
+  p.ldc = out.stride(0);
+  p.R = nullptr; p.ldr = 0;
+  p.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
+  p.ntiles_dev = ntiles.data_ptr<int>();
+  p.ag_rows = 0; p.rs_rows = 0; p.rs_rank = 0;
+  const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  const int BN = use256 ? 256 : 128;
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = make_tmap_2d(a.data_ptr(), bf, 2, K, a.size(0), a.stride(0), 64, 128);
+  CUtensorMap tb = b_mn ? make_tmap_3d(b.data_ptr(), bf, 2, N, K, E, N, (uint64_t)N * K, 64, 64, 1)
+                        : make_tmap_3d(b.data_ptr(), bf, 2, K, N, E, K, (uint64_t)N * K, 64, BN, 1);
+  CUtensorMap tc = ta;   // grouped epilogue stores directly
+  const int grid = std::min(cap * ((N + BN - 1) / BN), num_sms(a.get_device()));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (use256) {
+    if (b_mn) gemm::launch<256, 4, false, true>(ta, tb, tc, p, grid, st);
+    else gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st);
+  } else {
+    if (b_mn) gemm::launch<128, 6, false, true>(ta, tb, tc, p, grid, st);
+    else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st);
+  }
+}
+
+// Per-expert weight gradient over expert-major, 64-row-padded operands:
+// out[e] (=|+=) dy[rows_e]^T . x[rows_e], rows_e = [offsets[e], offsets[e+1])
+// (device int32, multiples of 64; padding rows are zero). dy [P, M], x [P, N],
+// out [E, M, N] (M % 128 == 0). One launch for all experts, no host offsets.
+void gemm_grouped_wgrad(const at::Tensor& dy, const at::Tensor& x, at::Tensor& out, const at::Tensor& offsets,
+                        bool accumulate) {
+  TORCH_CHECK(dy.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16 && dy.is_contiguous() &&
+                  x.is_contiguous() && out.is_contiguous() && out.dim() == 3, "grouped wgrad: layouts");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.is_cuda(), "grouped wgrad: int32 device offsets");
+  const int E = out.size(0), M = out.size(1), N = out.size(2);
+  const int P = dy.size(0);
+  TORCH_CHECK(dy.size(1) == M && x.size(1) == N && x.size(0) == P && offsets.numel() == E + 1,
+              "grouped wgrad: shapes");
+  TORCH_CHECK(M % 128 == 0 && N % 64 == 0, "grouped wgrad: M % 128 and N % 64");
+  const bool f32 = out.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || out.scalar_type() == at::kBFloat16, "grouped wgrad: out bf16 or fp32");
+  if (P == 0 || E == 0) return;
+  c10::cuda::CUDAGuard guard(dy.device());
+  gemm::Params p;
+  p.M = M; p.N = N; p.K = P;
+  p.alpha = 1.f;
+  p.accumulate = accumulate ? 1 : 0;
+  p.out_f32 = f32 ? 1 : 0;
+  p.C_read = out.data_ptr();
+  p.C_write = out.data_ptr();
+  p.ldc = N;
+  p.R = nullptr; p.ldr = 0;
+  p.tiles = nullptr;
+  p.ag_rows = 0; p.rs_rows = 0; p.rs_rank = 0;
+  p.wg_offs = offsets.data_ptr<int>();
+  p.wg_E = E;
+  const bool use256 = N % 256 == 0;
+  const int BN = use256 ? 256 : 128;
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = make_tmap_2d(dy.data_ptr(), bf, 2, M, P, M, 64, 64);
+  CUtensorMap tb = make_tmap_2d(x.data_ptr(), bf, 2, N, P, N, 64, 64);
+  CUtensorMap tc = f32 ? make_tmap_2d(out.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, (uint64_t)E * M, N, 32, 32)
+                       : make_tmap_2d(out.data_ptr(), bf, 2, N, (uint64_t)E * M, N, 64, 32);
+  const int items = E * (M / 128) * ((N + BN - 1) / BN);
+  const int grid = std::min(items, num_sms(dy.get_device()));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (use256) gemm::launch<256, 4, true, true>(ta, tb, tc, p, grid, st);
+  else gemm::launch<128, 6, true, true>(ta, tb, tc, p, grid, st);
 }
 
 }  // namespace kore

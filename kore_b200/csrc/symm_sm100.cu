@@ -405,10 +405,11 @@ namespace symm {
 // dst_row[i] (P2P stores over NVLink). One warp per pair, 16-byte vectors.
 __global__ void ep_scatter_kernel(const __nv_bfloat16* __restrict__ x, const long* __restrict__ src_row,
                                   const int* __restrict__ dst_rank, const long* __restrict__ dst_row,
-                                  const float* __restrict__ scale, PeerPtrs dst, int n, int H) {
+                                  const float* __restrict__ scale, PeerPtrs dst, int n, int H, long cap) {
   const long i = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (i >= n) return;
+  if (cap > 0 && dst_row[i] >= cap) return;     // receive buffer too small: the plan flagged it
   const __nv_bfloat16* s = x + src_row[i] * (long)H;
   __nv_bfloat16* d = reinterpret_cast<__nv_bfloat16*>(dst.p[dst_rank[i]]) + dst_row[i] * (long)H;
   const float sc = scale ? scale[i] : 1.f;
@@ -490,7 +491,7 @@ __global__ void ep_gather_kernel(PeerPtrs src, const int* __restrict__ rank, con
 
 void symm_ep_scatter(int64_t id, int64_t buf_offset, const at::Tensor& x, const at::Tensor& src_row,
                      const at::Tensor& dst_rank, const at::Tensor& dst_row,
-                     const c10::optional<at::Tensor>& scale) {
+                     const c10::optional<at::Tensor>& scale, int64_t cap) {
   auto& h = *g_heaps.at(id);
   const int n = src_row.numel(), H = x.size(1);
   TORCH_CHECK(H % 8 == 0 && x.is_contiguous(), "ep_scatter: contiguous rows, H % 8");
@@ -498,7 +499,7 @@ void symm_ep_scatter(int64_t id, int64_t buf_offset, const at::Tensor& x, const 
   symm::PeerPtrs dst = peer_ptrs(h, buf_offset, false);
   symm::ep_scatter_kernel<<<(n + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)x.data_ptr(), src_row.data_ptr<long>(), dst_rank.data_ptr<int>(),
-      dst_row.data_ptr<long>(), scale ? scale->data_ptr<float>() : nullptr, dst, n, H);
+      dst_row.data_ptr<long>(), scale ? scale->data_ptr<float>() : nullptr, dst, n, H, (long)cap);
   check_cuda(cudaGetLastError(), "ep_scatter");
 }
 

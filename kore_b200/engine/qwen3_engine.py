@@ -214,13 +214,14 @@ class Qwen3Engine:
         probs, idx, wts = moe.route(logits, c.num_experts_per_tok, c.norm_topk_prob)
         if self.ep is not None:
             return self.ep.forward(self, W, hn2, x2, probs, idx, wts)
-        src, pos, offs = moe.permutation(idx, c.num_experts)
-        xp = moe.gather_rows(hn2, src)
-        gu = moe.grouped_mm(xp, W["experts_gate_up"], offs)
+        # device routing plan (padded expert-major rows): no host synchronisation
+        pl = moe.plan(idx, c.num_experts)
+        xp = moe.plan_gather(hn2, pl)
+        gu = moe.plan_mm(xp, W["experts_gate_up"], pl)
         a = ops.swiglu_fwd(gu)
-        yp = moe.grouped_mm(a, W["experts_down"], offs)
-        x3 = moe.combine(yp, pos, wts, resid=x2)
-        return x3, dict(probs=probs, idx=idx, wts=wts, src=src, pos=pos, offs=offs, xp=xp, gu=gu, a=a, yp=yp)
+        yp = moe.plan_mm(a, W["experts_down"], pl)
+        x3 = moe.combine(yp, pl.pos, wts, resid=x2)
+        return x3, dict(probs=probs, idx=idx, wts=wts, plan=pl, pos=pl.pos, xp=xp, gu=gu, a=a, yp=yp)
 
     def _moe_bwd(self, W, G, ctx, dx3, acc):
         """Returns d(hn2) of the MoE block; accumulates expert and router grads."""
@@ -229,20 +230,29 @@ class Qwen3Engine:
         if self.ep is not None:
             dhn2, dw = self.ep.backward(self, W, G, ctx, dx3)
         else:
-            offs = ctx["offs"]
-            dyp, dw = moe.combine_bwd(dx3, ctx["yp"], ctx["pos"], ctx["wts"])
-            da = moe.grouped_mm(dyp, W["experts_down"], offs, w_t=False)
-            self._expert_wgrad(G["experts_down"], dyp, ctx["a"], offs)
+            pl = ctx["plan"]
+            dyp, dw = moe.combine_bwd(dx3, ctx["yp"], pl.pos, ctx["wts"])
+            da = moe.plan_mm(dyp, W["experts_down"], pl, w_t=False)
+            self._plan_wgrad(G["experts_down"], dyp, ctx["a"], pl)
             dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])
             del da
-            dxp = moe.grouped_mm(dgu, W["experts_gate_up"], offs, w_t=False)
-            self._expert_wgrad(G["experts_gate_up"], dgu, ctx["xp"], offs)
-            dhn2 = moe.combine(dxp, ctx["pos"], None)
+            dxp = moe.plan_mm(dgu, W["experts_gate_up"], pl, w_t=False)
+            self._plan_wgrad(G["experts_gate_up"], dgu, ctx["xp"], pl)
+            dhn2 = moe.combine(dxp, pl.pos, None)
         dlogits = moe.route_bwd(ctx["probs"], ctx["idx"], ctx["wts"], dw, c.norm_topk_prob)
         dl = dlogits.to(self.dtype)
         self._mm(dl, W["router"], b_t=False, out=dhn2, accumulate=True)
         self._mm(dl, ctx["hn2"], a_t=True, b_t=False, out=G["router"], accumulate=acc)
         return dhn2
+
+    def _plan_wgrad(self, Gw, dy, x, pl):
+        """dW[e] += dy_e^T x_e for every expert in one launch when the gradient
+        shapes tile (rows of dW a multiple of 128); else per expert."""
+        from ..ops import moe
+        if not dy.is_cuda or (Gw.shape[1] % 128 == 0 and Gw.shape[2] % 64 == 0):
+            moe.plan_wgrad(dy, x, pl, Gw, accumulate=True)
+        else:
+            self._expert_wgrad(Gw, dy, x, pl.offsets.tolist())
 
     def _expert_wgrad(self, Gw, dy, x, offs, expert_base: int = 0):
         """dW[e] += dy_e^T x_e for each expert with rows (gradients are zeroed

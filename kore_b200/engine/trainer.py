@@ -256,4 +256,7 @@ class CausalLMTrainer:
         dev = self.ctx.device
         ids = ids_host.to(dev, non_blocking=True)
         mask = loss_mask_host.to(dev, non_blocking=True) if loss_mask_host is not None else None
-        return float(self.train_step_device(ids, mask).item())
+        loss = float(self.train_step_device(ids, mask).item())
+        if hasattr(self.eng.ep, "check_overflow"):
+            self.eng.ep.check_overflow()          # one flag read per step (the step synchronised already)
+        return loss

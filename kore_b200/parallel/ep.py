@@ -128,18 +128,27 @@ class ExpertParallel:
 
 
 class FusedExpertParallel(ExpertParallel):
-    """Expert parallelism on the symmetric peer-memory heap (path d).
+    """Expert parallelism on the symmetric peer-memory heap (path d), with no
+    host synchronisation.
 
-    Dispatch: every rank stores its token rows straight into the owner
-    rank's receive buffer, already in the owner's expert-major order, with
-    NVLink P2P stores (one kernel; no all-to-all and no receive-side
-    permutation). The owner runs the grouped tcgen05 expert GEMMs in place.
-    Combine: each source rank pulls its pairs' expert outputs from the
-    owners' heaps with P2P loads and reduces them with the routing weights
-    and the residual in the same kernel. The backward pushes w * dy rows to
-    the owners (scaled P2P stores), pulls dot products for the routing-weight
-    gradient, and pulls the input gradients back. Device barriers (epoch
-    flags) order the phases; only the per-expert counts (E ints) cross NCCL.
+    Plan: per-expert counts (a scatter-add on the device) are all-gathered
+    with NCCL straight into a device buffer; one kernel turns them into every
+    local pair's owner rank and row in the owner's receive buffer (expert-major,
+    each expert padded to 64 rows, source ranks in rank order), and the owner's
+    padded expert offsets and grouped-GEMM tile table. Nothing returns to the
+    host; a receive buffer that is too small sets a device flag that
+    ``check_overflow`` reads once per optimizer step.
+
+    Dispatch: every rank stores its token rows straight into the owners'
+    receive buffers with NVLink P2P stores; the owner zeroes its pad rows and
+    runs the grouped tcgen05 expert GEMMs over the device tile table. Combine:
+    each source rank pulls its pairs' expert outputs from the owners' heaps and
+    reduces them with the routing weights and the residual in the same kernel.
+    Backward: the expert side is recomputed from the saved token rows (one more
+    dispatch and gate/up GEMM) instead of keeping receive-buffer-sized
+    activations per layer; w * dy rows are pushed to the owners, the routing
+    gradient's dot products and the input gradients are pulled back. Device
+    barriers (epoch flags) order the phases.
     """
 
     def __init__(self, ctx, cfg, lo, hi, heap, cap_rows: int):
@@ -147,70 +156,66 @@ class FusedExpertParallel(ExpertParallel):
         H = cfg.hidden_size
         I = cfg.moe_intermediate_size
         self.heap = heap
-        self.cap = int(cap_rows)
+        self.cap = int(cap_rows) // 64 * 64
         self.o_recv, self.recv = heap.alloc(self.cap * H)
         self.o_y, self.ybuf = heap.alloc(self.cap * H)
         self.o_dy, self.dybuf = heap.alloc(self.cap * H)
         self.o_dx, self.dxbuf = heap.alloc(self.cap * H)
         self.H, self.I = H, I
+        self.overflow = torch.zeros(1, dtype=torch.int32, device=ctx.device)
 
-    def _counts(self, idx):
-        flat = idx.reshape(-1).long()
-        counts = torch.bincount(flat, minlength=self.E).to(torch.int64)
-        allc = torch.empty(self.W * self.E, dtype=torch.int64, device=counts.device)
-        dist.all_gather_into_tensor(allc, counts, group=self.ctx.group)
-        return flat, counts, allc.view(self.W, self.E)
-
-    def _route_rows(self, idx):
-        """Destination rank/row of every local pair, and this rank's receive plan."""
+    def _plan(self, idx):
         T, k = idx.shape
-        flat, counts, C = self._counts(idx)
-        Ch = C.tolist()
-        W, El, r = self.W, self.El, self.ctx.rank
-        base = [0] * self.E          # first row of expert e in its owner's buffer
-        for d in range(W):
-            acc = 0
-            for e in range(d * El, (d + 1) * El):
-                base[e] = acc
-                acc += sum(Ch[s][e] for s in range(W))
-        off_me = torch.tensor([base[e] + sum(Ch[s][e] for s in range(r)) for e in range(self.E)],
-                              dtype=torch.long, device=idx.device)
-        order = torch.argsort(flat, stable=True)
-        start = torch.cumsum(counts, 0) - counts                       # my first sorted index per expert
-        e_sorted = flat[order]
-        p = torch.arange(order.numel(), device=idx.device)
-        dst_row_sorted = off_me[e_sorted] + (p - start[e_sorted])
-        dst_row = torch.empty_like(dst_row_sorted)
-        dst_row[order] = dst_row_sorted
-        dst_rank = (flat // El).to(torch.int32)
-        offs = [0]
-        for e in range(self.lo, self.hi):
-            offs.append(offs[-1] + sum(Ch[s][e] for s in range(W)))
-        rmax = max(sum(Ch[s][e] for s in range(W) for e in range(d * El, (d + 1) * El)) for d in range(W))
-        return dst_rank, dst_row, offs, rmax
+        dev = idx.device
+        flat = idx.reshape(-1).long()
+        counts = torch.zeros(self.E, dtype=torch.int32, device=dev)
+        counts.scatter_add_(0, flat, torch.ones_like(flat, dtype=torch.int32))
+        allc = torch.empty(self.W * self.E, dtype=torch.int32, device=dev)
+        dist.all_gather_into_tensor(allc, counts, group=self.ctx.group)
+        dst_rank = torch.empty(T * k, dtype=torch.int32, device=dev)
+        dst_row = torch.empty(T * k, dtype=torch.long, device=dev)
+        offs = torch.empty(self.El + 1, dtype=torch.int32, device=dev)
+        tot = torch.empty(self.El, dtype=torch.int32, device=dev)
+        ncap = self.cap // 128 + self.El
+        tiles = torch.zeros(ncap * 4, dtype=torch.int32, device=dev)
+        ntiles = torch.zeros(1, dtype=torch.int32, device=dev)
+        ops.native().moe_ep_plan(idx.int().contiguous(), allc, self.W, self.ctx.rank, self.cap, dst_rank, dst_row,
+                                 offs, tot, tiles, ntiles, self.overflow)
+        return dict(dst_rank=dst_rank, dst_row=dst_row,
+                    plan=moe.Plan(None, None, offs, tiles, ntiles, tot, self.cap))
+
+    def check_overflow(self) -> None:
+        if int(self.overflow.item()):
+            self.overflow.zero_()
+            raise RuntimeError("expert-parallel receive buffer overflow: raise ep_capacity")
+
+    def _dispatch_and_up(self, W, hn2, pl):
+        """Rows to the owners, pad rows zeroed, gate/up GEMM + SwiGLU on the receive buffer."""
+        C = ops.native()
+        T, k = pl["dst_rank"].numel() // self.k, self.k
+        src_row = torch.arange(T * k, device=hn2.device) // k
+        C.symm_ep_scatter(self.heap.id, self.o_recv, hn2, src_row, pl["dst_rank"], pl["dst_row"], None, self.cap)
+        self.heap.barrier()                                   # all rows delivered
+        xp = self.recv[: self.cap * self.H].view(self.cap, self.H)
+        C.moe_zero_pad_rows(xp, pl["plan"].offsets, pl["plan"].counts, self.H)
+        gu = moe.plan_mm(xp, W["experts_gate_up"], pl["plan"])
+        return xp, gu
 
     def forward(self, eng, W, hn2, x2, probs, idx, wts):
         T, k = idx.shape
-        dst_rank, dst_row, offs, rmax = self._route_rows(idx)
-        if rmax > self.cap:
-            return super().forward(eng, W, hn2, x2, probs, idx, wts)
-        C = ops.native()
-        src_row = torch.arange(T * k, device=hn2.device) // k
-        C.symm_ep_scatter(self.heap.id, self.o_recv, hn2, src_row, dst_rank, dst_row, None)
-        self.heap.barrier()                                   # all rows delivered
-        R = offs[-1]
-        H = self.H
-        xp = self.recv[: R * H].view(R, H).clone()            # kept for the weight gradient
-        gu = moe.grouped_mm(xp, W["experts_gate_up"], offs)
+        self.k = k
+        pl = self._plan(idx)
+        xp, gu = self._dispatch_and_up(W, hn2, pl)
         a = ops.swiglu_fwd(gu)
-        yp = self.ybuf[: R * H].view(R, H)
-        moe.grouped_mm(a, W["experts_down"], offs, out=yp)
+        yp = self.ybuf[: self.cap * self.H].view(self.cap, self.H)
+        moe.plan_mm(a, W["experts_down"], pl["plan"], out=yp)
+        del gu, a
         self.heap.barrier()                                   # expert outputs ready
         y = torch.empty_like(x2)
-        C.symm_ep_gather(self.heap.id, self.o_y, dst_rank.view(T, k), dst_row.view(T, k), wts.float().contiguous(),
-                         x2, y, None, None, H)
-        ctx = dict(probs=probs, idx=idx, wts=wts, fused=True, dst_rank=dst_rank, dst_row=dst_row, offs=offs,
-                   xp=xp, gu=gu, a=a)
+        ops.native().symm_ep_gather(self.heap.id, self.o_y, pl["dst_rank"].view(T, k), pl["dst_row"].view(T, k),
+                                    wts.float().contiguous(), x2, y, None, None, self.H)
+        self.heap.barrier()                                   # pulls done before ybuf is reused
+        ctx = dict(probs=probs, idx=idx, wts=wts, fused=True, hn2=hn2, **pl)
         return y, ctx
 
     def backward(self, eng, W, G, ctx, dx3):
@@ -219,24 +224,30 @@ class FusedExpertParallel(ExpertParallel):
         C = ops.native()
         T, k = ctx["idx"].shape
         H = self.H
-        offs = ctx["offs"]
-        R = offs[-1]
         dev = dx3.device
+        pl = ctx["plan"]
+        # recompute the expert side: dispatch, gate/up, SwiGLU, down (y is needed for the routing gradient)
+        xp, gu = self._dispatch_and_up(W, ctx["hn2"], ctx)
+        a = ops.swiglu_fwd(gu)
+        yp = self.ybuf[: self.cap * H].view(self.cap, H)
+        moe.plan_mm(a, W["experts_down"], pl, out=yp)
+        self.heap.barrier()                                   # expert outputs ready for the pulls
         dw = torch.empty(T, k, dtype=torch.float32, device=dev)
-        # routing-weight gradient: <dy[t], y_expert> pulled from the owners (outputs still in their heaps)
         C.symm_ep_gather(self.heap.id, self.o_y, ctx["dst_rank"].view(T, k), ctx["dst_row"].view(T, k), None, None,
                          dx3, dx3, dw, H)
         src_row = torch.arange(T * k, device=dev) // k
         C.symm_ep_scatter(self.heap.id, self.o_dy, dx3, src_row, ctx["dst_rank"], ctx["dst_row"],
-                          ctx["wts"].reshape(-1).float().contiguous())
+                          ctx["wts"].reshape(-1).float().contiguous(), self.cap)
         self.heap.barrier()                                   # w * dy rows delivered; y reads done
-        dyp = self.dybuf[: R * H].view(R, H)
-        da = moe.grouped_mm(dyp, W["experts_down"], offs, w_t=False)
-        eng._expert_wgrad(G["experts_down"], dyp, ctx["a"], offs)
-        dgu = ops.swiglu_bwd(da, ctx["gu"], ctx["gu"])
-        dxp = self.dxbuf[: R * H].view(R, H)
-        moe.grouped_mm(dgu, W["experts_gate_up"], offs, w_t=False, out=dxp)
-        eng._expert_wgrad(G["experts_gate_up"], dgu, ctx["xp"], offs)
+        dyp = self.dybuf[: self.cap * H].view(self.cap, H)
+        C.moe_zero_pad_rows(dyp, pl.offsets, pl.counts, H)
+        da = moe.plan_mm(dyp, W["experts_down"], pl, w_t=False)
+        eng._plan_wgrad(G["experts_down"], dyp, a, pl)
+        dgu = ops.swiglu_bwd(da, gu, gu)
+        del da
+        dxp = self.dxbuf[: self.cap * H].view(self.cap, H)
+        moe.plan_mm(dgu, W["experts_gate_up"], pl, w_t=False, out=dxp)
+        eng._plan_wgrad(G["experts_gate_up"], dgu, xp, pl)
         self.heap.barrier()                                   # input grads ready
         dhn2 = torch.empty(T, H, dtype=dx3.dtype, device=dev)
         C.symm_ep_gather(self.heap.id, self.o_dx, ctx["dst_rank"].view(T, k), ctx["dst_row"].view(T, k), None, None,

@@ -254,34 +254,68 @@ class GRPOTrainer:
             tr.contexts, tr.gens, tr.gen_logps, tr.finish = o.contexts, o.gens, o.logps, o.finish
         return groups
 
-    def memory_plan(self, trajectories: int, transcript: int) -> Dict[str, bool]:
-        """Which state to park in host memory during the phases of a step.
+    def memory_plan(self, trajectories: int, transcript: int) -> Dict[str, object]:
+        """What leaves HBM during the rollout and reference phases of a step.
 
-        ``opt``: the optimizer moments / master leave HBM for the rollout and
-        the reference forward when the KV cache of ``trajectories`` transcripts
-        of ``transcript`` tokens would not fit next to them. ``ref``: the frozen
-        reference model leaves HBM for the update when the update's activations
-        would not fit next to everything else. Decided with every piece of
-        state resident; ``offload_state`` = always / never overrides."""
-        from ..engine.offload import optimizer_slots, slots_bytes, weight_slots
+        The KV cache of ``trajectories`` transcripts of ``transcript`` tokens
+        must fit next to the weights. In that order, and only as far as needed:
+        (1) the gradient buffers are dropped (they are zeroed at the start of
+        every update anyway, so nothing is copied) when they are plain tensors;
+        (2) optimizer state tensors (second moments first, then first moments,
+        then the fp32 master) are parked in host memory, which is bounded too.
+        ``ref``: a resident frozen reference leaves HBM for the update when the
+        update's activations would not fit. ``offload_state`` = always parks
+        all optimizer state; never parks nothing."""
+        from ..engine.offload import optimizer_slots, slots_bytes
         mode = self.cfg.offload_state
         dev = self.ctx.device
+        none = {"grads": False, "opt": [], "ref": False}
         if mode == "never" or dev.type != "cuda":
-            return {"opt": False, "ref": False}
+            return none
+        slots = optimizer_slots(self.trainer.opt)
+        order = sorted(slots, key=lambda s: {"v": 0, "m": 1, "master": 2}.get(self._slot_kind(s), 3))
         if mode == "always":
-            return {"opt": True, "ref": self.ref_w is not None and self.ref_stream is None}
+            return {"grads": self.trainer.heap is None, "opt": order,
+                    "ref": self.ref_w is not None and self.ref_stream is None}
         free, _ = torch.cuda.mem_get_info(dev)
         free += torch.cuda.memory_reserved(dev) - torch.cuda.memory_allocated(dev)
         kv = trajectories * transcript * self.rollout.kv_bytes_per_token()
-        margin = 10e9
-        opt_bytes = slots_bytes(optimizer_slots(self.trainer.opt))
-        need_opt = kv + margin > free
-        if need_opt and kv + margin > free + opt_bytes:
-            raise RuntimeError(f"rollout KV cache ({kv / 1e9:.1f} GB) does not fit even with the optimizer "
-                               f"state ({opt_bytes / 1e9:.1f} GB) parked in host memory")
+        need = kv + 10e9 - free
+        plan: Dict[str, object] = dict(none)
+        if need > 0 and self.trainer.heap is None:
+            gbytes = sum(g.numel() * g.element_size() for g in self.trainer.eng.grads if g is not None)
+            plan["grads"] = True
+            need -= gbytes
+        picked = []
+        for s in order:
+            if need <= 0:
+                break
+            picked.append(s)
+            need -= slots_bytes([s])
+        if need > 0:
+            raise RuntimeError(f"rollout KV cache ({kv / 1e9:.1f} GB) does not fit even with the gradients "
+                               f"dropped and the optimizer state parked in host memory")
+        plan["opt"] = picked
         act = 16e9 if self.trainer.eng.keep_layers == 0 else 16e9 + 40e9
-        need_ref = self.ref_w is not None and self.ref_stream is None and act > free
-        return {"opt": need_opt, "ref": need_ref}
+        plan["ref"] = self.ref_w is not None and self.ref_stream is None and act > free
+        return plan
+
+    def _slot_kind(self, slot) -> str:
+        c, _ = slot
+        for name in ("m", "v", "master"):
+            if c is getattr(self.trainer.opt, name, None):
+                return name
+        return "other"
+
+    def _drop_grads(self) -> None:
+        eng = self.trainer.eng
+        self._grad_shapes = [(g.numel(), g.dtype) if g is not None else None for g in eng.grads]
+        eng.grads = [None] * len(eng.grads)
+
+    def _restore_grads(self) -> None:
+        eng = self.trainer.eng
+        eng.grads = [None if spec is None else torch.zeros(spec[0], dtype=spec[1], device=self.ctx.device)
+                     for spec in self._grad_shapes]
 
     def _batched_ok(self, max_new: int) -> bool:
         cfg = self.cfg
@@ -492,7 +526,7 @@ class GRPOTrainer:
         ph = pt.phase("rollout")
         ph.__enter__()
         max_new = max_new_tokens or cfg.max_response_length
-        plan = {"opt": False, "ref": False}
+        plan = {"grads": False, "opt": [], "ref": False}
         batched = self._batched_ok(max_new) and not cfg.dynamic_sampling and not cfg.agentic \
             and self.prefilter is None
         if batched:
@@ -502,8 +536,10 @@ class GRPOTrainer:
             plan = self.memory_plan(target * len(mine), plen + cfg.num_turns * (max_new + fb) + 1)
             if not hasattr(self, "_opt_stash"):
                 self._opt_stash, self._ref_stash = HostStash(), HostStash()
+            if plan["grads"]:
+                self._drop_grads()
             if plan["opt"]:
-                self._opt_stash.park(optimizer_slots(self.trainer.opt))
+                self._opt_stash.park(plan["opt"])
         if batched:
             batch_tasks = [tasks[i % len(tasks)] for i in range(target)]
             for gi, trajs in enumerate(self.rollout_batch(batch_tasks, mine, max_new_tokens=max_new)):
@@ -540,7 +576,9 @@ class GRPOTrainer:
             if plan["ref"]:
                 self._ref_stash.park(weight_slots(self.ref_w))
             if plan["opt"]:
-                self._opt_stash.restore(optimizer_slots(self.trainer.opt), self.ctx.device)
+                self._opt_stash.restore(plan["opt"], self.ctx.device)
+            if plan["grads"]:
+                self._restore_grads()
         with pt.phase("update"):
             stats = self.update(samples, micro_batch_tokens)
         if plan["ref"]:
@@ -559,7 +597,9 @@ class GRPOTrainer:
                       "samples": len(samples), "gen_tokens": gen_tokens, "traj_tokens": traj_tokens,
                       "adv_absmean": sum(abs(s.adv) for s in samples) / max(1, len(samples)),
                       "rollout_s": t_roll, "step_s": time.time() - t0,
-                      "offload_opt": plan["opt"], "offload_ref": plan["ref"],
+                      "offload_opt_gb": round(sum(c[k].numel() * c[k].element_size() for c, k in plan["opt"]
+                                                  if c[k] is not None) / 1e9, 2),
+                      "dropped_grads": plan["grads"], "offload_ref": plan["ref"],
                       "grad_norm": self.trainer.opt.grad_norm()})
         stats.update({f"ms_{k}": v for k, v in pt.summary(self.ctx).items()})
         if self.ctx.is_main and (self.step_idx % max(1, cfg.logging_steps) == 0):
