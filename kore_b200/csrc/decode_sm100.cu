@@ -310,10 +310,13 @@ __global__ void __launch_bounds__(kWarps * 32) paged_decode_kernel(AttnParams p)
 // kv head's K and V through a STAGES-deep ring of shared-memory buffers with
 // plain (non-multicast) TMA tile loads (one 64-key page per stage, two 64-column
 // boxes per matrix so the 128-byte swizzle applies); warps 1..4 consume a page
-// together, 16 keys each: for the scores, two lanes share a key (one half of D
-// each, combined with one shuffle); for P.V the lanes spread over D. Two CTAs
-// fit an SM, so eight consumer warps hide the arithmetic latency while the
-// loads run STAGES pages ahead.
+// together, 16 keys each, on mma.sync tensor-core fragments: the G query heads
+// are the rows of one 16-row A operand (rows G..15 zero), K fragments come from
+// ldmatrix on the swizzled tile (16-byte chunk c of row r sits at chunk c ^ (r % 8)),
+// V fragments from ldmatrix.trans, and P moves from the score accumulators into
+// the A operand of P.V without leaving registers. Decode attention is bound by
+// HBM; the tensor-core fragments only keep the instruction count far below the
+// bytes the TMA ring delivers. Two CTAs fit an SM.
 constexpr int kTmaStages = 3;
 constexpr int kPage = 64;                          // keys per stage (= cache page size)
 constexpr int kStageK = kPage * D * 2;             // 16 KB of K per stage
@@ -328,23 +331,14 @@ struct TmaDecodeSmem {
   static constexpr int TOTAL = BAR_OFF + 64 + 1024;
 };
 
-// Element offset of (row, col) inside a 64-row x 64-column bf16 box written by
-// TMA with the 128-byte swizzle: 16-byte chunks of a row are XORed with row % 8.
-KORE_DEV int swz(int row, int col) {
-  return row * 64 + ((((col >> 3) ^ (row & 7)) << 3) | (col & 7));
-}
-
 template <int G>
 __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
     const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnParams p) {
   extern __shared__ __align__(1024) uint8_t dsm_raw[];
   uint8_t* dsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm_raw) + 1023) & ~uintptr_t(1023));
-  const __nv_bfloat16* sK = reinterpret_cast<const __nv_bfloat16*>(dsm + TmaDecodeSmem::K_OFF);
-  const __nv_bfloat16* sV = reinterpret_cast<const __nv_bfloat16*>(dsm + TmaDecodeSmem::V_OFF);
   uint64_t* full = reinterpret_cast<uint64_t*>(dsm + TmaDecodeSmem::BAR_OFF);
   uint64_t* empty = full + kTmaStages;
   __shared__ __align__(16) float sq[G][D];
-  __shared__ float sp[kConsumers][G][kKeysPerWarp];
   __shared__ float sm_m[kConsumers][G], sm_l[kConsumers][G];
   __shared__ int s_abort;
   // the merge buffer reuses the K stages once every page has been consumed
@@ -374,12 +368,6 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
   }
   __syncthreads();
 
-  float m[G], l[G], acc[G][4];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    m[g] = -INFINITY; l[g] = 0.f;
-    acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.f;
-  }
   if (warp == 0) {
     // ---------------------------------------------------------- producer
     if (lane == 0) {
@@ -400,66 +388,114 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------- consumers
+    // ---------------------------------------------------------- consumers (mma.sync)
+    // Per page each warp owns 16 keys. S[16 x 16] = Q[16 x 128] K^T with the G
+    // query heads in rows 0..G-1 (rows G..15 zero), then O[16 x 128] += P V. The
+    // K fragments come from ldmatrix on the swizzled tile, the V fragments from
+    // ldmatrix.trans; P goes from the S accumulators straight into A fragments.
     const int cw = warp - 1;
-    const int kl = lane >> 1;                  // this lane pair's key within the warp's 16
-    const int half = lane & 1;                 // which 64 columns of D this lane scores
-    const int r = cw * kKeysPerWarp + kl;      // key row within the page
-    const int col = (lane * 4) & 63;           // P.V: columns [4 lane, 4 lane + 4) of box lane / 16
+    const int gid = lane >> 2, tig = lane & 3;
+    uint32_t qa[8][4];                          // Q A-fragments, 8 k-steps of 16 dims
+    {
+      const bool hv = gid < G;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int d0 = kk * 16 + 2 * tig;
+        qa[kk][0] = hv ? pack_bf16(sq[gid][d0], sq[gid][d0 + 1]) : 0u;
+        qa[kk][1] = 0u;                          // rows 8..15: padding
+        qa[kk][2] = hv ? pack_bf16(sq[gid][d0 + 8], sq[gid][d0 + 9]) : 0u;
+        qa[kk][3] = 0u;
+      }
+    }
+    float o[16][4];
+#pragma unroll
+    for (int nt = 0; nt < 16; ++nt) o[nt][0] = o[nt][1] = o[nt][2] = o[nt][3] = 0.f;
+    float mrow = -INFINITY, lrow = 0.f;          // softmax state of head `gid` (replicated in the quad)
     int stage = 0;
     uint32_t phase = 0;
+    const uint32_t kbase0 = smem_u32(dsm + TmaDecodeSmem::K_OFF);
+    const uint32_t vbase0 = smem_u32(dsm + TmaDecodeSmem::V_OFF);
     for (int pg = pg0; pg < pg1 && !s_abort; ++pg) {
       if (!mbar_wait(&full[stage], phase)) { s_abort = 1; break; }
-      const __nv_bfloat16* Kp = sK + stage * (kStageK / 2) + half * (kPage * 64);
-      const __nv_bfloat16* Vp = sV + stage * (kStageK / 2) + (lane / 16) * (kPage * 64);
-      const int key = pg * kPage + r;
-      const bool valid = key < nkeys;
-      float s[G];
+      const uint32_t kb = kbase0 + stage * kStageK;
+      const uint32_t vb = vbase0 + stage * kStageK;
+      const int key0 = cw * kKeysPerWarp;        // first key of this warp in the page
+      // ---- scores: two n8 tiles (keys key0..+7, key0+8..+15)
+      float sc[2][4];
 #pragma unroll
-      for (int g = 0; g < G; ++g) s[g] = 0.f;
+      for (int t = 0; t < 2; ++t) sc[t][0] = sc[t][1] = sc[t][2] = sc[t][3] = 0.f;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint4 u = *reinterpret_cast<const uint4*>(Kp + swz(r, c * 8));
-        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-        const float2 k0 = __bfloat1622float2(h[0]), k1 = __bfloat1622float2(h[1]);
-        const float2 k2 = __bfloat1622float2(h[2]), k3 = __bfloat1622float2(h[3]);
-        const int d0 = half * 64 + c * 8;
+      for (int kp = 0; kp < 4; ++kp) {           // pairs of k-steps: 32 dims per ldmatrix.x4
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float4 qa = *reinterpret_cast<const float4*>(&sq[g][d0]);
-          const float4 qb = *reinterpret_cast<const float4*>(&sq[g][d0 + 4]);
-          s[g] += qa.x * k0.x + qa.y * k0.y + qa.z * k1.x + qa.w * k1.y +
-                  qb.x * k2.x + qb.y * k2.y + qb.z * k3.x + qb.w * k3.y;
+        for (int t = 0; t < 2; ++t) {
+          const int mi = lane >> 3, r = lane & 7;
+          const int row = key0 + t * 8 + r;
+          const int d = kp * 32 + mi * 8;       // 8-dim chunk this lane addresses
+          const uint32_t addr = kb + (d >> 6) * (kStageK / 2) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4);
+          uint32_t b0, b1, b2, b3;
+          asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(addr));
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t* A = qa[2 * kp + h];
+            const uint32_t bb0 = h == 0 ? b0 : b2, bb1 = h == 0 ? b1 : b3;
+            asm volatile(
+                "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                "{%0,%1,%2,%3};"
+                : "+f"(sc[t][0]), "+f"(sc[t][1]), "+f"(sc[t][2]), "+f"(sc[t][3])
+                : "r"(A[0]), "r"(A[1]), "r"(A[2]), "r"(A[3]), "r"(bb0), "r"(bb1));
+          }
         }
       }
+      // ---- online softmax of row gid over this warp's 16 keys (4 values per thread)
+      float v[4];
+      int kv[4];
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const float full_s = s[g] + __shfl_xor_sync(0xffffffff, s[g], 1);
-        float cm = valid ? full_s : -INFINITY;
+      for (int t = 0; t < 2; ++t)
 #pragma unroll
-        for (int o = 16; o > 1; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffff, cm, o));
-        const float mn = fmaxf(m[g], cm);
-        const float corr = mn == -INFINITY ? 1.f : exp2f(m[g] - mn);
-        const float e = valid ? exp2f(full_s - mn) : 0.f;
-        l[g] = l[g] * corr + (half == 0 ? e : 0.f);     // each key counted once
-        acc[g][0] *= corr; acc[g][1] *= corr; acc[g][2] *= corr; acc[g][3] *= corr;
-        m[g] = mn;
-        if (half == 0) sp[cw][g][kl] = e;
-      }
-      __syncwarp();
-      const int nk = min(kKeysPerWarp, nkeys - (pg * kPage + cw * kKeysPerWarp));
-#pragma unroll 4
-      for (int kk = 0; kk < kKeysPerWarp; ++kk) {
-        if (kk >= nk) break;
-        const int row = cw * kKeysPerWarp + kk;
-        const uint2 vu = *reinterpret_cast<const uint2*>(Vp + swz(row, col));
-        const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.x));
-        const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&vu.y));
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float pe = sp[cw][g][kk];
-          acc[g][0] += pe * va.x; acc[g][1] += pe * va.y; acc[g][2] += pe * vb.x; acc[g][3] += pe * vb.y;
+        for (int c = 0; c < 2; ++c) {
+          kv[2 * t + c] = pg * kPage + key0 + t * 8 + 2 * tig + c;
+          v[2 * t + c] = kv[2 * t + c] < nkeys ? sc[t][c] : -INFINITY;   // q carries the log2 scale
         }
+      float mx = fmaxf(fmaxf(v[0], v[1]), fmaxf(v[2], v[3]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffff, mx, 2));
+      const float mn = fmaxf(mrow, mx);
+      const float corr = mn == -INFINITY ? 1.f : exp2f(mrow - mn);
+      float e[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) e[i] = v[i] == -INFINITY ? 0.f : exp2f(v[i] - mn);
+      lrow = lrow * corr + (e[0] + e[1]) + (e[2] + e[3]);
+      mrow = mn;
+      if (corr != 1.f) {
+#pragma unroll
+        for (int nt = 0; nt < 16; ++nt) { o[nt][0] *= corr; o[nt][1] *= corr; }
+      }
+      // ---- O += P V: P (16 x 16 keys) as one A fragment, V via ldmatrix.trans
+      uint32_t pa[4];
+      pa[0] = pack_bf16(e[0], e[1]);             // row gid, keys 2tig..      (tile 0)
+      pa[1] = 0u;                                 // row gid + 8: padding
+      pa[2] = pack_bf16(e[2], e[3]);             // row gid, keys 8 + 2tig..  (tile 1)
+      pa[3] = 0u;
+#pragma unroll
+      for (int np = 0; np < 8; ++np) {           // 16 dims (two n8 tiles) per ldmatrix.x4.trans
+        const int mi = lane >> 3, r = lane & 7;
+        const int row = key0 + (mi & 1) * 8 + r;
+        const int d = np * 16 + (mi >> 1) * 8;
+        const uint32_t addr = vb + (d >> 6) * (kStageK / 2) + row * 128 + ((((d & 63) >> 3) ^ (row & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(b0), "=r"(b1), "=r"(b2), "=r"(b3) : "r"(addr));
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(o[2 * np][0]), "+f"(o[2 * np][1]), "+f"(o[2 * np][2]), "+f"(o[2 * np][3])
+            : "r"(pa[0]), "r"(pa[1]), "r"(pa[2]), "r"(pa[3]), "r"(b0), "r"(b1));
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(o[2 * np + 1][0]), "+f"(o[2 * np + 1][1]), "+f"(o[2 * np + 1][2]), "+f"(o[2 * np + 1][3])
+            : "r"(pa[0]), "r"(pa[1]), "r"(pa[2]), "r"(pa[3]), "r"(b2), "r"(b3));
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[stage]);
@@ -467,15 +503,15 @@ __global__ void __launch_bounds__(kTmaThreads) paged_decode_tma_kernel(
     }
     // every consumer is done reading the K stages before any overwrites them
     asm volatile("bar.sync 1, %0;" ::"n"(32 * kConsumers) : "memory");
-    // per-warp row sums, then publish for the merge
+    float lsum = lrow + __shfl_xor_sync(0xffffffff, lrow, 1);
+    lsum += __shfl_xor_sync(0xffffffff, lsum, 2);
+    if (gid < G) {
+      if (tig == 0) { sm_m[cw][gid] = mrow; sm_l[cw][gid] = lsum; }
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float t = l[g];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffff, t, o);
-      if (lane == 0) { sm_m[cw][g] = m[g]; sm_l[cw][g] = t; }
-#pragma unroll
-      for (int e = 0; e < 4; ++e) sm_acc[cw][g][lane * 4 + e] = acc[g][e];
+      for (int nt = 0; nt < 16; ++nt) {
+        sm_acc[cw][gid][nt * 8 + 2 * tig] = o[nt][0];
+        sm_acc[cw][gid][nt * 8 + 2 * tig + 1] = o[nt][1];
+      }
     }
   }
   __syncthreads();
