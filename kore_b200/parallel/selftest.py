@@ -8,7 +8,8 @@ replicas stay bit-identical across ranks; (2) ZeRO-3 matches ZeRO-2 in loss
 and final parameters; (3) expert parallelism over NCCL all-to-all and over
 the fused peer-memory dispatch/combine agree; (4) the tensor-parallel rollout
 engine's sampled log-probs match an fp32 single-GPU reference forward that
-scores the same tokens (teacher forcing).
+scores the same tokens (teacher forcing); (5) a GRPO step runs with the TP
+engine in the loop and its shard equals the updated weights after the sync.
 Prints one JSON line per check from rank 0 and exits non-zero on failure.
 """
 from __future__ import annotations
@@ -125,8 +126,39 @@ def main(argv=None):
         print(json.dumps({"check": "tp_rollout_vs_fp32_reference", "world": ctx.world,
                           "ok": all(r["lp_err_teacher_forced"] < 5e-2 for r in res_all), "ranks": res_all,
                           "device_error": err3}), flush=True)
+    del tp, one
+    # one GRPO step with the TP engine in the loop (multi-turn rollout, update,
+    # in-place weight sync) next to the same step on the replicated engine
+    from ..env.base import SyntheticRewardEnv
+    from ..policy.configs import GRPOConfig
+    from ..policy.grpo import GRPOTrainer
+    from .tp import TPShard
+    gstats = {}
+    for mode in ("replica", "tp"):
+        gw = Qwen3Weights(tcfg, device="cuda", dtype=torch.bfloat16, seed=4, pad_multiple=128 * ctx.world)
+        gc = GRPOConfig(num_trajectories=4, num_turns=2, tasks_per_step=2, max_response_length=32,
+                        max_prompt_length=1024, learning_rate=1e-4, temperature=1.0, dynamic_sampling=False,
+                        starpo_s=False, total_steps=2, overlong_mask=False, rollout_parallel=mode)
+        env = SyntheticRewardEnv(seed=0, prompt_len=96, feedback_len=8, vocab_size=tcfg.vocab_size)
+        gt = GRPOTrainer(gc, weights=gw, env=env, ctx=ctx,
+                         rollout_kwargs=dict(num_pages=256, page_size=64, max_seq_len=1024))
+        st = gt.train_step(["a", "b"])
+        st_ok = st["gen_tokens"] > 0 and bool(torch.isfinite(torch.tensor(st["loss"])))
+        if mode == "tp":
+            fresh = TPShard(gt.w, ctx.rank, ctx.world)
+            st_ok = st_ok and all(torch.equal(a[k], b[k]) for a, b in zip(gt.tp.shard.layers, fresh.layers)
+                                  for k in a)
+        gstats[mode] = {"ok": st_ok, "gen_tokens": st["gen_tokens"], "loss": st["loss"],
+                        "ms_rollout": st.get("ms_rollout"), "ms_sync": st.get("ms_sync")}
+        del gt, gw
+    err4 = check_device_error()
+    gok = all(v["ok"] for v in gstats.values()) and err4 == 0
+    gall = ctx.all_gather_object(gok)
+    if ctx.is_main:
+        print(json.dumps({"check": "grpo_tp_step", "world": ctx.world, "ok": all(gall), "steps": gstats,
+                          "device_error": err4}), flush=True)
     torch.distributed.barrier()
-    return 0 if (ok and same and err == 0 and mok and err2 == 0 and tok_ok) else 1
+    return 0 if (ok and same and err == 0 and mok and err2 == 0 and tok_ok and all(gall)) else 1
 
 
 if __name__ == "__main__":

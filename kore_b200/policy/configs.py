@@ -225,6 +225,7 @@ class GRPOConfig(DistributedMixin):
     old_logp_source: str = "trainer"    # "trainer" (policy forward of the update) | "sampler"
     offload_state: str = "auto"         # optimizer state / frozen ref to host between phases: auto|always|never
     ref_placement: str = "auto"         # frozen KL reference: resident | host (streamed) | shard (all-gathered) | auto
+    rollout_parallel: str = "replica"   # several GPUs: replica (each rank decodes its own rows) | tp (heads split)
 
 
 @dataclass

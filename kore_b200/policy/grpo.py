@@ -246,6 +246,11 @@ class GRPOTrainer:
         fb_cap = cfg.max_feedback_tokens
         if isinstance(self.env, SyntheticRewardEnv):
             fb_cap = min(fb_cap, self.env.feedback_len)
+        if self._use_tp():
+            outs = self._rollout_tp(prompts, max_new, fb_cap, feedback, on_turn)
+            for o, tr in zip(outs, flat):
+                tr.contexts, tr.gens, tr.gen_logps, tr.finish = o.contexts, o.gens, o.logps, o.finish
+            return groups
         outs = MultiTurnRollout(self.rollout).run(
             prompts, num_turns=cfg.num_turns, max_new=max_new, feedback=feedback, share_keys=keys,
             max_feedback=fb_cap, temperature=cfg.temperature, top_p=cfg.top_p,
@@ -253,6 +258,52 @@ class GRPOTrainer:
         for o, tr in zip(outs, flat):
             tr.contexts, tr.gens, tr.gen_logps, tr.finish = o.contexts, o.gens, o.logps, o.finish
         return groups
+
+    def _use_tp(self) -> bool:
+        return getattr(self.cfg, "rollout_parallel", "replica") == "tp" and self.ctx.world > 1
+
+    def _rollout_tp(self, prompts, max_new: int, fb_cap: int, feedback, on_turn):
+        """Multi-turn rollout on the tensor-parallel engine: every rank holds
+        1/world of each layer's heads and FFN columns and all ranks decode all
+        ranks' rows together (AG->GEMM / GEMM->RS over peer memory). Turn t+1
+        extends the cache by the last sampled token and the feedback only."""
+        from ..engine.multiturn import TrajectoryOut
+        from ..parallel.tp import TPRolloutEngine
+        cfg = self.cfg
+        n = len(prompts)
+        cap = max(len(p) for p in prompts) + cfg.num_turns * (max_new + fb_cap) + 1
+        cap = self.ctx.all_gather_object(cap) if self.ctx.world > 1 else [cap]
+        cap = max(cap)
+        if getattr(self, "tp", None) is None or self.tp.S < n or self.tp.max_seq_len < cap:
+            self.tp = None
+            if self.ctx.device.type == "cuda":
+                torch.cuda.empty_cache()
+            self.tp = TPRolloutEngine(self.w, self.ctx, max_rows=4096, max_seqs=n, max_seq_len=cap)
+        tp = self.tp
+        tp.reset()
+        outs = [TrajectoryOut() for _ in range(n)]
+        ctxs = [list(p) for p in prompts]
+        pending = [list(p) for p in prompts]
+        eos = set(int(e) for e in self.eos)
+        for turn in range(cfg.num_turns):
+            for i in range(n):
+                outs[i].contexts.append(list(ctxs[i]))
+            toks, lps = tp.generate(pending, max_new, temperature=cfg.temperature, top_p=cfg.top_p,
+                                    eos_ids=self.eos, seed=cfg.seed * 1000003 + self.step_idx * 97 + turn)
+            for i in range(n):
+                outs[i].gens.append(toks[i])
+                outs[i].logps.append(lps[i])
+                outs[i].finish.append("stop" if toks[i] and int(toks[i][-1]) in eos else "length")
+                ctxs[i] += toks[i]
+            if on_turn is not None:
+                on_turn(turn, outs)
+            if turn + 1 < cfg.num_turns:
+                for i in range(n):
+                    fb = list(feedback(turn, i, toks[i]))[:fb_cap]
+                    ctxs[i] += fb
+                    pending[i] = ([toks[i][-1]] if toks[i] else []) + fb
+        tp.release_cache()
+        return outs
 
     def memory_plan(self, trajectories: int, transcript: int) -> Dict[str, object]:
         """What leaves HBM during the rollout and reference phases of a step.
@@ -581,6 +632,9 @@ class GRPOTrainer:
                 self._restore_grads()
         with pt.phase("update"):
             stats = self.update(samples, micro_batch_tokens)
+        if getattr(self, "tp", None) is not None:
+            with pt.phase("sync"):
+                self.tp.shard.sync_from(self.w)      # in place: this rank's head / FFN slices
         if plan["ref"]:
             with pt.phase("offload"):
                 self._ref_stash.restore(weight_slots(self.ref_w), self.ctx.device)

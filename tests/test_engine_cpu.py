@@ -131,3 +131,23 @@ def test_kept_layer_contexts_match_recompute():
         for a, c in zip(g_full, eng.grads):
             assert torch.allclose(a, c, atol=1e-6, rtol=1e-5)
     assert eng.activation_bytes_per_layer(10) > 0
+
+
+def test_tp_shard_sync_in_place():
+    """The TP rollout shard is refilled in place after an optimizer step and
+    equals a freshly sliced shard (no new tensors)."""
+    from kore_b200.parallel.tp import TPShard
+    cfg = qwen3_tiny(vocab=512)
+    w = Qwen3Weights(cfg, device="cpu", dtype=torch.float32, seed=0)
+    W = 2
+    for r in range(W):
+        sh = TPShard(w, r, W)
+        ptrs = [t.data_ptr() for L in sh.layers for t in L.values()]
+        for u in range(w.num_units):
+            w.bufs[u].add_(torch.randn_like(w.bufs[u]) * 0.1)
+        sh.sync_from(w)
+        fresh = TPShard(w, r, W)
+        assert ptrs == [t.data_ptr() for L in sh.layers for t in L.values()]
+        for a, b in zip(sh.layers, fresh.layers):
+            for k in a:
+                assert torch.equal(a[k], b[k]), k

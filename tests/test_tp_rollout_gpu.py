@@ -1,0 +1,54 @@
+"""Tensor-parallel rollout engine on one GPU (world 1): chunked prefill,
+multi-turn extend and compacted decode, scored by the training engine."""
+import pytest
+import torch
+
+from kore_b200.engine.smoke import smoke_config
+from kore_b200.models import Qwen3Weights
+
+pytestmark = pytest.mark.gpu
+
+
+def test_tp_engine_multiturn_teacher_forced():
+    from kore_b200.engine.qwen3_engine import Batch, Qwen3Engine
+    from kore_b200.ops import check_device_error
+    from kore_b200.parallel.dist import DistContext
+    from kore_b200.parallel.tp import TPRolloutEngine
+    cfg = smoke_config()
+    w = Qwen3Weights(cfg, device="cuda", dtype=torch.bfloat16, seed=2)
+    ctx = DistContext(device=torch.device("cuda"))
+    g = torch.Generator().manual_seed(7)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (150, 70, 33, 300, 5)]
+    # 128 rows per chunk: the 150- and 300-token prompts are split across chunks
+    eng = TPRolloutEngine(w, ctx, max_rows=128, max_seqs=8, max_seq_len=1024)
+    ctxs = [list(p) for p in prompts]
+    pending = [list(p) for p in prompts]
+    turns = []
+    eos = None
+    for turn in range(3):
+        toks, lps = eng.generate(pending, 24, temperature=0.0, eos_ids=() if eos is None else (eos,))
+        assert check_device_error() == 0
+        turns.append([(list(c), t, l) for c, t, l in zip(ctxs, toks, lps)])
+        if eos is None:
+            eos = toks[1][5]                         # a token that ends sequence 1 early next turn
+        fb = [[(13 * turn + 5 * i + k) % cfg.vocab_size for k in range(7)] for i in range(len(prompts))]
+        pending = [[t[-1]] + f if t else [] for t, f in zip(toks, fb)]
+        for i, t in enumerate(toks):
+            ctxs[i] += t + fb[i]
+        assert all(eng.lens[0][i] == len(ctxs[i]) - len(fb[i]) - 1 for i in range(len(prompts)) if toks[i])
+    scorer = Qwen3Engine(w, allocate_grads=False)
+    err, n = 0.0, 0
+    for turn in turns:
+        for c, t, l in turn:
+            assert len(t) == len(l) and 0 < len(t) <= 24
+            if not t:
+                continue
+            b = Batch.from_sequences([torch.tensor(c + t)], device="cuda")
+            lp, _ = scorer.token_logprobs(b)
+            lp = lp.float().cpu()
+            for j, v in enumerate(l):
+                err = max(err, abs(v - float(lp[len(c) - 1 + j])))
+                n += 1
+    assert n > 200 and err < 6e-2, err
+    eng.release_cache()
+    assert eng.kc is None
