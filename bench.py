@@ -27,6 +27,12 @@ import sys
 import threading
 import time
 
+if any(a in ("grpo", "dpo", "--metric=grpo", "--metric=dpo") for a in sys.argv) and "reference" not in sys.argv:
+    # the GRPO / DPO phases free and re-allocate tens of GB in blocks of
+    # different sizes every step (KV cache, gradients, reference layers):
+    # growable segments keep that from fragmenting the 180 GB
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 

@@ -501,6 +501,28 @@ struct PairSmem {
   static constexpr int TOTAL = BAR_OFF + 256 + 1024;
 };
 
+// Bytes CTA ``r`` of a pair loads per K block of tile (tm, tn): a box whose
+// first row (A) or column (B) is past the matrix is skipped.
+template <int BN, bool A_MN, bool B_MN>
+KORE_DEV uint32_t pair_box_bytes(const Params& p, int tm, int tn, int r) {
+  const int m0 = tm * 2 * BM + r * BM;
+  const int n0 = tn * BN + r * (BN / 2);
+  uint32_t b = 0;
+  if (!A_MN) {
+    b += m0 < p.M ? (uint32_t)(BM * BK * 2) : 0u;
+  } else {
+#pragma unroll
+    for (int j = 0; j < BM / 64; ++j) b += (m0 + 64 * j < p.M) ? 8192u : 0u;
+  }
+  if (!B_MN) {
+    b += n0 < p.N ? (uint32_t)((BN / 2) * BK * 2) : 0u;
+  } else {
+#pragma unroll
+    for (int j = 0; j < BN / 128; ++j) b += (n0 + 64 * j < p.N) ? 8192u : 0u;
+  }
+  return b;
+}
+
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -560,19 +582,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sA = smem + stage * S::STAGE_BYTES;
           uint8_t* sB = sA + S::A_BYTES;
           const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
-          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], 2 * S::STAGE_BYTES);
+          // boxes that lie wholly past M or N are not issued (their rows / columns
+          // of the accumulator are never stored); the leader expects the bytes
+          // both CTAs actually load
+          if (rank == 0)
+            mbar_arrive_expect_tx(&full_bar[stage], pair_box_bytes<BN, A_MN, B_MN>(p, tm, tn, 0) +
+                                                        pair_box_bytes<BN, A_MN, B_MN>(p, tm, tn, 1));
           const int k0 = kb * BK;
           if (!A_MN) {
-            tma_load_2d_pair(sA, &tmA, fb, k0, m0);
+            if (m0 < p.M) tma_load_2d_pair(sA, &tmA, fb, k0, m0);
           } else {
 #pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(sA + j * 8192, &tmA, fb, m0 + 64 * j, k0);
+            for (int j = 0; j < BM / 64; ++j)
+              if (m0 + 64 * j < p.M) tma_load_2d_pair(sA + j * 8192, &tmA, fb, m0 + 64 * j, k0);
           }
           if (!B_MN) {
-            tma_load_2d_pair(sB, &tmB, fb, k0, n0);
+            if (n0 < p.N) tma_load_2d_pair(sB, &tmB, fb, k0, n0);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 128; ++j) tma_load_2d_pair(sB + j * 8192, &tmB, fb, n0 + 64 * j, k0);
+            for (int j = 0; j < BN / 128; ++j)
+              if (n0 + 64 * j < p.N) tma_load_2d_pair(sB + j * 8192, &tmB, fb, n0 + 64 * j, k0);
           }
           if (++stage == STAGES) { stage = 0; phase ^= 1; }
         }
@@ -892,7 +921,7 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a
                         : make_tmap_2d(a.data_ptr(), bf, 2, K, M, a.stride(0), 64, 128);
   cudaStream_t st0 = at::cuda::getCurrentCUDAStream();
   const int pair_tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  if (g_gemm_pair_mode == 1 && splits == 1 && max_ctas <= 0 && use256 && pair_tiles >= sms) {
+  if (g_gemm_pair_mode == 1 && splits == 1 && max_ctas <= 0 && use256 && M > gemm::BM && pair_tiles >= sms) {
     // 2-CTA pairs: each CTA loads half of the 256-column B tile
     CUtensorMap tbp = b_mn ? make_tmap_2d(b.data_ptr(), bf, 2, N, K, b.stride(0), 64, 64)
                            : make_tmap_2d(b.data_ptr(), bf, 2, K, N, b.stride(0), 64, 128);

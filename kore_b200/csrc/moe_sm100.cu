@@ -403,6 +403,7 @@ void moe_plan(const at::Tensor& idx, int64_t lo, int64_t hi, at::Tensor& pos, at
   c10::cuda::CUDAGuard g(idx.device());
   auto st = at::cuda::getCurrentCUDAStream();
   pos.fill_(-1);
+  src_row.fill_(-1);   // rows past the last expert's padded block stay pad rows
   moe::plan_count_kernel<<<El, moe::kPlanThreads, 0, st>>>(idx.data_ptr<int>(), P, (int)lo, counts.data_ptr<int>());
   check_cuda(cudaGetLastError(), "moe plan count");
   moe::plan_assign_kernel<<<El, moe::kPlanThreads, 0, st>>>(

@@ -328,8 +328,8 @@ class GRPOTrainer:
         if mode == "always":
             return {"grads": self.trainer.heap is None, "opt": order,
                     "ref": self.ref_w is not None and self.ref_stream is None}
+        torch.cuda.empty_cache()                 # count only memory a fresh allocation can get
         free, _ = torch.cuda.mem_get_info(dev)
-        free += torch.cuda.memory_reserved(dev) - torch.cuda.memory_allocated(dev)
         kv = trajectories * transcript * self.rollout.kv_bytes_per_token()
         need = kv + 10e9 - free
         plan: Dict[str, object] = dict(none)

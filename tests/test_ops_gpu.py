@@ -50,10 +50,13 @@ def test_gemm_epilogues():
     assert ops.check_device_error() == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(8192, 7168, 512), (4000, 5120, 1024), (5120, 34816, 256)])
+@pytest.mark.parametrize("M,N,K", [(8192, 7168, 512), (4000, 5120, 1024), (5120, 34816, 256),
+                                   (1000, 9536, 512), (4200, 5120, 256)])
 @pytest.mark.parametrize("a_t,b_t", [(False, True), (False, False), (True, False), (True, True)])
 def test_gemm_pair_kernel(M, N, K, a_t, b_t):
-    """2-CTA (cta_group::2) kernel: every operand layout, ragged M."""
+    """2-CTA (cta_group::2) kernel: every operand layout, ragged M and N
+    (including last tiles where the second CTA's rows or columns lie wholly
+    past the matrix)."""
     C = ops.native()
     torch.manual_seed(5)
     A = (torch.randn(K, M) if a_t else torch.randn(M, K)).cuda().bfloat16()
