@@ -161,6 +161,7 @@ def grpo_main(args) -> None:
                     overlong_mask=False, total_steps=args.warmup + args.steps, kv_page_size=64,
                     reward_env="synthetic", seed=0, offload_state=args.offload)
     gc.comm = args.comm
+    gc.rollout_parallel = args.rollout_parallel
     env = SyntheticRewardEnv(seed=0, prompt_len=args.prompt_len, feedback_len=32, vocab_size=cfg.vocab_size)
     w = Qwen3Weights(cfg, device=ctx.device, dtype=torch.bfloat16, seed=0, pad_multiple=128 * max(1, W))
     tr = GRPOTrainer(gc, weights=w, env=env, ctx=ctx,
@@ -203,7 +204,8 @@ def grpo_main(args) -> None:
                        "trajectories_per_gpu": 8 * G, "prompt_len": args.prompt_len, "turns": args.turns,
                        "max_new_per_turn": args.gen_len, "feedback_tokens": 32,
                        "tokens_per_step": tokens, "gen_tokens_per_step_rank0": st["gen_tokens"],
-                       "parallelism": f"dp{W} replicated rollout" + (f", zero2-{args.comm}" if W > 1 else ""),
+                       "parallelism": (f"dp{W} replicated rollout" if W == 1 or args.rollout_parallel == "replica"
+                                       else f"tp{W} rollout") + (f", zero2-{args.comm}" if W > 1 else ""),
                        "clip": 0.2, "kl_beta": 0.01, "temperature": 1.0,
                        "offload": {"optimizer_state_gb_parked": st.get("offload_opt_gb"),
                                    "gradients_dropped_during_rollout": st.get("dropped_grads"),
@@ -314,6 +316,8 @@ def main(argv=None):
     ap.add_argument("--turns", type=int, default=3, help="grpo: turns per trajectory")
     ap.add_argument("--gen-len", type=int, default=2048, help="grpo: max sampled tokens per turn")
     ap.add_argument("--prompt-len", type=int, default=1024, help="grpo: prompt tokens")
+    ap.add_argument("--rollout-parallel", default="replica", choices=["replica", "tp"],
+                    help="grpo, several GPUs: each rank decodes its own rows, or heads split over ranks")
     ap.add_argument("--micro-tokens", type=int, default=8192, help="grpo: tokens per update micro-batch")
     ap.add_argument("--offload", default="auto", choices=["auto", "always", "never"],
                     help="grpo: park optimizer state / reference model in host memory between phases")

@@ -10,7 +10,8 @@
 //               max/sum in the log2 domain, P (bf16) written to shared memory
 //               in the 128B-swizzled K-major layout UMMA reads; O in TMEM is
 //               only rescaled when the running max grows by more than 2^8
-//               (lazy rescaling), then normalised in the epilogue.
+//               (lazy rescaling; only then does a softmax warp wait for the
+//               previous PV product), then normalised in the epilogue.
 // Backward (one CTA per (128-row key block, kv head)): loops over the query
 //   heads of the GQA group and the causal query blocks, recomputing
 //   S^T = K Q^T, P^T = exp(S^T - lse), dP^T = V dO^T, dS^T = P^T (dP^T - delta)
@@ -111,8 +112,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   uint64_t* v_empty = bars + 7;   // [kFwdStages]
   uint64_t* s_full = bars + 9;    // [2]
   uint64_t* p_full = bars + 11;   // [2]
-  uint64_t* o_done = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+  uint64_t* o_done = bars + 13;   // one phase per PV product
+  uint64_t* o_final = bars + 14;  // the last PV product
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   // ---- work item: longest (latest) query blocks first
@@ -141,6 +143,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&p_full[i], 4);
     }
     mbar_init(o_done, 1);
+    mbar_init(o_final, 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -208,6 +211,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         umma_commit(&v_empty[vs]);
         umma_commit(o_done);
       }
+      if (ok) umma_commit(o_final);
       if (!ok) *abort_flag = 1;
     }
     __syncwarp();
@@ -233,24 +237,36 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]) * p.scale_log2;
+          for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(r[c][i]);   // raw scores
       }
       const int kv0 = j * FBKV;
       const bool edge = (kv0 + FBKV > q0) || (kv0 + FBKV > len);
+      if (edge) {
+#pragma unroll
+        for (int i = 0; i < FBKV; ++i)
+          if (kv0 + i > qi || kv0 + i >= len) sv[i] = -INFINITY;
+      }
+      // row max of the raw scores (the log2 scale is positive, so it commutes)
       float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int i = 0; i < FBKV; ++i) {
-        if (edge && (kv0 + i > qi || kv0 + i >= len)) sv[i] = -INFINITY;
-        mx4[i & 3] = fmaxf(mx4[i & 3], sv[i]);
+      for (int i = 0; i < FBKV; i += 8) {
+        mx4[0] = fmax3f(mx4[0], sv[i], sv[i + 1]);
+        mx4[1] = fmax3f(mx4[1], sv[i + 2], sv[i + 3]);
+        mx4[2] = fmax3f(mx4[2], sv[i + 4], sv[i + 5]);
+        mx4[3] = fmax3f(mx4[3], sv[i + 6], sv[i + 7]);
       }
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * p.scale_log2;
       float m_new = fmaxf(m, mx);
       const bool need = (m == -INFINITY) ? true : (m_new > m + 8.f);
       if (j > 0) {
-        if (!mbar_wait(o_done, (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
+        // O is touched only when a row's max grew past the lazy threshold; only
+        // then wait for PV_{j-1}. Parity waits on o_done are unambiguous here:
+        // S_j's commit implies PV_{j-2} is done and PV_j is not yet issued, so
+        // o_done has completed j-1 or j phases.
         const float alpha = need ? exp2f(m - m_new) : 1.f;
         if (__any_sync(0xffffffff, need && m != -INFINITY)) {
+          if (!mbar_wait(o_done, (j - 1) & 1)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t r[32];
@@ -267,13 +283,24 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       if (need) m = m_new;
       const float mref = (m == -INFINITY) ? 0.f : m;
-      float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+      // p = 2^(s * scale_log2 - m): one packed FMA per two scores, packed row sums
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
+      const uint64_t nm2 = f2_pack(-mref, -mref);
+      uint64_t rs2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
-      for (int i = 0; i < FBKV; ++i) {
-        sv[i] = exp2f(sv[i] - mref);
-        rs4[i & 3] += sv[i];
+      for (int i = 0; i < FBKV; i += 2) {
+        float a, b;
+        f2_unpack(f2_fma(f2_pack(sv[i], sv[i + 1]), sc2, nm2), a, b);
+        sv[i] = exp2f(a);
+        sv[i + 1] = exp2f(b);
+        rs2[(i >> 1) & 1] = f2_add(rs2[(i >> 1) & 1], f2_pack(sv[i], sv[i + 1]));
       }
-      l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+      {
+        float a0, b0, a1, b1;
+        f2_unpack(rs2[0], a0, b0);
+        f2_unpack(rs2[1], a1, b1);
+        l += (a0 + b0) + (a1 + b1);
+      }
       {   // P_j as packed bf16 pairs over the first 32 columns of its S buffer
         uint32_t pk[32];
 #pragma unroll
@@ -285,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[st]);
     }
-    if (ok && mbar_wait(o_done, (nkv - 1) & 1)) {
+    if (ok && mbar_wait(o_final, 0)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool valid = qi < len;

@@ -652,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        mapa_shared(smem_u32(&tempty_bar[1]), 0)};
     int buf = 0, it = 0;
     const int CH = p.out_f32 ? 32 : 64;
-    for (int t = pair; t < num_tiles && !*abort_flag; t += npairs, ++it) {
+    for (int t = pair; t < num_tiles && !*abort_flag; t += npairs) {
       int tm, tn;
       tile_coords(t, num_m, num_n, tm, tn);
       const int m0 = tm * 2 * BM + (int)rank * BM;
