@@ -22,10 +22,12 @@ def run(x):
 def test_transform_sequence_and_budget():
     from kore_b200.transform.calculus import EpsBudget, apply_sequence
     from kore_b200.transform.library import LIBRARY, admissible, get_transform
-    names = [t.name for t in admissible(SRC)]
-    assert "block_x2" in names and "exp_to_exp2" in names and "warps_8" in names
-    out, applied = apply_sequence(SRC, [get_transform("block_x2"), get_transform("warps_8")])
-    assert "BLOCK=256" in out and "num_warps=8" in out and applied == ["block_x2", "warps_8"]
+    names = {a.transform.name for a in admissible(SRC)}
+    assert {"retile_block", "exp_to_exp2", "set_num_warps"} <= names
+    out, applied = apply_sequence(SRC, [get_transform("retile_block(f=x2,name=BLOCK)"),
+                                        get_transform("set_num_warps(n=8)")])
+    assert "BLOCK=256" in out and "num_warps=8" in out
+    assert applied == ["retile_block(f=x2,name=BLOCK)", "set_num_warps(n=8)"]
     b = EpsBudget(total=0.0)
     approx = [t for t in LIBRARY if t.kind == "approx"][0]
     assert not b.can_afford(approx)
