@@ -62,8 +62,16 @@ class FrozenLayerStream:
         self.copy_stream = torch.cuda.Stream(device=dev) if self.cuda else None
         self.bytes_moved = 0
 
+    def free_ring(self) -> None:
+        """Release the two device slots (the layers stay in their store)."""
+        self.slot = [None, None]
+        self.owner = [-1, -1]
+        self.ev = [None, None]
+
     def _fetch(self, u: int) -> None:
         k = u % 2
+        if self.slot[k] is None:
+            self.slot[k] = torch.empty(self.n, dtype=self.w.dtype, device=self.w.device)
         if self.owner[k] == u:
             return
         self.owner[k] = u

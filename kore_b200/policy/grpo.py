@@ -348,8 +348,17 @@ class GRPOTrainer:
                                f"dropped and the optimizer state parked in host memory")
         plan["opt"] = picked
         act = 16e9 if self.trainer.eng.keep_layers == 0 else 16e9 + 40e9
-        plan["ref"] = self.ref_w is not None and self.ref_stream is None and act > free
+        plan["ref"] = self.ref_w is not None and act > free
         return plan
+
+    def _ref_slots(self):
+        """Device tensors of the frozen reference that are parked for the update
+        (its resident units; a streamed reference also frees its layer ring,
+        which is refilled from its store on the next use)."""
+        from ..engine.offload import weight_slots
+        if self.ref_stream is not None:
+            self.ref_stream.free_ring()
+        return weight_slots(self.ref_w)
 
     def _slot_kind(self, slot) -> str:
         c, _ = slot
@@ -625,7 +634,7 @@ class GRPOTrainer:
         t_roll = time.time() - t0
         with pt.phase("offload"):
             if plan["ref"]:
-                self._ref_stash.park(weight_slots(self.ref_w))
+                self._ref_stash.park(self._ref_slots())
             if plan["opt"]:
                 self._opt_stash.restore(plan["opt"], self.ctx.device)
             if plan["grads"]:
@@ -637,7 +646,7 @@ class GRPOTrainer:
                 self.tp.shard.sync_from(self.w)      # in place: this rank's head / FFN slices
         if plan["ref"]:
             with pt.phase("offload"):
-                self._ref_stash.restore(weight_slots(self.ref_w), self.ctx.device)
+                self._ref_stash.restore(self._ref_slots(), self.ctx.device)
         self.step_idx += 1
         if self.curriculum is not None:
             self.curriculum.record([t for t, _ in traj_groups], [g for _, g in traj_groups])
