@@ -99,7 +99,8 @@ class SearchDistill:
         _, task, code = best
         kenv = tr.env._env(task)
         res = search_from_kernel(code, kenv, budget=cfg.search_budget, k_expand=cfg.search_k_expand,
-                                 max_depth=cfg.search_max_depth or 6, bnb=cfg.search_bnb)
+                                 max_depth=cfg.search_max_depth or 6, bnb=cfg.search_bnb,
+                                 task=getattr(kenv, "task", None))
         won = False
         if res.best_src and res.best_score:
             won = self.sink.add(str(task), res.best_src, float(res.best_score),
