@@ -35,21 +35,43 @@ from . import rl_math as M
 
 # ----------------------------------------------------------------------------- curriculum
 class CurriculumHook:
+    """Co-evolution curriculum in the GRPO loop: the controller picks the
+    step's tasks; per-task outcomes (solve rate, best verified speedup) are
+    gathered over ranks before the archive update, so every rank serves the
+    same tasks. Optional minting and competitor anchor from the config."""
+
     def __init__(self, trainer, space=None):
-        from ..openended.core import CurriculumController
+        import json
+
+        from ..openended.controller import CoevolutionController
+        from ..openended.proposer import Proposer
+        cfg = trainer.cfg
         self.tr = trainer
-        self.ctrl = CurriculumController(space=space, seed=trainer.cfg.seed)
+        comp = None
+        if getattr(cfg, "coevolve_regret_vs_opus", False) and getattr(cfg, "coevolve_opus_scores_path", None):
+            try:
+                with open(cfg.coevolve_opus_scores_path) as f:
+                    comp = json.load(f)
+            except (OSError, ValueError):
+                comp = None
+        self.ctrl = CoevolutionController(space=space, seed=cfg.seed, proposer=Proposer(competitor=comp),
+                                          batch=cfg.coevolve_batch or 8, ctx=trainer.ctx,
+                                          mint=bool(getattr(cfg, "coevolve_mint", False)),
+                                          mint_batch=int(getattr(cfg, "coevolve_mint_batch", 6)))
 
     def choose(self, fallback: Sequence[Any], k: int) -> List[Any]:
         picked = self.ctrl.next_task_id(k)
         return picked if picked else list(fallback)[:k]
 
     def record(self, tasks: Sequence[Any], groups) -> None:
+        out = []
         for task, trajs in zip(tasks, groups):
-            ok = any(r.correct for t in trajs for r in t.results)
-            speed = max((getattr(r.obs, "speedup", None) or 0.0 for t in trajs for r in t.results
+            res = [r for t in trajs for r in t.results]
+            rate = sum(1 for r in res if r.correct) / max(1, len(res))
+            speed = max((getattr(r.obs, "speedup", None) or 0.0 for r in res
                          if r.correct and r.obs is not None), default=0.0)
-            self.ctrl.record(str(task), ok, regret=max(0.0, 1.0 - speed) if ok else 1.0)
+            out.append((str(task), rate, speed if rate > 0 else None))
+        self.ctrl.record_batch(out)
 
 
 # ----------------------------------------------------------------------------- value prefilter

@@ -159,4 +159,5 @@ def test_minted_task_materializes(tmp_path):
     d = materialize(tid, str(tmp_path))
     from kore_b200.tasks.base import Task
     t = Task.from_dir(d)
-    assert t.task_id == tid and t.shape("primary").dims == {"M": 4096, "N": 4096}
+    from kore_b200.tasks.ops_library import SPECS
+    assert t.task_id == tid and t.shape("primary").dims == SPECS[tid].shapes["primary"]
