@@ -19,7 +19,7 @@ from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch
 
-from .adversarial import Genome, apply_regime, coevolve_tests
+from .adversarial import Genome, coevolve_tests
 
 
 class AdversarialRegistry:
@@ -44,7 +44,7 @@ class AdversarialRegistry:
             os.replace(tmp, self.path)
 
     def genomes(self, operation: str, dtype: str) -> List[Genome]:
-        return [Genome(d["regime"], d["scale"], d["sparsity"], d["seed"])
+        return [Genome(d["regime"], d["scale"], d["sparsity"], d["seed"], d.get("offset", 0.0), d.get("slot", -1))
                 for d in self.items.get(self.key(operation, dtype), [])]
 
 
@@ -67,7 +67,7 @@ class AdversarialHook:
                candidate: Callable, oracle: Callable) -> Tuple[bool, Optional[str]]:
         """Run the registry's genomes against a candidate: (passed, failing regime)."""
         for g in self.reg.genomes(operation, dtype):
-            ins = tuple(apply_regime(t, g.regime, g.scale, g.sparsity, g.seed) for t in make_inputs(g.seed))
+            ins = g.inputs(tuple(make_inputs(g.seed)))
             try:
                 if rel_err(candidate(*ins), oracle(*ins)) > self.tol:
                     return False, g.regime
