@@ -63,7 +63,10 @@ class FrozenLayerStream:
         self.bytes_moved = 0
 
     def free_ring(self) -> None:
-        """Release the two device slots (the layers stay in their store)."""
+        """Release the two device slots (the layers stay in their store); the
+        model's views into them are dropped too."""
+        for u in self.store:
+            self.w.bufs[u] = None
         self.slot = [None, None]
         self.owner = [-1, -1]
         self.ev = [None, None]

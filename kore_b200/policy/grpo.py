@@ -356,9 +356,11 @@ class GRPOTrainer:
         (its resident units; a streamed reference also frees its layer ring,
         which is refilled from its store on the next use)."""
         from ..engine.offload import weight_slots
+        slots = weight_slots(self.ref_w)
         if self.ref_stream is not None:
             self.ref_stream.free_ring()
-        return weight_slots(self.ref_w)
+            slots = [(c, k) for c, k in slots if not (c is self.ref_w.bufs and k in self.ref_stream.store)]
+        return slots
 
     def _slot_kind(self, slot) -> str:
         c, _ = slot
