@@ -142,8 +142,20 @@ def flops_bytes(operation: str, dims: Dict[str, int], dtype: str) -> Optional[Tu
         if ("cross_entropy" in op or "logprob" in op or "log_softmax" in op):
             M, N = dims["M"], dims["N"]
             return 6.0 * M * N, float(2 * M * N * e)
-        if "softmax" in op and "moe" not in op:
+        if op == "optimizer":
+            N = dims["N"]                    # param + grad in the dtype, fp32 moments read and written
+            return 12.0 * N, float(N * (3 * e + 16))
+        if op == "newton_schulz":
+            a, b = sorted((dims["M"], dims["N"]))
+            return 5 * (4.0 * a * a * b + 2.0 * a ** 3), float(2 * a * b * e)
+        if op == "loss_bwd":
             M, N = dims["M"], dims["N"]
+            return 8.0 * M * N, float(2 * M * N * e)
+        if op == "linear_attention":
+            B, H, L, K = dims["B"], dims["H"], dims["L"], dims["K"]
+            return 4.0 * B * H * L * K * K, float(5 * B * H * L * K * e)
+        if "softmax" in op and "moe" not in op:
+            M, N = dims["M"], get("N", "V")
             return 5.0 * M * N, float(2 * M * N * e)
         if "rope" in op:
             S, B, H, D = dims["S"], get("B", default=1), dims["H"], dims["D"]
