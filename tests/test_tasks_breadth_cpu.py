@@ -11,7 +11,7 @@ BREADTH = sorted(n for n in SPECS if n.startswith("genb_"))
 
 
 def test_breadth_size_and_split():
-    assert len(BREADTH) >= 450
+    assert len(BREADTH) >= 900
     tr, ho = split_tasks()
     assert not set(tr) & set(ho)
     assert any("genb_quant_" in h for h in ho) and any("_sliding" in h for h in ho)
