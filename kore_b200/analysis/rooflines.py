@@ -158,12 +158,15 @@ def flops_bytes(operation: str, dims: Dict[str, int], dtype: str) -> Optional[Tu
             M, N = dims["M"], get("N", "V")
             return 5.0 * M * N, float(2 * M * N * e)
         if "rope" in op:
-            S, B, H, D = dims["S"], get("B", default=1), dims["H"], dims["D"]
+            S, B, H, D = get("S", "T"), get("B", default=1), dims["H"], dims["D"]
             n = S * B * H * D
             return 6.0 * n, float(2 * n * e + S * D * e)
         if "quant" in op:
             M, N = dims["M"], dims["N"]
             return 2.0 * M * N, float(M * N * 3 + M * 4)
+        if op == "moe_sum_combine":            # weighted sum of the top-k expert rows per token
+            M, D, k = dims["M"], dims["D"], get("topk", "k", default=8)
+            return 2.0 * M * k * D, float((M * k * D + M * D) * e + M * k * 8)
         if op in ("moe_permute", "moe_combine"):
             M, D, k = dims["M"], dims["D"], get("K", "topk", default=1)
             moved = M * k * D

@@ -124,6 +124,7 @@ def build_parser() -> argparse.ArgumentParser:
     sub.add_parser("eval", help="evaluation suite")
     sub.add_parser("campaign", help="staged campaign with a resumable manifest")
     sub.add_parser("supervise", help="relaunch-with-resume supervisor / monitor")
+    sub.add_parser("proof", help="smokes and proofs (env, sft, grpo, breadth, ops, grpo-repro)")
     return ap
 
 
@@ -137,6 +138,7 @@ def main(argv: Optional[List[str]] = None) -> int:
             "soup": lambda: cmd_soup(args), "bench": lambda: cmd_bench(args, rest),
             "datagen": lambda: cmd_datagen(args, rest), "build-datasets": lambda: cmd_build(args, rest),
             "value-train": lambda: cmd_value(args, rest), "eval": lambda: cmd_eval(args, rest),
+            "proof": lambda: __import__("kore_b200.proofs", fromlist=["main"]).main(rest),
             "campaign": lambda: __import__("kore_b200.campaign.orchestrator", fromlist=["main"]).main(rest),
             "supervise": lambda: __import__("kore_b200.campaign.supervise", fromlist=["main"]).main(rest)}[args.cmd]()
 
