@@ -627,13 +627,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       // P and dS overwrite the raw registers in place (no extra live arrays)
       float* pv = reinterpret_cast<float*>(rs);
       float* dv = reinterpret_cast<float*>(rp);
+      // P^T = 2^(S^T scale_log2 - lse2), dS^T = P^T (dP^T - delta): packed pairs
+      const uint64_t sc2 = f2_pack(p.scale_log2, p.scale_log2);
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
+      for (int e = 0; e < 32; e += 2) {
         const int qc = half * 32 + e;
-        float pr = exp2f(__uint_as_float(rs[e]) * p.scale_log2 - lse2[e]);
-        if ((diag && q0 + qc < kvi) || kvi >= len) pr = 0.f;
-        dv[e] = pr * (__uint_as_float(rp[e]) - dlt[e]);
-        pv[e] = pr;
+        float a0, a1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(rs[e]), __uint_as_float(rs[e + 1])), sc2,
+                         f2_pack(-lse2[e], -lse2[e + 1])), a0, a1);
+        float pr0 = exp2f(a0), pr1 = exp2f(a1);
+        if ((diag && q0 + qc < kvi) || kvi >= len) pr0 = 0.f;
+        if ((diag && q0 + qc + 1 < kvi) || kvi >= len) pr1 = 0.f;
+        const uint64_t pp = f2_pack(pr0, pr1);
+        f2_unpack(f2_mul(pp, f2_add(f2_pack(__uint_as_float(rp[e]), __uint_as_float(rp[e + 1])),
+                                    f2_pack(-dlt[e], -dlt[e + 1]))), dv[e], dv[e + 1]);
+        pv[e] = pr0;
+        pv[e + 1] = pr1;
       }
       store_row32_sw128(smem + S::PT_OFF + st * PTILE_BYTES, row, half, pv);
       store_row32_sw128(smem + S::DS_OFF + st * PTILE_BYTES, row, half, dv);

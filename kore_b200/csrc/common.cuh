@@ -3,7 +3,7 @@
 // Everything here is hand-written inline PTX for Blackwell (sm_100a):
 //   * mbarrier init / arrive / bounded try_wait (every wait has a time limit and
 //     records an error code instead of spinning forever),
-//   * TMA tiled loads/stores (cp.async.bulk.tensor, never with .multicast::cluster),
+//   * TMA tiled loads/stores (cp.async.bulk.tensor; no load uses cluster multicast),
 //   * tcgen05 TMEM alloc/dealloc, MMA issue, commit, and TMEM->register loads,
 //   * UMMA shared-memory and instruction descriptors.
 #pragma once
@@ -357,6 +357,11 @@ KORE_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 KORE_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+KORE_DEV uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
 KORE_DEV float fmax3f(float a, float b, float c) {
