@@ -405,9 +405,31 @@ class Qwen3Engine:
         return x
 
     @torch.no_grad()
+    def token_logprobs_many(self, batches: List[Batch], want_entropy: bool = False):
+        """``token_logprobs`` of several micro-batches, layer-major: each
+        decoder layer is acquired once and applied to every batch's hidden
+        states before the next layer. With a parameter provider that streams
+        layers from host memory or gathers them over ranks, the weights then
+        move once per call instead of once per micro-batch (the hidden states
+        of all batches stay resident)."""
+        xs = [ops.embed_fwd(b.ids, self.w.views(0)["embed"]) for b in batches]
+        hook = self.param_hook
+        last = self.w.num_units - 2
+        for u in range(1, self.w.num_units - 1):
+            if hook is not None:
+                hook.acquire(u, u + 1 if u < last else None)
+            for i, b in enumerate(batches):
+                xs[i], _ = self._layer_fwd(u, xs[i], b, keep=False)
+            if hook is not None and hasattr(hook, "release"):
+                hook.release(u)
+        return [self._logprobs_from_hidden(x, b, want_entropy) for x, b in zip(xs, batches)]
+
+    @torch.no_grad()
     def token_logprobs(self, b: Batch, want_entropy: bool = False):
         """Per-token log p(target) (0 where target == -1), optional entropy."""
-        x = self.forward_hidden(b)
+        return self._logprobs_from_hidden(self.forward_hidden(b), b, want_entropy)
+
+    def _logprobs_from_hidden(self, x: torch.Tensor, b: Batch, want_entropy: bool):
         Wn = self.w.views(self.w.num_units - 1)["norm"]
         hn = ops.rmsnorm_fwd(x, Wn, self.eps)
         rows = torch.nonzero(b.targets >= 0).reshape(-1)

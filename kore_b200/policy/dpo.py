@@ -180,12 +180,18 @@ class DPOTrainer:
         eng = self.tr.eng
         eng.zero_grad()
         total = 0.0
-        for s0 in range(0, len(pairs), self.micro_pairs):
+        starts = list(range(0, len(pairs), self.micro_pairs))
+        batches = [self._batch([x for p in pairs[s0:s0 + self.micro_pairs] for x in p]) for s0 in starts]
+        if getattr(self, "_ref_stream", None) is not None:
+            # streamed / gathered reference: each layer moves once for the whole step
+            ref_lps = [lp for lp, _ in self.ref.token_logprobs_many(batches)]
+        else:
+            ref_lps = [None] * len(batches)
+        for s0, b, lp_pre in zip(starts, batches, ref_lps):
             chunk = pairs[s0:s0 + self.micro_pairs]
             items = [x for p in chunk for x in p]
-            b = self._batch(items)
             seg, wt = self._token_weights(b, items)
-            lp_ref, _ = self.ref.token_logprobs(b)
+            lp_ref = lp_pre if lp_pre is not None else self.ref.token_logprobs(b)[0]
             n = len(items)
             ref_sums = torch.zeros(n, dtype=torch.float64, device=lp_ref.device)
             ref_sums.index_add_(0, seg.clamp_min(0), torch.where(seg >= 0, (lp_ref * wt).double(),

@@ -503,9 +503,13 @@ class GRPOTrainer:
     def fill_ref_logps(self, samples: List[TrainSample], budget: int):
         if self.ref_eng is None:
             return
-        for chunk in self._pack(self._rows(samples), budget):
-            b, flat, seg = self._batch(chunk)
-            lp, _ = self.ref_eng.token_logprobs(b)
+        chunks = [self._batch(c) for c in self._pack(self._rows(samples), budget)]
+        if self.ref_stream is not None:
+            # streamed / gathered reference: every layer moves once for the whole step
+            lps = [lp for lp, _ in self.ref_eng.token_logprobs_many([b for b, _, _ in chunks])]
+        else:
+            lps = [self.ref_eng.token_logprobs(b)[0] for b, _, _ in chunks]
+        for (b, flat, seg), lp in zip(chunks, lps):
             for s, v in zip(flat, self._sample_means(lp, seg, flat)):
                 s.ref_logp = v
 

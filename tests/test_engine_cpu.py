@@ -151,3 +151,21 @@ def test_tp_shard_sync_in_place():
         for a, b in zip(sh.layers, fresh.layers):
             for k in a:
                 assert torch.equal(a[k], b[k]), k
+
+
+def test_token_logprobs_many_layer_major_matches():
+    """Layer-major scoring of several batches (one pass of the weights, here
+    streamed through a two-slot ring) equals per-batch scoring."""
+    from kore_b200.engine.frozen_stream import FrozenLayerStream
+    cfg, w, b1 = _setup(3)
+    _, _, b2 = _setup(4)
+    eng = Qwen3Engine(w, allocate_grads=False)
+    want = [eng.token_logprobs(b)[0] for b in (b1, b2)]
+    ref = Qwen3Weights(cfg, device="cpu", dtype=torch.float32, allocate=False)
+    ref.bufs = [w.bufs[u].clone() if u in (0, w.num_units - 1) else None for u in range(w.num_units)]
+    stream = FrozenLayerStream(ref, source="host", layers_from=w)
+    reng = Qwen3Engine(ref, allocate_grads=False)
+    reng.param_hook = stream
+    got = [lp for lp, _ in reng.token_logprobs_many([b1, b2])]
+    for a, b in zip(got, want):
+        assert torch.allclose(a, b, atol=1e-5)
