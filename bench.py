@@ -127,6 +127,16 @@ def reference_arm(args) -> None:
     ra.run(args, ClockSampler)
 
 
+def _recompute_note(trainer, cfg) -> str:
+    L = cfg.num_hidden_layers
+    sh = getattr(trainer, "_shuttle", None)
+    if sh is not None and sh.keep_mid is not None:
+        return (f"second moments in pinned host memory during micro-batches 2..{sh.n - 1} (copied out and back on "
+                f"a side stream, overlapped with the first and last micro-batch); those micro-batches keep "
+                f"{sh.keep_mid} of {L} layer contexts, the first and last recompute all {L}")
+    return f"{L - trainer.eng.keep_layers} of {L} layers recompute their GEMMs"
+
+
 def grpo_main(args) -> None:
     """GRPO-step tokens/s (BASELINE GRPO row): multi-turn rollout + reference
     log-probs + update + weight sync, one optimizer step per GRPO step.
@@ -438,8 +448,7 @@ def main(argv=None):
                            (f"-zero2-{args.comm}" if args.zero == 2 else "-zero3-nccl") if ctx.world > 1 else ""),
                        "loss": "last 50% of each sequence", "micro_batch": args.micro_batch,
                        "optimizer": f"AdamW fp32 moments, master={trainer.master_mode}",
-                       "activation_recompute": f"{cfg.num_hidden_layers - trainer.eng.keep_layers} of "
-                                               f"{cfg.num_hidden_layers} layers recompute their GEMMs",
+                       "activation_recompute": _recompute_note(trainer, cfg),
                        "l2": "inputs larger than L2 (29.5 GB of weights streamed per step)"},
             "loss": loss_v, "clocks": clocks, "gpu_launches": launches, "e2e": e2e, "memory": memory,
             "impl": "kore",

@@ -43,7 +43,7 @@ class CausalLMTrainer:
                  warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
                  weights: Optional[Qwen3Weights] = None, micro_tokens_hint: int = 8192,
                  ep_capacity: float = 2.0, zero_stage: int = 2, recompute: str = "auto",
-                 activation_reserve_gb: float = 12.0):
+                 activation_reserve_gb: float = 12.0, moment_offload: str = "auto"):
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device
@@ -122,8 +122,25 @@ class CausalLMTrainer:
         if recompute not in ("auto", "full", "none"):
             raise ValueError("recompute must be auto|full|none")
         self.recompute = recompute
+        self.moment_offload = moment_offload
         self.reserve_bytes = int(activation_reserve_gb * 1e9)
         self._planned_tokens = None
+
+    def _moment_shuttle(self, n_micro: int, micro_tokens: int):
+        """On one GPU where the weights, gradients and fp32 moments leave no
+        room to keep layer contexts, move the second moments to pinned host
+        memory for the middle of the step (see :class:`MomentShuttle`)."""
+        if self.moment_offload == "never" or self.ctx.world > 1 or self.ctx.device.type != "cuda":
+            return None
+        if not isinstance(self.opt, AdamW) or self.recompute != "auto" or self.cfg.is_moe or n_micro < 3:
+            return None
+        L = self.cfg.num_hidden_layers
+        if self.moment_offload == "auto" and self.eng.keep_layers >= L:
+            return None
+        if getattr(self, "_shuttle", None) is None:
+            self._shuttle = MomentShuttle(self, micro_tokens)
+        self._shuttle.start(n_micro)
+        return self._shuttle
 
     def plan_activations(self, micro_tokens: int) -> int:
         """Choose how many decoder layers keep their whole forward context
@@ -169,12 +186,18 @@ class CausalLMTrainer:
         self.ctx.all_reduce(self._count)
         self.eng.zero_grad()
         loss = torch.zeros((), dtype=torch.float32, device=ids.device)
-        for s in range(0, B, self.mbs):
+        starts = list(range(0, B, self.mbs))
+        shuttle = self._moment_shuttle(len(starts), min(self.mbs, B) * S)
+        for i, s in enumerate(starts):
+            if shuttle is not None:
+                shuttle.before(i)
             b = Batch.from_dense(ids[s:s + self.mbs], None if loss_mask is None
                                  else loss_mask[s:s + self.mbs])
             coef = torch.where(b.targets >= 0, -1.0 / self._count, torch.zeros((), device=ids.device))
             out = self.eng.forward_backward(b, coef=coef)
             loss += out["loss"]
+        if shuttle is not None:
+            shuttle.finish()
         self.opt.step()
         self.ctx.all_reduce(loss)
         return loss
@@ -260,3 +283,72 @@ class CausalLMTrainer:
         if hasattr(self.eng.ep, "check_overflow"):
             self.eng.ep.check_overflow()          # one flag read per step (the step synchronised already)
         return loss
+
+
+class MomentShuttle:
+    """Second moments out of HBM for the middle micro-batches of a step.
+
+    A 14B model on one GPU holds bf16 weights and gradients and fp32 moments
+    (177 GB), so every layer recomputes its forward GEMMs in the backward. The
+    shuttle copies the second moments (59 GB) to pinned host memory on a side
+    stream while the first micro-batch runs, lets the middle micro-batches keep
+    their whole layer contexts in the freed HBM (no recompute), and copies the
+    moments back on the side stream while the last micro-batch runs with
+    recompute, so neither copy is on the critical path. The optimizer step
+    waits for the copy back."""
+
+    def __init__(self, trainer: "CausalLMTrainer", micro_tokens: int):
+        self.tr = trainer
+        self.stream = torch.cuda.Stream(device=trainer.ctx.device)
+        self.keys = sorted(trainer.opt.v)
+        self.host = {}
+        self.micro_tokens = micro_tokens
+        self.ev = None
+        self.n = 0
+        self.keep_mid = None
+        for k in self.keys:
+            t = trainer.opt.v[k]
+            try:
+                self.host[k] = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+            except RuntimeError:             # page-locking refused: pageable copies still work
+                self.host[k] = torch.empty(t.shape, dtype=t.dtype)
+
+    def start(self, n_micro: int) -> None:
+        self.n = n_micro
+        opt = self.tr.opt
+        main = torch.cuda.current_stream()
+        self.stream.wait_stream(main)                    # v is final after the previous step
+        with torch.cuda.stream(self.stream):
+            for k in self.keys:
+                t = opt.v[k]
+                self.host[k].copy_(t, non_blocking=True)
+                t.record_stream(self.stream)
+                opt.v[k] = None
+            self.ev = torch.cuda.Event()
+            self.ev.record()
+        self.tr.eng.keep_layers = 0
+
+    def before(self, i: int) -> None:
+        eng = self.tr.eng
+        if i == 1:
+            self.ev.synchronize()                        # the moments have left HBM
+            if self.keep_mid is None:
+                torch.cuda.empty_cache()
+                self.tr.plan_activations(self.micro_tokens)
+                self.keep_mid = eng.keep_layers
+            eng.keep_layers = self.keep_mid
+        elif i == self.n - 1:
+            eng.keep_layers = 0                          # room for the moments coming back
+            main = torch.cuda.current_stream()
+            opt = self.tr.opt
+            for k in self.keys:
+                opt.v[k] = torch.empty(self.host[k].shape, dtype=self.host[k].dtype, device=self.tr.ctx.device)
+            self.stream.wait_stream(main)
+            with torch.cuda.stream(self.stream):
+                for k in self.keys:
+                    opt.v[k].copy_(self.host[k], non_blocking=True)
+                self.ev = torch.cuda.Event()
+                self.ev.record()
+
+    def finish(self) -> None:
+        torch.cuda.current_stream().wait_event(self.ev)

@@ -38,3 +38,29 @@ def test_engine_gpu_grads_vs_fp32_reference():
 def test_smoke():
     out = run_smoke("cuda:0")
     assert out["loss_after"] < out["loss_before"]
+
+
+def test_moment_shuttle_matches_plain_step():
+    """Second moments parked in host memory for the middle micro-batches (those
+    keep their layer contexts) give the same parameters as the plain step."""
+    from kore_b200.engine.smoke import smoke_config
+    from kore_b200.engine.trainer import CausalLMTrainer
+    from kore_b200.ops import check_device_error
+    from kore_b200.parallel.dist import DistContext
+    cfg = smoke_config()
+    ctx = DistContext(device=torch.device("cuda"))
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, cfg.vocab_size, (4, 256), generator=g).cuda()
+    res = {}
+    for mode in ("never", "always"):
+        tr = CausalLMTrainer(cfg, ctx, lr=1e-3, seed=0, moment_offload=mode)
+        losses = [float(tr.train_step_device(ids)) for _ in range(2)]
+        res[mode] = (losses, [b.float().clone() for b in tr.w.bufs], [v.clone() for v in tr.opt.v.values()])
+        if mode == "always":
+            assert tr._shuttle is not None and tr._shuttle.keep_mid == cfg.num_hidden_layers
+    assert check_device_error() == 0
+    assert all(abs(a - b) < 1e-3 for a, b in zip(res["never"][0], res["always"][0]))
+    for a, b in zip(res["never"][1], res["always"][1]):
+        assert torch.allclose(a, b, atol=1e-3, rtol=0)
+    for a, b in zip(res["never"][2], res["always"][2]):
+        assert torch.allclose(a, b, rtol=1e-3, atol=1e-12)
