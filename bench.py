@@ -366,7 +366,7 @@ def main(argv=None):
     ops.native()  # fail loudly if the extension is missing
     trainer = CausalLMTrainer(cfg, ctx, lr=1e-5, max_grad_norm=1.0, seed=0,
                               micro_batch_size=args.micro_batch,
-                              comm=args.comm if args.zero == 2 else "nccl", zero_stage=args.zero,
+                              comm=args.comm, zero_stage=args.zero,
                               recompute=args.recompute)
     B, S = args.seqs_per_gpu, args.seq
     g = torch.Generator().manual_seed(1234 + ctx.rank)
@@ -445,7 +445,9 @@ def main(argv=None):
                        "layers": cfg.num_hidden_layers,
                        "global_batch": B * ctx.world, "seq_len": S,
                        "parallelism": f"dp{ctx.world}" + (
-                           (f"-zero2-{args.comm}" if args.zero == 2 else "-zero3-nccl") if ctx.world > 1 else ""),
+                           (f"-zero2-{args.comm}" if args.zero == 2 else
+                            ("-zero3-copy-engine-gathers" if args.comm == "fused" else "-zero3-nccl"))
+                           if ctx.world > 1 else ""),
                        "loss": "last 50% of each sequence", "micro_batch": args.micro_batch,
                        "optimizer": f"AdamW fp32 moments, master={trainer.master_mode}",
                        "activation_recompute": _recompute_note(trainer, cfg),

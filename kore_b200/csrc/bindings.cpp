@@ -98,6 +98,7 @@ void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<in
 void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x, const c10::optional<at::Tensor>& g,
                     const c10::optional<at::Tensor>& hn, double eps);
 std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset);
+void symm_gather_ce(int64_t id, int64_t src_offset, int64_t bytes, at::Tensor& dst);
 int64_t device_wait_flag(const at::Tensor& flag, int64_t want, double timeout_s);
 int read_and_clear_device_error();
 }  // namespace kore
@@ -155,5 +156,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("flags") = py::none(), py::arg("epoch") = 0);
   m.def("tp_reduce_norm", &kore::tp_reduce_norm);
   m.def("symm_peer_addrs", &kore::symm_peer_addrs);
+  m.def("symm_gather_ce", &kore::symm_gather_ce, "all-gather of heap shards on the copy engines");
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

@@ -600,6 +600,27 @@ std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset) {
   return out;
 }
 
+// All-gather on the copy engines: for every rank p, ``bytes`` from peer p's
+// heap at ``src_offset`` into ``dst`` at p * bytes, one cudaMemcpyAsync per
+// rank on the current stream (NVLink peer copies, no SM time). The caller
+// orders the copies after the peers wrote their shards (a device barrier or a
+// collective) and before the peers overwrite them.
+void symm_gather_ce(int64_t id, int64_t src_offset, int64_t bytes, at::Tensor& dst) {
+  auto& h = *g_heaps.at(id);
+  TORCH_CHECK(dst.is_cuda() && dst.is_contiguous(), "gather dst must be contiguous CUDA");
+  TORCH_CHECK((int64_t)dst.numel() * dst.element_size() >= bytes * h.world, "gather dst too small");
+  TORCH_CHECK(src_offset >= 0 && (size_t)(src_offset + bytes) <= h.bytes, "gather source outside the heap");
+  c10::cuda::CUDAGuard g(dst.device());
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  uint8_t* out = reinterpret_cast<uint8_t*>(dst.data_ptr());
+  for (int p = 0; p < h.world; ++p) {
+    // start with this rank's own shard: the local copy finishes while the peers' stream in
+    const int q = (h.rank + p) % h.world;
+    check_cuda(cudaMemcpyAsync(out + (size_t)q * bytes, h.peers[q] + src_offset, bytes, cudaMemcpyDeviceToDevice, st),
+               "symm gather copy");
+  }
+}
+
 }  // namespace kore
 
 // ============================================================== bounded flag wait (health check)

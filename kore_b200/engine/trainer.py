@@ -52,8 +52,9 @@ class CausalLMTrainer:
         ep = (self.ctx.rank, self.ctx.world) if (cfg.is_moe and self.ctx.world > 1) else None
         fused = comm == "fused" and self.ctx.world > 1 and dev.type == "cuda"
         self.zero_stage = zero_stage if self.ctx.world > 1 else 0
-        if self.zero_stage == 3 and fused:
-            raise ValueError("zero_stage=3 runs on NCCL collectives (comm='nccl')")
+        gather_ce = fused and self.zero_stage == 3     # ZeRO-3: layer gathers on the copy engines
+        if gather_ce:
+            fused = False
         if fused:
             from ..parallel.symmetric import SymmetricHeap
             per = 128 * self.ctx.world
@@ -97,7 +98,7 @@ class CausalLMTrainer:
                                          total_steps=total_steps, seed=seed)
         elif self.zero_stage == 3:
             from ..parallel.fsdp import FullShard, FullShardAdamW
-            self.fs = FullShard(self.w, self.eng, self.ctx)
+            self.fs = FullShard(self.w, self.eng, self.ctx, peer_gather=gather_ce)
             self.eng.param_hook = self.fs
             self.opt = FullShardAdamW(self.w, self.eng, self.ctx, self.fs, lr=lr, betas=betas,
                                       weight_decay=weight_decay, max_grad_norm=max_grad_norm,

@@ -14,6 +14,13 @@ buffers; layer gradients likewise in a ring of two full buffers:
 The embedding and head units (a vocabulary-sized matrix each) stay resident
 and use the ZeRO-2 step (reduce-scatter, sharded AdamW, all-gather).
 
+With ``peer_gather`` (the trainer's ``comm="fused"`` at ZeRO-3) the layer
+shards live in a symmetric peer-memory heap and each gather is one
+``cudaMemcpyAsync`` per rank on the comm stream: NVLink peer reads executed by
+the copy engines, so the gathers take no SM time from the GEMMs they overlap
+and need no NCCL kernel. Device barriers before and after the optimizer step
+order every rank's shard update against the other ranks' reads.
+
 Why gather into HBM rather than fusing the gather into the consuming GEMM:
 a weight tile is read by every M tile of the GEMM (T/128 times per pass,
 three passes per layer with recompute), so streaming it from a peer inside
@@ -40,7 +47,7 @@ from .zero import ShardedAdamW
 class FullShard:
     """Parameter / gradient provider hooked into :class:`Qwen3Engine`."""
 
-    def __init__(self, weights, engine, ctx: DistContext):
+    def __init__(self, weights, engine, ctx: DistContext, peer_gather: bool = False):
         self.w, self.eng, self.ctx = weights, engine, ctx
         W, r = ctx.world, ctx.rank
         self.units = list(range(1, weights.num_units - 1))
@@ -55,8 +62,18 @@ class FullShard:
         self.cuda = dev.type == "cuda" and ctx.backend == "nccl"
         self.pshard: Dict[int, torch.Tensor] = {}
         self.gshard: Dict[int, torch.Tensor] = {}
+        self.heap, self.poff = None, {}
+        if peer_gather and self.cuda:
+            from .symmetric import SymmetricHeap
+            esz = torch.empty((), dtype=weights.dtype).element_size()
+            self.heap = SymmetricHeap(ctx, len(self.units) * (self.s * esz + 256))
         for u in self.units:
-            self.pshard[u] = weights.bufs[u][r * self.s:(r + 1) * self.s].clone()
+            src = weights.bufs[u][r * self.s:(r + 1) * self.s]
+            if self.heap is not None:
+                self.poff[u], self.pshard[u] = self.heap.alloc(self.s, weights.dtype)
+                self.pshard[u].copy_(src)
+            else:
+                self.pshard[u] = src.clone()
             self.gshard[u] = torch.zeros(self.s, dtype=engine.grad_dtype, device=dev)
             weights.bufs[u] = None                     # drop the full copy
             engine.grads[u] = None
@@ -86,10 +103,20 @@ class FullShard:
         free.record()                                  # compute that last read this slot is enqueued
         with torch.cuda.stream(self.comm):
             self.comm.wait_event(free)
-            dist.all_gather_into_tensor(self.pslot[k], self.pshard[u], group=self.ctx.group)
+            if self.heap is not None:        # copy-engine peer reads: no SMs, no NCCL kernel
+                ops.native().symm_gather_ce(self.heap.id, self.poff[u], self.s * self.pshard[u].element_size(),
+                                            self.pslot[k])
+            else:
+                dist.all_gather_into_tensor(self.pslot[k], self.pshard[u], group=self.ctx.group)
             ev = torch.cuda.Event()
             ev.record()
         self.gather_ev[k] = ev
+
+    def sync_shards(self) -> None:
+        """Device barrier over the ranks (peer-gather mode): orders every
+        rank's shard update against the other ranks' next reads of it."""
+        if self.heap is not None:
+            self.heap.barrier()
 
     def acquire(self, u: int, nxt: Optional[int] = None) -> None:
         if u not in self.pshard:
@@ -189,6 +216,7 @@ class FullShardAdamW(ShardedAdamW):
     def step(self, grad_scale: float = 1.0, scattered: bool = False) -> None:
         fs, r = self.fs, self.ctx.rank
         fs.finish()
+        fs.sync_shards()                               # every rank's last gather of this step is done
         resident = [u for u in range(self.w.num_units) if u not in fs.pshard]
         for u in resident:
             self.reduce_scatter_unit(u)
@@ -217,4 +245,5 @@ class FullShardAdamW(ShardedAdamW):
             if u not in fs.pshard:
                 self.all_gather_unit(u)
         fs.owner = [-1, -1]                            # gathered copies are stale now
+        fs.sync_shards()                               # shards updated everywhere before the next gathers
         fs.zero_grad()

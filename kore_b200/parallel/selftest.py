@@ -5,7 +5,8 @@
 Checks: (1) three ZeRO-2 steps with NCCL collectives and with the fused
 peer-memory optimizer give the same parameters (bf16 tolerance) and the
 replicas stay bit-identical across ranks; (2) ZeRO-3 matches ZeRO-2 in loss
-and final parameters; (3) expert parallelism over NCCL all-to-all and over
+and final parameters, and ZeRO-3 with copy-engine peer gathers matches ZeRO-3
+over NCCL; (3) expert parallelism over NCCL all-to-all and over
 the fused peer-memory dispatch/combine agree; (4) the tensor-parallel rollout
 engine's sampled log-probs match an fp32 single-GPU reference forward that
 scores the same tokens (teacher forcing); (5) a GRPO step runs with the TP
@@ -65,11 +66,27 @@ def main(argv=None):
     z3ok = all(abs(a - b) < 2e-2 * max(1.0, abs(a)) for a, b in zip(res["nccl"][0], l3))
     for a, b in zip(res["nccl"][1], full.bufs):
         z3ok = z3ok and torch.allclose(a, b.float(), atol=2e-2, rtol=0)
+    z3_params = [b.float().clone() for b in full.bufs]
     del tr, full
     if ctx.is_main:
         print(json.dumps({"check": "zero3_vs_zero2", "world": ctx.world, "ok": z3ok, "loss_zero2": res["nccl"][0],
                           "loss_zero3": l3}), flush=True)
     ok = ok and z3ok
+    # ZeRO-3 with the layer gathers on the copy engines (peer reads of the symmetric heap)
+    tr = CausalLMTrainer(cfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm="fused", master="fp32",
+                         zero_stage=3, micro_batch_size=1)
+    l3f = [float(tr.train_step_device(mine)) for _ in range(3)]
+    full = tr.full_weights()
+    torch.cuda.synchronize()
+    z3f = all(abs(a - b) < 1e-3 * max(1.0, abs(a)) for a, b in zip(l3, l3f))
+    for a, b in zip(z3_params, full.bufs):
+        z3f = z3f and torch.allclose(a, b.float(), atol=1e-3, rtol=0)
+    errz = check_device_error()
+    del tr, full
+    if ctx.is_main:
+        print(json.dumps({"check": "zero3_copy_engine_gather_vs_nccl", "world": ctx.world, "ok": z3f and errz == 0,
+                          "loss_nccl": l3, "loss_ce_gather": l3f, "device_error": errz}), flush=True)
+    ok = ok and z3f and errz == 0
     # expert parallelism: NCCL all-to-all vs fused peer-memory dispatch/combine
     mcfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
                        num_attention_heads=4, num_key_value_heads=2, head_dim=128, model_type="qwen3_moe",
