@@ -192,8 +192,8 @@ class Qwen3Engine:
         if self.w.layouts[u].kind == "moe_layer":
             x3, mctx = self._moe_fwd(W, hn2, x2)
             if keep:
-                ctx = dict(rstd1=rstd1, hn=hn, qkv=qkv, qk=qk, o=o, lse=lse, x2=x2, rstd2=rstd2,
-                           hn2=hn2, **mctx)
+                ctx = dict(rstd1=rstd1, hn=hn, qkv=qkv, qk=qk, o=o, lse=lse, x2=x2, rstd2=rstd2, hn2=hn2)
+                ctx.update(mctx)             # the expert-parallel context may carry its own hn2
             return x3, ctx
         gu = self._mm(hn2, W["gate_up"])
         a = ops.swiglu_fwd(gu)

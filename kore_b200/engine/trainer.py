@@ -73,6 +73,11 @@ class CausalLMTrainer:
                     a[: b.numel()].copy_(b[: a.numel()])
                 for u, b in weights.expert_bufs.items():
                     nw.expert_bufs[u].copy_(b)
+                # ownership moves into the heap: release the source buffers now
+                # (the caller may still hold the old object)
+                weights.bufs = [None] * len(weights.bufs)
+                weights.expert_bufs = {}
+                torch.cuda.empty_cache()
                 weights = nw
         self.w = weights or Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed,
                                          pad_multiple=128 * max(1, self.ctx.world), ep=ep)

@@ -331,6 +331,12 @@ class GRPOTrainer:
         torch.cuda.empty_cache()                 # count only memory a fresh allocation can get
         free, _ = torch.cuda.mem_get_info(dev)
         kv = trajectories * transcript * self.rollout.kv_bytes_per_token()
+        if self._use_tp() and getattr(self, "tp", None) is None:
+            # the tensor-parallel engine is built at the first rollout: its head /
+            # FFN slice of every layer and its peer-memory buffers
+            W, H = self.ctx.world, self.w.cfg.hidden_size
+            layers = sum(self.w.padded_numel(u) for u in range(1, self.w.num_units - 1))
+            kv += layers * 2 // W + 4096 * H * 2 * (1 + 2 * W)
         need = kv + 10e9 - free
         plan: Dict[str, object] = dict(none)
         if need > 0 and self.trainer.heap is None:
