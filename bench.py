@@ -331,7 +331,7 @@ def main(argv=None):
     ap.add_argument("--micro-tokens", type=int, default=8192, help="grpo: tokens per update micro-batch")
     ap.add_argument("--offload", default="auto", choices=["auto", "always", "never"],
                     help="grpo: park optimizer state / reference model in host memory between phases")
-    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl", "nvls"],
                     help="data plane of the sharded optimizer (N > 1)")
     ap.add_argument("--recompute", default="auto", choices=["auto", "full", "none"],
                     help="activation recompute: auto keeps whole layers' contexts while HBM allows")

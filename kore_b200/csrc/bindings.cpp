@@ -99,6 +99,11 @@ void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x
                     const c10::optional<at::Tensor>& hn, double eps);
 std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset);
 void symm_gather_ce(int64_t id, int64_t src_offset, int64_t bytes, at::Tensor& dst);
+void nvls_sumsq(int64_t mc_grad, int64_t n, double gscale, at::Tensor& out);
+void nvls_adamw(int64_t mc_grad, int64_t mc_param, const at::Tensor& own_param,
+                const c10::optional<at::Tensor>& master, at::Tensor& m, at::Tensor& v, int64_t elem0, double gscale,
+                double lr, double b1, double b2, double eps, double wd, int64_t step,
+                const c10::optional<at::Tensor>& sumsq, double max_norm, int64_t seed);
 int64_t device_wait_flag(const at::Tensor& flag, int64_t want, double timeout_s);
 int read_and_clear_device_error();
 }  // namespace kore
@@ -157,5 +162,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_norm", &kore::tp_reduce_norm);
   m.def("symm_peer_addrs", &kore::symm_peer_addrs);
   m.def("symm_gather_ce", &kore::symm_gather_ce, "all-gather of heap shards on the copy engines");
+  m.def("nvls_sumsq", &kore::nvls_sumsq, "sum of squares of the switch-reduced gradient shard (multimem)");
+  m.def("nvls_adamw", &kore::nvls_adamw, "AdamW on the switch-reduced gradient shard, multicast parameter store");
   m.def("read_and_clear_device_error", &kore::read_and_clear_device_error);
 }

@@ -55,14 +55,28 @@ class CausalLMTrainer:
         gather_ce = fused and self.zero_stage == 3     # ZeRO-3: layer gathers on the copy engines
         if gather_ce:
             fused = False
-        if fused:
+        nvls = comm == "nvls" and self.ctx.world > 1 and dev.type == "cuda"
+        if nvls and (self.zero_stage != 2 or cfg.is_moe):
+            raise ValueError("comm='nvls' runs the dense ZeRO-2 step")
+        self.nvls = None
+        if fused or nvls:
             from ..parallel.symmetric import SymmetricHeap
             per = 128 * self.ctx.world
             from ..models.qwen3 import unit_layouts, _round_up
             tot = sum(_round_up(l.numel, per) for l in unit_layouts(cfg))
-            self.heap = SymmetricHeap(self.ctx, 2 * tot * 2 + 256 * 4 * len(unit_layouts(cfg)))
-            alloc = lambda n, dt: self.heap.alloc(n, dt)[1]
-            grad_alloc = alloc
+            n_units = len(unit_layouts(cfg))
+            if nvls:
+                from ..parallel.nvls import NVLSBuffers
+                pbuf = NVLSBuffers(self.ctx, tot + 128 * n_units, dtype)
+                gbuf = NVLSBuffers(self.ctx, tot + 128 * n_units, dtype)
+                self.nvls = (pbuf, gbuf)
+                self.heap = SymmetricHeap(self.ctx, 1 << 16)          # barrier / scalar signal pads only
+                alloc = lambda n, dt: pbuf.alloc(n, dt)
+                grad_alloc = lambda n, dt: gbuf.alloc(n, dt)
+            else:
+                self.heap = SymmetricHeap(self.ctx, 2 * tot * 2 + 256 * 4 * n_units)
+                alloc = lambda n, dt: self.heap.alloc(n, dt)[1]
+                grad_alloc = alloc
             if weights is None:
                 weights = Qwen3Weights(cfg, device=dev, dtype=dtype, seed=seed, pad_multiple=per,
                                        alloc=alloc, ep=ep)
@@ -95,7 +109,13 @@ class CausalLMTrainer:
             master = pick_master_mode(cfg, self.ctx.world, dev)
         self.master_mode = master
         self.mbs = micro_batch_size
-        if fused:
+        if nvls:
+            from ..parallel.nvls import NVLSShardedAdamW
+            self.opt = NVLSShardedAdamW(self.w, self.eng, self.ctx, self.nvls[0], self.nvls[1], self.heap, lr=lr,
+                                        betas=betas, weight_decay=weight_decay, max_grad_norm=max_grad_norm,
+                                        master=master, schedule=schedule, warmup_steps=warmup_steps,
+                                        total_steps=total_steps, seed=seed)
+        elif fused:
             from ..parallel.zero import FusedShardedAdamW
             self.opt = FusedShardedAdamW(self.w, self.eng, self.ctx, self.heap, lr=lr, betas=betas,
                                          weight_decay=weight_decay, max_grad_norm=max_grad_norm,

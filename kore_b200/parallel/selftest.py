@@ -6,7 +6,8 @@ Checks: (1) three ZeRO-2 steps with NCCL collectives and with the fused
 peer-memory optimizer give the same parameters (bf16 tolerance) and the
 replicas stay bit-identical across ranks; (2) ZeRO-3 matches ZeRO-2 in loss
 and final parameters, and ZeRO-3 with copy-engine peer gathers matches ZeRO-3
-over NCCL; (3) expert parallelism over NCCL all-to-all and over
+over NCCL; ZeRO-2 through the NVLink switch (multimem reduce / multicast
+store) matches NCCL; (3) expert parallelism over NCCL all-to-all and over
 the fused peer-memory dispatch/combine agree; (4) the tensor-parallel rollout
 engine's sampled log-probs match an fp32 single-GPU reference forward that
 scores the same tokens (teacher forcing); (5) a GRPO step runs with the TP
@@ -57,6 +58,31 @@ def main(argv=None):
         print(json.dumps({"check": "zero2_fused_vs_nccl", "world": ctx.world, "ok": ok and same and err == 0,
                           "loss_nccl": res["nccl"][0], "loss_fused": res["fused"][0],
                           "replicas_identical": same, "device_error": err}), flush=True)
+    # NVLink SHARP: gradients reduced in the switch, parameters multicast back
+    from .nvls import NVLSUnavailable
+    try:
+        tr = CausalLMTrainer(cfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm="nvls", master="fp32")
+        ln = [float(tr.train_step_device(mine)) for _ in range(3)]
+        torch.cuda.synchronize()
+        nv_ok = all(abs(a - b) < 2e-2 * max(1.0, abs(a)) for a, b in zip(res["nccl"][0], ln))
+        for a, b in zip(res["nccl"][1], tr.w.bufs):
+            nv_ok = nv_ok and torch.allclose(a, b.float(), atol=2e-2, rtol=0)
+        csn = torch.tensor([float(sum(b.double().sum() for b in tr.w.bufs))], device="cuda", dtype=torch.float64)
+        lo2, hi2 = csn.clone(), csn.clone()
+        torch.distributed.all_reduce(lo2, op=torch.distributed.ReduceOp.MIN)
+        torch.distributed.all_reduce(hi2, op=torch.distributed.ReduceOp.MAX)
+        errn = check_device_error()
+        nv_ok = nv_ok and float(lo2) == float(hi2) and errn == 0
+        del tr
+        if ctx.is_main:
+            print(json.dumps({"check": "zero2_nvls_vs_nccl", "world": ctx.world, "ok": nv_ok, "loss_nccl": res["nccl"][0],
+                              "loss_nvls": ln, "replicas_identical": float(lo2) == float(hi2),
+                              "device_error": errn}), flush=True)
+        ok = ok and nv_ok
+    except NVLSUnavailable as e:
+        if ctx.is_main:
+            print(json.dumps({"check": "zero2_nvls_vs_nccl", "world": ctx.world, "ok": True, "unavailable": str(e)}),
+                  flush=True)
     # full sharding (ZeRO-3 layers: per-use gathers, per-micro-batch reduce-scatter on a comm stream)
     tr = CausalLMTrainer(cfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm="nccl", master="fp32",
                          zero_stage=3, micro_batch_size=1)
