@@ -1,16 +1,32 @@
-"""Multi-turn agent loop: render -> generate -> parse tool calls -> execute
--> tool results back into the conversation, until ``keep`` or the turn
-budget. The episode is scored by its best correct kernel; per-turn rewards,
-correctness, speedups, codes and potentials are traced for GRPO credit.
-``WinsKB`` retrieves few-shot winning trajectories for the same operation.
-Reference parity: kore/agent/harness.py:52-436."""
+"""Multi-turn tool-use loop over the kernel environment.
+
+render -> generate -> parse reflection and tool calls -> execute -> tool
+results back into the conversation, until ``keep`` or the turn budget.
+
+* Kevin credit: the episode is scored by its best correct candidate (by
+  reward), not its last turn; ``turn_rewards`` / ``turn_correct`` are recorded
+  per assistant turn, unrounded.
+* Phase switch: the system prompt asks for correctness until the first
+  correct kernel, then for speed.
+* Reseed escape: after ``reseed_patience`` turns without a better correct
+  candidate the working lineage restarts from the seed; the best kernel is
+  kept.
+* Per-turn physics trace, index-aligned with ``turn_rewards``:
+  ``turn_speedups`` (measured, benched correct turns only), ``turn_phis``
+  (roofline potential for potential-based shaping) and ``codes``.
+* ``WinsKB`` retrieves prior wins of the same (family, dtype) as few-shot
+  examples; never another family's.
+
+Reference behaviour: kore/agent/harness.py:52-436.
+"""
 from __future__ import annotations
 
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional
 
-from .format import build_agent_system_prompt, format_tool_result, parse_tool_calls
-from .tools import ToolExecutor, tool_use_reward
+from .format import (build_agent_system_prompt, format_tool_result, parse_reflection, parse_tool_calls,
+                     reflection_is_grounded)
+from .tools import EVAL_TOOLS, ToolExecutor, tool_use_reward
 
 
 @dataclass
@@ -19,81 +35,145 @@ class Episode:
     turn_rewards: List[float] = field(default_factory=list)
     turn_correct: List[bool] = field(default_factory=list)
     codes: List[str] = field(default_factory=list)
+    turn_speedups: List[Optional[float]] = field(default_factory=list)
+    turn_phis: List[Optional[float]] = field(default_factory=list)
     best_correct: Optional[str] = None
     best_ms: Optional[float] = None
+    best_speedup: Optional[float] = None
     tool_reward: float = 0.0
+    reflections: int = 0
+    reseeds: int = 0
+
+    @property
+    def turn_codes(self) -> List[str]:
+        return self.codes
+
+    def to_record(self, task_id: str):
+        from .schema import AgenticTrajectoryRecord
+        return AgenticTrajectoryRecord(task_id, self.messages, [], list(self.turn_rewards), list(self.turn_correct),
+                                       self.best_correct, self.best_speedup)
+
+
+AgentEpisode = Episode
 
 
 class WinsKB:
-    """Few-shot retriever over WinRecords keyed by operation."""
+    """Few-shot retriever over WinRecords keyed by (family, dtype)."""
 
     def __init__(self, records=()):
-        self.by_op: Dict[str, list] = {}
+        self.by_key: Dict[tuple, list] = {}
         for r in records:
-            self.by_op.setdefault(r.operation or "", []).append(r)
+            self.by_key.setdefault(self._key(r), []).append(r)
 
-    def examples(self, operation: str, k: int = 1) -> List:
-        rs = sorted(self.by_op.get(operation, []), key=lambda r: -(r.speedup or 0))
-        return rs[:k]
+    @staticmethod
+    def _key(r) -> tuple:
+        fam = getattr(r, "family", None) or getattr(r, "operation", "") or ""
+        return (fam, getattr(r, "dtype", None) or "")
+
+    def examples(self, family: str, dtype: str = "", k: int = 1) -> List:
+        rs = self.by_key.get((family, dtype), []) or (self.by_key.get((family, ""), []) if not dtype else [])
+        return sorted(rs, key=lambda r: -(getattr(r, "speedup", 0) or 0))[:k]
 
 
 class AgentHarness:
     def __init__(self, env, task, *, max_turns: int = 8, transforms: bool = False, kb: Optional[WinsKB] = None,
-                 reward_fn: Optional[Callable] = None):
+                 reward_fn: Optional[Callable] = None, reseed_patience: int = 3, arch: Optional[str] = None):
         self.env, self.task = env, task
         self.max_turns = max_turns
         self.exec = ToolExecutor(env, task, transforms=transforms, current=task.seed_src)
         self.kb = kb
         self.reward_fn = reward_fn
+        self.reseed_patience = reseed_patience
+        self.arch = arch
+        self.phase = "correctness"
+
+    def _system(self) -> str:
+        return build_agent_system_prompt(self.exec.tools(), arch=self.arch, phase=self.phase)
 
     def initial_messages(self) -> List[dict]:
         from ..policy.format import build_task_prompt
-        sys_p = build_agent_system_prompt(self.exec.tools())
         user = build_task_prompt(self.task)
         if self.kb:
-            for ex in self.kb.examples(self.task.operation):
-                user += f"\n\nA previous winning kernel for {ex.operation} ({ex.speedup:.2f}x):\n{ex.final_kernel}"
-        return [{"role": "system", "content": sys_p}, {"role": "user", "content": user}]
+            fam = getattr(self.task, "family", "") or getattr(self.task, "operation", "")
+            for ex in self.kb.examples(fam, getattr(self.task, "dtype", "")):
+                user += (f"\n\nA previous winning kernel for a {fam} task ({(ex.speedup or 0):.2f}x):\n"
+                         f"{ex.final_kernel}")
+        return [{"role": "system", "content": self._system()}, {"role": "user", "content": user}]
 
     def run(self, policy) -> Episode:
-        """Drive the tool loop. ``turn_rewards`` / ``turn_correct`` / ``codes``
-        have one entry per assistant turn (the best evaluation among that
-        turn's test/bench/keep calls; 0 and incorrect for a turn without one),
-        so they align with the policy's recorded generations."""
+        """Drive the tool loop. The per-turn lists have one entry per assistant
+        turn (the best evaluation among that turn's calls; 0 and incorrect
+        for a turn without one), aligned with the policy's generations."""
         msgs = self.initial_messages()
         ep = Episode(messages=msgs)
+        ex = self.exec
+        stall, last_res, best_key = 0, None, None
         for _ in range(self.max_turns):
             resp = policy.generate(msgs)
-            turn_best = None
             msgs.append({"role": "assistant", "content": resp})
+            refl = parse_reflection(resp)
+            if reflection_is_grounded(refl, last_res):
+                ep.reflections += 1
             calls = parse_tool_calls(resp)
             if not calls:
                 from ..policy.format import parse_response
                 k = parse_response(resp).get("kernel")
                 calls = [{"name": "keep", "arguments": {"source": k}}] if k else []
             if not calls:
-                ep.turn_correct.append(False)
-                ep.turn_rewards.append(0.0)
-                ep.codes.append(self.exec.current)
+                self._record(ep, None)
                 break
-            stop = False
+            stop, turn_best = False, None
             for c in calls:
-                res = self.exec.call(c["name"], c["arguments"])
+                res = ex.call(c["name"], c["arguments"])
+                last_res = res
                 msgs.append({"role": "tool", "content": format_tool_result(c["name"], res)})
-                if c["name"] in ("test", "bench", "keep"):
-                    ok = bool(res.get("correct"))
-                    r = self.reward_fn(res) if self.reward_fn else (0.3 if ok else 0.0)
+                if c["name"] in EVAL_TOOLS:
+                    ok = ex.candidate_correct
+                    r = self.reward_fn(res) if self.reward_fn else (ex.candidate_reward or 0.0)
+                    cand = (ok, r, ex.current, ex.candidate_speedup, ex.candidate_phi)
                     if turn_best is None or (ok, r) > (turn_best[0], turn_best[1]):
-                        turn_best = (ok, r, self.exec.current)
-                if c["name"] == "keep":
+                        turn_best = cand
+                if c["name"] == "keep" and ex.candidate_correct:
                     stop = True
-            ok, r, code = turn_best if turn_best is not None else (False, 0.0, self.exec.current)
-            ep.turn_correct.append(ok)
-            ep.turn_rewards.append(r)
-            ep.codes.append(code)
+            self._record(ep, turn_best)
+            if turn_best is not None and turn_best[0]:
+                if self.phase == "correctness":          # first correct kernel: optimise from here on
+                    self.phase = "optimize"
+                    msgs[0] = {"role": "system", "content": self._system()}
+                key = turn_best[1]
+                if best_key is None or key > best_key:
+                    best_key, stall = key, 0
+                else:
+                    stall += 1
+            else:
+                stall += 1
             if stop:
                 break
-        ep.best_correct = self.exec.kept or self.exec.best
-        ep.best_ms = self.exec.best_ms
-        ep.tool_reward = tool_use_reward(self.exec.trace, ep.best_correct is not None)
+            if stall >= self.reseed_patience:
+                ex.reseed()
+                ep.reseeds += 1
+                stall = 0
+                msgs.append({"role": "user", "content": "No progress for several turns: the working kernel was "
+                                                        "reset to the seed (your best kernel is kept). Try a "
+                                                        "different approach."})
+        ep.best_correct = ex.kept or ex.best_reward_src or ex.best
+        ep.best_ms = ex.best_ms
+        ep.best_speedup = ex.best_speedup
+        n_turns = len(ep.turn_rewards)
+        ep.tool_reward = tool_use_reward(ex.trace, ep.best_correct is not None, ep.reflections, n_turns)
         return ep
+
+    def _record(self, ep: Episode, best) -> None:
+        if best is None:
+            ep.turn_correct.append(False)
+            ep.turn_rewards.append(0.0)
+            ep.codes.append(self.exec.current)
+            ep.turn_speedups.append(None)
+            ep.turn_phis.append(None)
+            return
+        ok, r, code, sp, phi = best
+        ep.turn_correct.append(bool(ok))
+        ep.turn_rewards.append(float(r))
+        ep.codes.append(code)
+        ep.turn_speedups.append(sp if ok else None)
+        ep.turn_phis.append(phi if ok else None)

@@ -1,31 +1,70 @@
 """Kernel-engineering tools for the agent and their executor.
 
-Tools: ``build`` (compile / import check), ``test`` (correctness on all
-shapes), ``bench`` (verified timing vs the vendor baseline), ``pmc``
-(ncu counters), ``keep`` (commit the current kernel as the answer),
-``revert`` (go back to the best kernel), and optionally
-``list_transforms`` / ``apply_transform`` (the transform calculus). The
-executor is a small state machine over (current, best) kernels and records a
-per-call trace used for the tool-use shaping reward. Reference parity:
-kore/agent/tools.py:60-800.
+Base tools: ``build`` (compile / import check), ``test`` (correctness on every
+shape), ``bench`` (verified timing against the vendor baseline), ``pmc``
+(Nsight Compute counters), ``keep`` (commit a kernel as the answer),
+``revert`` (return to the best kernel). Opt-in transform tools:
+``list_transforms`` (the typed rewrites admissible for the working kernel under
+the episode's remaining epsilon budget) and ``apply_transform`` (one rewrite
+with budget accounting; an inadmissible move is refused and the source left
+unchanged). The executor is the episode's state machine:
+
+* it grades every evaluated candidate with the system's reward
+  (``compute_kernel_reward``; mode from ``KORE_REWARD_MODE``, default
+  ``speedup``) and keeps the best correct candidate by reward (the Kevin
+  scoring key) and, separately, the measured-speedup frontier;
+* a ``bench`` result carries ``best_speedup_so_far``, ``delta_vs_best`` and
+  ``improved_frontier`` (the frontier snapshotted before this candidate);
+* per evaluation it records ``candidate_speedup`` (only for a benched correct
+  kernel) and ``candidate_phi`` (the roofline potential for shaping);
+* ``reseed`` restarts the working lineage from the seed while keeping the best
+  kernel and resetting the epsilon budget;
+* ``trace`` feeds the tool-use shaping reward.
+
+Tool schemas are OpenAI-style function descriptions.
+Reference behaviour: kore/agent/tools.py:60-800.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
 
-TOOLS = [
-    {"name": "build", "description": "compile/import the kernel", "parameters": {"source": "string"}},
-    {"name": "test", "description": "run correctness on all shapes", "parameters": {"source": "string"}},
-    {"name": "bench", "description": "verified timing vs the vendor baseline", "parameters": {"source": "string"}},
-    {"name": "pmc", "description": "Nsight Compute counters of the kernel", "parameters": {"source": "string"}},
-    {"name": "keep", "description": "commit this kernel as the answer", "parameters": {"source": "string"}},
-    {"name": "revert", "description": "return to the best kernel so far", "parameters": {}},
+
+def _fn(name: str, desc: str, props: Dict[str, dict], required=()) -> Dict:
+    return {"type": "function", "function": {"name": name, "description": desc,
+                                             "parameters": {"type": "object", "properties": props,
+                                                            "required": list(required)}}}
+
+
+_SRC = {"source": {"type": "string", "description": "the complete kernel module (defaults to the working kernel)"}}
+TOOL_SCHEMAS = [
+    _fn("build", "Compile / import the kernel module and report errors.", _SRC),
+    _fn("test", "Run the correctness check (SNR against the fp32 reference) on every shape.", _SRC),
+    _fn("bench", "Verified timing against the vendor baseline, with the speedup frontier of this episode.", _SRC),
+    _fn("pmc", "Nsight Compute counters of the kernel (DRAM / tensor-pipe utilisation, stalls).", _SRC),
+    _fn("keep", "Commit this kernel as the final answer (it must be correct).", _SRC),
+    _fn("revert", "Make the best kernel of this episode the working kernel again.", {}),
 ]
-TRANSFORM_TOOLS = [
-    {"name": "list_transforms", "description": "list applicable source transforms", "parameters": {}},
-    {"name": "apply_transform", "description": "apply a named transform", "parameters": {"name": "string"}},
+TRANSFORM_SCHEMAS = [
+    _fn("list_transforms", "Typed source rewrites admissible for the working kernel under the remaining "
+                           "approximation budget.", {}),
+    _fn("apply_transform", "Apply one typed rewrite (with its parameters) to the working kernel.",
+        {"name": {"type": "string", "description": "transform family or family(k=v,...)"},
+         "params": {"type": "object", "description": "parameters of the family"}}, required=("name",)),
 ]
+# flat schema list kept for callers that want name / description only
+TOOLS = [{"name": t["function"]["name"], "description": t["function"]["description"],
+          "parameters": {k: v["type"] for k, v in t["function"]["parameters"]["properties"].items()}}
+         for t in TOOL_SCHEMAS]
+TRANSFORM_TOOLS = [{"name": t["function"]["name"], "description": t["function"]["description"],
+                    "parameters": {k: v["type"] for k, v in t["function"]["parameters"]["properties"].items()}}
+                   for t in TRANSFORM_SCHEMAS]
+EVAL_TOOLS = ("build", "test", "bench", "pmc", "keep")
+
+
+def agent_tool_schemas(transforms: bool = False) -> List[Dict]:
+    return TOOL_SCHEMAS + (TRANSFORM_SCHEMAS if transforms else [])
 
 
 @dataclass
@@ -34,56 +73,141 @@ class ToolExecutor:
     task: object
     transforms: bool = False
     current: str = ""
-    best: Optional[str] = None
+    best: Optional[str] = None                 # fastest correct kernel by measured time
     best_ms: Optional[float] = None
+    best_reward: Optional[float] = None        # Kevin key: best correct candidate by reward
+    best_reward_src: Optional[str] = None
+    best_speedup: Optional[float] = None       # measured-speedup frontier
     kept: Optional[str] = None
+    candidate_speedup: Optional[float] = None  # of the last evaluation (benched + correct only)
+    candidate_phi: Optional[float] = None
+    candidate_reward: Optional[float] = None
+    candidate_correct: bool = False
     trace: List[Dict] = field(default_factory=list)
+    reward_mode: str = field(default_factory=lambda: os.environ.get("KORE_REWARD_MODE", "speedup"))
+    budget: object = None                      # per-episode epsilon budget of the transform tools
+    seed_src: str = ""
+
+    def __post_init__(self):
+        self.seed_src = self.seed_src or self.current
 
     def tools(self) -> List[Dict]:
         return TOOLS + (TRANSFORM_TOOLS if self.transforms else [])
 
+    def schemas(self) -> List[Dict]:
+        return agent_tool_schemas(self.transforms)
+
+    # ------------------------------------------------------------------ grading
+    def _grade(self, obs, src: str):
+        try:
+            from ..reward.physics import compute_kernel_reward
+            rr = compute_kernel_reward(obs, src, self.task, mode=self.reward_mode,
+                                       dtype=getattr(self.task, "dtype", "fp32"))
+            return float(rr.reward), bool(rr.correct), rr.speedup
+        except Exception:  # noqa: BLE001 - a reward failure must not end the episode
+            ok = bool(getattr(obs, "validation_passed", False))
+            return (0.3 if ok else 0.0), ok, None
+
+    def _phi(self, obs) -> Optional[float]:
+        try:
+            from ..reward.whitebox import phi_potential
+            return phi_potential(self.task, obs)
+        except Exception:  # noqa: BLE001 - a physics gap is a shaping boundary
+            return None
+
+    def _budget(self):
+        if self.budget is None:
+            from ..transform.budget import ErrorBudget
+            self.budget = ErrorBudget.for_op(getattr(self.task, "operation", ""), getattr(self.task, "dtype", "fp32"))
+        return self.budget
+
+    # ------------------------------------------------------------------ dispatch
     def call(self, name: str, args: Dict) -> Dict:
-        src = args.get("source") or self.current
-        self.current = src
-        if name in ("build", "test", "bench", "pmc", "keep"):
-            obs = self.env.step(src)
-            res: Dict = {"compiled": obs.compiled, "correct": bool(obs.validation_passed),
-                         "snr_db": obs.snr_by_shape or obs.snr_db}
-            if obs.flagged_hack:
-                res["rejected"] = obs.hack_reason
-            if name in ("bench", "keep", "pmc") and obs.validation_passed:
-                res.update({"wall_ms": obs.wall_by_shape, "baseline_ms": obs.baseline_by_shape})
-                if obs.wall_ms and (self.best_ms is None or obs.wall_ms < self.best_ms):
-                    self.best, self.best_ms = src, obs.wall_ms
-            if name == "pmc" and obs.validation_passed:
-                from ..verifier.pmc import collect_counters
-                res["counters"] = getattr(obs, "counters", None) or {}
-            if not obs.compiled:
-                res["error"] = (obs.error_text or "")[-1500:]
-            if name == "keep":
-                self.kept = src if obs.validation_passed else self.kept
-            self.trace.append({"tool": name, "ok": bool(obs.validation_passed), "ms": obs.wall_ms})
-            return res
+        args = args or {}
+        if name in EVAL_TOOLS:
+            return self._evaluate(name, args.get("source") or self.current)
         if name == "revert":
-            self.current = self.best or self.current
+            self.current = self.best or self.best_reward_src or self.current
             self.trace.append({"tool": name, "ok": True, "ms": self.best_ms})
             return {"source": self.current}
         if name == "list_transforms":
-            from ..transform.library import admissible
-            return {"transforms": [t.name for t in admissible(self.current)]}
+            from ..transform.calculus import admissible_actions
+            acts = admissible_actions(self.current, budget=self._budget())
+            self.trace.append({"tool": name, "ok": True})
+            return {"transforms": [{"name": a.name, "relation": a.kind, "epsilon": a.eps} for a in acts],
+                    "budget_remaining": self._budget().remaining()}
         if name == "apply_transform":
+            from ..transform.calculus import apply_sequence
+            step = args.get("name", "")
+            params = args.get("params") or {}
             from ..transform.library import get_transform
-            t = get_transform(args.get("name", ""))
-            new = t.apply(self.current) if t else None
-            if new:
+            t = get_transform(step)
+            if t is None:
+                self.trace.append({"tool": name, "ok": False})
+                return {"applied": False, "reason": f"unknown transform {step!r}", "source": self.current}
+            if params and hasattr(t, "actions"):
+                from ..transform.calculus import Action
+                t = Action(t, dict(params))
+            new, applied, rejected, state = apply_sequence(self.current, [t], self._budget(), audit=True)
+            ok = bool(applied)
+            if ok:
                 self.current = new
-            return {"applied": bool(new), "source": self.current}
+            self.trace.append({"tool": name, "ok": ok})
+            out = {"applied": ok, "source": self.current, "budget_remaining": state["remaining"]}
+            if not ok and rejected:
+                out["reason"] = rejected[0].reason
+            return out
         return {"error": f"unknown tool {name!r}"}
 
+    def _evaluate(self, name: str, src: str) -> Dict:
+        self.current = src
+        obs = self.env.step(src)
+        reward, correct, speedup = self._grade(obs, src)
+        self.candidate_reward, self.candidate_correct = reward, correct
+        self.candidate_speedup = None
+        self.candidate_phi = None
+        res: Dict = {"compiled": bool(obs.compiled), "correct": correct,
+                     "snr_db": getattr(obs, "snr_by_shape", None) or getattr(obs, "snr_db", None)}
+        if getattr(obs, "flagged_hack", False):
+            res["rejected"] = obs.hack_reason
+        if not obs.compiled:
+            res["error"] = (getattr(obs, "error_text", "") or "")[-1500:]
+        timed = name in ("bench", "keep", "pmc") and correct and obs.wall_ms
+        if correct and (self.best_reward is None or reward > self.best_reward):
+            self.best_reward, self.best_reward_src = reward, src
+        if timed:
+            res.update({"wall_ms": obs.wall_by_shape, "baseline_ms": obs.baseline_by_shape})
+            if self.best_ms is None or obs.wall_ms < self.best_ms:
+                self.best, self.best_ms = src, obs.wall_ms
+            prev = self.best_speedup
+            self.candidate_speedup = speedup
+            self.candidate_phi = self._phi(obs)
+            if speedup is not None:
+                res["speedup"] = speedup
+                res["best_speedup_so_far"] = max(prev or speedup, speedup)
+                res["delta_vs_best"] = None if prev is None else speedup - prev
+                res["improved_frontier"] = prev is None or speedup > prev
+                if prev is None or speedup > prev:
+                    self.best_speedup = speedup
+        if name == "pmc" and correct:
+            res["counters"] = getattr(obs, "counters", None) or {}
+        if name == "keep" and correct:
+            self.kept = src
+        self.trace.append({"tool": name, "ok": correct, "ms": obs.wall_ms, "reward": reward})
+        return res
 
-def tool_use_reward(trace: List[Dict], final_correct: bool) -> float:
-    """Small shaping for disciplined tool use in [-0.1, 0.2]: test before
-    bench, bench before keep, no repeated failing builds."""
+    def reseed(self) -> None:
+        """Restart the working lineage from the seed (the best kernel and the
+        frontier survive; the epsilon budget starts over)."""
+        self.current = self.seed_src
+        self.budget = None
+        self.trace.append({"tool": "reseed", "ok": True})
+
+
+def tool_use_reward(trace: List[Dict], final_correct: bool, reflections: int = 0, turns: int = 0) -> float:
+    """Shaping for disciplined tool use, in [-0.1, 0.25]: test before bench,
+    keep on a correct kernel, grounded reflections, few repeated failures.
+    Small against the verified kernel reward it is added to."""
     if not trace:
         return -0.1
     names = [t["tool"] for t in trace]
@@ -92,6 +216,8 @@ def tool_use_reward(trace: List[Dict], final_correct: bool) -> float:
         r += 0.1
     if "keep" in names and final_correct:
         r += 0.1
-    fails = sum(1 for t in trace if not t.get("ok"))
+    if turns and reflections:
+        r += 0.05 * min(1.0, reflections / turns)
+    fails = sum(1 for t in trace if t["tool"] in EVAL_TOOLS and not t.get("ok"))
     r -= 0.02 * max(0, fails - 2)
-    return max(-0.1, min(0.2, r))
+    return max(-0.1, min(0.25, r))

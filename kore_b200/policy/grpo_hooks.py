@@ -185,7 +185,8 @@ def rollout_agentic(trainer, task, traj_ids: Sequence[int], max_new: int):
             tr.gen_logps.append(lps)
             tr.finish.append(fin)
             tr.results.append(TurnResult(reward=float(rewards[i]), correct=bool(correct[i]),
-                                         code=ep.codes[i] if i < len(ep.codes) else ""))
+                                         code=ep.codes[i] if i < len(ep.codes) else "",
+                                         phi=ep.turn_phis[i] if i < len(ep.turn_phis) else None))
         out.append(tr)
     return out
 
