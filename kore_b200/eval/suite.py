@@ -95,3 +95,24 @@ def write_report(path: str, title: str, sections: Dict[str, Dict]) -> str:
     with open(path, "w") as f:
         f.write(text)
     return text
+
+
+def champion_verdict(claimed: Optional[float], *, correct: bool, correct_unseen: bool = True,
+                     hack_reason: Optional[str] = None, cv_pct: Optional[float] = None,
+                     speedup: Optional[float] = None, collapse: float = 0.7, max_cv_pct: float = 5.0) -> Dict:
+    """Certify a champion kernel re-measured under harder conditions than
+    training: correct on the training shapes AND on unseen shapes, no static
+    reward hack, low timing variance, and a re-measured speedup that did not
+    collapse below ``collapse`` x the claimed one."""
+    reasons = []
+    if not correct:
+        reasons.append("incorrect on the training shapes")
+    if not correct_unseen:
+        reasons.append("incorrect on unseen shapes")
+    if hack_reason:
+        reasons.append(f"static check: {hack_reason}")
+    if cv_pct is not None and cv_pct > max_cv_pct:
+        reasons.append(f"timing variance {cv_pct:.1f}% > {max_cv_pct}%")
+    if claimed and (speedup or 0.0) < collapse * claimed:
+        reasons.append(f"speedup {speedup or 0.0:.2f}x collapsed below {collapse} x claimed {claimed:.2f}x")
+    return {"certified": not reasons, "reasons": reasons, "claimed": claimed, "remeasured": speedup}
