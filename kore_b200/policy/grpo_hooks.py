@@ -86,13 +86,13 @@ class ValuePrefilter:
             with open(cfg.value_model_path) as f:
                 self.model = ValueModel.from_json(f.read())
 
-    def pick(self, codes: Sequence[str]) -> List[int]:
-        """Indices of the candidates to verify (value-ranked top k; the first
-        k when no model is loaded)."""
-        if self.model is None or len(codes) <= self.k:
-            return list(range(min(self.k, len(codes))))
-        from ..value.model import rank_candidates
-        return list(rank_candidates(self.model, list(codes)))[: self.k]
+    def pick(self, codes: Sequence[str], task=None) -> List[int]:
+        """Indices of the candidates to verify: the value model's top k, or the
+        schedule heuristic's when no (or only a degenerate) model is loaded."""
+        if len(codes) <= self.k:
+            return list(range(len(codes)))
+        from ..value.rerank import rank_candidates
+        return rank_candidates(list(codes), task=task, model=self.model)[: self.k]
 
 
 # ----------------------------------------------------------------------------- search -> distill

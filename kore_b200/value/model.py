@@ -65,8 +65,11 @@ class ValueModel:
         self.w_snr = _logreg(X, correct.astype(float))
         m = correct.astype(bool)
         if m.sum() >= 2:
+            # throughput weighting: fast kernels dominate the fit (weight = max(speedup, 0.1))
             Xm = X[m]
-            self.w_speed = np.linalg.solve(Xm.T @ Xm + 1e-1 * np.eye(X.shape[1]), Xm.T @ log_speed[m])
+            wts = np.maximum(np.exp(log_speed[m]), 0.1)
+            A = Xm.T @ (Xm * wts[:, None]) + 1e-1 * np.eye(X.shape[1])
+            self.w_speed = np.linalg.solve(A, Xm.T @ (wts * log_speed[m]))
         else:
             self.w_speed = np.zeros(X.shape[1])
         if pairs:
