@@ -117,7 +117,11 @@ def flops_bytes(operation: str, dims: Dict[str, int], dtype: str) -> Optional[Tu
             io = (M * K + K * N) * (1 if fp8 else e) + M * N * (2 if fp8 else e)
             return 2.0 * B * M * N * K, float(B * io)
         if "gemm" in op or "matmul" in op or op == "linear":
-            M, N, K = dims["M"], dims["N"], dims["K"]
+            if "K" not in dims and "N_out" in dims:
+                # a fused pipeline's GEMM stage: the M x N input times an N_out x N weight
+                M, N, K = dims["M"], dims["N_out"], dims["N"]
+            else:
+                M, N, K = dims["M"], dims["N"], dims["K"]
             io = (M * K + K * N) * (1 if fp8 else e) + M * N * (2 if fp8 else e)
             return 2.0 * M * N * K, float(io)
         if ("rmsnorm" in op and "fused" in op) or "fused_add" in op:

@@ -170,7 +170,10 @@ class TaskMinter:
             tid = f"minted_{p.name}_{dtype}_{bh[:6]}"[:80]
             if tid in self.registry:
                 continue
-            mt = MintedTask(tid, p, dtype, {"minimal": {"M": 64, "N": 256}, "primary": shape, "validation": []},
+            shapes = {"minimal": {"M": 64, "N": 256}, "primary": dict(shape), "validation": []}
+            if "matmul" in p.stages:
+                shapes["primary"]["N_out"] = p.width_out or shape["N"]
+            mt = MintedTask(tid, p, dtype, shapes,
                             move, bh)
             self._register(mt)
             self.minted.append(mt)

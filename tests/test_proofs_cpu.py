@@ -7,7 +7,8 @@ from kore_b200.campaign.nodes import array_manifest, manifest_shard, merge_shard
 
 def test_proofs_cpu():
     assert proofs.smoke_sft("cpu")["ok"]
-    assert proofs.prove_ops()["ok"]
+    r = proofs.prove_ops()
+    assert r["ok"], r
     assert proofs.verify_breadth(limit=60)["ok"]
     assert proofs.repro_grpo_step(world=2, port=29641)["ok"]
     assert proofs.smoke_env(device="cpu")["ok"]            # skipped without a GPU
