@@ -360,12 +360,13 @@ for _n, (_e, _r) in _BINARY.items():
 # generated breadth families (kore_b200.tasks.breadth)
 def _register_breadth():
     from .breadth import build
+    from .breadth_attn import build as build_attn
     from .breadth_ext import build as build_ext
     from .breadth_fx import build as build_fx
     from .breadth_train import build as build_train
     from .core_ext import build as build_core
     from .genops import build as build_gen
-    for _s in build() + build_train() + build_ext() + build_fx():
+    for _s in build() + build_train() + build_ext() + build_fx() + build_attn():
         if _s.name not in SPECS:
             _add(_s)
     for _n, _s in list(build_gen().items()) + list(build_core().items()):

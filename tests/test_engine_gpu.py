@@ -65,5 +65,8 @@ def test_moment_shuttle_matches_plain_step():
     # sign of a tiny gradient can move it 2 lr per step
     for a, b in zip(res["never"][1], res["always"][1]):
         assert (a - b).abs().max() <= 4 * 1e-3 + 1e-6 and (a - b).abs().mean() < 1e-4
+    # second moments are squares of those gradients: compare them relative to
+    # each tensor's own scale, not element by element near zero
     for a, b in zip(res["never"][2], res["always"][2]):
-        assert torch.allclose(a, b, rtol=5e-2, atol=1e-10)
+        assert ((a - b).norm() / b.norm().clamp(min=1e-30)).item() < 2e-2
+        assert torch.allclose(a, b, rtol=1e-1, atol=1e-3 * b.abs().max().item())

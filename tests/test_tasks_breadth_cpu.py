@@ -78,3 +78,12 @@ def test_core_and_vendor_families_are_well_formed():
         assert torch.isfinite(ref).all(), n
         assert ((out - ref).norm() / (ref.norm() + 1e-12)).item() < 2e-2, n
         s.baseline(*x)
+
+
+def test_attention_ext_family_and_corpus_size():
+    """The attention-variant family (biases, masks, layouts, fp8, backward) and
+    the whole corpus reach the reference's task count."""
+    from kore_b200.tasks.registry import all_tasks
+    ext = [n for n in SPECS if n.startswith("genb_attn2_")]
+    assert len(ext) >= 100
+    assert len({t.task_id for t in all_tasks()}) >= 1334
