@@ -102,6 +102,21 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_fwd_kernel(
 
 // ---------------------------------------------------------------- RMSNorm bwd
 // dx = rstd * (w*dy - xhat * mean(xhat*w*dy)) (+ dres);  dw += sum_rows dy*xhat
+// Persistent blocks walk rows with a stride of the grid. Each thread keeps the
+// raw bf16 vectors of its columns (x, dy, dres) and loads the NEXT row's
+// vectors before it reduces the current one, so two rows' loads are in
+// flight per thread across the block-wide reduction; dw accumulates in
+// registers and is added once per block at the end.
+KORE_DEV void unpack8(const uint4& u, float (&f)[8]) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = __bfloat1622float2(h[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
 template <int THREADS, int VPT>
 __global__ void __launch_bounds__(THREADS) rmsnorm_bwd_kernel(
     const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
@@ -115,44 +130,67 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_bwd_kernel(
   for (int i = 0; i < VPT; ++i)
 #pragma unroll
     for (int e = 0; e < 8; ++e) dwacc[i][e] = 0.f;
-  for (int r = blockIdx.x; r < rows; r += gridDim.x) {
+  uint4 cx[VPT], cg[VPT], cr[VPT];
+  auto load_row = [&](int r, uint4 (&px)[VPT], uint4 (&pg)[VPT], uint4 (&pr)[VPT]) {
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      const int j = threadIdx.x + i * THREADS;
+      if (j < nvec) {
+        px[i] = __ldg(reinterpret_cast<const uint4*>(x + (size_t)r * H + j * 8));
+        pg[i] = __ldg(reinterpret_cast<const uint4*>(dy + (size_t)r * H + j * 8));
+        if (dres) pr[i] = __ldg(reinterpret_cast<const uint4*>(dres + (size_t)r * H + j * 8));
+      }
+    }
+  };
+  int r = blockIdx.x;
+  if (r < rows) load_row(r, cx, cg, cr);
+  for (; r < rows; r += gridDim.x) {
+    uint4 nx[VPT], ng[VPT], nr[VPT];
+    const int rn = r + gridDim.x;
+    if (rn < rows) load_row(rn, nx, ng, nr);
     const float rs = rstd[r];
-    float xv[VPT][8], g[VPT][8];
     float dot = 0.f;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      int j = threadIdx.x + i * THREADS;
+      const int j = threadIdx.x + i * THREADS;
       if (j < nvec) {
-        float wv[8];
-        load8(x + (size_t)r * H + j * 8, xv[i]);
-        load8(dy + (size_t)r * H + j * 8, g[i]);
+        float xv[8], g[8], wv[8];
+        unpack8(cx[i], xv);
+        unpack8(cg[i], g);
         load8(w + j * 8, wv);
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          float xh = xv[i][e] * rs;
-          dwacc[i][e] += g[i][e] * xh;
-          g[i][e] *= wv[e];
-          dot += g[i][e] * xh;
-          xv[i][e] = xh;
+          const float xh = xv[e] * rs;
+          dwacc[i][e] += g[e] * xh;
+          dot += g[e] * wv[e] * xh;
         }
       }
     }
     dot = block_sum<THREADS>(dot, red) / H;
 #pragma unroll
     for (int i = 0; i < VPT; ++i) {
-      int j = threadIdx.x + i * THREADS;
+      const int j = threadIdx.x + i * THREADS;
       if (j < nvec) {
-        float o[8];
+        float xv[8], g[8], wv[8], o[8];
+        unpack8(cx[i], xv);
+        unpack8(cg[i], g);
+        load8(w + j * 8, wv);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] = rs * (g[i][e] - xv[i][e] * dot);
+        for (int e = 0; e < 8; ++e) o[e] = rs * (g[e] * wv[e] - xv[e] * rs * dot);
         if (dres) {
           float d[8];
-          load8(dres + (size_t)r * H + j * 8, d);
+          unpack8(cr[i], d);
 #pragma unroll
           for (int e = 0; e < 8; ++e) o[e] += d[e];
         }
         store8(dx + (size_t)r * H + j * 8, o);
       }
+    }
+#pragma unroll
+    for (int i = 0; i < VPT; ++i) {
+      cx[i] = nx[i];
+      cg[i] = ng[i];
+      cr[i] = nr[i];
     }
   }
   if (dw) {

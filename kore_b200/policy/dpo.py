@@ -142,6 +142,24 @@ class DPOTrainer:
         self._ref_hook = self._ref_stream
         return ref
 
+    def _park_ref(self):
+        """One GPU with the reference streamed from host memory: once all its
+        log-probs of the step are computed, its resident units (embedding and
+        head) move to pinned host memory and its layer ring is freed for the
+        policy update; ``step`` brings them back after the optimizer step.
+        Returns the parked slots, or None when nothing is parked."""
+        if self.ctx.world > 1 or self.ctx.device.type != "cuda" or self.ref_placement != "host":
+            return None
+        from ..engine.offload import HostStash, weight_slots
+        if not hasattr(self, "_ref_stash"):
+            self._ref_stash = HostStash()
+        st = self._ref_stream
+        st.free_ring()
+        rw = self.ref.w
+        slots = [(c, k) for c, k in weight_slots(rw) if not (c is rw.bufs and k in st.store)]
+        self._ref_stash.park(slots)
+        return slots
+
     def _batch(self, items):
         from ..engine.qwen3_engine import Batch
         seqs, masks = [], []
@@ -187,7 +205,13 @@ class DPOTrainer:
             ref_lps = [lp for lp, _ in self.ref.token_logprobs_many(batches)]
         else:
             ref_lps = [None] * len(batches)
-        for s0, b, lp_pre in zip(starts, batches, ref_lps):
+        parked = self._park_ref() if ref_lps[0] is not None else None
+        # one GPU: the second moments leave HBM for the middle micro-batches, which
+        # then keep their layer contexts instead of recomputing (None elsewhere)
+        shuttle = self.tr._moment_shuttle(len(batches), max(b.num_tokens for b in batches))
+        for i, (s0, b, lp_pre) in enumerate(zip(starts, batches, ref_lps)):
+            if shuttle is not None:
+                shuttle.before(i)
             chunk = pairs[s0:s0 + self.micro_pairs]
             items = [x for p in chunk for x in p]
             seg, wt = self._token_weights(b, items)
@@ -220,7 +244,11 @@ class DPOTrainer:
 
             out = eng.forward_backward(b, coef_fn=coef_fn)
             total += float(out["loss"])
+        if shuttle is not None:
+            shuttle.finish()
         self.tr.opt.step()
+        if parked is not None:
+            self._ref_stash.restore(parked, self.ctx.device)
         loss = torch.tensor([total], device=self.ctx.device)
         self.ctx.all_reduce(loss)
         return float(loss.item())
