@@ -466,6 +466,7 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   const int H = x.size(-1);
   const long rows = x.numel() / H;
   if (rows == 0) return;
+  TORCH_CHECK(H % 8 == 0 && H <= 256 * 4 * 8, "rmsnorm_bwd: unsupported H");
   if (dw) TORCH_CHECK(dw->scalar_type() == at::kFloat && dw->numel() == H, "dw must be fp32 [H]");
   c10::cuda::CUDAGuard g(x.device());
   const int nvec = H / 8;
@@ -481,8 +482,7 @@ void rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
   if (nvec <= 256) KORE_RMS_BWD(256, 1);
   else if (nvec <= 512) KORE_RMS_BWD(256, 2);
   else if (nvec <= 768) KORE_RMS_BWD(256, 3);
-  else if (nvec <= 1024) KORE_RMS_BWD(256, 4);
-  else KORE_RMS_BWD(128, 8);
+  else KORE_RMS_BWD(256, 4);
 #undef KORE_RMS_BWD
   check_cuda(cudaGetLastError(), "rmsnorm_bwd");
 }
