@@ -206,55 +206,73 @@ __global__ void __launch_bounds__(THREADS) rmsnorm_bwd_kernel(
 
 // ------------------------------------------- q/k per-head RMSNorm + RoPE (fwd)
 // qkv: [T, (Hq + 2*Hkv) * D] raw projections. out: [T, (Hq + Hkv) * D] normed+rotated q,k.
-// One warp per (token, head); D == 128 (4 elements per lane; lane l pairs with l^16).
+// One 256-thread block per token; warp w handles heads w, w + 8, ... (up to
+// kQkMaxHeadsPerWarp each), D == 128 (4 elements per lane; lane l pairs with
+// l^16 for rotate-half). The token's position and its cos/sin row are read
+// once per warp, and all of a warp's head loads are issued before the first
+// reduction, so a warp keeps several rows in flight.
 // cos/sin tables: [max_pos, D/2] fp32.
-__global__ void qk_norm_rope_fwd_kernel(const __nv_bfloat16* __restrict__ qkv,
-                                        const __nv_bfloat16* __restrict__ qw,
-                                        const __nv_bfloat16* __restrict__ kw,
-                                        const int* __restrict__ pos, const float* __restrict__ cos_t,
-                                        const float* __restrict__ sin_t,
-                                        __nv_bfloat16* __restrict__ out, float* __restrict__ rstd,
-                                        int T, int Hq, int Hkv, float eps) {
+constexpr int kQkMaxHeadsPerWarp = 12;   // Hq + Hkv <= 96
+
+__global__ void __launch_bounds__(256) qk_norm_rope_fwd_kernel(
+    const __nv_bfloat16* __restrict__ qkv, const __nv_bfloat16* __restrict__ qw,
+    const __nv_bfloat16* __restrict__ kw, const int* __restrict__ pos, const float* __restrict__ cos_t,
+    const float* __restrict__ sin_t, __nv_bfloat16* __restrict__ out, float* __restrict__ rstd, int T,
+    int Hq, int Hkv, float eps) {
   constexpr int D = 128;
-  const int lane = threadIdx.x & 31;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int heads = Hq + Hkv;
-  const long gw = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
-  if (gw >= (long)T * heads) return;
-  const int t = gw / heads, h = gw % heads;
+  const int t = blockIdx.x;
+  if (t >= T) return;
   const int in_stride = (Hq + 2 * Hkv) * D;
-  const __nv_bfloat16* src = qkv + (size_t)t * in_stride + h * D + lane * 4;
-  float v[4];
-  {
-    uint2 u = *reinterpret_cast<const uint2*>(src);
-    float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.x));
-    float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&u.y));
-    v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+  const __nv_bfloat16* src = qkv + (size_t)t * in_stride + lane * 4;
+  uint2 raw[kQkMaxHeadsPerWarp];
+#pragma unroll
+  for (int i = 0; i < kQkMaxHeadsPerWarp; ++i) {
+    const int h = warp + 8 * i;
+    if (h < heads) raw[i] = __ldg(reinterpret_cast<const uint2*>(src + h * D));
   }
-  float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-  ss = warp_sum(ss);
-  const float rs = rsqrtf(ss / D + eps);
-  if (rstd && lane == 0) rstd[(size_t)t * heads + h] = rs;
-  const __nv_bfloat16* wt = (h < Hq ? qw : kw) + lane * 4;
-  float n[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) n[e] = v[e] * rs * __bfloat162float(wt[e]);
-  // rotate_half: x1 = n[:64], x2 = n[64:]; out1 = x1*c - x2*s; out2 = x2*c + x1*s
-  float partner[4];
-#pragma unroll
-  for (int e = 0; e < 4; ++e) partner[e] = __shfl_xor_sync(0xffffffff, n[e], 16);
   const int p = pos[t];
   const int fi = (lane & 15) * 4;
-  float o[4];
+  const float4 c4 = __ldg(reinterpret_cast<const float4*>(cos_t + (size_t)p * (D / 2) + fi));
+  const float4 s4 = __ldg(reinterpret_cast<const float4*>(sin_t + (size_t)p * (D / 2) + fi));
+  const float cs[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+  float wq[4], wk[4];
 #pragma unroll
   for (int e = 0; e < 4; ++e) {
-    float c = cos_t[(size_t)p * (D / 2) + fi + e];
-    float s = sin_t[(size_t)p * (D / 2) + fi + e];
-    o[e] = lane < 16 ? n[e] * c - partner[e] * s : n[e] * c + partner[e] * s;
+    wq[e] = __bfloat162float(qw[lane * 4 + e]);
+    wk[e] = __bfloat162float(kw[lane * 4 + e]);
   }
-  uint2 u;
-  u.x = pack_bf16(o[0], o[1]);
-  u.y = pack_bf16(o[2], o[3]);
-  *reinterpret_cast<uint2*>(out + (size_t)t * heads * D + h * D + lane * 4) = u;
+#pragma unroll
+  for (int i = 0; i < kQkMaxHeadsPerWarp; ++i) {
+    const int h = warp + 8 * i;
+    if (h >= heads) break;
+    float v[4];
+    {
+      float2 a = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&raw[i].x));
+      float2 b = __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&raw[i].y));
+      v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+    }
+    float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / D + eps);
+    if (rstd && lane == 0) rstd[(size_t)t * heads + h] = rs;
+    const bool is_q = h < Hq;
+    float n[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) n[e] = v[e] * rs * (is_q ? wq[e] : wk[e]);
+    // rotate_half: x1 = n[:64], x2 = n[64:]; out1 = x1*c - x2*s; out2 = x2*c + x1*s
+    float o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffff, n[e], 16);
+      o[e] = lane < 16 ? n[e] * cs[e] - partner * sn[e] : n[e] * cs[e] + partner * sn[e];
+    }
+    uint2 u;
+    u.x = pack_bf16(o[0], o[1]);
+    u.y = pack_bf16(o[2], o[3]);
+    *reinterpret_cast<uint2*>(out + (size_t)t * heads * D + h * D + lane * 4) = u;
+  }
 }
 
 // --------------------------------------------------- q/k norm + RoPE (bwd)
@@ -497,10 +515,12 @@ void qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& qw, const at::Ten
   TORCH_CHECK(pos.scalar_type() == at::kInt && pos.numel() == T, "pos must be int32 [T]");
   if (T == 0) return;
   c10::cuda::CUDAGuard g(qkv.device());
-  const long warps = T * (Hq + Hkv);
-  const int threads = 256;
-  const int grid = (int)((warps * 32 + threads - 1) / threads);
-  qk_norm_rope_fwd_kernel<<<grid, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  TORCH_CHECK(Hq + Hkv <= 8 * kQkMaxHeadsPerWarp, "qk_norm_rope: at most 96 q + k heads");
+  TORCH_CHECK(cos_t.stride(0) == 64 && sin_t.stride(0) == 64 && cos_t.stride(1) == 1 && sin_t.stride(1) == 1 &&
+                  (reinterpret_cast<uintptr_t>(cos_t.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(sin_t.data_ptr()) & 15) == 0,
+              "qk_norm_rope: contiguous, 16-byte aligned [max_pos, 64] fp32 cos/sin tables");
+  qk_norm_rope_fwd_kernel<<<(int)T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (const __nv_bfloat16*)qkv.data_ptr(), (const __nv_bfloat16*)qw.data_ptr(),
       (const __nv_bfloat16*)kw.data_ptr(), pos.data_ptr<int>(), cos_t.data_ptr<float>(),
       sin_t.data_ptr<float>(), (__nv_bfloat16*)out.data_ptr(),
