@@ -98,6 +98,13 @@ void gemm_tp_bf16(const c10::optional<at::Tensor>& a_local, const std::vector<in
 void tp_reduce_norm(const at::Tensor& slots, int64_t W, int64_t R, at::Tensor& x, const c10::optional<at::Tensor>& g,
                     const c10::optional<at::Tensor>& hn, double eps);
 std::vector<int64_t> symm_peer_addrs(int64_t id, int64_t offset);
+void symm_ep_index_push(int64_t id, int64_t index_offset, const at::Tensor& dst_rank, const at::Tensor& dst_row,
+                        int64_t k, int64_t cap);
+void moe_index_pads(at::Tensor& index, const at::Tensor& offsets, const at::Tensor& totals);
+void gemm_grouped_dev_pull(at::Tensor& stage, const at::Tensor& b, at::Tensor& out, const at::Tensor& tiles,
+                           const at::Tensor& ntiles, const std::vector<int64_t>& tok_peers, int64_t lda,
+                           const at::Tensor& index, const at::Tensor& rows_dev, at::Tensor& flags, int64_t epoch,
+                           bool b_mn);
 void symm_gather_ce(int64_t id, int64_t src_offset, int64_t bytes, at::Tensor& dst);
 void nvls_sumsq(int64_t mc_grad, int64_t n, double gscale, at::Tensor& out);
 void nvls_adamw(int64_t mc_grad, int64_t mc_param, const at::Tensor& own_param,
@@ -147,6 +154,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_ep_plan", &kore::moe_ep_plan, "expert-parallel plan from gathered counts (device)");
   m.def("moe_zero_pad_rows", &kore::moe_zero_pad_rows);
   m.def("gemm_grouped_dev", &kore::gemm_grouped_dev, "grouped GEMM over a device tile table");
+  m.def("gemm_grouped_dev_pull", &kore::gemm_grouped_dev_pull,
+        "grouped GEMM with the expert-parallel pull dispatch staged in its prologue");
+  m.def("symm_ep_index_push", &kore::symm_ep_index_push, "pull-dispatch index entries into the owners' heaps");
+  m.def("moe_index_pads", &kore::moe_index_pads, "pad entries of the pull-dispatch index");
   m.def("gemm_grouped_wgrad", &kore::gemm_grouped_wgrad, "per-expert weight gradient, device offsets");
   m.def("moe_route_bwd", &kore::moe_route_bwd);
   m.def("moe_combine", &kore::moe_combine);

@@ -61,6 +61,13 @@ struct Params {
   int ag_epoch = 0;
   int ag_lda = 0;
   int ag_rot = 0;   // M-block rotation so each rank starts on its own (local) rows
+  // expert-parallel pull dispatch (grouped mode): staged row r is a copy of row
+  // (ag_index[r] & 0x3FFFFFF) of peer (ag_index[r] >> 26)'s token buffer
+  // ag_src[peer] (row stride ag_lda), or zeros for ag_index[r] < 0 (pad rows);
+  // only rows [0, min(*ag_rows_dev, ag_cap)) are staged (64-row groups)
+  const int* ag_index = nullptr;
+  const int* ag_rows_dev = nullptr;
+  int ag_cap = 0;
   // tensor-parallel GEMM->reduce-scatter: output row r is stored (P2P) into
   // peer r / rs_rows, slot rs_rank, i.e. rs_out[peer] + (rs_rank*rs_rows + r%rs_rows)*ldc.
   int rs_rows;
@@ -151,7 +158,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (p.ag_flags != nullptr) {
+  // rows of A that the staging copy fills (flag waits never look past them)
+  const int stage_rows = p.ag_index != nullptr ? min(min(*p.ag_rows_dev, p.ag_cap), p.M) : p.M;
+  if (p.ag_flags != nullptr && p.ag_index != nullptr) {
+    // ------------------------------------- expert-parallel pull dispatch copy
+    // 64-row groups round-robin over CTAs; each row comes from the peer and
+    // token row its index entry names (pad rows are zero-filled); 8
+    // outstanding 16-byte loads per thread keep NVLink reads in flight.
+    const int groups = stage_rows / 64;
+    const int vpr = p.K / 8;
+    const int total = 64 * vpr;
+    const int sstride = p.ag_lda / 8;
+    for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ag_stage) + (size_t)g * 64 * p.K);
+      for (int base = threadIdx.x; base < total; base += kThreads * 8) {
+        uint4 buf[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * kThreads;
+          if (idx < total) {
+            const int code = p.ag_index[g * 64 + idx / vpr];
+            if (code < 0) {
+              buf[u] = make_uint4(0, 0, 0, 0);
+            } else {
+              const uint4* src = reinterpret_cast<const uint4*>(p.ag_src[code >> 26]);
+              buf[u] = src[(size_t)(code & 0x3FFFFFF) * sstride + idx % vpr];
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int idx = base + u * kThreads;
+          if (idx < total) dst[(size_t)(idx / vpr) * vpr + idx % vpr] = buf[u];
+        }
+      }
+      fence_proxy_async_global();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        __threadfence();
+        st_release_gpu_s32(&p.ag_flags[g], p.ag_epoch);
+      }
+    }
+  } else if (p.ag_flags != nullptr) {
     // ---------------------------------------------- staged all-gather copy
     // 64-row groups round-robin over CTAs; 8 outstanding 16-byte loads per
     // thread keep enough peer reads in flight to fill the NVLink pipe.
@@ -212,7 +260,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (p.ag_flags != nullptr) {   // staged all-gather: this tile's row groups must be in ag_stage
           bool ready = true;
-          for (int g = m0 / 64; g < min(m0 + BM, p.M) / 64 && ready; ++g)
+          for (int g = m0 / 64; g < min(m0 + BM, stage_rows) / 64 && ready; ++g)
             ready = wait_flag_ge(&p.ag_flags[g], p.ag_epoch);
           if (!ready) { *abort_flag = 1; break; }
           fence_proxy_async_global();    // generic-proxy copies -> TMA reads
@@ -1177,6 +1225,81 @@ void gemm_grouped_dev(const at::Tensor& a, const at::Tensor& b, at::Tensor& out,
   } else {
     if (b_mn) gemm::launch<128, 6, false, true>(ta, tb, tc, p, grid, st);
     else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st);
+  }
+}
+
+// Grouped GEMM with the expert-parallel dispatch in its prologue (pull
+// dispatch): every CTA first copies its share of 64-row groups of the
+// receive buffer ``stage`` [cap, K] from the peers' token buffers (addresses
+// ``tok_peers``, row stride ``lda``) as ``index`` says (int32 [cap]: peer << 26
+// | token row, -1 for pad rows), publishes flags[g] = epoch, and then runs the
+// grouped GEMM of gemm_grouped_dev, each tile's producer waiting (bounded) for
+// its groups. rows_dev: int32 [1] device count of the receive rows in use (the
+// plan's last offset). Cooperative launch: CTAs wait on each other's copies.
+void gemm_grouped_dev_pull(at::Tensor& stage, const at::Tensor& b, at::Tensor& out, const at::Tensor& tiles,
+                           const at::Tensor& ntiles, const std::vector<int64_t>& tok_peers, int64_t lda,
+                           const at::Tensor& index, const at::Tensor& rows_dev, at::Tensor& flags, int64_t epoch,
+                           bool b_mn) {
+  TORCH_CHECK(stage.is_cuda() && b.is_cuda() && out.is_cuda() && stage.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16,
+              "pull grouped gemm: bf16 CUDA tensors");
+  TORCH_CHECK(stage.dim() == 2 && stage.is_contiguous() && b.dim() == 3 && b.is_contiguous() && out.dim() == 2 &&
+                  out.stride(1) == 1, "pull grouped gemm: stage [cap, K] contiguous, b [E,..], out [cap, N]");
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && ntiles.scalar_type() == at::kInt && index.scalar_type() == at::kInt &&
+                  rows_dev.scalar_type() == at::kInt && flags.scalar_type() == at::kInt && tiles.is_cuda() &&
+                  ntiles.is_cuda() && index.is_cuda() && rows_dev.is_cuda() && flags.is_cuda(),
+              "pull grouped gemm: int32 device tables");
+  const int E = b.size(0);
+  const int K = stage.size(1);
+  const long cap_rows = stage.size(0);
+  const int N = b_mn ? b.size(2) : b.size(1);
+  TORCH_CHECK((b_mn ? b.size(1) : b.size(2)) == K, "pull grouped gemm: K mismatch");
+  TORCH_CHECK(out.size(1) == N && out.size(0) == cap_rows, "pull grouped gemm: out shape");
+  TORCH_CHECK(N % 8 == 0 && K % 8 == 0 && out.stride(0) % 8 == 0 && lda % 8 == 0 && lda >= K, "alignment");
+  TORCH_CHECK(cap_rows % 64 == 0 && index.numel() >= cap_rows && flags.numel() >= cap_rows / 64,
+              "pull grouped gemm: cap % 64, index >= cap, flags >= cap / 64");
+  TORCH_CHECK(!tok_peers.empty() && tok_peers.size() <= 8 && epoch > 0, "pull grouped gemm: 1..8 peers, epoch > 0");
+  for (int64_t a : tok_peers) TORCH_CHECK(a % 16 == 0, "pull grouped gemm: peer rows must be 16-byte aligned");
+  const int cap = (int)(tiles.numel() / 4);
+  if (cap == 0) return;
+  c10::cuda::CUDAGuard guard(stage.device());
+  gemm::Params p;
+  p.M = cap * 128; p.N = N; p.K = K;
+  p.alpha = 1.f;
+  p.accumulate = 0;
+  p.out_f32 = 0;
+  p.C_read = out.data_ptr();
+  p.C_write = out.data_ptr();
+  p.ldc = out.stride(0);
+  p.R = nullptr; p.ldr = 0;
+  p.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
+  p.ntiles_dev = ntiles.data_ptr<int>();
+  p.ag_rows = 0; p.rs_rows = 0; p.rs_rank = 0;
+  for (int i = 0; i < 8; ++i) { p.rs_out[i] = nullptr; p.ag_src[i] = nullptr; }
+  for (size_t i = 0; i < tok_peers.size(); ++i) p.ag_src[i] = reinterpret_cast<const void*>(tok_peers[i]);
+  p.ag_stage = stage.data_ptr();
+  p.ag_flags = flags.data_ptr<int>();
+  p.ag_epoch = (int)epoch;
+  p.ag_lda = (int)lda;
+  p.ag_rot = 0;
+  p.ag_index = index.data_ptr<int>();
+  p.ag_rows_dev = rows_dev.data_ptr<int>();
+  p.ag_cap = (int)cap_rows;
+  const bool use256 = N >= 256 && (N % 256 == 0 || N > 1024);
+  const int BN = use256 ? 256 : 128;
+  auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap ta = make_tmap_2d(stage.data_ptr(), bf, 2, K, cap_rows, K, 64, 128);
+  CUtensorMap tb = b_mn ? make_tmap_3d(b.data_ptr(), bf, 2, N, K, E, N, (uint64_t)N * K, 64, 64, 1)
+                        : make_tmap_3d(b.data_ptr(), bf, 2, K, N, E, K, (uint64_t)N * K, 64, BN, 1);
+  CUtensorMap tc = ta;   // grouped epilogue stores directly
+  const int grid = std::min(cap * ((N + BN - 1) / BN), num_sms(stage.get_device()));
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (use256) {
+    if (b_mn) gemm::launch<256, 4, false, true>(ta, tb, tc, p, grid, st, true);
+    else gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, true);
+  } else {
+    if (b_mn) gemm::launch<128, 6, false, true>(ta, tb, tc, p, grid, st, true);
+    else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, true);
   }
 }
 

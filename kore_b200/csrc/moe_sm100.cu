@@ -380,6 +380,15 @@ __global__ void zero_pad_rows_kernel(__nv_bfloat16* __restrict__ buf, const int*
     *reinterpret_cast<uint4*>(buf + a * H + i) = make_uint4(0, 0, 0, 0);
 }
 
+// pad entries [off + total, next offset) of every local expert's block of the
+// pull-dispatch index: -1 (the staging copy zero-fills those rows)
+__global__ void index_pads_kernel(int* __restrict__ index, const int* __restrict__ offsets,
+                                  const int* __restrict__ totals, long cap) {
+  const int el = blockIdx.x;
+  const long a = (long)offsets[el] + totals[el], b = min((long)offsets[el + 1], cap);
+  for (long i = a + threadIdx.x; i < b; i += blockDim.x) index[i] = -1;
+}
+
 inline int warps_grid(long n, int warps_per_block = 8) {
   return (int)((n + warps_per_block - 1) / warps_per_block);
 }
@@ -436,6 +445,17 @@ void moe_zero_pad_rows(at::Tensor& buf, const at::Tensor& offsets, const at::Ten
   moe::zero_pad_rows_kernel<<<El, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       (__nv_bfloat16*)buf.data_ptr(), offsets.data_ptr<int>(), totals.data_ptr<int>(), (int)H);
   check_cuda(cudaGetLastError(), "moe zero pad rows");
+}
+
+void moe_index_pads(at::Tensor& index, const at::Tensor& offsets, const at::Tensor& totals) {
+  TORCH_CHECK(index.scalar_type() == at::kInt && offsets.scalar_type() == at::kInt &&
+                  totals.scalar_type() == at::kInt && index.is_cuda(), "index pads: int32 device tensors");
+  const int El = totals.numel();
+  if (El == 0) return;
+  c10::cuda::CUDAGuard g(index.device());
+  moe::index_pads_kernel<<<El, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      index.data_ptr<int>(), offsets.data_ptr<int>(), totals.data_ptr<int>(), (long)index.numel());
+  check_cuda(cudaGetLastError(), "moe index pads");
 }
 
 void moe_gather_rows(const at::Tensor& x, const at::Tensor& src_row, at::Tensor& out) {

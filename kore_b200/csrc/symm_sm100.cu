@@ -427,6 +427,18 @@ __global__ void ep_scatter_kernel(const __nv_bfloat16* __restrict__ x, const lon
   }
 }
 
+// Pull-dispatch index: pair i (token i / k) tells its owner which row of
+// which rank's token buffer lands in receive row dst_row[i]:
+// owner.index[dst_row[i]] = rank << 26 | (i / k). 4 bytes cross NVLink per pair.
+__global__ void ep_index_push_kernel(PeerPtrs dst, const int* __restrict__ dst_rank,
+                                     const long* __restrict__ dst_row, int n, int k, int rank, long cap) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const long r = dst_row[i];
+  if (r >= cap) return;                      // receive buffer too small: the plan flagged it
+  reinterpret_cast<int*>(dst.p[dst_rank[i]])[r] = (rank << 26) | (i / k);
+}
+
 // Pull-combine from peers: y[t] = sum_j w[t,j] * peer[rank[t,j]][row[t,j]] (+ resid[t]);
 // with dw != nullptr also dw[t,j] = <g[t], peer row> (the combine backward's weight grad).
 __global__ void ep_gather_kernel(PeerPtrs src, const int* __restrict__ rank, const long* __restrict__ row,
@@ -501,6 +513,20 @@ void symm_ep_scatter(int64_t id, int64_t buf_offset, const at::Tensor& x, const 
       (const __nv_bfloat16*)x.data_ptr(), src_row.data_ptr<long>(), dst_rank.data_ptr<int>(),
       dst_row.data_ptr<long>(), scale ? scale->data_ptr<float>() : nullptr, dst, n, H, (long)cap);
   check_cuda(cudaGetLastError(), "ep_scatter");
+}
+
+void symm_ep_index_push(int64_t id, int64_t index_offset, const at::Tensor& dst_rank, const at::Tensor& dst_row,
+                        int64_t k, int64_t cap) {
+  auto& h = *g_heaps.at(id);
+  const int n = dst_rank.numel();
+  TORCH_CHECK(dst_rank.scalar_type() == at::kInt && dst_row.scalar_type() == at::kLong && dst_row.numel() == n,
+              "ep_index_push: dst_rank int32, dst_row int64 of equal length");
+  TORCH_CHECK(index_offset % 4 == 0 && n / k < (1 << 26) && h.world <= 32, "ep_index_push: offsets and ranges");
+  if (n == 0) return;
+  symm::PeerPtrs dst = peer_ptrs(h, index_offset, false);
+  symm::ep_index_push_kernel<<<(n + 255) / 256, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      dst, dst_rank.data_ptr<int>(), dst_row.data_ptr<long>(), n, (int)k, h.rank, (long)cap);
+  check_cuda(cudaGetLastError(), "ep_index_push");
 }
 
 void symm_ep_gather(int64_t id, int64_t buf_offset, const at::Tensor& rank, const at::Tensor& row,

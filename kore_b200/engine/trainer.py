@@ -43,7 +43,7 @@ class CausalLMTrainer:
                  warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
                  weights: Optional[Qwen3Weights] = None, micro_tokens_hint: int = 8192,
                  ep_capacity: float = 2.0, zero_stage: int = 2, recompute: str = "auto",
-                 activation_reserve_gb: float = 12.0, moment_offload: str = "auto"):
+                 activation_reserve_gb: float = 12.0, moment_offload: str = "auto", ep_dispatch: str = "pull"):
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device
@@ -99,10 +99,11 @@ class CausalLMTrainer:
         if self.w.ep is not None:
             from ..parallel.ep import ExpertParallel, FusedExpertParallel
             if fused:
+                from ..parallel.symmetric import SymmetricHeap
                 cap = int(ep_capacity * micro_tokens_hint * cfg.num_experts_per_tok)
-                ehp = __import__("kore_b200.parallel.symmetric", fromlist=["SymmetricHeap"]).SymmetricHeap(
-                    self.ctx, 4 * cap * cfg.hidden_size * 2 + (1 << 20))
-                self.eng.ep = FusedExpertParallel(self.ctx, cfg, self.w.expert_lo, self.w.expert_hi, ehp, cap)
+                ehp = SymmetricHeap(self.ctx, FusedExpertParallel.heap_bytes(cfg, cap, ep_dispatch) + (1 << 20))
+                self.eng.ep = FusedExpertParallel(self.ctx, cfg, self.w.expert_lo, self.w.expert_hi, ehp, cap,
+                                                  dispatch=ep_dispatch)
             else:
                 self.eng.ep = ExpertParallel(self.ctx, cfg, self.w.expert_lo, self.w.expert_hi)
         if master == "auto":

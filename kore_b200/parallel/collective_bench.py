@@ -15,9 +15,11 @@ baselines, each reported against its roofline (run under torchrun, >= 2 GPUs):
     reduce-scatter (P2P-store epilogue + fused reduce) versus GEMM + NCCL
     reduce-scatter. Roofline: max(FLOPs / measured bf16 peak, NVLink bytes /
     link bandwidth).
-(d) MoE dispatch and combine (P2P scatter into the owners' expert-major
-    buffers; pull-combine with routing weights and residual) versus permute +
-    NCCL all-to-all. Roofline: the token rows crossing NVLink at link bandwidth.
+(d) MoE dispatch fused with the gate/up grouped GEMM (the GEMM pulls its
+    receive rows from the peers in its prologue) versus P2P push + GEMM and
+    versus NCCL all-to-all + GEMM; pull-combine with routing weights and
+    residual versus NCCL all-to-all back. Rooflines: max(GEMM FLOPs at the
+    measured bf16 peak, token rows over NVLink at link bandwidth).
 
 Every number is CUDA-event time on the launching stream after warm-up, max
 over ranks. Prints one JSON line per path from rank 0.
@@ -159,32 +161,41 @@ def bench_tp(ctx, rows: int, K: int, N_local: int) -> list:
 
 
 def bench_ep(ctx, tokens: int) -> list:
-    """(d) MoE dispatch / combine for the Qwen3-Coder-30B-A3B shape (H 2048,
-    128 experts, top-8): fused P2P scatter into the owners' expert-major
-    buffers vs permute + NCCL all-to-all; fused pull-combine with the routing
-    weights and residual vs NCCL all-to-all back + weighted sum."""
+    """(d) MoE for the Qwen3-Coder-30B-A3B shape (H 2048, 128 experts, top-8,
+    expert FFN 768): dispatch + the gate/up grouped GEMM, three ways:
+    pull (index push, one barrier, the GEMM stages its receive rows from the
+    peers in its prologue), push (P2P scatter, barrier, pad zeroing, grouped
+    GEMM) and NCCL (all-to-all of the rows, then the same grouped GEMM);
+    then the combine: fused pull-combine with the routing weights and
+    residual versus NCCL all-to-all back + weighted sum. Roofline of dispatch
+    + GEMM: max(GEMM FLOPs at the measured bf16 peak, token rows over NVLink
+    at link bandwidth); of the combine: the rows over NVLink."""
     from .. import ops
     from ..models.config import qwen3_coder_30b_a3b
+    from ..ops import moe as moe_ops
     from .ep import FusedExpertParallel
     from .symmetric import SymmetricHeap
     C = ops.native()
     cfg = qwen3_coder_30b_a3b()
     W, r = ctx.world, ctx.rank
-    E, k, H = cfg.num_experts, cfg.num_experts_per_tok, cfg.hidden_size
+    E, k, H, I = cfg.num_experts, cfg.num_experts_per_tok, cfg.hidden_size, cfg.moe_intermediate_size
     El = E // W
     cap = int(2.0 * tokens * k)
-    heap = SymmetricHeap(ctx, 4 * cap * H * 2 + (1 << 20))
-    fep = FusedExpertParallel(ctx, cfg, r * El, (r + 1) * El, heap, cap)
+    heap = SymmetricHeap(ctx, FusedExpertParallel.heap_bytes(cfg, cap, "pull") + (1 << 20))
+    fep = FusedExpertParallel(ctx, cfg, r * El, (r + 1) * El, heap, cap, dispatch="pull")
+    fep.k = k
     g = torch.Generator(device="cuda").manual_seed(11 + r)
     logits = torch.randn(tokens, E, device="cuda", generator=g)
     wts, idx = torch.softmax(logits, -1).topk(k, -1)
     wts = (wts / wts.sum(-1, keepdim=True)).float().contiguous()
+    idx = idx.int().contiguous()
     x = torch.randn(tokens, H, device="cuda", dtype=torch.bfloat16)
-    dst_rank, dst_row, offs, rmax = fep._route_rows(idx)
-    fep.ybuf.zero_()
-    src_row = torch.arange(tokens * k, device="cuda") // k
+    wgu = torch.randn(El, 2 * I, H, device="cuda", dtype=torch.bfloat16) * 0.02
+    pl = fep._plan(idx)
     y = torch.empty_like(x)
+    _, peak_flops = _peaks()
     # NCCL arm: rows grouped by destination rank; split sizes exchanged once, outside the timing
+    dst_rank = pl["dst_rank"]
     order = torch.argsort(dst_rank.long(), stable=True)
     send = torch.bincount(dst_rank.long(), minlength=W)
     recv = torch.empty_like(send)
@@ -192,19 +203,28 @@ def bench_ep(ctx, tokens: int) -> list:
     ss, rs_ = send.tolist(), recv.tolist()
     rbuf = torch.empty(sum(rs_), H, device="cuda", dtype=torch.bfloat16)
     back = torch.empty(tokens * k, H, device="cuda", dtype=torch.bfloat16)
+    src_row = torch.arange(tokens * k, device="cuda") // k
+    xp = fep.recv[: fep.cap * H].view(fep.cap, H)
+    gu = torch.empty(fep.cap, 2 * I, device="cuda", dtype=torch.bfloat16)
+    Wd = {"experts_gate_up": wgu}
 
-    def disp_fused():
-        C.symm_ep_scatter(heap.id, fep.o_recv, x, src_row, dst_rank, dst_row, None)
-        heap.barrier()
+    def disp_pull():
+        fep._pull_and_up(Wd, x, pl)
+
+    def disp_push():
+        fep.dispatch = "push"
+        fep._dispatch_and_up(Wd, x, pl)
+        fep.dispatch = "pull"
 
     def disp_nccl():
         sbuf = x.index_select(0, src_row[order])
         dist.all_to_all_single(rbuf, sbuf, rs_, ss, group=ctx.group)
+        moe_ops.plan_mm(xp, wgu, pl["plan"], out=gu)
 
     def comb_fused():
         heap.barrier()
-        C.symm_ep_gather(heap.id, fep.o_y, dst_rank.view(tokens, k), dst_row.view(tokens, k), wts, x, y, None,
-                         None, H)
+        C.symm_ep_gather(heap.id, fep.o_y, dst_rank.view(tokens, k), pl["dst_row"].view(tokens, k), wts, x, y,
+                         None, None, H)
 
     def comb_nccl():
         dist.all_to_all_single(back, rbuf, ss, rs_, group=ctx.group)
@@ -212,14 +232,31 @@ def bench_ep(ctx, tokens: int) -> list:
         rows[order] = back
         torch.add(x, (rows.view(tokens, k, H).float() * wts[..., None]).sum(1).to(x.dtype), out=y)
 
+    # the pulled receive rows and GEMM output equal the pushed ones
+    fep.dispatch = "push"
+    xp_push, gu_push = fep._dispatch_and_up(Wd, x, pl)
+    xp_push, gu_push = xp_push.clone(), gu_push.clone()
+    fep.dispatch = "pull"
+    xp_pull, gu_pull = fep._pull_and_up(Wd, x, pl)
+    used = int(pl["plan"].offsets[-1])
+    same = bool(torch.equal(xp_pull[:used], xp_push[:used]) and torch.equal(gu_pull[:used], gu_push[:used]))
     link = 2.0 * tokens * k * H * (W - 1) / W
+    flops = 2.0 * tokens * k * H * 2 * I              # gate/up GEMM rows received per rank (balanced routing)
     res = []
-    for name, ff, fn in (("d_moe_dispatch", disp_fused, disp_nccl), ("d_moe_combine", comb_fused, comb_nccl)):
-        tf, tn = _time(ff, ctx), _time(fn, ctx)
-        roof = link / LINK_BPS * 1e3
-        res.append({"path": name, "world": W, "tokens": tokens, "H": H, "topk": k, "fused_ms": tf, "nccl_ms": tn,
-                    "roofline_ms": roof, "fused_frac_of_roofline": roof / tf, "nccl_frac_of_roofline": roof / tn,
-                    "speedup_vs_nccl": tn / tf})
+    tp, tpush, tn = _time(disp_pull, ctx), _time(disp_push, ctx), _time(disp_nccl, ctx)
+    roof = max(link / LINK_BPS, flops / peak_flops) * 1e3
+    res.append({"path": "d_moe_dispatch_gateup", "world": W, "tokens": tokens, "H": H, "topk": k,
+                "pull_fused_ms": tp, "push_ms": tpush, "nccl_ms": tn, "roofline_ms": roof,
+                "pull_frac_of_roofline": roof / tp, "push_frac_of_roofline": roof / tpush,
+                "nccl_frac_of_roofline": roof / tn, "pull_speedup_vs_nccl": tn / tp,
+                "pull_speedup_vs_push": tpush / tp, "pull_equals_push": same})
+    tf, tn = _time(comb_fused, ctx), _time(comb_nccl, ctx)
+    roof = link / LINK_BPS * 1e3
+    res.append({"path": "d_moe_combine", "world": W, "tokens": tokens, "H": H, "topk": k, "fused_ms": tf,
+                "nccl_ms": tn, "roofline_ms": roof, "fused_frac_of_roofline": roof / tf,
+                "nccl_frac_of_roofline": roof / tn, "speedup_vs_nccl": tn / tf})
+    from ..ops import check_device_error
+    res[-1]["device_error"] = check_device_error()
     return res
 
 
@@ -230,13 +267,18 @@ def main(argv=None) -> int:
     ap.add_argument("--units", type=int, default=8)
     ap.add_argument("--rows", type=int, default=2048, help="TP rows per rank")
     ap.add_argument("--ep-tokens", type=int, default=8192, help="MoE tokens per rank")
+    ap.add_argument("--only", default="", choices=["", "optimizer", "tp", "ep"])
     a = ap.parse_args(argv)
     ctx = init_distributed()
-    out = [bench_optimizer(ctx, a.params, a.units)]
     W = ctx.world
-    out += bench_tp(ctx, a.rows, 5120, (40 + 16) * 128 // W)    # QKV projection of the 14B model
-    out += bench_tp(ctx, a.rows, 5120, 2 * 17408 // W)          # gate|up projection
-    out += bench_ep(ctx, a.ep_tokens)
+    out = []
+    if a.only in ("", "optimizer"):
+        out.append(bench_optimizer(ctx, a.params, a.units))
+    if a.only in ("", "tp"):
+        out += bench_tp(ctx, a.rows, 5120, (40 + 16) * 128 // W)    # QKV projection of the 14B model
+        out += bench_tp(ctx, a.rows, 5120, 2 * 17408 // W)          # gate|up projection
+    if a.only in ("", "ep"):
+        out += bench_ep(ctx, a.ep_tokens)
     if ctx.is_main:
         for r in out:
             print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}), flush=True)

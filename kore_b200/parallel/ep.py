@@ -139,9 +139,17 @@ class FusedExpertParallel(ExpertParallel):
     host; a receive buffer that is too small sets a device flag that
     ``check_overflow`` reads once per optimizer step.
 
-    Dispatch: every rank stores its token rows straight into the owners'
-    receive buffers with NVLink P2P stores; the owner zeroes its pad rows and
-    runs the grouped tcgen05 expert GEMMs over the device tile table. Combine:
+    Dispatch (``dispatch="pull"``, the default): every rank copies its token
+    rows into its heap token buffer and pushes one 4-byte index entry per
+    (token, expert) pair into the owner's heap index (which rank, which
+    token row, at the pair's receive row); after one device barrier the
+    owner's gate/up grouped GEMM stages the receive buffer itself in its
+    prologue: each CTA pulls 64-row groups from the peers' token buffers over
+    NVLink (pad rows zero-filled), publishes a per-group flag, and the tiles
+    start as soon as their groups are in, so each token row crosses NVLink
+    once, inside the GEMM launch. ``dispatch="push"``: every rank stores its
+    token rows straight into the owners' receive buffers with P2P stores, then
+    a barrier, a pad-zeroing pass and the grouped GEMM. Combine:
     each source rank pulls its pairs' expert outputs from the owners' heaps and
     reduces them with the routing weights and the residual in the same kernel.
     Backward: the expert side is recomputed from the saved token rows (one more
@@ -151,8 +159,10 @@ class FusedExpertParallel(ExpertParallel):
     barriers (epoch flags) order the phases.
     """
 
-    def __init__(self, ctx, cfg, lo, hi, heap, cap_rows: int):
+    def __init__(self, ctx, cfg, lo, hi, heap, cap_rows: int, dispatch: str = "pull"):
         super().__init__(ctx, cfg, lo, hi)
+        if dispatch not in ("pull", "push"):
+            raise ValueError("dispatch must be pull|push")
         H = cfg.hidden_size
         I = cfg.moe_intermediate_size
         self.heap = heap
@@ -163,6 +173,24 @@ class FusedExpertParallel(ExpertParallel):
         self.o_dx, self.dxbuf = heap.alloc(self.cap * H)
         self.H, self.I = H, I
         self.overflow = torch.zeros(1, dtype=torch.int32, device=ctx.device)
+        self.dispatch = dispatch
+        if dispatch == "pull":
+            self.tok_rows = max(1, self.cap // max(1, cfg.num_experts_per_tok))
+            self.o_tok, self.tok = heap.alloc(self.tok_rows * H)
+            self.o_index, self.index = heap.alloc(self.cap, dtype=torch.int32)
+            self.tok_peers = ops.native().symm_peer_addrs(heap.id, self.o_tok)
+            self.flags = torch.zeros(self.cap // 64, dtype=torch.int32, device=ctx.device)
+            self._stage_epoch = 0
+
+    @staticmethod
+    def heap_bytes(cfg, cap_rows: int, dispatch: str = "pull") -> int:
+        """Symmetric-heap bytes the buffers of ``cap_rows`` receive rows need."""
+        cap = int(cap_rows) // 64 * 64
+        H = cfg.hidden_size
+        n = 4 * cap * H * 2 + 4 * 256
+        if dispatch == "pull":
+            n += max(1, cap // max(1, cfg.num_experts_per_tok)) * H * 2 + cap * 4 + 2 * 256
+        return n
 
     def _plan(self, idx):
         T, k = idx.shape
@@ -190,7 +218,9 @@ class FusedExpertParallel(ExpertParallel):
             raise RuntimeError("expert-parallel receive buffer overflow: raise ep_capacity")
 
     def _dispatch_and_up(self, W, hn2, pl):
-        """Rows to the owners, pad rows zeroed, gate/up GEMM + SwiGLU on the receive buffer."""
+        """Rows to the owners, pad rows zeroed, gate/up GEMM on the receive buffer."""
+        if self.dispatch == "pull" and hn2.shape[0] <= self.tok_rows:
+            return self._pull_and_up(W, hn2, pl)
         C = ops.native()
         T, k = pl["dst_rank"].numel() // self.k, self.k
         src_row = torch.arange(T * k, device=hn2.device) // k
@@ -199,6 +229,24 @@ class FusedExpertParallel(ExpertParallel):
         xp = self.recv[: self.cap * self.H].view(self.cap, self.H)
         C.moe_zero_pad_rows(xp, pl["plan"].offsets, pl["plan"].counts, self.H)
         gu = moe.plan_mm(xp, W["experts_gate_up"], pl["plan"])
+        return xp, gu
+
+    def _pull_and_up(self, W, hn2, pl):
+        """Pull dispatch: index entries to the owners, then the gate/up grouped
+        GEMM that stages its own receive rows from the peers' token buffers."""
+        C = ops.native()
+        T, H = hn2.shape
+        self.tok[: T * H].view(T, H).copy_(hn2)
+        C.symm_ep_index_push(self.heap.id, self.o_index, pl["dst_rank"], pl["dst_row"], self.k, self.cap)
+        plan = pl["plan"]
+        C.moe_index_pads(self.index, plan.offsets, plan.counts)
+        self.heap.barrier()                                   # every rank's token rows and index entries are in
+        xp = self.recv[: self.cap * H].view(self.cap, H)
+        wgu = W["experts_gate_up"]
+        gu = torch.empty(self.cap, wgu.shape[1], dtype=hn2.dtype, device=hn2.device)
+        self._stage_epoch += 1
+        C.gemm_grouped_dev_pull(xp, wgu, gu, plan.tiles, plan.ntiles, self.tok_peers, H, self.index,
+                                plan.offsets[-1:], self.flags, self._stage_epoch, False)
         return xp, gu
 
     def forward(self, eng, W, hn2, x2, probs, idx, wts):

@@ -24,12 +24,51 @@ import time
 import torch
 
 
+def check_ep(ctx, g) -> bool:
+    """Expert parallelism: three training steps over NCCL all-to-all, over the
+    fused push dispatch and over the fused pull dispatch (the gate/up GEMM
+    stages its receive rows from the peers) agree in loss and expert weights."""
+    from ..engine.trainer import CausalLMTrainer
+    from ..models import Qwen3Config
+    from ..ops import check_device_error
+    ok = True
+    mcfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
+                       num_attention_heads=4, num_key_value_heads=2, head_dim=128, model_type="qwen3_moe",
+                       num_experts=8 * ctx.world, num_experts_per_tok=4, moe_intermediate_size=256,
+                       max_position_embeddings=2048)
+    ids_m = torch.randint(0, mcfg.vocab_size, (ctx.world * 2, 256), generator=g)[ctx.rank * 2:(ctx.rank + 1) * 2].cuda()
+    mres = {}
+    for comm, disp in (("nccl", "pull"), ("fused", "push"), ("fused", "pull")):
+        tr = CausalLMTrainer(mcfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm=comm, master="fp32",
+                             micro_tokens_hint=512, ep_dispatch=disp)
+        losses = [tr.train_step_device(ids_m) for _ in range(3)]
+        torch.cuda.synchronize()
+        key = comm if comm == "nccl" else f"fused_{disp}"
+        mres[key] = ([float(l) for l in losses], [b.float().clone() for b in tr.w.expert_bufs.values()])
+        del tr
+    err2 = check_device_error()
+    for key in ("fused_push", "fused_pull"):
+        mok = all(abs(a - b) < 2e-2 * max(1.0, abs(a)) for a, b in zip(mres["nccl"][0], mres[key][0]))
+        for a, b in zip(mres["nccl"][1], mres[key][1]):
+            mok = mok and torch.allclose(a, b, atol=2e-2, rtol=0)
+        if ctx.is_main:
+            print(json.dumps({"check": f"ep_{key}_vs_nccl", "world": ctx.world, "ok": mok and err2 == 0,
+                              "loss_nccl": mres["nccl"][0], "loss_fused": mres[key][0], "device_error": err2}),
+                  flush=True)
+        ok = ok and mok
+    return ok and err2 == 0
+
+
 def main(argv=None):
     from ..engine.trainer import CausalLMTrainer
     from ..models import Qwen3Config
     from .dist import init_distributed
 
     ctx = init_distributed()
+    if os.environ.get("KORE_SELFTEST_ONLY") == "ep":      # the expert-parallel check alone
+        ok = check_ep(ctx, torch.Generator().manual_seed(123))
+        torch.distributed.barrier()
+        return 0 if ok else 1
     cfg = Qwen3Config(vocab_size=4096, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
                       num_attention_heads=4, num_key_value_heads=2, head_dim=128, max_position_embeddings=2048)
     g = torch.Generator().manual_seed(123)
@@ -114,27 +153,9 @@ def main(argv=None):
                           "loss_nccl": l3, "loss_ce_gather": l3f, "device_error": errz}), flush=True)
     ok = ok and z3f and errz == 0
     # expert parallelism: NCCL all-to-all vs fused peer-memory dispatch/combine
-    mcfg = Qwen3Config(vocab_size=2048, hidden_size=512, intermediate_size=1024, num_hidden_layers=2,
-                       num_attention_heads=4, num_key_value_heads=2, head_dim=128, model_type="qwen3_moe",
-                       num_experts=8 * ctx.world, num_experts_per_tok=4, moe_intermediate_size=256,
-                       max_position_embeddings=2048)
-    ids_m = torch.randint(0, mcfg.vocab_size, (ctx.world * 2, 256), generator=g)[ctx.rank * 2:(ctx.rank + 1) * 2].cuda()
-    mres = {}
-    for comm in ("nccl", "fused"):
-        tr = CausalLMTrainer(mcfg, ctx, lr=1e-3, max_grad_norm=1.0, seed=0, comm=comm, master="fp32",
-                             micro_tokens_hint=512)
-        losses = [tr.train_step_device(ids_m) for _ in range(3)]
-        torch.cuda.synchronize()
-        mres[comm] = ([float(l) for l in losses], [b.float().clone() for b in tr.w.expert_bufs.values()])
-        del tr
-    mok = all(abs(a - b) < 2e-2 * max(1.0, abs(a)) for a, b in zip(mres["nccl"][0], mres["fused"][0]))
-    for a, b in zip(mres["nccl"][1], mres["fused"][1]):
-        mok = mok and torch.allclose(a, b, atol=2e-2, rtol=0)
-    err2 = check_device_error()
-    if ctx.is_main:
-        print(json.dumps({"check": "ep_fused_vs_nccl", "world": ctx.world, "ok": mok and err2 == 0,
-                          "loss_nccl": mres["nccl"][0], "loss_fused": mres["fused"][0], "device_error": err2}),
-              flush=True)
+    mok = check_ep(ctx, g)
+    err2 = 0
+    ok = ok and mok
     # tensor-parallel rollout (AG->GEMM / GEMM->RS over peer memory) vs the 1-GPU engine
     from ..engine.rollout import GenRequest, RolloutEngine
     from ..models import Qwen3Weights

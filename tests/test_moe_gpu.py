@@ -109,3 +109,42 @@ def test_device_plan_grouped_and_wgrad_vs_cpu():
     moe.plan_wgrad(dy.cuda(), xp_g, pg, gw_g)
     assert _rel(gw_g.cpu(), gw_c) < 1e-2
     assert float(gw_g[7].abs().sum()) == 0.0          # expert without rows: untouched
+
+
+def test_pull_dispatch_grouped_gemm_matches_gathered():
+    """The grouped GEMM that stages its own receive rows in its prologue (the
+    expert-parallel pull dispatch, here with this GPU as the only peer) gives
+    the same expert outputs as gathering the rows first and running the
+    grouped GEMM, on two calls in a row (the per-group flags are epoch-tagged)."""
+    from kore_b200.ops import check_device_error, native
+    from kore_b200.ops import moe as M
+    from kore_b200.parallel.dist import DistContext
+    from kore_b200.parallel.symmetric import SymmetricHeap
+    C = native()
+    torch.manual_seed(5)
+    T, H, E, k, N = 300, 256, 8, 2, 512
+    ctx = DistContext(device=torch.device("cuda"))
+    idx = torch.randint(0, E, (T, k), device="cuda", dtype=torch.int32)
+    w = (torch.randn(E, N, H, device="cuda") * 0.05).bfloat16()
+    p = M.plan(idx, E)
+    cap = (p.rows + 63) // 64 * 64
+    heap = SymmetricHeap(ctx, T * H * 2 + cap * 4 + (1 << 16))
+    o_tok, tok = heap.alloc(T * H)
+    peers = C.symm_peer_addrs(heap.id, o_tok)
+    index = torch.full((cap,), -1, dtype=torch.int32, device="cuda")
+    index[: p.rows] = p.src_row                        # this rank (0) << 26 | token row; -1 = pad
+    flags = torch.zeros(cap // 64, dtype=torch.int32, device="cuda")
+    stage = torch.empty(cap, H, dtype=torch.bfloat16, device="cuda")
+    used = int(p.offsets[-1])
+    for epoch in (1, 2):
+        x = torch.randn(T, H, device="cuda").bfloat16()
+        tok.view(T, H).copy_(x)
+        stage.fill_(float("nan"))                       # every staged row must be written, pads as zeros
+        out = torch.empty(cap, N, dtype=torch.bfloat16, device="cuda")
+        C.gemm_grouped_dev_pull(stage, w, out, p.tiles, p.ntiles, peers, H, index, p.offsets[-1:], flags, epoch,
+                                False)
+        ref = M.plan_mm(M.plan_gather(x, p), w, p)
+        torch.cuda.synchronize()
+        assert check_device_error() == 0
+        assert torch.equal(stage[:used], M.plan_gather(x, p)[:used])
+        assert torch.allclose(out[:used].float(), ref[:used].float(), atol=2e-2, rtol=2e-2)
