@@ -34,6 +34,10 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 constexpr int kEpiWarps = 4;
+// expert-parallel pull dispatch: four more warps per CTA stage the receive
+// rows while the producer, MMA and epilogue warps run the GEMM
+constexpr int kCopyWarps = 4;
+constexpr int kThreadsPull = kThreads + 32 * kCopyWarps;
 constexpr int kStageBytesC = 32 * 128;  // one epilogue staging buffer: 32 rows x 128 B
 
 struct Params {
@@ -116,7 +120,7 @@ KORE_DEV void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
 }
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreadsPull, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const __grid_constant__ CUtensorMap tmC, Params p) {
   using S = Smem<BN, STAGES>;
@@ -160,46 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // rows of A that the staging copy fills (flag waits never look past them)
   const int stage_rows = p.ag_index != nullptr ? min(min(*p.ag_rows_dev, p.ag_cap), p.M) : p.M;
-  if (p.ag_flags != nullptr && p.ag_index != nullptr) {
-    // ------------------------------------- expert-parallel pull dispatch copy
-    // 64-row groups round-robin over CTAs; each row comes from the peer and
-    // token row its index entry names (pad rows are zero-filled); 8
-    // outstanding 16-byte loads per thread keep NVLink reads in flight.
-    const int groups = stage_rows / 64;
-    const int vpr = p.K / 8;
-    const int total = 64 * vpr;
-    const int sstride = p.ag_lda / 8;
-    for (int g = blockIdx.x; g < groups; g += gridDim.x) {
-      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ag_stage) + (size_t)g * 64 * p.K);
-      for (int base = threadIdx.x; base < total; base += kThreads * 8) {
-        uint4 buf[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int idx = base + u * kThreads;
-          if (idx < total) {
-            const int code = p.ag_index[g * 64 + idx / vpr];
-            if (code < 0) {
-              buf[u] = make_uint4(0, 0, 0, 0);
-            } else {
-              const uint4* src = reinterpret_cast<const uint4*>(p.ag_src[code >> 26]);
-              buf[u] = src[(size_t)(code & 0x3FFFFFF) * sstride + idx % vpr];
-            }
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          const int idx = base + u * kThreads;
-          if (idx < total) dst[(size_t)(idx / vpr) * vpr + idx % vpr] = buf[u];
-        }
-      }
-      fence_proxy_async_global();
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        __threadfence();
-        st_release_gpu_s32(&p.ag_flags[g], p.ag_epoch);
-      }
-    }
-  } else if (p.ag_flags != nullptr) {
+  if (p.ag_flags != nullptr && p.ag_index == nullptr) {
     // ---------------------------------------------- staged all-gather copy
     // 64-row groups round-robin over CTAs; 8 outstanding 16-byte loads per
     // thread keep enough peer reads in flight to fill the NVLink pipe.
@@ -342,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + kEpiWarps) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int lane = threadIdx.x & 31;
@@ -494,6 +459,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) tma_store_wait_all<0>();
     __syncwarp();
+  } else if (p.ag_index != nullptr) {
+    // ------------------------------------- expert-parallel pull dispatch copy
+    // (copy warps, launched only in this mode) 64-row groups round-robin over
+    // CTAs, in the order the tiles consume them; each row comes from the peer
+    // and token row its index entry names (pad rows are zero-filled). The
+    // group's 64 entries are read once into shared memory; 16 outstanding
+    // 16-byte loads per thread keep NVLink reads in flight. A group's flag is
+    // released after its rows are written; tiles wait for their groups.
+    __shared__ int s_codes[64];
+    const int ct = threadIdx.x - 32 * (2 + kEpiWarps);     // 0 .. 32 * kCopyWarps - 1
+    constexpr int CT = 32 * kCopyWarps;
+    const int groups = stage_rows / 64;
+    const int vpr = p.K / 8;
+    const int total = 64 * vpr;
+    const int sstride = p.ag_lda / 8;
+    for (int g = blockIdx.x; g < groups; g += gridDim.x) {
+      uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.ag_stage) + (size_t)g * 64 * p.K);
+      asm volatile("bar.sync 1, %0;" ::"r"(CT));           // the previous group's entries are no longer read
+      if (ct < 64) s_codes[ct] = p.ag_index[g * 64 + ct];
+      asm volatile("bar.sync 1, %0;" ::"r"(CT));
+      for (int base = ct; base < total; base += CT * 16) {
+        uint4 buf[16];
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int idx = base + u * CT;
+          if (idx < total) {
+            const int code = s_codes[idx / vpr];
+            if (code < 0) {
+              buf[u] = make_uint4(0, 0, 0, 0);
+            } else {
+              const uint4* src = reinterpret_cast<const uint4*>(p.ag_src[code >> 26]);
+              buf[u] = src[(size_t)(code & 0x3FFFFFF) * sstride + idx % vpr];
+            }
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          const int idx = base + u * CT;
+          if (idx < total) dst[(size_t)(idx / vpr) * vpr + idx % vpr] = buf[u];
+        }
+      }
+      fence_proxy_async_global();
+      asm volatile("bar.sync 1, %0;" ::"r"(CT));
+      if (ct == 0) {
+        __threadfence();
+        st_release_gpu_s32(&p.ag_flags[g], p.ag_epoch);
+      }
+    }
   }
 
   tc_fence_before();
@@ -506,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int BN, int STAGES, bool A_MN, bool B_MN>
 void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const Params& p,
-            int grid, cudaStream_t stream, bool cooperative = false) {
+            int grid, cudaStream_t stream, bool cooperative = false, int threads = kThreads) {
   auto k = gemm_kernel<BN, STAGES, A_MN, B_MN>;
   constexpr int smem = Smem<BN, STAGES>::TOTAL;
   static bool attr_set[64] = {};  // per template instance and device
@@ -522,11 +535,11 @@ void launch(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
     CUtensorMap a = ta, b = tb, c = tc;
     Params pp = p;
     void* args[] = {&a, &b, &c, &pp};
-    check_cuda(cudaLaunchCooperativeKernel((const void*)k, dim3(grid), dim3(kThreads), args, smem, stream),
+    check_cuda(cudaLaunchCooperativeKernel((const void*)k, dim3(grid), dim3(threads), args, smem, stream),
                "gemm cooperative launch");
     return;
   }
-  k<<<grid, kThreads, smem, stream>>>(ta, tb, tc, p);
+  k<<<grid, threads, smem, stream>>>(ta, tb, tc, p);
   check_cuda(cudaGetLastError(), "gemm launch");
 }
 
@@ -1294,12 +1307,13 @@ void gemm_grouped_dev_pull(at::Tensor& stage, const at::Tensor& b, at::Tensor& o
   CUtensorMap tc = ta;   // grouped epilogue stores directly
   const int grid = std::min(cap * ((N + BN - 1) / BN), num_sms(stage.get_device()));
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  constexpr int thr = gemm::kThreadsPull;
   if (use256) {
-    if (b_mn) gemm::launch<256, 4, false, true>(ta, tb, tc, p, grid, st, true);
-    else gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, true);
+    if (b_mn) gemm::launch<256, 4, false, true>(ta, tb, tc, p, grid, st, true, thr);
+    else gemm::launch<256, 4, false, false>(ta, tb, tc, p, grid, st, true, thr);
   } else {
-    if (b_mn) gemm::launch<128, 6, false, true>(ta, tb, tc, p, grid, st, true);
-    else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, true);
+    if (b_mn) gemm::launch<128, 6, false, true>(ta, tb, tc, p, grid, st, true, thr);
+    else gemm::launch<128, 6, false, false>(ta, tb, tc, p, grid, st, true, thr);
   }
 }
 
