@@ -43,7 +43,7 @@ class CausalLMTrainer:
                  warmup_steps: int = 0, total_steps: int = 1, comm: str = "nccl",
                  weights: Optional[Qwen3Weights] = None, micro_tokens_hint: int = 8192,
                  ep_capacity: float = 2.0, zero_stage: int = 2, recompute: str = "auto",
-                 activation_reserve_gb: float = 12.0, moment_offload: str = "auto", ep_dispatch: str = "pull"):
+                 activation_reserve_gb: float = 12.0, moment_offload: str = "auto", ep_dispatch: str = "push"):
         self.ctx = ctx or get_context()
         self.cfg = cfg
         dev = self.ctx.device

@@ -139,7 +139,10 @@ class FusedExpertParallel(ExpertParallel):
     host; a receive buffer that is too small sets a device flag that
     ``check_overflow`` reads once per optimizer step.
 
-    Dispatch (``dispatch="pull"``, the default): every rank copies its token
+    Dispatch, two forms. ``dispatch="push"`` (the default, measured faster):
+    every rank stores its token rows straight into the owners' receive
+    buffers with P2P stores, then a barrier, a pad-zeroing pass and the
+    grouped GEMM. ``dispatch="pull"``: every rank copies its token
     rows into its heap token buffer and pushes one 4-byte index entry per
     (token, expert) pair into the owner's heap index (which rank, which
     token row, at the pair's receive row); after one device barrier the
@@ -147,9 +150,9 @@ class FusedExpertParallel(ExpertParallel):
     prologue: each CTA pulls 64-row groups from the peers' token buffers over
     NVLink (pad rows zero-filled), publishes a per-group flag, and the tiles
     start as soon as their groups are in, so each token row crosses NVLink
-    once, inside the GEMM launch. ``dispatch="push"``: every rank stores its
-    token rows straight into the owners' receive buffers with P2P stores, then
-    a barrier, a pad-zeroing pass and the grouped GEMM. Combine:
+    once, inside the GEMM launch. On B200 the pull form measured slower than
+    push + GEMM (the in-kernel copy warps slow the tiles more than a separate
+    full-occupancy copy pass costs), so it is kept as an option. Combine:
     each source rank pulls its pairs' expert outputs from the owners' heaps and
     reduces them with the routing weights and the residual in the same kernel.
     Backward: the expert side is recomputed from the saved token rows (one more
@@ -159,7 +162,7 @@ class FusedExpertParallel(ExpertParallel):
     barriers (epoch flags) order the phases.
     """
 
-    def __init__(self, ctx, cfg, lo, hi, heap, cap_rows: int, dispatch: str = "pull"):
+    def __init__(self, ctx, cfg, lo, hi, heap, cap_rows: int, dispatch: str = "push"):
         super().__init__(ctx, cfg, lo, hi)
         if dispatch not in ("pull", "push"):
             raise ValueError("dispatch must be pull|push")
@@ -183,7 +186,7 @@ class FusedExpertParallel(ExpertParallel):
             self._stage_epoch = 0
 
     @staticmethod
-    def heap_bytes(cfg, cap_rows: int, dispatch: str = "pull") -> int:
+    def heap_bytes(cfg, cap_rows: int, dispatch: str = "push") -> int:
         """Symmetric-heap bytes the buffers of ``cap_rows`` receive rows need."""
         cap = int(cap_rows) // 64 * 64
         H = cfg.hidden_size
