@@ -23,7 +23,7 @@ import re
 from dataclasses import dataclass
 from typing import List, Optional
 
-from .rl_math import EPS
+EPS = 1e-6        # the group-advantage epsilon of rl_math (kept here so either module imports first)
 
 HIGH_REWARD_TOKEN = "<|high_reward|>"
 LOW_REWARD_TOKEN = "<|low_reward|>"
