@@ -190,7 +190,12 @@ class ToolExecutor:
                 if prev is None or speedup > prev:
                     self.best_speedup = speedup
         if name == "pmc" and correct:
-            res["counters"] = getattr(obs, "counters", None) or {}
+            c = getattr(obs, "counters", None) or {}
+            res["counters"] = c
+            if c:
+                from ..verifier.pmc import diagnose, top_stalls
+                res["diagnosis"] = diagnose(c)
+                res["top_stalls"] = top_stalls(c)
         if name == "keep" and correct:
             self.kept = src
         self.trace.append({"tool": name, "ok": correct, "ms": obs.wall_ms, "reward": reward})

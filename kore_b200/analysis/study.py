@@ -152,10 +152,11 @@ def attained_fraction(flops: float, bytes_: float, measured_ms: float, peaks: di
 
 def bottleneck_from_counters(c: Dict[str, float]) -> str:
     """Limiter of one kernel from ncu counters (percent metrics in [0, 100])."""
-    tensor = c.get("sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active", 0.0)
-    dram = c.get("gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed", 0.0)
-    sm = c.get("sm__throughput.avg.pct_of_peak_sustained_elapsed", 0.0)
-    dur_ns = c.get("gpu__time_duration.sum", 0.0)
+    from ..verifier.pmc import counter
+    tensor = counter(c, "sm__pipe_tensor_cycles_active.avg.pct_of_peak_sustained_active") or 0.0
+    dram = counter(c, "gpu__dram_throughput.avg.pct_of_peak_sustained_elapsed") or 0.0
+    sm = counter(c, "sm__throughput.avg.pct_of_peak_sustained_elapsed") or 0.0
+    dur_ns = counter(c, "gpu__time_duration.sum") or 0.0
     if dur_ns and dur_ns < 5000:
         return "launch"
     if tensor >= 60:
