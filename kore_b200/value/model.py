@@ -48,9 +48,44 @@ def _logreg(X, y, l2=1e-2, iters=300, lr=0.5):
 
 
 class ValueModel:
-    def __init__(self):
+    """``featurizer``: "v2" (schedule of Triton or CUDA sources plus the task
+    context, :mod:`kore_b200.value.features`) for new models; "v1" (the
+    Triton-knob vector of :func:`features`) for models saved before it."""
+
+    def __init__(self, featurizer: str = "v2"):
         self.w_compile = self.w_snr = self.w_speed = self.w_rank = None
         self.mu = self.sd = None
+        self.featurizer = featurizer
+
+    def featurize(self, sources: Sequence[str], meta: Optional[dict] = None) -> np.ndarray:
+        if self.featurizer == "v1":
+            ai = float((meta or {}).get("intensity") or 0.0)
+            return np.stack([features(s, ai) for s in sources])
+        from .features import featurize_many
+        return featurize_many(sources, meta)
+
+    def fit_groups(self, groups: Sequence[Sequence[dict]]) -> "ValueModel":
+        """Fit from ranked groups of rows {"source", "compiled", "correct",
+        "speedup" (None unless correct), "meta"}: the three heads on every row
+        and the pairwise head on every (faster correct, slower or incorrect)
+        pair inside a group."""
+        F, comp, corr, ls, pairs = [], [], [], [], []
+        for g in groups:
+            i0 = len(F)
+            for r in g:
+                F.append(self.featurize([r.get("source", "")], r.get("meta"))[0])
+                comp.append(bool(r.get("compiled")))
+                corr.append(bool(r.get("correct")))
+                su = r.get("speedup")
+                ls.append(math.log(su) if su else 0.0)
+            for a in range(len(g)):
+                for b in range(len(g)):
+                    sa, sb = g[a].get("speedup"), g[b].get("speedup")
+                    if sa is not None and (sb is None or sa > sb * 1.02):
+                        pairs.append((i0 + a, i0 + b))
+        if not F:
+            raise ValueError("no training rows")
+        return self.fit(np.stack(F), np.array(comp), np.array(corr), np.array(ls), pairs)
 
     def _x(self, F: np.ndarray) -> np.ndarray:
         return (F - self.mu) / self.sd if self.mu is not None else F
@@ -87,35 +122,54 @@ class ValueModel:
         return out
 
     def to_json(self) -> str:
-        return json.dumps({k: (v.tolist() if v is not None else None) for k, v in
-                           dict(w_compile=self.w_compile, w_snr=self.w_snr, w_speed=self.w_speed,
-                                w_rank=self.w_rank, mu=self.mu, sd=self.sd).items()})
+        d = {k: (v.tolist() if v is not None else None) for k, v in
+             dict(w_compile=self.w_compile, w_snr=self.w_snr, w_speed=self.w_speed,
+                  w_rank=self.w_rank, mu=self.mu, sd=self.sd).items()}
+        d["featurizer"] = self.featurizer
+        return json.dumps(d)
 
     @classmethod
     def from_json(cls, s: str) -> "ValueModel":
         d = json.loads(s)
-        m = cls()
+        m = cls(featurizer=d.pop("featurizer", "v1"))
         for k, v in d.items():
             setattr(m, k, None if v is None else np.asarray(v))
         return m
 
 
+def refit_online(buffer: List[List[dict]], new_groups: Sequence[Sequence[dict]], max_groups: int = 2000,
+                 featurizer: str = "v2") -> ValueModel:
+    """Append ``new_groups`` (measured this step) to the replay ``buffer``
+    (oldest dropped beyond ``max_groups``) and refit a model on it."""
+    buffer.extend(list(g) for g in new_groups)
+    del buffer[: max(0, len(buffer) - max_groups)]
+    return ValueModel(featurizer).fit_groups(buffer)
+
+
 def rank_candidates(model: ValueModel, sources: Sequence[str], ai: float = 0.0) -> List[int]:
-    F = np.stack([features(s, ai) for s in sources])
+    F = model.featurize(sources, {"intensity": ai})
     p = model.predict(F)
     key = p.get("rank_score", p["utility"])
     return list(np.argsort(-key))
 
 
-def train_from_groups(paths: Sequence[str]) -> ValueModel:
+def train_from_groups(paths: Sequence[str], featurizer: str = "v2") -> ValueModel:
+    """Fit from RankedGroupRecord JSONL files: the heads on every candidate
+    (speedup = the parent's wall time over the candidate's) and the pairwise
+    head on the records' own preference pairs."""
     from ..data.schemas import RankedGroupRecord, read_records
+    from .features import meta_from_record
+    m = ValueModel(featurizer)
     F, comp, corr, ls, pairs = [], [], [], [], []
+    metas: Dict[str, dict] = {}
     for p in paths:
         for r in read_records(p, RankedGroupRecord):
+            if r.task_id not in metas:
+                metas[r.task_id] = meta_from_record(r.task_id, r.operation, r.shape)
             base = r.parent_wall_us
             idx0 = len(F)
             for c in r.candidates:
-                F.append(features(c.get("source", "")))
+                F.append(m.featurize([c.get("source", "")], metas[r.task_id])[0])
                 comp.append(c.get("snr_db") is not None)
                 corr.append(bool(c.get("correct")))
                 w = c.get("wall_us")
@@ -123,4 +177,4 @@ def train_from_groups(paths: Sequence[str]) -> ValueModel:
             pairs += [(idx0 + a, idx0 + b) for a, b in r.preferences]
     if not F:
         raise ValueError("no training rows")
-    return ValueModel().fit(np.stack(F), np.array(comp), np.array(corr), np.array(ls), pairs)
+    return m.fit(np.stack(F), np.array(comp), np.array(corr), np.array(ls), pairs)

@@ -26,7 +26,7 @@ from typing import List, Optional, Sequence
 
 import numpy as np
 
-from .model import ValueModel, features
+from .model import ValueModel
 
 _DEFAULT: Optional[ValueModel] = None
 
@@ -86,18 +86,11 @@ def score_candidates(sources: Sequence[str], task=None, model: Optional[ValueMod
     if not sources:
         return []
     model = model if model is not None else _DEFAULT
-    ai = 0.0
-    if task is not None:
-        try:
-            from ..analysis.rooflines import flops_bytes
-            sh = task.shape("primary") or task.shapes[0]
-            fb = flops_bytes(task.operation, sh.dims, task.dtype)
-            ai = fb[0] / fb[1] if fb and fb[1] else 0.0
-        except Exception:  # noqa: BLE001 - context features are optional
-            ai = 0.0
+    from .features import task_meta
+    meta = task_meta(task)
     if model is not None:
         try:
-            p = model.predict(np.stack([features(s, ai) for s in sources]))
+            p = model.predict(model.featurize(sources, meta))
             vals = np.asarray(p.get("rank_score", p["utility"]), dtype=np.float64)
             if np.all(np.isfinite(vals)) and not _degenerate(vals, sources):
                 return [float(v) + _tiebreak(s) for v, s in zip(vals, sources)]
@@ -149,3 +142,26 @@ def benches_to_best(order: Sequence[int], speedups: Sequence[Optional[float]]) -
 
 def expected_random_benches(n: int) -> float:
     return (n + 1) / 2.0
+
+
+def top_k_recall(scores: Sequence[float], speedups: Sequence[Optional[float]], k: int) -> float:
+    """1.0 when the fastest correct candidate is among the ``k`` highest scores
+    (0.0 otherwise; nan when nothing is correct)."""
+    order = sorted(range(len(scores)), key=lambda i: -scores[i])
+    pos = benches_to_best(order, speedups)
+    return float("nan") if pos is None else float(pos <= k)
+
+
+def groupwise_spearman(score_fn, groups: Sequence[Sequence[dict]]) -> float:
+    """Mean within-group Spearman correlation between ``score_fn(rows)`` and
+    the measured speedups of the correct rows (groups with < 2 correct rows
+    are skipped)."""
+    vals = []
+    for g in groups:
+        rows = [r for r in g if r.get("speedup") is not None]
+        if len(rows) < 2:
+            continue
+        rho = spearman(score_fn(rows), [r["speedup"] for r in rows])
+        if rho == rho:
+            vals.append(rho)
+    return sum(vals) / len(vals) if vals else float("nan")

@@ -57,7 +57,7 @@ def test_value_model_roundtrip_and_rank():
     srcs = [SRC.replace("BLOCK=128", f"BLOCK={b}") for b in (32, 64, 128, 256, 512, 1024)]
     F = np.stack([features(s) for s in srcs])
     ls = np.array([math.log2(b) / 10 for b in (32, 64, 128, 256, 512, 1024)])
-    m = ValueModel().fit(F, np.ones(6), np.ones(6), ls, pairs=[(5, 0), (4, 1), (3, 2)])
+    m = ValueModel("v1").fit(F, np.ones(6), np.ones(6), ls, pairs=[(5, 0), (4, 1), (3, 2)])
     m2 = ValueModel.from_json(m.to_json())
     assert np.allclose(m.predict(F)["utility"], m2.predict(F)["utility"])
     assert rank_candidates(m2, srcs)[0] == 5
