@@ -7,6 +7,7 @@ kore/cli.py:187-259, plus midtrain / soup / bench / launch).
     kore datagen {repair,groups,wins,evolve} ...
     kore build-datasets {sft,dpo,rft} ...
     kore value-train ...
+    kore study --tasks A,B --out p0.json | kore residual-transfer p0.json | kore calibrate
     kore eval ...
     kore bench [--gpus N ...]
     kore launch <stage> <config.json> [--gpus N] [--dry-run]
@@ -125,6 +126,9 @@ def build_parser() -> argparse.ArgumentParser:
     sub.add_parser("campaign", help="staged campaign with a resumable manifest")
     sub.add_parser("supervise", help="relaunch-with-resume supervisor / monitor")
     sub.add_parser("proof", help="smokes and proofs (env, sft, grpo, breadth, ops, grpo-repro)")
+    sub.add_parser("study", help="speed-of-light study (eta vs speedup, residual model, monotone valley)")
+    sub.add_parser("residual-transfer", help="does the residual model transfer across families")
+    sub.add_parser("calibrate", help="measure HBM copy and bf16 GEMM peaks on this GPU")
     return ap
 
 
@@ -139,6 +143,10 @@ def main(argv: Optional[List[str]] = None) -> int:
             "datagen": lambda: cmd_datagen(args, rest), "build-datasets": lambda: cmd_build(args, rest),
             "value-train": lambda: cmd_value(args, rest), "eval": lambda: cmd_eval(args, rest),
             "proof": lambda: __import__("kore_b200.proofs", fromlist=["main"]).main(rest),
+            "study": lambda: __import__("kore_b200.analysis.p0_runner", fromlist=["main"]).main(rest),
+            "residual-transfer": lambda: __import__("kore_b200.analysis.residual_transfer",
+                                                    fromlist=["main"]).main(rest),
+            "calibrate": lambda: __import__("kore_b200.analysis.calibrate", fromlist=["main"]).main(rest),
             "campaign": lambda: __import__("kore_b200.campaign.orchestrator", fromlist=["main"]).main(rest),
             "supervise": lambda: __import__("kore_b200.campaign.supervise", fromlist=["main"]).main(rest)}[args.cmd]()
 
