@@ -14,7 +14,9 @@
      for all shapes (candidate and vendor baseline alternated, cold L2,
      randomised iteration counts), repeated until the CV is low enough; the
      candidate's output is re-verified after timing (poisoned-result check);
-  7. optional ncu counters (``collect_counters``) for the white-box reward;
+  7. optional ncu counters (``collect_counters``) of one candidate call and
+     one vendor-baseline call (``--profile-run``, an NVTX-selected capture)
+     for the white-box reward and the counter-relative profile score;
   8. cache the observation.
 Failures are classified as compile / incorrect / infra (timeouts, OOM,
 signals, CUDA errors, missing modules are infra and are never cached or
@@ -167,8 +169,12 @@ class KoreEnv:
                 return obs
             self._bench(obs, kpath, work, thr)
             if self.collect_pmc and obs.validation_passed:
+                from ..reward.profile_reward import profile_efficiency_score
                 from ..verifier.pmc import collect_counters
                 obs.counters = collect_counters(self, kpath, work)
+                ref = collect_counters(self, kpath, work, impl="baseline") if obs.counters else {}
+                if ref:
+                    obs.profile_efficiency = profile_efficiency_score(obs.counters, ref)
             return obs
         finally:
             shutil.rmtree(work, ignore_errors=True)

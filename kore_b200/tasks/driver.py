@@ -157,6 +157,21 @@ def run_bench(task, fn, shapes, warmup, iters):
         print(f"POST_VERIFY_SNR {name} {snr_db(out, spec.reference(*inputs)):.2f}")
 
 
+def run_profile(task, fn, dims, warmup: int = 2):
+    """Warm-up calls, then one call inside the NVTX range ``kore_profile``
+    that a counter capture selects (``ncu --nvtx --nvtx-include kore_profile/``)."""
+    spec = SPECS[task.spec]
+    inputs = spec.make_inputs(dims, 0, "cuda", task_torch_dtype(task.dtype))
+    for _ in range(warmup):
+        fn(*inputs)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("kore_profile")
+    fn(*inputs)
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print("PROFILE_RUN_OK")
+
+
 def main(argv=None) -> int:
     p = argparse.ArgumentParser()
     p.add_argument("--task", required=True)
@@ -170,6 +185,9 @@ def main(argv=None) -> int:
     p.add_argument("--adversarial", action="store_true")
     p.add_argument("--atol", type=float, default=1e-2)
     p.add_argument("--rtol", type=float, default=1e-2)
+    p.add_argument("--profile-run", choices=["candidate", "baseline"], default=None,
+                   help="run one call of the candidate or the vendor baseline inside an NVTX range "
+                        "named kore_profile (for a counter capture), no verification")
     a = p.parse_args(argv)
     task = get_task(a.task)
     try:
@@ -179,6 +197,13 @@ def main(argv=None) -> int:
         return 3
     if a.bench_both:
         run_bench(task, fn, [s for s in a.shapes.split(",") if s], a.warmup, a.iters)
+        return 0
+    if a.profile_run:
+        sh = task.shape(a.shape)
+        if sh is None:
+            print(f"unknown shape {a.shape}", file=sys.stderr)
+            return 2
+        run_profile(task, fn if a.profile_run == "candidate" else SPECS[task.spec].baseline, sh.dims)
         return 0
     sh = task.shape(a.shape)
     if sh is None:

@@ -104,9 +104,12 @@ def ncu_available() -> bool:
 
 
 def ncu_command(metrics: List[str], target: List[str], kernel_regex: Optional[str] = None,
-                skip: int = 0) -> List[str]:
-    """One small capture: listed metrics, one launch, clocks left alone."""
+                skip: int = 0, nvtx_range: Optional[str] = None) -> List[str]:
+    """One small capture: listed metrics, one launch, clocks left alone;
+    ``nvtx_range`` restricts it to launches inside that NVTX push/pop range."""
     cmd = ["ncu", "--clock-control", "none", "--csv", "--metrics", ",".join(metrics), "-c", "1"]
+    if nvtx_range:
+        cmd += ["--nvtx", "--nvtx-include", f"{nvtx_range}/"]
     if skip:
         cmd += ["-s", str(int(skip))]
     if kernel_regex:
@@ -115,19 +118,21 @@ def ncu_command(metrics: List[str], target: List[str], kernel_regex: Optional[st
 
 
 def collect_counters(env, kpath: str, work: str, kernel_regex: Optional[str] = None,
-                     metric_set: str = "standard") -> Dict[str, float]:
-    """Counters of one launch of the candidate on the task's primary shape,
-    merged over the set's passes; {} without ncu or when a pass fails."""
+                     metric_set: str = "standard", impl: str = "candidate") -> Dict[str, float]:
+    """Counters of the first kernel launch of one call of the candidate (or,
+    with ``impl="baseline"``, of the task's vendor baseline) on the task's
+    primary shape, merged over the set's passes; {} without ncu or when a pass
+    fails."""
     if not ncu_available():
         return {}
     prim = env.task.shape("primary") or env.task.shapes[0]
     target = [env.python, "-m", "kore_b200.tasks.driver", "--task", env.task.task_id, "--kernel", kpath,
-              "--shape", prim.name, "--trials", "5"]
+              "--shape", prim.name, "--profile-run", impl]
     out: Dict[str, float] = {}
     for group in metric_passes(metric_set):
         try:
-            r = subprocess.run(ncu_command(group, target, kernel_regex), cwd=work, capture_output=True,
-                               text=True, timeout=env.timeout, env=env._env())
+            r = subprocess.run(ncu_command(group, target, kernel_regex, nvtx_range="kore_profile"), cwd=work,
+                               capture_output=True, text=True, timeout=env.timeout, env=env._env())
         except subprocess.TimeoutExpired:
             return out
         out.update(parse_ncu_csv(r.stdout))

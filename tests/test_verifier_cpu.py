@@ -143,3 +143,24 @@ def test_nvcc_diagnostics():
     assert [e["line"] for e in errs if e["file"]] == [12]
     assert any("too much shared data" in e["message"] for e in errs)
     assert len(warns) == 2 and warns[0]["line"] == 40
+
+
+def test_collect_counters_runs_small_nvtx_captures(monkeypatch):
+    import subprocess as sp
+    from types import SimpleNamespace
+
+    from kore_b200.tasks.registry import get_task
+    calls = []
+
+    def fake_run(cmd, **kw):
+        calls.append(cmd)
+        return SimpleNamespace(stdout=LONG, returncode=0)
+    monkeypatch.setattr(pmc, "ncu_available", lambda: True)
+    monkeypatch.setattr(sp, "run", fake_run)
+    env = SimpleNamespace(task=get_task("gen_silu_bf16"), python="python", timeout=60, _env=lambda: {})
+    c = pmc.collect_counters(env, "k.py", "/tmp", impl="baseline", metric_set="grounding")
+    assert len(calls) == len(pmc.metric_passes("grounding"))
+    for cmd in calls:
+        assert cmd[:3] == ["ncu", "--clock-control", "none"] and "--nvtx-include" in cmd
+        assert cmd[cmd.index("--nvtx-include") + 1] == "kore_profile/" and cmd[-2:] == ["--profile-run", "baseline"]
+    assert c["gpu__time_duration.sum"] == 93888.0
