@@ -26,6 +26,7 @@ import re
 from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 from ..obs import get_logger
+from .knowledge import ExperienceLedger, generation_messages
 from ..policy.format import (SYSTEM_PROMPT, build_task_prompt, build_turn_feedback, format_assistant_turn,
                              parse_response)
 from .schemas import RankedGroupRecord, RepairRecord, WinRecord, write_records
@@ -96,7 +97,7 @@ def generate_repairs(tasks, teacher, env_factory, *, per_task: int = 2, seed: in
             fail = "compile_fail" if not obs.compiled else "snr_fail"
             fb = build_turn_feedback(obs)
             msgs = _messages(task, broken, fb)
-            resp = teacher.generate(msgs)
+            resp = teacher.generate(generation_messages(msgs, task))
             fixed = parse_response(resp)["kernel"]
             if not fixed:
                 continue
@@ -118,13 +119,17 @@ def generate_groups(tasks, teacher, env_factory, *, k: int = 4, out_path: Option
         env = env_factory(task)
         parent = env.step(task.seed_src)
         cands = []
+        ledger = ExperienceLedger()
         for i in range(k):
-            resp = teacher.generate(_messages(task, task.seed_src))
+            resp = teacher.generate(generation_messages(_messages(task, task.seed_src), task, ledger))
             src = parse_response(resp)["kernel"]
             if not src:
                 continue
             obs = env.step(src)
             ok = obs.compiled and obs.validation_passed and obs.wall_ms
+            ledger.record(task.task_id, task.seed_src, src, compiled=obs.compiled,
+                          correct=bool(obs.validation_passed), parent_ms=parent.wall_ms, child_ms=obs.wall_ms,
+                          error=obs.error_text or "")
             cands.append({"source": src, "response": resp, "wall_us": (obs.wall_ms or 0) * 1e3 if ok else None,
                           "snr_db": obs.snr_db, "correct": bool(ok)})
         ranked = sorted(range(len(cands)), key=lambda i: (not cands[i]["correct"],
@@ -144,8 +149,13 @@ def generate_groups(tasks, teacher, env_factory, *, k: int = 4, out_path: Option
 
 
 def generate_wins(tasks, teacher, env_factory, *, turns: int = 3, min_speedup: float = 1.05,
-                  out_path: Optional[str] = None) -> List[WinRecord]:
+                  out_path: Optional[str] = None, ledger: Optional[ExperienceLedger] = None) -> List[WinRecord]:
+    """Multi-turn optimisation trajectories that end faster than the seed. The
+    teacher sees the B200 playbook and the ledger of this task's failed or
+    slower attempts (shared across calls when ``ledger`` is passed); the
+    stored trajectory keeps the canonical system prompt and feedback only."""
     out = []
+    ledger = ledger if ledger is not None else ExperienceLedger()
     for task in tasks:
         env = env_factory(task)
         first = env.step(task.seed_src)
@@ -155,13 +165,17 @@ def generate_wins(tasks, teacher, env_factory, *, turns: int = 3, min_speedup: f
         msgs = _messages(task, cur)
         traj = list(msgs)
         for _ in range(turns):
-            resp = teacher.generate(traj)
+            resp = teacher.generate(generation_messages(traj, task, ledger))
             traj.append({"role": "assistant", "content": resp})
             src = parse_response(resp)["kernel"]
             obs = env.step(src) if src else None
             traj.append({"role": "user", "content": "Verifier feedback:\n" + build_turn_feedback(obs)})
+            if obs is not None:
+                ledger.record(task.task_id, cur, src, compiled=obs.compiled, correct=bool(obs.validation_passed),
+                              parent_ms=best_ms, child_ms=obs.wall_ms, error=obs.error_text or "")
             if obs is not None and obs.validation_passed and obs.wall_ms and obs.wall_ms < best_ms:
                 best_ms, best_src = obs.wall_ms, src
+                cur = src
         sp = first.wall_ms / best_ms
         if sp >= min_speedup:
             out.append(WinRecord(task_id=task.task_id, trajectory=traj, initial_wall_us=first.wall_ms * 1e3,

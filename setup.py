@@ -18,6 +18,7 @@ setup(
     name="kore_b200",
     version="0.1.0",
     packages=find_packages(include=["kore_b200*", "kore*"]),
+    package_data={"kore_b200": ["data/knowledge/*.md", "eval/data/*.jsonl"]},
     ext_modules=[
         CUDAExtension(
             name="kore_b200._C",
