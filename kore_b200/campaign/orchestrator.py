@@ -128,11 +128,23 @@ def _grpo_two_phase(c: Campaign, cfg: dict) -> dict:
 
 
 def _stage_reverify(c: Campaign, m: dict) -> dict:
+    """Write the train / held-out split; with ``configs["reverify"]["inputs"]``
+    (earlier datagen JSONL files) also re-measure those records under the
+    current verifier into ``data/reverified.jsonl``."""
     from ..tasks.registry import split_tasks
     tr, ho = split_tasks()
     p = c.out_dir / "split.json"
     p.write_text(json.dumps({"train": tr, "heldout": ho}))
-    return {"split": str(p), "n_train": len(tr), "n_heldout": len(ho)}
+    out = {"split": str(p), "n_train": len(tr), "n_heldout": len(ho)}
+    inputs = (c.configs.get("reverify") or {}).get("inputs") or []
+    if inputs and not c.dry_run:
+        from ..data.reverify import default_env_factory, reverify_file, rigorous_env
+        dst = c.out_dir / "data" / "reverified.jsonl"
+        dst.parent.mkdir(parents=True, exist_ok=True)
+        with rigorous_env((c.configs.get("reverify") or {}).get("trials", 10)):
+            out["reverify"] = reverify_file(list(inputs), str(dst), default_env_factory())
+        out["reverified"] = str(dst)
+    return out
 
 
 def _datagen(kind: str):
