@@ -175,6 +175,15 @@ def _stage_build(c: Campaign, m: dict) -> dict:
         if not c.dry_run and srcs:
             build_datasets.main([kind, "--inputs", ",".join(srcs), "--out", p])
         out[kind] = p
+    mp = str(d / "midtrain_corpus.jsonl")
+    if not c.dry_run:
+        from ..data.midtrain_corpus import build_midtrain_corpus
+        from ..data.schemas import WinRecord, read_records
+        wins = [w for q in sorted(d.glob("wins*.jsonl")) for w in read_records(str(q), WinRecord)]
+        mc = dict(c.configs.get("midtrain_corpus", {}))
+        rep = build_midtrain_corpus(mp, wins=wins, **mc)
+        out["midtrain_docs"] = rep["docs"]
+    out["midtrain"] = mp
     return out
 
 
