@@ -26,7 +26,7 @@ from typing import Callable, Dict, List, Optional
 
 from .format import (build_agent_system_prompt, format_tool_result, parse_reflection, parse_tool_calls,
                      reflection_is_grounded)
-from .tools import EVAL_TOOLS, ToolExecutor, tool_use_reward
+from .tools import EVAL_TOOLS, ToolExecutor, tool_use_breakdown
 
 
 @dataclass
@@ -41,7 +41,9 @@ class Episode:
     best_ms: Optional[float] = None
     best_speedup: Optional[float] = None
     tool_reward: float = 0.0
-    reflections: int = 0
+    tool_breakdown: Dict[str, float] = field(default_factory=dict)
+    reflections: int = 0                                   # reflections grounded in the last tool result
+    reflection_texts: List[str] = field(default_factory=list)
     reseeds: int = 0
 
     @property
@@ -112,6 +114,8 @@ class AgentHarness:
             resp = policy.generate(msgs)
             msgs.append({"role": "assistant", "content": resp})
             refl = parse_reflection(resp)
+            if refl:
+                ep.reflection_texts.append(refl)
             if reflection_is_grounded(refl, last_res):
                 ep.reflections += 1
             calls = parse_tool_calls(resp)
@@ -160,7 +164,10 @@ class AgentHarness:
         ep.best_ms = ex.best_ms
         ep.best_speedup = ex.best_speedup
         n_turns = len(ep.turn_rewards)
-        ep.tool_reward = tool_use_reward(ex.trace, ep.best_correct is not None, ep.reflections, n_turns)
+        ep.tool_breakdown = tool_use_breakdown(ex.trace, ep.best_correct is not None,
+                                               reflections=ep.reflection_texts, turns=n_turns,
+                                               decisions=ex.decisions)
+        ep.tool_reward = ep.tool_breakdown["total"]
         return ep
 
     def _record(self, ep: Episode, best) -> None:

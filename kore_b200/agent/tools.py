@@ -67,6 +67,41 @@ def agent_tool_schemas(transforms: bool = False) -> List[Dict]:
     return TOOL_SCHEMAS + (TRANSFORM_SCHEMAS if transforms else [])
 
 
+_JSON_TYPES = {"string": str, "object": dict, "number": (int, float), "integer": int, "boolean": bool,
+               "array": list}
+
+
+def validate_tool_call(name: str, arguments, schemas: Optional[List[Dict]] = None) -> Dict:
+    """Check a parsed call against the OpenAI-style schemas: a known tool
+    name, an object of arguments, every required parameter present, no
+    unknown parameter, each of the declared JSON type. Returns
+    {"valid_name", "valid_params", "error"} (error None when valid)."""
+    schemas = schemas if schemas is not None else agent_tool_schemas(True)
+    by_name = {s["function"]["name"]: s["function"]["parameters"] for s in schemas}
+    if name not in by_name:
+        return {"valid_name": False, "valid_params": False,
+                "error": f"unknown tool {name!r}; available: {', '.join(sorted(by_name))}"}
+    if arguments is None:
+        arguments = {}
+    if not isinstance(arguments, dict):
+        return {"valid_name": True, "valid_params": False, "error": "arguments must be a JSON object"}
+    spec = by_name[name]
+    props = spec.get("properties", {})
+    missing = [r for r in spec.get("required", []) if r not in arguments]
+    if missing:
+        return {"valid_name": True, "valid_params": False, "error": f"missing required parameter(s): {missing}"}
+    unknown = [k for k in arguments if k not in props]
+    if unknown:
+        return {"valid_name": True, "valid_params": False,
+                "error": f"unknown parameter(s) {unknown}; {name} takes {sorted(props) or 'none'}"}
+    for k, v in arguments.items():
+        t = _JSON_TYPES.get(props[k].get("type", ""))
+        if t is not None and v is not None and not isinstance(v, t):
+            return {"valid_name": True, "valid_params": False,
+                    "error": f"parameter {k!r} must be a {props[k]['type']}"}
+    return {"valid_name": True, "valid_params": True, "error": None}
+
+
 @dataclass
 class ToolExecutor:
     env: object
@@ -87,6 +122,7 @@ class ToolExecutor:
     reward_mode: str = field(default_factory=lambda: os.environ.get("KORE_REWARD_MODE", "speedup"))
     budget: object = None                      # per-episode epsilon budget of the transform tools
     seed_src: str = ""
+    decisions: List[Dict] = field(default_factory=list)   # keep / revert decisions and whether they were right
 
     def __post_init__(self):
         self.seed_src = self.seed_src or self.current
@@ -123,12 +159,23 @@ class ToolExecutor:
 
     # ------------------------------------------------------------------ dispatch
     def call(self, name: str, args: Dict) -> Dict:
+        v = validate_tool_call(name, args, self.schemas())
+        if v["error"]:
+            self.trace.append({"tool": name, "ok": False, "valid_name": v["valid_name"],
+                               "valid_params": v["valid_params"], "error": v["error"]})
+            return {"error": v["error"]}
         args = args or {}
         if name in EVAL_TOOLS:
             return self._evaluate(name, args.get("source") or self.current)
         if name == "revert":
+            # right when the last evaluated kernel was not the best correct one
+            last = next((t for t in reversed(self.trace) if t["tool"] in EVAL_TOOLS and "reward" in t), None)
+            right = last is not None and (not last["ok"] or (self.best_reward is not None
+                                                                and last["reward"] < self.best_reward))
+            self.decisions.append({"action": "revert", "right": bool(right)})
             self.current = self.best or self.best_reward_src or self.current
-            self.trace.append({"tool": name, "ok": True, "ms": self.best_ms})
+            self.trace.append({"tool": name, "ok": True, "ms": self.best_ms, "valid_name": True,
+                               "valid_params": True})
             return {"source": self.current}
         if name == "list_transforms":
             from ..transform.calculus import admissible_actions
@@ -196,9 +243,18 @@ class ToolExecutor:
                 from ..verifier.pmc import diagnose, top_stalls
                 res["diagnosis"] = diagnose(c)
                 res["top_stalls"] = top_stalls(c)
-        if name == "keep" and correct:
-            self.kept = src
-        self.trace.append({"tool": name, "ok": correct, "ms": obs.wall_ms, "reward": reward})
+        if name == "keep":
+            # right when the kept kernel is correct and at least as good as the best seen so far
+            self.decisions.append({"action": "keep", "right": bool(correct and (self.best_reward is None
+                                                                                or reward >= self.best_reward))})
+            if correct:
+                self.kept = src
+        ent = {"tool": name, "ok": correct, "ms": obs.wall_ms, "reward": reward, "valid_name": True,
+               "valid_params": True}
+        if not correct:
+            ent["error"] = ((getattr(obs, "error_text", "") or "") or
+                            ("snr %s" % (getattr(obs, "snr_db", None),)))[-600:]
+        self.trace.append(ent)
         return res
 
     def reseed(self) -> None:
@@ -209,20 +265,67 @@ class ToolExecutor:
         self.trace.append({"tool": "reseed", "ok": True})
 
 
-def tool_use_reward(trace: List[Dict], final_correct: bool, reflections: int = 0, turns: int = 0) -> float:
-    """Shaping for disciplined tool use, in [-0.1, 0.25]: test before bench,
-    keep on a correct kernel, grounded reflections, few repeated failures.
-    Small against the verified kernel reward it is added to."""
-    if not trace:
-        return -0.1
+_TOKEN = __import__("re").compile(r"[a-z0-9_]{4,}")
+
+
+def _grounded(text: str, errors: List[str]) -> bool:
+    """The text shares a word of four or more characters with an error the
+    episode's tools reported."""
+    words = set(_TOKEN.findall((text or "").lower()))
+    return bool(words) and any(words & set(_TOKEN.findall(e.lower())) for e in errors)
+
+
+def tool_use_breakdown(trace: List[Dict], final_correct: bool, *, reflections: Optional[List[str]] = None,
+                       turns: int = 0, decisions: Optional[List[Dict]] = None) -> Dict[str, float]:
+    """Components of the tool-use shaping reward, each in [0, 1] unless noted:
+
+    * ``name`` / ``params``: fractions of calls naming a real tool with valid
+      arguments;
+    * ``order``: 1 when correctness was tested before the first bench;
+    * ``commit``: 1 when a correct kernel was kept;
+    * ``decisions``: mean of +1 (right) / -1 (wrong) keep and revert decisions,
+      in [-1, 1];
+    * ``reflection``: fraction of reflections that cite an error the tools
+      reported (grounded), scaled by how many turns reflected;
+    * ``failed``: fraction of evaluation calls that failed beyond the first
+      two (a penalty).
+
+    ``total`` = 0.03 name + 0.03 params + 0.05 order + 0.07 commit + 0.04
+    decisions + 0.05 reflection - 0.1 failed, clipped to [-0.1, 0.25]: small
+    against the verified kernel reward it is added to."""
+    n = len(trace)
+    if n == 0:
+        return {"name": 0.0, "params": 0.0, "order": 0.0, "commit": 0.0, "decisions": 0.0, "reflection": 0.0,
+                "failed": 0.0, "total": -0.1}
     names = [t["tool"] for t in trace]
-    r = 0.0
-    if "test" in names and "bench" in names and names.index("test") < names.index("bench"):
-        r += 0.1
-    if "keep" in names and final_correct:
-        r += 0.1
-    if turns and reflections:
-        r += 0.05 * min(1.0, reflections / turns)
-    fails = sum(1 for t in trace if t["tool"] in EVAL_TOOLS and not t.get("ok"))
-    r -= 0.02 * max(0, fails - 2)
-    return max(-0.1, min(0.25, r))
+    name_ok = sum(1 for t in trace if t.get("valid_name", True)) / n
+    params_ok = sum(1 for t in trace if t.get("valid_params", True)) / n
+    order = 1.0 if ("test" in names and "bench" in names and names.index("test") < names.index("bench")) else 0.0
+    commit = 1.0 if ("keep" in names and final_correct) else 0.0
+    ds = decisions or []
+    dec = sum(1.0 if d.get("right") else -1.0 for d in ds) / len(ds) if ds else 0.0
+    errors = [t["error"] for t in trace if t.get("error")]
+    refl = 0.0
+    if reflections:
+        grounded = sum(1 for r in reflections if _grounded(r, errors) or not errors)
+        refl = (grounded / len(reflections)) * min(1.0, len(reflections) / max(1, turns or len(reflections)))
+    evals = [t for t in trace if t["tool"] in EVAL_TOOLS]
+    fails = sum(1 for t in evals if not t.get("ok"))
+    failed = max(0, fails - 2) / max(1, len(evals))
+    total = (0.03 * name_ok + 0.03 * params_ok + 0.05 * order + 0.07 * commit + 0.04 * dec + 0.05 * refl
+             - 0.1 * failed)
+    return {"name": name_ok, "params": params_ok, "order": order, "commit": commit, "decisions": dec,
+            "reflection": refl, "failed": failed, "total": max(-0.1, min(0.25, total))}
+
+
+def tool_use_reward(trace: List[Dict], final_correct: bool, reflections=0, turns: int = 0,
+                    decisions: Optional[List[Dict]] = None) -> float:
+    """Total of :func:`tool_use_breakdown`; ``reflections`` is the list of the
+    episode's reflection texts (an int count is accepted and treated as that
+    many grounded reflections)."""
+    if isinstance(reflections, int):
+        refl = ["grounded"] * reflections
+        trace = [dict(t, error=None) for t in trace]              # counts were already judged grounded
+    else:
+        refl = list(reflections or [])
+    return tool_use_breakdown(trace, final_correct, reflections=refl, turns=turns, decisions=decisions)["total"]

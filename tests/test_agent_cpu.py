@@ -109,3 +109,49 @@ def test_wins_kb_same_family_only():
     kb = WinsKB([Win("gemm", "bf16", 2.0, "KGEMM"), Win("norm", "bf16", 5.0, "KNORM")])
     assert [w.final_kernel for w in kb.examples("gemm", "bf16")] == ["KGEMM"]
     assert kb.examples("attention", "bf16") == []
+
+
+def test_tool_call_validation_and_reward_breakdown():
+    from kore_b200.agent.tools import tool_use_breakdown, validate_tool_call
+    assert validate_tool_call("bench", {"source": "x"})["error"] is None
+    assert validate_tool_call("benchmark", {})["valid_name"] is False
+    v = validate_tool_call("bench", {"src": "x"})
+    assert v["valid_name"] and not v["valid_params"] and "unknown parameter" in v["error"]
+    assert "must be a string" in validate_tool_call("bench", {"source": 3})["error"]
+    assert "missing" in validate_tool_call("apply_transform", {})["error"]
+    assert validate_tool_call("revert", None)["error"] is None
+    trace = [{"tool": "build", "ok": False, "error": "ptxas error: shared memory overflow in kernel"},
+             {"tool": "test", "ok": True}, {"tool": "bench", "ok": True}, {"tool": "keep", "ok": True},
+             {"tool": "benchmark", "ok": False, "valid_name": False, "valid_params": False}]
+    good = tool_use_breakdown(trace, True, reflections=["the shared memory overflow came from BLOCK 256"], turns=2,
+                              decisions=[{"action": "keep", "right": True}])
+    bad = tool_use_breakdown(trace, True, reflections=["nice weather today"], turns=2,
+                             decisions=[{"action": "keep", "right": False}])
+    assert good["order"] == 1.0 and good["commit"] == 1.0 and good["name"] == 0.8
+    assert good["reflection"] > bad["reflection"] and good["decisions"] == 1.0 and bad["decisions"] == -1.0
+    assert -0.1 <= bad["total"] < good["total"] <= 0.25
+    assert tool_use_breakdown([], False)["total"] == -0.1
+
+
+def test_executor_rejects_bad_calls_and_tracks_decisions():
+    from types import SimpleNamespace
+
+    from kore_b200.agent.tools import ToolExecutor
+    from kore_b200.tasks.registry import get_task
+    t = get_task("gen_silu_bf16")
+
+    class Env:
+        def step(self, src):
+            ok = "bad" not in src
+            return SimpleNamespace(compiled=True, validation_passed=ok, wall_ms=1.0 if ok else None, snr_db=60.0,
+                                   flagged_hack=False, error_text=None if ok else "SNR 2 dB mismatch",
+                                   wall_by_shape={"primary": 1.0}, baseline_by_shape={"primary": 1.0},
+                                   speedup_by_shape={"primary": 1.0}, counters=None)
+    ex = ToolExecutor(Env(), t, current=t.seed_src)
+    r = ex.call("frobnicate", {})
+    assert "unknown tool" in r["error"] and ex.trace[-1]["valid_name"] is False
+    ex.call("test", {"source": "bad kernel"})
+    assert "mismatch" in ex.trace[-1]["error"]
+    ex.call("revert", {})
+    ex.call("keep", {"source": t.seed_src})
+    assert [d["action"] for d in ex.decisions] == ["revert", "keep"]
