@@ -49,11 +49,11 @@ class CurriculumHook:
         self.tr = trainer
         comp = None
         if getattr(cfg, "coevolve_regret_vs_opus", False) and getattr(cfg, "coevolve_opus_scores_path", None):
-            try:
-                with open(cfg.coevolve_opus_scores_path) as f:
-                    comp = json.load(f)
-            except (OSError, ValueError):
-                comp = None
+            from ..openended.competitor import build_competitor_scores, load_scores
+            path = cfg.coevolve_opus_scores_path
+            # a scores JSON, or the teacher's verified datagen records (JSONL) to mine them from
+            comp = (build_competitor_scores([p for p in path.split(",") if p]) if path.endswith(".jsonl")
+                    else load_scores(path)) or None
         self.ctrl = CoevolutionController(space=space, seed=cfg.seed, proposer=Proposer(competitor=comp),
                                           batch=cfg.coevolve_batch or 8, ctx=trainer.ctx,
                                           mint=bool(getattr(cfg, "coevolve_mint", False)),

@@ -104,3 +104,26 @@ def test_controller_mints_into_the_space():
     c = CoevolutionController(seed=1, batch=4, mint=True, mint_every=1, mint_batch=2)
     c.next_task_id(4)
     assert len(c.minted) == 2 and all(c.space.by_id(t) for t in c.minted)
+
+
+def test_competitor_scores_mined_from_teacher_records(tmp_path):
+    import json
+
+    from kore_b200.openended import competitor as C
+    p = tmp_path / "d.jsonl"
+    rows = [{"type": "win", "task_id": "a", "speedup": 4.0},
+            {"type": "win", "task_id": "b", "speedup": 0.9},
+            {"type": "ranked_group", "task_id": "c", "parent_wall_us": 100.0,
+             "candidates": [{"correct": True, "wall_us": 50.0, "snr_db": 60}, {"correct": False, "wall_us": 10.0}]},
+            {"type": "win", "task_id": "d", "speedup": "nan?"}]
+    p.write_text("\n".join(json.dumps(r) for r in rows) + "\nnot json\n")
+    best = C.mine_teacher_speedups([str(p), str(tmp_path / "missing.jsonl")])
+    assert best == {"a": 4.0, "b": 0.9, "c": 2.0}
+    s = C.strength_scores(best, ref_percentile=1.0)
+    assert s["a"] == 1.0 and s["b"] == 0.0 and 0.4 < s["c"] < 0.6
+    r = C.build_competitor_scores([str(p)], ours={"a": 4.0, "c": 1.0})
+    assert r["a"] == 0.0 and r["c"] == 0.5
+    f = tmp_path / "s.json"
+    C.save_scores(s, str(f))
+    assert C.load_scores(str(f)) == pytest.approx(s) and C.load_scores(str(tmp_path / "x.json")) == {}
+    assert C.summarize(s)["tasks"] == 3 and C.summarize({}) == {"tasks": 0}
