@@ -41,8 +41,6 @@ class CurriculumHook:
     same tasks. Optional minting and competitor anchor from the config."""
 
     def __init__(self, trainer, space=None):
-        import json
-
         from ..openended.controller import CoevolutionController
         from ..openended.proposer import Proposer
         cfg = trainer.cfg
