@@ -313,6 +313,82 @@ def _rsqrt(src: str) -> Optional[str]:
     return pat.sub("tl.rsqrt(", src, count=1)
 
 
+# ----------------------------------------------------------------------------- CUDA C++ sources
+_KERNEL_SIG = re.compile(r"__global__\s+(?:__launch_bounds__\([^)]*\)\s+)?void\s+(\w+)\s*\(([^)]*)\)")
+
+
+def _is_cuda(src: str) -> bool:
+    return "__global__" in src
+
+
+def _launch_bounds_domain(src: str) -> List[Params]:
+    if not _is_cuda(src):
+        return []
+    m = re.search(r"<<<[^,>]+,\s*(\d+)", src) or re.search(r"blockDim\s*=\s*dim3\((\d+)", src)
+    n = int(m.group(1)) if m else 256
+    return [{"threads": n, "min_blocks": b} for b in (1, 2)]
+
+
+def _launch_bounds(src: str, threads: int = 256, min_blocks: int = 1) -> Optional[str]:
+    """Add (or replace) ``__launch_bounds__(threads, min_blocks)`` on the first
+    kernel: register allocation only, the arithmetic is unchanged. The launch
+    must not use more than ``threads`` threads per block (side condition)."""
+    m = re.search(r"__global__\s+(__launch_bounds__\([^)]*\)\s+)?void", src)
+    if not m:
+        return None
+    lb = f"__launch_bounds__({int(threads)}, {int(min_blocks)}) "
+    if m.group(1):
+        return src[: m.start(1)] + lb + src[m.end(1):]
+    return src[: m.start()] + "__global__ " + lb + "void" + src[m.end():]
+
+
+def _launch_bounds_conditions(src: str, p: Params) -> List[str]:
+    out = []
+    for n in re.findall(r"<<<[^,>]+,\s*(\d+)", src):
+        if int(n) > int(p.get("threads", 256)):
+            out.append("launch uses more threads than the bound")
+    return out
+
+
+def _restrict(src: str) -> Optional[str]:
+    """Mark the first kernel's pointer parameters ``__restrict__`` (lets the
+    compiler use the read-only path and reorder loads)."""
+    m = _KERNEL_SIG.search(src)
+    if not m or "__restrict__" in m.group(2):
+        return None
+    params = m.group(2).split(",")
+    new, changed = [], False
+    for prm in params:
+        if "*" in prm and "__restrict__" not in prm:
+            head, _, name = prm.rpartition("*")
+            new.append(f"{head}* __restrict__{name if name.startswith(' ') else ' ' + name.strip()}")
+            changed = True
+        else:
+            new.append(prm)
+    if not changed:
+        return None
+    return src[: m.start(2)] + ",".join(new) + src[m.end(2):]
+
+
+def _restrict_conditions(src: str, p: Params) -> List[str]:
+    """Legal only when no two pointer arguments of a launch are the same buffer."""
+    for args in re.findall(r"<<<[^>]*>>>\s*\(([^;]*)\)", src):
+        names = [a.strip() for a in args.split(",") if a.strip()]
+        if len(names) != len(set(names)):
+            return ["a launch passes the same argument twice (possible aliasing)"]
+    return []
+
+
+def _unroll(src: str) -> Optional[str]:
+    """``#pragma unroll`` on the first constant-trip ``for`` loop without one."""
+    for m in re.finditer(r"(?m)^([ \t]*)for\s*\(\s*int\s+\w+\s*=\s*0\s*;\s*\w+\s*<\s*(\d+|[A-Z_][A-Z0-9_]*)\s*;", src):
+        prev = src[: m.start()].rstrip().splitlines()[-1:] if src[: m.start()].strip() else []
+        if prev and prev[0].strip().startswith("#pragma unroll"):
+            continue
+        return src[: m.start()] + f"{m.group(1)}#pragma unroll\n" + src[m.start():]
+    return None
+
+
 def _one(params: Params):
     return lambda src: [dict(params)]
 
@@ -352,6 +428,13 @@ LIBRARY: List[Transformation] = [
     Transformation("exp_to_exp2", APPROX, _exp2, eps=1e-6, knob="fast_math",
                    doc="exp through exp2 with a log2(e) pre-scale (rounding differs)"),
     Transformation("rsqrt", APPROX, _rsqrt, eps=0.01, knob="fast_math", doc="1/sqrt -> rsqrt"),
+    Transformation("cuda_launch_bounds", EXACT, _launch_bounds, knob="launch_bounds", domain=_launch_bounds_domain,
+                   side_conditions=_launch_bounds_conditions,
+                   doc="__launch_bounds__(threads, min blocks): register budget of a CUDA kernel"),
+    Transformation("cuda_restrict", EXACT, _restrict, knob="aliasing", side_conditions=_restrict_conditions,
+                   doc="__restrict__ pointer parameters (no two arguments alias)"),
+    Transformation("cuda_unroll", EXACT, _unroll, knob="unroll",
+                   doc="#pragma unroll on a constant-trip loop"),
 ]
 EXACT_LIBRARY = [t for t in LIBRARY if t.kind == EXACT]
 APPROX_LIBRARY = [t for t in LIBRARY if t.kind == APPROX]

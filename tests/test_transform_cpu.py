@@ -139,3 +139,28 @@ def test_discovered_families_are_opt_in_and_approx():
     assert len(ext) == len(LIBRARY) + len(found)
     fused = [t for t in found if t.name == "fuse_epilogue"][0].apply(src)
     assert "tl.store(Y + row * N + cols, (x * r), mask=m)" in fused
+
+
+CUDA_SRC = '''__global__ void scale(const float* x, float* y, int n) {
+  for (int i = 0; i < 4; ++i) { y[i] = x[i]; }
+}
+void run(const float* x, float* y, int n) { scale<<<n / 256, 256>>>(x, y, n); }
+'''
+
+
+def test_cuda_rewrite_families():
+    from kore_b200.transform.library import EXACT_LIBRARY, get_transform
+    names = {t.name for t in EXACT_LIBRARY}
+    assert {"cuda_launch_bounds", "cuda_restrict", "cuda_unroll"} <= names
+    lb = get_transform("cuda_launch_bounds")
+    assert lb.domain(CUDA_SRC)[0] == {"threads": 256, "min_blocks": 1}
+    out = lb.apply(CUDA_SRC)
+    assert "__launch_bounds__(256, 1) void scale" in out
+    assert "__launch_bounds__(512, 2)" in lb.apply(out, threads=512, min_blocks=2)      # replaces, not stacks
+    assert lb.apply(CUDA_SRC, threads=128, min_blocks=1) is None                          # launch uses 256
+    r = get_transform("cuda_restrict").apply(CUDA_SRC)
+    assert "const float* __restrict__ x, float* __restrict__ y, int n" in r
+    assert get_transform("cuda_restrict").apply(CUDA_SRC.replace("(x, y, n)", "(x, x, n)")) is None
+    u = get_transform("cuda_unroll").apply(CUDA_SRC)
+    assert "#pragma unroll\n  for (int i = 0; i < 4" in u and get_transform("cuda_unroll").apply(u) is None
+    assert get_transform("cuda_unroll").apply("def f(x):\n    return x\n") is None
