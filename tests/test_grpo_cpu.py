@@ -190,3 +190,48 @@ def test_grpo_streamed_reference_matches_resident():
         tr.fill_ref_logps(samples, 4096)
         res[place] = [s.ref_logp for s in samples]
     assert res["resident"] == pytest.approx(res["host"], abs=1e-5)
+
+
+def test_grpo_update_gradient_matches_autograd_objective():
+    """The update's gradient equals autograd of the GRPO objective written
+    out directly: per sample the token-mean log-prob lp, ratio r = e^(lp - old),
+    term = -min(r A, clip(r, 1 - lo, 1 + hi) A) + c (e^(ref - lp) - (ref - lp) - 1),
+    loss = sum_s n_s term_s / total tokens. Old log-probs are offset so that
+    some ratios sit outside the clip band."""
+    from kore_b200.policy.grpo import TrainSample
+    cfg, w = _tiny()
+    lo, hi, c = 0.2, 0.28, 0.05
+    gc = GRPOConfig(num_trajectories=4, num_turns=1, tasks_per_step=1, max_response_length=8,
+                    max_prompt_length=256, learning_rate=1e-3, clip_ratio_low=lo, clip_ratio_high=hi,
+                    ref_anchor_coef=c, old_logp_source="sampler", dynamic_sampling=False, starpo_s=False,
+                    bf16=False, total_steps=2, overlong_mask=False)
+    env = SyntheticRewardEnv(seed=0, prompt_len=16, feedback_len=4, vocab_size=cfg.vocab_size)
+    tr = GRPOTrainer(gc, weights=w, env=env, rollout_kwargs=dict(num_pages=64, page_size=16, max_seq_len=256))
+    g = torch.Generator().manual_seed(3)
+    adv = [1.0, 0.5, -0.8, -1.2]           # samples 1 and 2 land on the clipped branch
+    offs = [0.0, 0.3, -0.3, 0.05]                   # old = lp - off: r = e^off
+    samples, lps = [], []
+    bufs = leaf_buffers(w)
+    for i in range(4):
+        L, n_ctx = 20 + 3 * i, 8 + i
+        ids = torch.randint(0, cfg.vocab_size, (L,), generator=g).tolist()
+        # the policy's log-probs at the sampling temperature, as the update scores them
+        lp, _ = forward_logprobs(w, bufs, Batch.from_sequences([torch.tensor(ids)]), temperature=gc.temperature)
+        m = lp[n_ctx - 1: L - 1].mean()
+        lps.append(m)
+        samples.append(TrainSample(ids, n_ctx, ret=0.0, adv=adv[i], old_logp=m.item() - offs[i],
+                                   ref_logp=m.item() + 0.1))
+    total = sum(s.n_gen for s in samples)
+    loss = 0.0
+    for s, m in zip(samples, lps):
+        r = torch.exp(m - s.old_logp)
+        pg = -torch.minimum(r * s.adv, r.clamp(1 - lo, 1 + hi) * s.adv)
+        d = s.ref_logp - m
+        loss = loss + s.n_gen * (pg + c * (torch.exp(d) - d - 1)) / total
+    loss.backward()
+    tr.trainer.opt.step = lambda *a, **k: None
+    st = tr.update(samples, budget=4096)
+    assert abs(st["loss"] - float(loss)) < 1e-5 * max(1.0, abs(float(loss)))
+    for u, (gr, rb) in enumerate(zip(tr.trainer.eng.grads, bufs)):
+        rel = ((gr - rb.grad).norm() / (rb.grad.norm() + 1e-12)).item()
+        assert rel < 1e-4, (u, rel)
