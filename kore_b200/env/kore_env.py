@@ -157,6 +157,21 @@ class KoreEnv:
                 snr_by[sh.name] = float(snrs[-1])
                 allclose_all = allclose_all and (acs[-1] == "True" if acs else False)
                 text_tail = out[-800:]
+            if self.cfg.shape_augment and all(v >= thr for v in snr_by.values()):
+                # augmented shapes: correctness only (row-like dims scaled and made non-aligned)
+                import json as _json
+
+                from ..tasks.augment import augment_shapes
+                for ash in augment_shapes(t, self.cfg.shape_augment_max):
+                    rc, out, to = self._exec(["--task", t.task_id, "--kernel", kpath, "--shape", "primary",
+                                              "--dims", _json.dumps(ash.dims), "--adversarial"], work)
+                    if self._classify(rc, out, to) == "infra":
+                        return Observation(compiled=True, infra_error=True, error_text=out[-2000:], dtype=t.dtype)
+                    snrs = _SNR.findall(out)
+                    snr_by[ash.name] = float(snrs[-1]) if snrs else -999.0
+                    if not snrs or float(snrs[-1]) < thr:
+                        text_tail = f"fails on augmented shape {ash.as_args()}: " + out[-600:]
+                        break
             passed = all(v >= thr for v in snr_by.values())
             obs = Observation(compiled=True, snr_by_shape=snr_by, snr_db=min(snr_by.values()),
                               validation_passed=passed, dtype=t.dtype,

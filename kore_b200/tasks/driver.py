@@ -185,6 +185,7 @@ def main(argv=None) -> int:
     p.add_argument("--adversarial", action="store_true")
     p.add_argument("--atol", type=float, default=1e-2)
     p.add_argument("--rtol", type=float, default=1e-2)
+    p.add_argument("--dims", default=None, help="JSON dims overriding the named shape's (augmented shapes)")
     p.add_argument("--profile-run", choices=["candidate", "baseline"], default=None,
                    help="run one call of the candidate or the vendor baseline inside an NVTX range "
                         "named kore_profile (for a counter capture), no verification")
@@ -206,10 +207,15 @@ def main(argv=None) -> int:
         run_profile(task, fn if a.profile_run == "candidate" else SPECS[task.spec].baseline, sh.dims)
         return 0
     sh = task.shape(a.shape)
-    if sh is None:
+    if a.dims:
+        import json
+        dims = json.loads(a.dims)
+    elif sh is None:
         print(f"unknown shape {a.shape}", file=sys.stderr)
         return 2
-    run_correctness(task, fn, sh.dims, max(5, a.trials), a.atol, a.rtol, a.adversarial)
+    else:
+        dims = sh.dims
+    run_correctness(task, fn, dims, max(5, a.trials), a.atol, a.rtol, a.adversarial)
     return 0
 
 
