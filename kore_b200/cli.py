@@ -52,6 +52,9 @@ def cmd_launch(args) -> int:
 
 def cmd_tasks(args) -> int:
     from .tasks.registry import all_tasks, split_tasks
+    if getattr(args, "audit", False):
+        from .tasks.audit import main as audit_main
+        return audit_main([])
     if args.split:
         tr, ho = split_tasks(seed=args.seed)
         ids = tr if args.split == "train" else ho
@@ -110,6 +113,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--dry-run", action="store_true")
     p = sub.add_parser("tasks", help="list kernel tasks")
     p.add_argument("--split", choices=["train", "heldout"])
+    p.add_argument("--audit", action="store_true", help="data-scale report of the corpus")
     p.add_argument("--seed", type=int, default=0)
     p = sub.add_parser("soup", help="WiSE-FT interpolation")
     p.add_argument("--base", required=True)

@@ -45,3 +45,12 @@ def test_env_fails_kernel_on_augmented_shape(monkeypatch):
     monkeypatch.setattr(env2, "_exec", fake_exec)
     monkeypatch.setattr(env2, "_bench", lambda *a, **k: None)
     assert env2.evaluate(t.seed_src + "\n").validation_passed
+
+
+def test_data_scale_audit():
+    from kore_b200.tasks.audit import audit
+    r = audit()
+    assert r.tasks >= 1334 and r.train + r.heldout == r.tasks and r.heldout >= 20
+    assert sum(r.families.values()) == r.tasks and sum(r.dtypes.values()) == r.tasks
+    assert r.with_roofline == r.tasks and r.augmented_shapes > r.tasks
+    assert "tasks" in r.render()
