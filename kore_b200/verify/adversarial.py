@@ -142,6 +142,13 @@ class Genome:
                       self.offset + rng.choice((0.0, 1e-3, -1e-3, 1e-6, -1e-6)),
                       self.slot if rng.random() < 0.8 else rng.choice((-1, 0, 1)))
 
+    def crossover(self, other: "Genome", rng: random.Random) -> "Genome":
+        """Uniform crossover: each field from one parent or the other."""
+        pick = lambda a, b: a if rng.random() < 0.5 else b          # noqa: E731
+        return Genome(pick(self.regime, other.regime), pick(self.scale, other.scale),
+                      pick(self.sparsity, other.sparsity), rng.randrange(1 << 30),
+                      pick(self.offset, other.offset), pick(self.slot, other.slot))
+
     def key(self) -> Tuple:
         return (self.regime, round(math.log10(self.scale), 1), self.slot)
 
@@ -151,6 +158,8 @@ class Genome:
 
 
 def _fitness(g: Genome, make_inputs, candidate, oracle, score) -> float:
+    """Error of the candidate (the worst of several, when a list is given) on
+    the genome's inputs; -inf when the oracle itself has no finite answer."""
     ins = g.inputs(tuple(make_inputs(g.seed)))
     try:
         ref = oracle(*ins)
@@ -158,18 +167,26 @@ def _fitness(g: Genome, make_inputs, candidate, oracle, score) -> float:
         return -math.inf
     if not bool(torch.isfinite(ref.float()).all()):
         return -math.inf                     # minimal criterion: the oracle must answer
-    try:
-        return float(score(candidate(*ins), ref))
-    except Exception:  # noqa: BLE001 - a crash on a valid input is maximal disagreement
-        return math.inf
+    worst = -math.inf
+    for c in (candidate if isinstance(candidate, (list, tuple)) else [candidate]):
+        try:
+            worst = max(worst, float(score(c(*ins), ref)))
+        except Exception:  # noqa: BLE001 - a crash on a valid input is maximal disagreement
+            return math.inf
+    return worst
 
 
 def coevolve_tests(make_inputs: Callable[[int], Sequence[torch.Tensor]], candidate: Callable, oracle: Callable,
                    score: Callable[[torch.Tensor, torch.Tensor], float], *, population: int = 8,
-                   generations: int = 4, seed: int = 0, novelty_bonus: float = 0.0) -> List[Tuple[Genome, float]]:
+                   generations: int = 4, seed: int = 0, novelty_bonus: float = 0.0,
+                   crossover_rate: float = 0.5, archive: Optional[dict] = None) -> List[Tuple[Genome, float]]:
     """Evolve genomes maximising ``score(candidate_out, oracle_out)`` (an
-    error: higher means a worse candidate). Returns the final population,
-    worst candidate error first; genomes invalid for the oracle score -inf."""
+    error: higher means a worse candidate; ``candidate`` may be a list, scored
+    by its worst member). Children come from crossover of two elites (with
+    probability ``crossover_rate``) followed by mutation. ``archive``, when
+    given, keeps the highest error seen per genome niche (pattern, scale
+    decade, operand). Returns the final population, worst candidate error
+    first; genomes invalid for the oracle score -inf."""
     rng = random.Random(seed)
     # stratified start: distinct patterns, the historically most breaking first
     order = list(_PRIOR) + [p for p in PATTERNS if p not in _PRIOR]
@@ -178,6 +195,8 @@ def coevolve_tests(make_inputs: Callable[[int], Sequence[torch.Tensor]], candida
 
     def fit(g: Genome) -> float:
         f = _fitness(g, make_inputs, candidate, oracle, score)
+        if archive is not None and f > archive.get(g.key(), (-math.inf, None))[0]:
+            archive[g.key()] = (f, g)
         if novelty_bonus and math.isfinite(f):
             f += novelty_bonus / (1 + seen.get(g.key(), 0))
         seen[g.key()] = seen.get(g.key(), 0) + 1
@@ -187,7 +206,12 @@ def coevolve_tests(make_inputs: Callable[[int], Sequence[torch.Tensor]], candida
     for _ in range(generations):
         scored.sort(key=lambda p: p[1], reverse=True)
         elite = [p for p in scored[: max(1, population // 2)] if p[1] > -math.inf] or scored[:1]
-        kids = [rng.choice(elite)[0].mutate(rng) for _ in range(population - len(elite))]
+        kids = []
+        for _ in range(population - len(elite)):
+            a = rng.choice(elite)[0]
+            if len(elite) > 1 and rng.random() < crossover_rate:
+                a = a.crossover(rng.choice(elite)[0], rng)
+            kids.append(a.mutate(rng))
         scored = elite + [(c, fit(c)) for c in kids]
     scored.sort(key=lambda p: p[1], reverse=True)
     return scored

@@ -89,3 +89,27 @@ def test_coevolved_breaks_fold_into_the_oracle():
     assert not v.verified and v.first_failure == "adversarial"
     ctrl = random_search(mk1, naive, ref, err, budget=8)
     assert len(ctrl) == 8
+
+
+def test_coevolution_crossover_archive_and_candidate_sets():
+    import math
+    import random
+
+    import torch
+
+    from kore_b200.verify.adversarial import Genome, coevolve_tests
+
+    def make(seed):
+        return (torch.randn(64, 16, generator=torch.Generator().manual_seed(seed)),)
+    oracle = lambda x: torch.softmax(x.float(), -1)                      # noqa: E731
+    good = oracle
+    naive = lambda x: torch.exp(x.float()) / torch.exp(x.float()).sum(-1, keepdim=True)   # overflows at large x
+    score = lambda o, r: float((o.float() - r).abs().nan_to_num(1e9).max())                # noqa: E731
+    arch = {}
+    pop = coevolve_tests(make, [good, naive], oracle, score, population=8, generations=4, seed=1, archive=arch)
+    assert pop[0][1] > 1e-3 and arch and max(v[0] for v in arch.values()) == pop[0][1]
+    only_good = coevolve_tests(make, good, oracle, score, population=6, generations=2, seed=1)
+    assert only_good[0][1] < 1e-5
+    a, b = Genome("zeros", 1.0, 1e-3, 1), Genome("huge", 100.0, 1e-2, 2, 1e-3, 0)
+    c = a.crossover(b, random.Random(0))
+    assert c.regime in ("zeros", "huge") and c.scale in (1.0, 100.0) and c.slot in (-1, 0)
