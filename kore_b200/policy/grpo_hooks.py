@@ -120,7 +120,8 @@ class SearchDistill:
         kenv = tr.env._env(task)
         res = search_from_kernel(code, kenv, budget=cfg.search_budget, k_expand=cfg.search_k_expand,
                                  max_depth=cfg.search_max_depth or 6, bnb=cfg.search_bnb,
-                                 task=getattr(kenv, "task", None))
+                                 task=getattr(kenv, "task", None),
+                                 value_fn="model" if getattr(cfg, "search_value_prior", True) else None)
         won = False
         if res.best_src and res.best_score:
             won = self.sink.add(str(task), res.best_src, float(res.best_score),

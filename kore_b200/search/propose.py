@@ -55,6 +55,20 @@ class TransformProposePolicy:
         return self.value_fn(child) if child else 0.0
 
 
+def model_value_fn(task=None, model=None) -> Callable[[str], float]:
+    """A per-source prior from the value model (the trained default model when
+    one is loaded, else its schedule heuristic), scored with the task's
+    context and memoised per source."""
+    from ..value.rerank import score_candidates
+    cache: Dict[str, float] = {}
+
+    def f(src: str) -> float:
+        if src not in cache:
+            cache[src] = float(score_candidates([src], task, model)[0])
+        return cache[src]
+    return f
+
+
 def env_evaluator(env, baseline_ms: Optional[float] = None, ceiling=None) -> Callable[[str], Eval]:
     """Grade a source on the environment: status and one speedup sample."""
     def evaluate(s: str) -> Eval:
@@ -76,7 +90,10 @@ def search_from_kernel(src: str, env, *, budget: int = 32, k_expand: int = 4, ma
                        bnb: bool = False, value_fn=None, baseline_ms: Optional[float] = None, task=None,
                        discover: bool = False, eps_budget: Optional[ErrorBudget] = None,
                        incumbent_min_measures: int = 1) -> SearchResult:
-    """Search the rewrites of ``src`` with verified evaluations on ``env``."""
+    """Search the rewrites of ``src`` with verified evaluations on ``env``;
+    ``value_fn="model"`` takes the priors from the value model."""
+    if value_fn == "model":
+        value_fn = model_value_fn(task)
     ceiling = make_roofline_ub_fn(task) if (bnb and task is not None) else None
     pol = TransformProposePolicy(value_fn, discover=discover)
     if eps_budget is None and task is not None:

@@ -102,3 +102,11 @@ def test_propose_fail_safe_on_torch_source():
     pol = TransformProposePolicy()
     assert pol.propose("import torch\n\ndef f(x):\n    return x * 2\n") == []
     assert pol.propose(SRC) and TransformProposePolicy(discover=True).propose(SRC)
+
+
+def test_model_value_prior_is_memoised_and_orders_sources():
+    from kore_b200.search.propose import model_value_fn
+    f = model_value_fn()
+    good = "acc = tl.zeros((BLOCK_M, BLOCK_N), dtype=tl.float32)\nBLOCK_M = 128\nacc += tl.dot(a, b)\n"
+    bad = "BLOCK_M = 8\nacc += tl.sum(a * b)\n"
+    assert f(good) > f(bad) and f(good) == f(good)
