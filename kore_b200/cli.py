@@ -132,6 +132,7 @@ def build_parser() -> argparse.ArgumentParser:
     sub.add_parser("proof", help="smokes and proofs (env, sft, grpo, breadth, ops, grpo-repro)")
     sub.add_parser("study", help="speed-of-light study (eta vs speedup, residual model, monotone valley)")
     sub.add_parser("residual-transfer", help="does the residual model transfer across families")
+    sub.add_parser("study-plots", help="SVG figures of a study report")
     sub.add_parser("calibrate", help="measure HBM copy and bf16 GEMM peaks on this GPU")
     return ap
 
@@ -150,6 +151,7 @@ def main(argv: Optional[List[str]] = None) -> int:
             "study": lambda: __import__("kore_b200.analysis.p0_runner", fromlist=["main"]).main(rest),
             "residual-transfer": lambda: __import__("kore_b200.analysis.residual_transfer",
                                                     fromlist=["main"]).main(rest),
+            "study-plots": lambda: __import__("kore_b200.analysis.plots", fromlist=["main"]).main(rest),
             "calibrate": lambda: __import__("kore_b200.analysis.calibrate", fromlist=["main"]).main(rest),
             "campaign": lambda: __import__("kore_b200.campaign.orchestrator", fromlist=["main"]).main(rest),
             "supervise": lambda: __import__("kore_b200.campaign.supervise", fromlist=["main"]).main(rest)}[args.cmd]()

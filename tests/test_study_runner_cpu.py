@@ -106,3 +106,21 @@ def test_residual_transfer():
     assert not RT.run(bad)["verdict"].startswith("TRANSFERS")
     dec = RT.family_decodability(rs)
     assert 0 <= dec["accuracy"] <= 1 and dec["chance"] == pytest.approx(0.25)
+
+
+def test_study_figures_are_valid_svg(tmp_path):
+    import xml.etree.ElementTree as ET
+
+    from kore_b200.analysis import plots
+    ms = []
+    for r in _records():
+        ms.append(P.KernelMeasure(r.task_id, r.family, "k", "primary", True, 60.0, r.t_measured_ms,
+                                  r.t_measured_ms * r.speedup, r.t_min_ms))
+    rep = json.loads(json.dumps(P.run(ms, iters=50), default=str))
+    paths = plots.write_all(rep, str(tmp_path))
+    assert len(paths) == 3
+    for p in paths:
+        root = ET.parse(p).getroot()
+        assert root.tag.endswith("svg") and len(list(root.iter("{http://www.w3.org/2000/svg}circle"))) > 10
+    empty = plots.scatter_svg({}, title="t", xlabel="x", ylabel="y")
+    assert ET.fromstring(empty).tag.endswith("svg")
