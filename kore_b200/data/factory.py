@@ -53,6 +53,41 @@ BREAKERS: Dict[str, Callable[[str], Optional[str]]] = {
     "drop_store_cast": _sub_first(r"\.to\(Y\.dtype\.element_ty\)", ".to(tl.float16)"),
     "exp_to_exp2": _sub_first(r"tl\.exp\(", "tl.exp2("),
     "half_block": _sub_first(r"BLOCK=triton\.next_power_of_2\(N\)", "BLOCK=triton.next_power_of_2(N) // 2"),
+    "wrong_axis": _sub_first(r"axis=1\)", "axis=0)"),
+    "drop_normalization": _sub_first(r"\s*/\s*N\b", ""),
+    "transpose_strides": _sub_first(r"stride_am, stride_ak", "stride_ak, stride_am"),
+    "drop_scale": _sub_first(r"\s*\*\s*scale\b", ""),
+    "fp8_variant": _sub_first(r"float8e4nv", "float8e5"),
+    # CUDA C++ sources (inline extensions)
+    "drop_syncthreads": _sub_first(r"__syncthreads\(\);", ";"),
+    "cuda_bound_off_by_one": _sub_first(r"(if\s*\(\s*\w+\s*)<(\s*\w+\s*\))", r"\1<=\2"),
+    "wrong_thread_index": _sub_first(r"threadIdx\.x", "threadIdx.y"),
+    "wrong_shuffle_offset": _sub_first(r"(__shfl_xor_sync\([^,]+,[^,]+,\s*)(\w+)", r"\g<1>(\2 + 1)"),
+    "cuda_half_accum": _sub_first(r"\bfloat(\s+acc\b)", r"__half\1"),
+}
+
+# what each breaker does, for analysis of repair data and the teacher's context
+BREAKER_HINTS: Dict[str, str] = {
+    "drop_mask": "a bounds mask was removed: the last partial tile reads / writes out of range",
+    "off_by_one_grid": "the grid misses the last program: rows at the end stay unwritten",
+    "wrong_eps": "the normalisation epsilon is wrong",
+    "fp16_accum": "the accumulator is fp16: long reductions lose precision",
+    "swap_operands": "an operand was replaced by another",
+    "syntax_slip": "a missing colon: the module does not compile",
+    "wrong_reduction": "max instead of sum in a reduction",
+    "drop_store_cast": "the output is cast to the wrong dtype",
+    "exp_to_exp2": "exp2 without the log2(e) scale",
+    "half_block": "the block covers half a row: the tail is not processed",
+    "wrong_axis": "a reduction runs over the wrong axis",
+    "drop_normalization": "the division by N of a mean is missing",
+    "transpose_strides": "an operand is read transposed (strides swapped)",
+    "drop_scale": "a scale factor (softmax / quantisation) is missing",
+    "fp8_variant": "the fp8 encoding is e5m2 instead of e4m3",
+    "drop_syncthreads": "a block barrier was removed: shared-memory race",
+    "cuda_bound_off_by_one": "a bounds check admits one element too many: out-of-range access",
+    "wrong_thread_index": "the y thread index is used instead of x",
+    "wrong_shuffle_offset": "a warp-shuffle reduction uses the wrong lane offset",
+    "cuda_half_accum": "a CUDA accumulator is fp16: precision loss",
 }
 
 

@@ -50,3 +50,26 @@ def test_inductor_corpus_cpu():
     assert len(recs) <= 1
     if recs:
         assert "operator: gen_silu_mul_fp32" in recs[0]["text"]
+
+
+def test_breakers_cover_triton_and_cuda_and_have_hints():
+    import random
+
+    from kore_b200.data.factory import BREAKER_HINTS, BREAKERS, mutate
+    assert set(BREAKERS) == set(BREAKER_HINTS)
+    cu = ("__global__ void k(const float* x, float* y, int n) {\n  __shared__ float s[256];\n"
+          "  int i = blockIdx.x * blockDim.x + threadIdx.x;\n  float acc = 0.f;\n  if (i < n) acc = x[i];\n"
+          "  s[threadIdx.x] = acc;\n  __syncthreads();\n"
+          "  acc += __shfl_xor_sync(0xffffffff, acc, off);\n  y[i] = acc;\n}\n")
+    for name in ("drop_syncthreads", "cuda_bound_off_by_one", "wrong_thread_index", "wrong_shuffle_offset",
+                 "cuda_half_accum"):
+        out = BREAKERS[name](cu)
+        assert out is not None and out != cu, name
+    assert "if (i <= n)" in BREAKERS["cuda_bound_off_by_one"](cu)
+    assert "(off + 1)" in BREAKERS["wrong_shuffle_offset"](cu)
+    tri = "m = tl.sum(x, axis=1) / N\ny = acc * scale\n"
+    assert BREAKERS["wrong_axis"](tri) == "m = tl.sum(x, axis=0) / N\ny = acc * scale\n"
+    assert "/ N" not in BREAKERS["drop_normalization"](tri)
+    assert "scale" not in BREAKERS["drop_scale"](tri)
+    broken, op = mutate(cu, random.Random(0))
+    assert broken != cu and op in BREAKERS
