@@ -95,6 +95,11 @@ def cmd_value(args, rest) -> int:
 
 
 def cmd_eval(args, rest) -> int:
+    """``kore eval --model ...`` (fast_p on a split) or ``kore eval vs-frontier ...``
+    (head-to-head against a frontier model)."""
+    if rest and rest[0] == "vs-frontier":
+        from .eval import vs_frontier
+        return vs_frontier.main(rest[1:])
     from .eval import cli as ecli
     return ecli.main(rest)
 
