@@ -5,7 +5,8 @@
 * DPO: preference pairs from ranked groups (chosen = faster correct kernel).
 * RFT: rejection-sampled fine-tuning set = correct, fastest candidates.
 Rows whose task is in the held-out split are dropped (leakage guard), then
-near-duplicates and low-quality kernels are filtered. CLI:
+near-duplicates and low-quality kernels are filtered; general-replay rows that
+near-duplicate a prompt of the bundled retention evaluations are dropped. CLI:
 ``kore build-datasets {sft,dpo,rft} --inputs a.jsonl,b.jsonl --out out.jsonl``.
 Reference parity: kore/data/build_datasets.py:124-686.
 """
@@ -25,6 +26,35 @@ def _heldout(seed: int = 0) -> set:
     return set(split_tasks(seed)[1])
 
 
+def eval_prompts() -> List[str]:
+    """Prompts of the bundled retention-evaluation sets (no row of a training
+    mix may near-duplicate one of them)."""
+    import glob
+    import json
+    import os
+    root = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "eval", "data")
+    out = []
+    for p in sorted(glob.glob(os.path.join(root, "*.jsonl"))):
+        with open(p) as f:
+            for line in f:
+                try:
+                    d = json.loads(line)
+                except json.JSONDecodeError:
+                    continue
+                for k in ("prompt", "question", "instruction", "turns"):
+                    v = d.get(k)
+                    if isinstance(v, list):
+                        v = "\n".join(str(x) for x in v)
+                    if isinstance(v, str) and len(v) >= 40:
+                        out.append(v)
+                        break
+    return out
+
+
+def _user_text(row: dict) -> str:
+    return "\n".join(m.get("content", "") for m in row.get("messages", []) if m.get("role") == "user")
+
+
 def build_sft(paths: Sequence[str], out: str, *, seed: int = 0, general: Optional[str] = None) -> int:
     held = _heldout(seed)
     rows = []
@@ -41,7 +71,9 @@ def build_sft(paths: Sequence[str], out: str, *, seed: int = 0, general: Optiona
     rows = dedup(rows, key=lambda r: r["messages"][-1]["content"])
     if general:
         from .datasets import read_jsonl
-        rows += read_jsonl(general)
+        from .hygiene import decontaminate
+        # general replay rows must not contain the retention evaluations' prompts
+        rows += decontaminate(read_jsonl(general), eval_prompts(), key=_user_text)
     write_jsonl(out, rows)
     return len(rows)
 

@@ -63,3 +63,21 @@ def test_dagger_and_parallel_datagen(tmp_path):
     assert len(shards) == 2 and {e for _, e in launched} == {"0", "1"}
     tasks = ",".join(c[c.index("--tasks") + 1] for c, _ in launched)
     assert "a" not in tasks.split(",") and sorted(tasks.split(",")) == ["b", "c", "d"]
+
+
+def test_general_replay_is_decontaminated_against_eval_prompts(tmp_path):
+    import json
+
+    from kore_b200.data.build_datasets import build_sft, eval_prompts
+    ev = eval_prompts()
+    assert len(ev) >= 5
+    gen = tmp_path / "general.jsonl"
+    rows = [{"messages": [{"role": "user", "content": ev[0]}, {"role": "assistant", "content": "x"}]},
+            {"messages": [{"role": "user", "content": "Write a haiku about the ocean at dawn, please, "
+                                                      "with a seasonal word."},
+                          {"role": "assistant", "content": "waves"}]}]
+    gen.write_text("\n".join(json.dumps(r) for r in rows) + "\n")
+    out = tmp_path / "sft.jsonl"
+    n = build_sft([], str(out), general=str(gen))
+    kept = [json.loads(l) for l in out.read_text().splitlines()]
+    assert n == 1 and "haiku" in kept[0]["messages"][0]["content"]
