@@ -143,8 +143,8 @@ def measure_kernel(task, label: str, source: str, shape, peaks: Dict[str, float]
             from ..verifier.pmc import METRIC_SETS, ncu_available, ncu_command, parse_ncu_csv
             if ncu_available():
                 for group in METRIC_SETS["grounding"]:
-                    rc, out = runner(ncu_command(group, base + ["--shape", shape.name, "--trials", "1"]), work,
-                                     timeout)
+                    rc, out = runner(ncu_command(group, base + ["--shape", shape.name, "--profile-run", "candidate"],
+                                                 nvtx_range="kore_profile"), work, timeout)
                     m.counters.update(parse_ncu_csv(out))
     return m
 
