@@ -12,6 +12,7 @@ def test_proofs_cpu():
     assert proofs.verify_breadth(limit=60)["ok"]
     assert proofs.repro_grpo_step(world=2, port=29641)["ok"]
     assert proofs.smoke_env(device="cpu")["ok"]            # skipped without a GPU
+    assert proofs.prove_value_cold_start(groups=120, holdout=30)["ok"]
 
 
 def test_datagen_array(tmp_path):
