@@ -120,6 +120,215 @@ def get_inputs():
 def get_init_inputs():
     return [2048]
 ''',
+    ("softmax", 1): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def forward(self, x):
+        return torch.softmax(x, dim=-1)
+
+
+def get_inputs():
+    return [torch.randn(4096, 8192)]
+
+
+def get_init_inputs():
+    return []
+''',
+    ("layernorm", 1): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.ln = nn.LayerNorm(d)
+
+    def forward(self, x):
+        return self.ln(x)
+
+
+def get_inputs():
+    return [torch.randn(8192, 1024)]
+
+
+def get_init_inputs():
+    return [1024]
+''',
+    ("sum_reduce", 1): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def forward(self, x):
+        return x.sum(dim=1)
+
+
+def get_inputs():
+    return [torch.randn(2048, 16384)]
+
+
+def get_init_inputs():
+    return []
+''',
+    ("conv2d", 1): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, cin, cout, k):
+        super().__init__()
+        self.conv = nn.Conv2d(cin, cout, k, padding=k // 2)
+
+    def forward(self, x):
+        return self.conv(x)
+
+
+def get_inputs():
+    return [torch.randn(16, 64, 56, 56)]
+
+
+def get_init_inputs():
+    return [64, 128, 3]
+''',
+    ("batched_matmul", 1): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def forward(self, a, b):
+        return torch.bmm(a, b)
+
+
+def get_inputs():
+    return [torch.randn(32, 512, 256), torch.randn(32, 256, 512)]
+
+
+def get_init_inputs():
+    return []
+''',
+    ("swiglu_mlp", 2): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, d, f):
+        super().__init__()
+        self.gate = nn.Linear(d, f, bias=False)
+        self.up = nn.Linear(d, f, bias=False)
+        self.down = nn.Linear(f, d, bias=False)
+
+    def forward(self, x):
+        return self.down(F.silu(self.gate(x)) * self.up(x))
+
+
+def get_inputs():
+    return [torch.randn(1024, 1024)]
+
+
+def get_init_inputs():
+    return [1024, 2816]
+''',
+    ("matmul_scale_residual", 2): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, n_in, n_out, scale):
+        super().__init__()
+        self.lin = nn.Linear(n_in, n_out)
+        self.scale = scale
+
+    def forward(self, x, r):
+        return self.lin(x) * self.scale + r
+
+
+def get_inputs():
+    return [torch.randn(2048, 1024), torch.randn(2048, 1024)]
+
+
+def get_init_inputs():
+    return [1024, 1024, 0.5]
+''',
+    ("conv_bn_relu", 2): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, c):
+        super().__init__()
+        self.conv = nn.Conv2d(c, c, 3, padding=1, bias=False)
+        self.bn = nn.BatchNorm2d(c)
+
+    def forward(self, x):
+        return torch.relu(self.bn(self.conv(x)))
+
+
+def get_inputs():
+    return [torch.randn(8, 64, 64, 64)]
+
+
+def get_init_inputs():
+    return [64]
+''',
+    ("attention_block", 3): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, d, h):
+        super().__init__()
+        self.h = h
+        self.qkv = nn.Linear(d, 3 * d, bias=False)
+        self.o = nn.Linear(d, d, bias=False)
+
+    def forward(self, x):
+        B, S, D = x.shape
+        q, k, v = self.qkv(x).view(B, S, 3, self.h, D // self.h).permute(2, 0, 3, 1, 4)
+        y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+        return self.o(y.transpose(1, 2).reshape(B, S, D))
+
+
+def get_inputs():
+    return [torch.randn(2, 512, 512)]
+
+
+def get_init_inputs():
+    return [512, 8]
+''',
+    ("transformer_mlp_block", 3): '''import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+
+class Model(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.ln = nn.LayerNorm(d)
+        self.fc1 = nn.Linear(d, 4 * d)
+        self.fc2 = nn.Linear(4 * d, d)
+
+    def forward(self, x):
+        return x + self.fc2(F.gelu(self.fc1(self.ln(x))))
+
+
+def get_inputs():
+    return [torch.randn(4, 256, 512)]
+
+
+def get_init_inputs():
+    return [512]
+''',
 }
 
 

@@ -60,3 +60,14 @@ def test_champion_verdict():
     assert champion_verdict(2.0, correct=True, speedup=1.8, cv_pct=1.0)["certified"]
     v = champion_verdict(2.0, correct=True, correct_unseen=False, speedup=1.0, cv_pct=9.0, hack_reason="cached output")
     assert not v["certified"] and len(v["reasons"]) == 4
+
+
+def test_bundled_kernelbench_problems_cover_three_levels():
+    from kore_b200.eval.kernelbench import _load_module, bundled_specs, spec_to_task
+    specs = bundled_specs()
+    assert len(specs) >= 14 and {s.level for s in specs} == {1, 2, 3}
+    for s in specs:
+        ns = _load_module(s)
+        assert callable(ns["get_inputs"]) and ns["Model"](*ns["get_init_inputs"]()) is not None
+        t = spec_to_task(s, "fp32")
+        assert t.family == f"kernelbench_l{s.level}" and "def kernel(" in t.seed_src
