@@ -67,7 +67,7 @@ def test_kernelbench_adapter_and_leakage():
 
     from kore_b200.eval import kernelbench as KB
     specs = KB.bundled_specs()
-    assert {s.level for s in specs} == {1, 2}
+    assert {s.level for s in specs} == {1, 2, 3}
     t = KB.spec_to_task(specs[0], "fp32")
     from kore_b200.tasks.ops_library import SPECS
     s = SPECS[t.task_id]
