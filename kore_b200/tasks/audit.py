@@ -28,6 +28,7 @@ class DataScaleReport:
     declared_shapes: int
     augmented_shapes: int
     with_roofline: int
+    external: int = 0            # problems registered at run time without an operation model (KernelBench)
 
     def as_dict(self) -> dict:
         return asdict(self)
@@ -48,8 +49,10 @@ def audit(augment_max: int = 6) -> DataScaleReport:
     ts = all_tasks()
     tr, ho = split_tasks()
     fam, dt, oc = Counter(), Counter(), Counter()
-    shapes = aug = roof = 0
+    shapes = aug = roof = ext = 0
     for t in ts:
+        if t.operation == "kernelbench":
+            ext += 1
         fam[t.family] += 1
         dt[t.dtype] += 1
         oc[op_class(t.operation)] += 1
@@ -58,7 +61,7 @@ def audit(augment_max: int = 6) -> DataScaleReport:
         sh = t.shape("primary") or (t.shapes[0] if t.shapes else None)
         if sh is not None and flops_bytes(t.operation, sh.dims, t.dtype) is not None:
             roof += 1
-    return DataScaleReport(len(ts), len(tr), len(ho), dict(fam), dict(dt), dict(oc), shapes, aug, roof)
+    return DataScaleReport(len(ts), len(tr), len(ho), dict(fam), dict(dt), dict(oc), shapes, aug, roof, ext)
 
 
 def main(argv=None) -> int:
