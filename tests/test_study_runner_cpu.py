@@ -124,3 +124,21 @@ def test_study_figures_are_valid_svg(tmp_path):
         assert root.tag.endswith("svg") and len(list(root.iter("{http://www.w3.org/2000/svg}circle"))) > 10
     empty = plots.scatter_svg({}, title="t", xlabel="x", ylabel="y")
     assert ET.fromstring(empty).tag.endswith("svg")
+
+
+def test_study_cli_on_replayed_records(tmp_path):
+    from kore_b200.data.schemas import RankedGroupRecord
+    recs = []
+    for i, tid in enumerate(["gen_silu_bf16", "gen_relu_bf16", "gen_add_bf16", "gen_mul_bf16", "gen_exp_bf16"]):
+        recs.append(RankedGroupRecord(tid, "p", [{"source": "a", "correct": True, "wall_us": 40.0 + 5 * i},
+                                                 {"source": "b", "correct": True, "wall_us": 80.0 + i}],
+                                      [[0, 1]], parent_wall_us=100.0))
+    p = tmp_path / "g.jsonl"
+    p.write_text("\n".join(json.dumps(r.to_dict()) for r in recs) + "\n")
+    out = tmp_path / "p0.json"
+    assert P.main(["--replay", str(p), "--out", str(out), "--iters", "50"]) == 0
+    rep = json.loads(out.read_text())
+    assert rep["n_measured"] == 10 and rep["n_records"] == 10 and "checks" in rep
+    assert (tmp_path / "p0.md").read_text().startswith("# Speed-of-light study")
+    res = RT.run(RT.records_from_report(str(out)))
+    assert "verdict" in res
